@@ -1,0 +1,571 @@
+"""Benchmark of the GDN decode / prefill hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode_b128|decode_b4|decode_b1024|prefill_p1|prefill_p2|prefill_p3]
+
+Prints ONE JSON line (rank 0).  Default workload: one GDN decode step over
+batch 128 (state 128 x 32 x 128 x 128 fp32 = 268 MB read + 268 MB written per
+step), the single-GPU configuration the headline metric is quoted on.  The
+line also carries a ``prefill`` object with the P1 (8 varlen sequences) and P2
+(one 32768-token sequence) prefill measurements.
+
+N > 1 (torchrun, one process per GPU): weak scaling -- every rank runs the
+same per-GPU workload on its own data (decode: 128 sequences per GPU, so N=8
+is the 1024-sequence configuration sharded by batch; prefill: the 64-sequence
+P3 set sharded by sequence with longest-first bin packing); there is no
+collective on the data path.  Time is the max over ranks of the device time.
+
+Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
+the launching stream, barrier + synchronize on both sides.  Inputs are larger
+than L2 (126 MB) and decode ping-pongs its state between two buffers.
+``--impl reference`` times the CPU restatement of the reference's algorithm
+(the oracle port; the reference itself is Triton-only and has no CPU path) on
+the host's cores, on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+PKG_NAME = "mlsys26-flashinfer-ai-kernel-generation-contest_b200"
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# --------------------------------------------------------------------------- helpers
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes (read + write) of the dominant kernel from the committed
+    ncu summary (profiles/ncu_traffic.txt: lines 'workload bytes ...')."""
+    p = REPO / "profiles" / "ncu_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == workload and not line.startswith("#"):
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during the timed region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], set()
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            # map the torch device to its NVML handle through the GPU UUID
+            self.h = None
+            uuid = getattr(torch.cuda.get_device_properties(device_index), "uuid", None)
+            if uuid is not None:
+                try:
+                    self.h = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}".encode())
+                except Exception:
+                    self.h = None
+            if self.h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[device_index]) if vis else device_index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _sample(self):
+        nv = self.nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        for bit, name in self.REASONS.items():
+            if r & bit:
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if s > 0]
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl"):
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            if torch.cuda.is_available() and self.pg.get_backend() == "nccl":
+                self.pg.barrier(device_ids=[self.local])
+            else:
+                self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        dev = torch.device("cuda", self.local) if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def lpt_shard(lengths, n):
+    """Longest-processing-time bin packing of sequence indices onto n ranks."""
+    bins = [[] for _ in range(n)]
+    load = [0] * n
+    for i in sorted(range(len(lengths)), key=lambda i: -lengths[i]):
+        j = min(range(n), key=lambda j: load[j])
+        bins[j].append(i)
+        load[j] += lengths[i]
+    return [sorted(b) for b in bins]
+
+
+# --------------------------------------------------------------------------- workloads
+class DecodeWork:
+    """One decode step over `batch` sequences; state ping-pongs between two buffers."""
+
+    def __init__(self, pkg, batch, dev, seed):
+        W = pkg.workloads
+        self.pkg, self.batch, self.dev = pkg, batch, dev
+        inp = W.decode_inputs(batch, seed=seed, device=str(dev))
+        self.inp = inp
+        self.s = [inp["state"], torch.empty_like(inp["state"])]
+        self.out = torch.empty_like(inp["v"])
+        self.i = 0
+        self.units = W.decode_state_bytes(batch)     # algorithmic bytes per step
+        self.io_bytes = W.decode_io_bytes(batch)
+        self.launches = 1
+
+    def step(self):
+        d = self.inp
+        src, dst = self.s[self.i], self.s[1 - self.i]
+        self.pkg.gdn_decode(d["q"], d["k"], d["v"], src, d["A_log"], d["a"], d["dt_bias"],
+                            d["b"], d["scale"], self.out, dst, use_qk_l2norm=True)
+        self.i ^= 1
+
+    def host_copies(self):
+        """Pinned host copies for the end-to-end leg."""
+        d = self.inp
+        self.h = {k: d[k].cpu().pin_memory() for k in ("q", "k", "v", "state", "a", "b")}
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h_ns = torch.empty(d["state"].shape, dtype=torch.float32).pin_memory()
+        self.d_in = {k: torch.empty_like(d[k]) for k in self.h}
+        self.d_ns = torch.empty_like(d["state"])
+        h2d = sum(t.numel() * t.element_size() for t in self.h.values())
+        d2h = self.h_out.numel() * 2 + self.h_ns.numel() * 4
+        return h2d, d2h
+
+    def e2e_step(self):
+        """Host inputs -> device -> the DPS entry point -> host outputs."""
+        di = self.d_in
+        for k_, t in self.h.items():
+            di[k_].copy_(t, non_blocking=True)
+        d = self.inp
+        self.pkg.decode_kernel(di["q"], di["k"], di["v"], di["state"], d["A_log"], di["a"],
+                               d["dt_bias"], di["b"], d["scale"], self.out, self.d_ns)
+        self.h_out.copy_(self.out, non_blocking=True)
+        self.h_ns.copy_(self.d_ns, non_blocking=True)
+
+
+class PrefillWork:
+    def __init__(self, pkg, cfg_name, dev, seed, shard=None):
+        W = pkg.workloads
+        self.pkg, self.dev = pkg, dev
+        inp = W.prefill_config_inputs(cfg_name, seed=seed, device="cpu")
+        cu = inp["cu_seqlens"].tolist()
+        lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
+        if shard is not None:
+            idx = shard
+            parts = [(cu[i], cu[i + 1]) for i in idx]
+            take = torch.cat([torch.arange(a, b) for a, b in parts]) if parts else \
+                torch.zeros(0, dtype=torch.long)
+            lens = [lens[i] for i in idx]
+            for k_ in ("q", "k", "v", "a", "b"):
+                inp[k_] = inp[k_][take].contiguous()
+            if inp["state"] is not None:
+                inp["state"] = inp["state"][idx].contiguous()
+            c = torch.zeros(len(lens) + 1, dtype=torch.int32)
+            if lens:
+                c[1:] = torch.tensor(lens).cumsum(0)
+            inp["cu_seqlens"] = c
+        self.lens = lens
+        self.inp = {k_: (v_.to(dev) if isinstance(v_, torch.Tensor) else v_) for k_, v_ in inp.items()}
+        self.cpu_inp = inp
+        T = self.inp["q"].shape[0]
+        N = len(lens)
+        self.out = torch.empty(T, self.inp["v"].shape[1], 128, dtype=torch.bfloat16, device=dev)
+        self.ns = torch.empty(N, self.inp["v"].shape[1], 128, 128, dtype=torch.float32, device=dev)
+        self.tokens = T
+        self.flops = T * W.prefill_flops_per_token()
+        self.launches = pkg.prefill.launches_per_call(T, N)
+
+    def step(self):
+        d = self.inp
+        self.pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
+                             d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
+                             use_qk_l2norm=True)
+
+    def host_copies(self):
+        d = self.inp
+        keys = [k_ for k_ in ("q", "k", "v", "state", "a", "b", "cu_seqlens") if d[k_] is not None]
+        self.h = {k_: d[k_].cpu().pin_memory() for k_ in keys}
+        self.d_in = {k_: torch.empty_like(d[k_]) for k_ in keys}
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h_ns = torch.empty(self.ns.shape, dtype=torch.float32).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in self.h.values())
+        d2h = self.h_out.numel() * 2 + self.h_ns.numel() * 4
+        return h2d, d2h
+
+    def e2e_step(self):
+        di = self.d_in
+        for k_, t in self.h.items():
+            di[k_].copy_(t, non_blocking=True)
+        d = self.inp
+        self.pkg.prefill_kernel(di["q"], di["k"], di["v"], di.get("state"), d["A_log"], di["a"],
+                                d["dt_bias"], di["b"], di["cu_seqlens"], d["scale"], self.out,
+                                self.ns)
+        self.h_out.copy_(self.out, non_blocking=True)
+        self.h_ns.copy_(self.ns, non_blocking=True)
+
+
+# --------------------------------------------------------------------------- timing
+def time_steps(fn, steps, warmup, dist, per_launch_events=True):
+    """Returns (max-over-ranks ms per step, mean kernel ms per step on this rank)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)] if per_launch_events else []
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        if per_launch_events:
+            ev[i][0].record(stream)
+        fn()
+        if per_launch_events:
+            ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    total = t0.elapsed_time(t1)
+    per_kernel = (sum(a.elapsed_time(b) for a, b in ev) / steps) if ev else total / steps
+    return dist.max(total) / steps, per_kernel
+
+
+def cpu_baseline_decode(batch, budget_s=10.0):
+    from oracle import gdn_oracle as O
+    pkg = importlib.import_module(PKG_NAME)
+    W = pkg.workloads
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    inp = W.decode_inputs(batch, seed=0)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+    O.decode(q[:1], k[:1], inp["v"][:1], inp["state"][:1], inp["A_log"], inp["a"][:1],
+             inp["dt_bias"], inp["b"][:1], inp["scale"])  # warm
+    reps, t_start = 0, time.perf_counter()
+    while True:
+        O.decode(q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                 inp["scale"])
+        reps += 1
+        el = time.perf_counter() - t_start
+        if el > budget_s or reps >= 5:
+            break
+    per = el / reps
+    gbs = W.decode_state_bytes(batch) / per / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full decode step(s) of batch {batch} (oracle, fp32 torch CPU)",
+            "sec_per_step": per}
+
+
+def cpu_baseline_prefill(cfg_name, budget_tokens=4096):
+    from oracle import gdn_oracle as O
+    pkg = importlib.import_module(PKG_NAME)
+    W = pkg.workloads
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    inp = W.prefill_config_inputs(cfg_name, seed=0)
+    cu = inp["cu_seqlens"].tolist()
+    n = 1
+    while n < len(cu) - 1 and cu[n] < budget_tokens:
+        n += 1
+    T = min(cu[n], budget_tokens)
+    sub_cu = torch.tensor([min(c, T) for c in cu[:n + 1]], dtype=torch.int32)
+    st = inp["state"][:n] if inp["state"] is not None else None
+    q, k = O.l2norm(inp["q"][:T]), O.l2norm(inp["k"][:T])
+    t0 = time.perf_counter()
+    O.prefill(q, k, inp["v"][:T], st, inp["A_log"], inp["a"][:T], inp["dt_bias"], inp["b"][:T],
+              sub_cu, inp["scale"])
+    el = time.perf_counter() - t0
+    return {"value": T / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"first {T} tokens of {cfg_name} ({n} sequence(s); oracle, fp32 torch CPU)"}
+
+
+# --------------------------------------------------------------------------- arms
+def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True):
+    w = DecodeWork(pkg, batch, dev, seed=dist.rank)
+    with ClockSampler(dev.index) as clk:
+        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+    total_bytes = w.units * dist.world
+    res = {"ms": ms, "kern_ms": kern_ms, "value": total_bytes / (ms * 1e-3) / 1e9,
+           "achieved": w.units / (kern_ms * 1e-3) / 1e9, "clocks": clk.summary(),
+           "launches": w.launches * steps, "units": w.units}
+    if with_e2e:
+        h2d, d2h = w.host_copies()
+        e2e_steps = max(3, min(steps, 20))
+        e_ms, _ = time_steps(w.e2e_step, e2e_steps, 2, dist, per_launch_events=False)
+        res["e2e"] = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "ms_per_step": e_ms, "steps": e2e_steps}
+    return res
+
+
+def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True):
+    w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard)
+    with ClockSampler(dev.index) as clk:
+        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+    tokens_all = w.tokens
+    if dist.pg:
+        t = torch.tensor([w.tokens], dtype=torch.float64, device=dev)
+        dist.pg.all_reduce(t)
+        tokens_all = int(t.item())
+    res = {"ms": ms, "kern_ms": kern_ms, "value": tokens_all / (ms * 1e-3),
+           "tflops": tokens_all * pkg.workloads.prefill_flops_per_token() / (ms * 1e-3) / 1e12,
+           "achieved": w.flops / (kern_ms * 1e-3) / 1e12, "clocks": clk.summary(),
+           "launches": w.launches * steps, "tokens": w.tokens, "tokens_all": tokens_all}
+    if with_e2e:
+        h2d, d2h = w.host_copies()
+        e2e_steps = max(2, min(steps, 5))
+        e_ms, _ = time_steps(w.e2e_step, e2e_steps, 1, dist, per_launch_events=False)
+        res["e2e"] = {"value": tokens_all / (e_ms * 1e-3), "unit": "tokens/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "ms_per_step": e_ms, "steps": e2e_steps}
+    return res
+
+
+def roofline(bound, achieved, workload, pk, src):
+    if bound == "hbm":
+        peak, unit = pk["hbm_gbs"], "GB/s"
+    else:
+        peak, unit = pk["bf16_tflops"], "TFLOP/s"
+    return {"bound": bound, "achieved": round(achieved, 3), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": ncu_traffic(workload),
+            "peak_source": f"{src} (burst; MEASURED_PEAKS.json)" if src == "measured"
+            else "fallback (no MEASURED_PEAKS.json)"}
+
+
+WORKLOADS = {
+    "decode_b4": ("decode", 4), "decode_b128": ("decode", 128), "decode_b1024": ("decode", 1024),
+    "prefill_p1": ("prefill", "P1"), "prefill_p2": ("prefill", "P2"),
+    "prefill_p3": ("prefill", "P3"),
+}
+
+
+def run_ours(args, dist):
+    pkg = importlib.import_module(PKG_NAME)
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    pk, src = peaks()
+    kind, param = WORKLOADS[args.workload]
+    line = {"impl": "ours"}
+    if kind == "decode":
+        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev)
+        line.update({
+            "metric": "decode state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+            "config": {"workload": f"GDN decode, batch {param} per GPU, 16 q/k + 32 v heads, "
+                                   f"head_dim 128, fp32 k-last state, q/k L2-normalised in-kernel",
+                       "batch_per_gpu": param, "global_batch": param * dist.world,
+                       "parallelism": f"batch-sharded x{dist.world}, no collective",
+                       "l2": "inputs > L2: 537 MB state traffic per step, state ping-pong"},
+            "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
+            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
+            "kernel_ms": round(r["kern_ms"], 5),
+        })
+    else:
+        shard = None
+        if dist.world > 1:
+            W = pkg.workloads
+            cfg = W.PREFILL_CONFIGS[param]
+            lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
+            shard = lpt_shard(lens, dist.world)[dist.rank]
+        r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
+        line.update({
+            "metric": "prefill tokens/s", "value": round(r["value"], 1), "unit": "tokens/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms"], 5), "higher_is_better": True,
+            "scaling": "strong" if dist.world > 1 else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": f"GDN prefill {param}", "tokens": r["tokens_all"],
+                       "parallelism": f"sequence-sharded x{dist.world} (LPT), no collective",
+                       "l2": "inputs > L2"},
+            "tflops": round(r["tflops"], 2),
+            "roofline": roofline("tensor", r["achieved"], args.workload, pk, src),
+            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
+            "kernel_ms": round(r["kern_ms"], 5),
+        })
+    # secondary: the prefill configurations next to the decode headline
+    if kind == "decode" and not args.no_prefill_extra:
+        extra = {}
+        names = ["P1", "P2"] if dist.world == 1 else ["P3"]
+        for nm in names:
+            shard = None
+            if dist.world > 1:
+                W = pkg.workloads
+                cfg = W.PREFILL_CONFIGS[nm]
+                shard = lpt_shard(W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0), dist.world)[dist.rank]
+            r = measure_prefill(pkg, dist, nm, max(3, min(args.steps, 10)), 3, dev, shard=shard,
+                                with_e2e=False)
+            extra[nm] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
+                         "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
+                         "roofline": roofline("tensor", r["achieved"], "prefill_" + nm.lower(),
+                                              pk, src)}
+        line["prefill"] = extra
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = (cpu_baseline_decode(param) if kind == "decode"
+                                else cpu_baseline_prefill(param))
+    return line
+
+
+def run_reference(args, dist):
+    """The reference's CPU path (oracle port) on the host cores, same workload/metric."""
+    if dist.rank != 0:
+        return None
+    kind, param = WORKLOADS[args.workload]
+    steps = []
+    if kind == "decode":
+        for _ in range(max(1, min(args.steps, 3))):
+            steps.append(cpu_baseline_decode(param, budget_s=5.0))
+        v = statistics.median(s["value"] for s in steps)
+        metric, unit = "decode state-traffic GB/s", "GB/s"
+        ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3
+    else:
+        for _ in range(max(1, min(args.steps, 2))):
+            steps.append(cpu_baseline_prefill(param))
+        v = statistics.median(s["value"] for s in steps)
+        metric, unit = "prefill tokens/s", "tokens/s"
+        ms = None
+    cb = dict(steps[0])
+    cb["value"] = v
+    cb.pop("sec_per_step", None)
+    return {"impl": "reference", "metric": metric, "value": round(v, 4), "unit": unit,
+            "n_gpus": dist.world, "steps": len(steps), "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic (seeded)",
+            "config": {"workload": args.workload, "note": "reference has no CPU path; the CPU "
+                       "restatement of its algorithm (oracle port) is timed"},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_b128")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill-extra", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+    dist = Dist()
+    if args.impl == "reference":
+        line = run_reference(args, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "error": "no CUDA device"}), flush=True)
+        sys.exit(1)
+    dist.init("nccl")
+    try:
+        line = run_ours(args, dist)
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,119 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet decode / prefill kernels.
+ *
+ * These entry points replace the two solution entry points of the reference
+ * repository (flashinfer-bench "destination passing style" callables):
+ *
+ *   gdn_decode_launch   <- gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale,
+ *                                      output, new_state)
+ *                          gdn_decode/solution/triton/kernel.py:221-272
+ *                          (entry point named in gdn_decode/config.toml:8)
+ *   gdn_prefill_launch  <- gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+ *                                       scale, output, new_state)
+ *                          gdn_prefill/solution/triton/kernel.py:253-337
+ *                          (entry point named in gdn_prefill/config.toml:8)
+ *
+ * and fill the empty CUDA template the reference ships for that purpose
+ * (gdn_decode/solution/cuda/kernel.cu:13-20, binding.py:14-25).
+ *
+ * Conventions (all entry points):
+ *   - Every tensor pointer is a DEVICE pointer to a dense, contiguous
+ *     (row-major) buffer on the device that is current for the calling thread.
+ *     bf16 tensors are passed as `const void*` / `void*` (IEEE bfloat16, 2 bytes).
+ *   - head_size must be 128; num_q_heads == num_k_heads; num_v_heads is a
+ *     multiple of num_q_heads (GVA: v-head h reads q/k head h / (HV/HQ)).
+ *   - `state` may be NULL, meaning an all-zero initial state.
+ *   - `scale` <= 0 (or NaN) means 1/sqrt(head_size), matching the reference's
+ *     "scale is None or scale == 0.0" default.
+ *   - `use_qk_l2norm` != 0 normalises q and k over head_dim in fp32,
+ *     x * rsqrt(sum(x^2) + 1e-6), before use.  0 reproduces the reference
+ *     (which does not normalise).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Launches are
+ *     asynchronous; no entry point synchronises, allocates, or reads device
+ *     memory on the host.
+ *   - Return value: GDN_OK (0) or a negative GDN_ERR_* code.  Nothing is
+ *     launched when an argument check fails.  No entry point aborts the process.
+ *   - new_state may alias state (in-place update is supported); outputs must
+ *     not otherwise overlap inputs.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_OK 0
+#define GDN_ERR_INVALID_ARGUMENT (-1) /* null pointer, bad size, misalignment     */
+#define GDN_ERR_UNSUPPORTED (-2)      /* head_size != 128, bad head ratio, ...    */
+#define GDN_ERR_LAUNCH (-3)           /* the CUDA launch itself reported an error */
+#define GDN_ERR_WORKSPACE (-4)        /* workspace missing or too small           */
+
+/* Library version, e.g. 100 for 0.1.0. */
+int gdn_b200_version(void);
+
+/* Human-readable name of a GDN_* status code (static storage). */
+const char* gdn_status_string(int status);
+
+/*
+ * One decode step (seq_len == 1) for `batch` sequences.
+ *   q       bf16 [batch, 1, num_q_heads, 128]
+ *   k       bf16 [batch, 1, num_k_heads, 128]
+ *   v       bf16 [batch, 1, num_v_heads, 128]
+ *   state   fp32 [batch, num_v_heads, 128 (v), 128 (k)]  (k-last) or NULL
+ *   A_log   fp32 [num_v_heads];  dt_bias fp32 [num_v_heads]
+ *   a, b    bf16 [batch, 1, num_v_heads]
+ *   output  bf16 [batch, 1, num_v_heads, 128]                       (written)
+ *   new_state fp32 [batch, num_v_heads, 128, 128]                   (written)
+ * Replaces gdn_decode_kernel (gdn_decode/solution/triton/kernel.py:71-218).
+ * batch == 0 is a no-op that returns GDN_OK.
+ */
+int gdn_decode_launch(const void* q, const void* k, const void* v, const float* state,
+                      const float* A_log, const void* a, const float* dt_bias, const void* b,
+                      float scale, void* output, float* new_state, int batch,
+                      int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+                      int use_qk_l2norm, void* stream);
+
+/*
+ * Bytes of device workspace gdn_prefill_launch needs for this problem (may be 0).
+ * `max_seqlen` is an upper bound on any single sequence length (total_tokens is
+ * always a valid bound).
+ */
+size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
+                                  int num_v_heads, int head_size);
+
+/*
+ * Variable-length prefill over `num_seqs` packed sequences.
+ *   q        bf16 [total_tokens, num_q_heads, 128]
+ *   k        bf16 [total_tokens, num_k_heads, 128]
+ *   v        bf16 [total_tokens, num_v_heads, 128]
+ *   state    fp32 [num_seqs, num_v_heads, 128, 128] (k-last) or NULL
+ *   A_log    fp32 [num_v_heads];  dt_bias fp32 [num_v_heads]
+ *   a, b     bf16 [total_tokens, num_v_heads]
+ *   cu_seqlens int32 (cu_seqlens_int64 == 0) or int64 [num_seqs + 1], on the device,
+ *            non-decreasing, cu_seqlens[0] == 0, cu_seqlens[num_seqs] == total_tokens
+ *   output   bf16 [total_tokens, max(num_q_heads, num_v_heads), 128]  (written)
+ *   new_state fp32 [num_seqs, max(num_q_heads, num_v_heads), 128, 128] (written)
+ *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes
+ *              (may be NULL when that size is 0)
+ * A sequence of length 0 gets an all-zero new_state slice (as the
+ * flashinfer-bench definition reference does).
+ * Replaces gdn_prefill_chunk_kernel (gdn_prefill/solution/triton/kernel.py:28-250)
+ * and its host wrapper's zero-fill / state copy passes (:281-299).
+ */
+int gdn_prefill_launch(const void* q, const void* k, const void* v, const float* state,
+                       const float* A_log, const void* a, const float* dt_bias, const void* b,
+                       const void* cu_seqlens, int cu_seqlens_int64, float scale,
+                       void* output, float* new_state, int total_tokens, int num_seqs,
+                       int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+                       int use_qk_l2norm, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* GDN_B200_H_ */

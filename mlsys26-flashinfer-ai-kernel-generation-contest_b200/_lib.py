@@ -1,0 +1,60 @@
+"""ctypes binding of the in-tree C-ABI library ``libgdn_b200.so`` (see include/gdn_b200.h).
+
+There is deliberately no fallback: if the library is missing the import fails
+with instructions to build it, and a failing launch raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libgdn_b200.so"
+
+GDN_OK = 0
+GDN_ERR_INVALID_ARGUMENT = -1
+GDN_ERR_UNSUPPORTED = -2
+GDN_ERR_LAUNCH = -3
+GDN_ERR_WORKSPACE = -4
+
+# Every symbol include/gdn_b200.h declares, with its ctypes signature.
+_vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+SIGNATURES = {
+    "gdn_b200_version": (_i, []),
+    "gdn_status_string": (ctypes.c_char_p, [_i]),
+    "gdn_decode_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
+                               _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "gdn_prefill_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp,
+                                _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH.name} is not built; run `python __graft_entry__.py` or "
+            f"`python {_PKG.name}/build.py` (needs nvcc with sm_100a support)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+LIB = _load()
+
+
+class GDNError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, where: str, status: int):
+        name = LIB.gdn_status_string(status).decode()
+        super().__init__(f"{where} failed: {name} ({status})")
+        self.status = status
+
+
+def check(where: str, status: int) -> None:
+    if status != GDN_OK:
+        raise GDNError(where, status)

@@ -1,0 +1,62 @@
+// Shared device helpers for the GDN sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gdn_b200.h"
+
+namespace gdn {
+
+constexpr int kHeadDim = 128;
+constexpr float kL2NormEps = 1e-6f;
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// Two packed bf16 (low half first in memory) -> two floats.
+__device__ __forceinline__ float2 bf2x2_to_f2(uint32_t u) {
+  float2 r;
+  r.x = __uint_as_float(u << 16);
+  r.y = __uint_as_float(u & 0xffff0000u);
+  return r;
+}
+
+// Per-token gates, fp32, as the definition reference computes them:
+//   g = exp(-exp(A_log) * softplus(a + dt_bias)),  softplus(x) = x for x > 20
+//   beta = sigmoid(b)
+// (flashinfer/trace/templates/gdn.py:51-53; reference decode kernel.py:122-131)
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float gate_log_g(float A_log, float a, float dt_bias) {
+  return -expf(A_log) * softplus_f(a + dt_bias);
+}
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
+// Streaming 128-bit global accesses: the state is touched exactly once.
+__device__ __forceinline__ float4 ld_stream_f4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream_f4(float* p, float4 v) {
+  asm volatile("st.global.L1::no_allocate.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float xor_sum8(float x) {
+  // Sum over the 8 lanes of an aligned 8-lane group.
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  return x;
+}
+
+__host__ __device__ inline float default_scale(float scale) {
+  // scale <= 0 or NaN -> 1/sqrt(128)
+  return (scale > 0.f) ? scale : 0.08838834764831845f;
+}
+
+}  // namespace gdn

@@ -1,0 +1,201 @@
+// GDN decode for sm_100a: one fused, single-pass HBM-streaming kernel.
+//
+// Replaces gdn_decode_kernel (reference gdn_decode/solution/triton/kernel.py:71-218).
+// Per (batch b, v-head h) the state S[v, k] (k-last, 128 x 128 fp32 = 64 KiB) is
+// read once and written once.  For every row v:
+//   sk = S[v,:].k   sq = S[v,:].q            (one shuffle-reduction pass)
+//   old = g * sk ;  delta = beta * (v_v - old)
+//   S'[v,:] = g * S[v,:] + delta * k
+//   o_v = scale * S'[v,:].q = scale * (g * sq + delta * (k.q))
+// so the output needs no second pass over the state (the reference's two-pass
+// K-tiled configurations re-read it, kernel.py:176-213).
+//
+// Thread mapping: 8 lanes own one 512-byte state row, each lane 4 float4 at
+// columns 4j + 32m (j = lane % 8, m = 0..3), so every 128-bit load instruction of
+// a warp covers four fully used 128-byte segments.  A warp owns RPW rows, a CTA
+// of 8 warps owns 8*RPW rows of one head; all of a thread's state loads are
+// issued before any arithmetic so each SM keeps ~64-128 KiB in flight.
+#include "gdn_common.cuh"
+
+namespace gdn {
+namespace {
+
+template <int RPW, bool L2NORM, bool HAS_STATE>
+__global__ void __launch_bounds__(256)
+    decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                  const __nv_bfloat16* __restrict__ v, const float* state,
+                  const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
+                  const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ b,
+                  float scale, __nv_bfloat16* __restrict__ out, float* new_state, int HQ,
+                  int HV, int ratio) {
+  constexpr int ROWS = 8 * RPW;            // state rows per CTA
+  constexpr int VSPLIT = kHeadDim / ROWS;  // CTAs per (b, h)
+  constexpr int NG = RPW / 4;              // 4-row groups per warp
+  const int cta = blockIdx.x;
+  const int bh = cta / VSPLIT;
+  const int vs = cta - bh * VSPLIT;
+  const int bidx = bh / HV;
+  const int h = bh - bidx * HV;
+  const int qh = h / ratio;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;
+  const int j = lane & 7;
+  const int row0 = vs * ROWS + warp * RPW + sub;  // rows row0 + 4r, r < NG
+  const size_t head_base = (size_t)bh * kHeadDim * kHeadDim;
+
+  // ---- issue the state loads first ----
+  float4 S[NG][4];
+  if constexpr (HAS_STATE) {
+    const float* sp = state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+#pragma unroll
+    for (int r = 0; r < NG; ++r)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) S[r][m] = ld_stream_f4(sp + r * 4 * kHeadDim + m * 32);
+  } else {
+#pragma unroll
+    for (int r = 0; r < NG; ++r)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) S[r][m] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  // ---- q, k slices (16 elements per lane), v values, gates ----
+  float kf[16], qf[16];
+  {
+    const __nv_bfloat16* qp = q + ((size_t)bidx * HQ + qh) * kHeadDim + 4 * j;
+    const __nv_bfloat16* kp = k + ((size_t)bidx * HQ + qh) * kHeadDim + 4 * j;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint2 uq = __ldg(reinterpret_cast<const uint2*>(qp + 32 * m));
+      const uint2 uk = __ldg(reinterpret_cast<const uint2*>(kp + 32 * m));
+      float2 t;
+      t = bf2x2_to_f2(uq.x); qf[4 * m + 0] = t.x; qf[4 * m + 1] = t.y;
+      t = bf2x2_to_f2(uq.y); qf[4 * m + 2] = t.x; qf[4 * m + 3] = t.y;
+      t = bf2x2_to_f2(uk.x); kf[4 * m + 0] = t.x; kf[4 * m + 1] = t.y;
+      t = bf2x2_to_f2(uk.y); kf[4 * m + 2] = t.x; kf[4 * m + 3] = t.y;
+    }
+  }
+  float vv[NG];
+  const __nv_bfloat16* vp = v + (size_t)bh * kHeadDim + row0;
+#pragma unroll
+  for (int r = 0; r < NG; ++r) vv[r] = bf2f(vp[4 * r]);
+  const float g = expf(gate_log_g(__ldg(A_log + h), bf2f(a[bh]), __ldg(dt_bias + h)));
+  const float beta = sigmoid_f(bf2f(b[bh]));
+
+  if constexpr (L2NORM) {
+    float ssk = 0.f, ssq = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      ssk = fmaf(kf[e], kf[e], ssk);
+      ssq = fmaf(qf[e], qf[e], ssq);
+    }
+    ssk = xor_sum8(ssk);
+    ssq = xor_sum8(ssq);
+    const float rk = rsqrtf(ssk + kL2NormEps);
+    const float rq = rsqrtf(ssq + kL2NormEps);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      kf[e] *= rk;
+      qf[e] *= rq;
+    }
+  }
+  float kq = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) kq = fmaf(kf[e], qf[e], kq);
+  kq = xor_sum8(kq);
+
+  scale = default_scale(scale);
+  float* nsp = new_state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+  __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
+#pragma unroll
+  for (int r = 0; r < NG; ++r) {
+    float sk = 0.f, sq = 0.f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float4 s = S[r][m];
+      sk = fmaf(s.x, kf[4 * m + 0], sk); sq = fmaf(s.x, qf[4 * m + 0], sq);
+      sk = fmaf(s.y, kf[4 * m + 1], sk); sq = fmaf(s.y, qf[4 * m + 1], sq);
+      sk = fmaf(s.z, kf[4 * m + 2], sk); sq = fmaf(s.z, qf[4 * m + 2], sq);
+      sk = fmaf(s.w, kf[4 * m + 3], sk); sq = fmaf(s.w, qf[4 * m + 3], sq);
+    }
+    sk = xor_sum8(sk);
+    sq = xor_sum8(sq);
+    const float old = g * sk;
+    const float delta = beta * (vv[r] - old);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      float4 s = S[r][m];
+      s.x = fmaf(g, s.x, delta * kf[4 * m + 0]);
+      s.y = fmaf(g, s.y, delta * kf[4 * m + 1]);
+      s.z = fmaf(g, s.z, delta * kf[4 * m + 2]);
+      s.w = fmaf(g, s.w, delta * kf[4 * m + 3]);
+      st_stream_f4(nsp + r * 4 * kHeadDim + m * 32, s);
+    }
+    if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
+  }
+}
+
+template <int RPW>
+cudaError_t launch_rpw(const void* q, const void* k, const void* v, const float* state,
+                       const float* A_log, const void* a, const float* dt_bias, const void* b,
+                       float scale, void* out, float* new_state, int batch, int HQ, int HV,
+                       bool l2norm, cudaStream_t stream) {
+  constexpr int VSPLIT = kHeadDim / (8 * RPW);
+  const long long ctas = (long long)batch * HV * VSPLIT;
+  const dim3 grid((unsigned)ctas), block(256);
+  const int ratio = HV / HQ;
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  auto A = static_cast<const __nv_bfloat16*>(a);
+  auto Bt = static_cast<const __nv_bfloat16*>(b);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  if (state != nullptr) {
+    if (l2norm)
+      decode_kernel<RPW, true, true><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+    else
+      decode_kernel<RPW, false, true><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+  } else {
+    if (l2norm)
+      decode_kernel<RPW, true, false><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+    else
+      decode_kernel<RPW, false, false><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+  }
+  return cudaGetLastError();
+}
+
+inline bool misaligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) != 0; }
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_decode_launch(const void* q, const void* k, const void* v, const float* state,
+                                 const float* A_log, const void* a, const float* dt_bias,
+                                 const void* b, float scale, void* output, float* new_state,
+                                 int batch, int num_q_heads, int num_k_heads, int num_v_heads,
+                                 int head_size, int use_qk_l2norm, void* stream) {
+  using namespace gdn;
+  if (batch < 0 || num_q_heads <= 0 || num_k_heads <= 0 || num_v_heads <= 0)
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (head_size != kHeadDim || num_k_heads != num_q_heads || num_v_heads % num_q_heads != 0)
+    return GDN_ERR_UNSUPPORTED;
+  if (batch == 0) return GDN_OK;
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
+      misaligned(new_state, 16) || (state && misaligned(state, 16)))
+    return GDN_ERR_INVALID_ARGUMENT;
+  const long long heads = (long long)batch * num_v_heads;
+  if (heads * 4 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool l2 = use_qk_l2norm != 0;
+  cudaError_t err;
+  // Enough CTAs to fill 148 SMs several times over; bigger CTAs when there are.
+  if (heads >= 4 * 148)
+    err = launch_rpw<16>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+  else if (heads >= 2 * 148)
+    err = launch_rpw<8>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+  else
+    err = launch_rpw<4>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}

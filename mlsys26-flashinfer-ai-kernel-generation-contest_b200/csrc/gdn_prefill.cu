@@ -1,0 +1,58 @@
+// C-ABI entry point of the GDN prefill: argument checks and kernel selection.
+//
+// Replaces the reference host wrapper gdn_prefill (reference
+// gdn_prefill/solution/triton/kernel.py:253-337).  Unlike that wrapper it
+// needs no output zero-fill pass and no state -> new_state copy pass: every
+// output row of every token and every new_state slice (zero for an empty
+// sequence) is written by the kernels themselves.
+#include "gdn_common.cuh"
+#include "gdn_prefill.cuh"
+
+namespace {
+inline bool misaligned(const void* p, uintptr_t n) {
+  return (reinterpret_cast<uintptr_t>(p) % n) != 0;
+}
+}  // namespace
+
+extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
+                                             int num_v_heads, int head_size) {
+  (void)total_tokens;
+  (void)num_seqs;
+  (void)num_q_heads;
+  (void)num_v_heads;
+  (void)head_size;
+  return 0;
+}
+
+extern "C" int gdn_prefill_launch(const void* q, const void* k, const void* v, const float* state,
+                                  const float* A_log, const void* a, const float* dt_bias,
+                                  const void* b, const void* cu_seqlens, int cu_seqlens_int64,
+                                  float scale, void* output, float* new_state, int total_tokens,
+                                  int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+                                  int head_size, int use_qk_l2norm, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  using namespace gdn;
+  if (total_tokens < 0 || num_seqs < 0 || num_q_heads <= 0 || num_k_heads <= 0 ||
+      num_v_heads <= 0)
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (head_size != kHeadDim || num_k_heads != num_q_heads || num_v_heads % num_q_heads != 0)
+    return GDN_ERR_UNSUPPORTED;
+  if (num_seqs == 0) return GDN_OK;
+  if (!cu_seqlens || !A_log || !dt_bias || !new_state) return GDN_ERR_INVALID_ARGUMENT;
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !output)) return GDN_ERR_INVALID_ARGUMENT;
+  if (misaligned(q, 8) || misaligned(k, 8) || misaligned(new_state, 16) ||
+      (state && misaligned(state, 16)) || misaligned(cu_seqlens, cu_seqlens_int64 ? 8 : 4))
+    return GDN_ERR_INVALID_ARGUMENT;
+  if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
+  const size_t need =
+      gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads, num_v_heads, head_size);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
+
+  PrefillArgs p{q,        k,     v,      state,      A_log,        a,           dt_bias,
+                b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,
+                (long long)total_tokens, num_seqs, num_q_heads, num_v_heads,
+                use_qk_l2norm != 0, workspace, workspace_bytes};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t err = launch_prefill_recurrent(p, 0, num_seqs, st);
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}

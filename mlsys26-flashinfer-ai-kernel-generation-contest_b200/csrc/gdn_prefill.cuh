@@ -1,0 +1,36 @@
+// Internal interface between the prefill C-ABI entry point and its kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace gdn {
+
+struct PrefillArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* state;  // may be null (zero initial state)
+  const float* A_log;
+  const void* a;
+  const float* dt_bias;
+  const void* b;
+  const void* cu;  // int32 or int64 [N+1]
+  bool cu_int64;
+  float scale;
+  void* out;
+  float* new_state;
+  long long T;
+  int N;
+  int HQ;
+  int HV;
+  bool l2norm;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).
+cudaError_t launch_prefill_recurrent(const PrefillArgs& p, int seq_offset, int nseq,
+                                     cudaStream_t st);
+
+}  // namespace gdn

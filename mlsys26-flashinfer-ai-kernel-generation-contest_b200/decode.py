@@ -1,0 +1,68 @@
+"""GDN decode entry point: drop-in for the reference's ``gdn_decode`` / ``kernel``.
+
+Mirrors ``gdn_decode`` of the reference (gdn_decode/solution/triton/kernel.py:221-272):
+same positional arguments, destination-passing outputs, same defaults
+(``state=None`` -> zero state, ``scale`` None/0 -> 1/sqrt(head_size),
+``output``/``new_state`` None -> allocated), same return value
+``(output, new_state)``.  The work is one launch of the sm_100a kernel in
+``csrc/gdn_decode.cu`` through the C ABI ``gdn_decode_launch``, on the current
+CUDA stream, with no host synchronisation.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _checks as C
+from ._lib import LIB, check
+
+
+def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_state=None,
+               *, use_qk_l2norm: bool = False):
+    """One decode step; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32)."""
+    dev = C.cuda_device(q)
+    C.tensor("q", q, torch.bfloat16, 4, dev)
+    C.tensor("k", k, torch.bfloat16, 4, dev)
+    C.tensor("v", v, torch.bfloat16, 4, dev)
+    B, T, HQ, D = q.shape
+    HK = k.shape[2]
+    HV = v.shape[2]
+    if T != 1:
+        raise ValueError(f"decode expects seq_len == 1, got {T}")
+    C.heads(HQ, HK, HV, D)
+    C.shape("k", k, (B, 1, HK, D))
+    C.shape("v", v, (B, 1, HV, D))
+    if state is not None:
+        C.tensor("state", state, torch.float32, 4, dev)
+        C.shape("state", state, (B, HV, D, D))
+    C.tensor("A_log", A_log, torch.float32, 1, dev)
+    C.shape("A_log", A_log, (HV,))
+    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev)
+    C.shape("dt_bias", dt_bias, (HV,))
+    C.tensor("a", a, torch.bfloat16, 3, dev)
+    C.shape("a", a, (B, 1, HV))
+    C.tensor("b", b, torch.bfloat16, 3, dev)
+    C.shape("b", b, (B, 1, HV))
+    sc = C.scale_arg(scale)
+    if output is None:
+        output = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev)
+    else:
+        C.tensor("output", output, torch.bfloat16, 4, dev)
+        C.shape("output", output, (B, 1, HV, D))
+    if new_state is None:
+        new_state = torch.empty(B, HV, D, D, dtype=torch.float32, device=dev)
+    else:
+        C.tensor("new_state", new_state, torch.float32, 4, dev)
+        C.shape("new_state", new_state, (B, HV, D, D))
+    status = LIB.gdn_decode_launch(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        state.data_ptr() if state is not None else None,
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), sc,
+        output.data_ptr(), new_state.data_ptr(), B, HQ, HK, HV, D, int(bool(use_qk_l2norm)),
+        C.stream_handle(dev))
+    check("gdn_decode_launch", status)
+    return output, new_state
+
+
+def kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+    """flashinfer-bench DPS entry point (11 parameters, no normalisation)."""
+    return gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)

@@ -1,0 +1,114 @@
+"""GDN prefill entry point: drop-in for the reference's ``gdn_prefill`` / ``kernel``.
+
+Mirrors ``gdn_prefill`` of the reference (gdn_prefill/solution/triton/kernel.py:253-337):
+same positional arguments, destination-passing outputs, same defaults
+(``state=None`` -> zero initial state, ``scale`` None/0 -> 1/sqrt(head_size),
+outputs allocated when None), same return ``(output, new_state)``.  Unlike the
+reference wrapper it accepts any head counts with num_v_heads a multiple of
+num_q_heads == num_k_heads (the reference asserts 4/4/8, kernel.py:271-274),
+and it issues no zero-fill or state-copy passes: the kernels write every
+output element themselves.  ``cu_seqlens`` is read on the device only (int32
+or int64), so the call never synchronises the host.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _checks as C
+from ._lib import LIB, check
+
+_ws_lock = threading.Lock()
+_ws_cache = {}
+
+
+def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Persistent per-device scratch buffer, grown on demand (contents are
+    rewritten by every call that uses them)."""
+    key = (dev.index if dev.index is not None else torch.cuda.current_device())
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+            _ws_cache[key] = buf
+        return buf
+
+
+def workspace_bytes(total_tokens: int, num_seqs: int, num_q_heads: int, num_v_heads: int,
+                    head_size: int = 128) -> int:
+    return int(LIB.gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads, num_v_heads,
+                                              head_size))
+
+
+def launches_per_call(total_tokens: int, num_seqs: int) -> int:
+    """Number of this library's kernels one prefill call launches."""
+    return 1 if num_seqs > 0 else 0
+
+
+def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
+                new_state=None, *, use_qk_l2norm: bool = False):
+    """Varlen prefill; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32)."""
+    dev = C.cuda_device(q)
+    C.tensor("q", q, torch.bfloat16, 3, dev)
+    C.tensor("k", k, torch.bfloat16, 3, dev)
+    C.tensor("v", v, torch.bfloat16, 3, dev)
+    T, HQ, D = q.shape
+    HK = k.shape[1]
+    HV = v.shape[1]
+    C.heads(HQ, HK, HV, D)
+    C.shape("k", k, (T, HK, D))
+    C.shape("v", v, (T, HV, D))
+    if not isinstance(cu_seqlens, torch.Tensor):
+        raise TypeError("cu_seqlens must be a torch.Tensor")
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+    if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+        raise ValueError("cu_seqlens must be 1-D with num_seqs + 1 entries")
+    if cu_seqlens.device != dev or not cu_seqlens.is_contiguous():
+        raise ValueError("cu_seqlens must be a contiguous tensor on the same device as q")
+    N = cu_seqlens.numel() - 1
+    H = max(HQ, HV)
+    if state is not None:
+        C.tensor("state", state, torch.float32, 4, dev)
+        C.shape("state", state, (N, HV, D, D))
+    C.tensor("A_log", A_log, torch.float32, 1, dev)
+    C.shape("A_log", A_log, (HV,))
+    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev)
+    C.shape("dt_bias", dt_bias, (HV,))
+    C.tensor("a", a, torch.bfloat16, 2, dev)
+    C.shape("a", a, (T, HV))
+    C.tensor("b", b, torch.bfloat16, 2, dev)
+    C.shape("b", b, (T, HV))
+    sc = C.scale_arg(scale)
+    if output is None:
+        output = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
+    else:
+        C.tensor("output", output, torch.bfloat16, 3, dev)
+        C.shape("output", output, (T, H, D))
+    if new_state is None:
+        new_state = torch.empty(N, H, D, D, dtype=torch.float32, device=dev)
+    else:
+        C.tensor("new_state", new_state, torch.float32, 4, dev)
+        C.shape("new_state", new_state, (N, H, D, D))
+    if N == 0:
+        return output, new_state
+    ws_n = workspace_bytes(T, N, HQ, HV, D)
+    ws = _workspace(dev, ws_n) if ws_n > 0 else None
+    status = LIB.gdn_prefill_launch(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        state.data_ptr() if state is not None else None,
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+        cu_seqlens.data_ptr(), int(cu_seqlens.dtype == torch.int64), sc,
+        output.data_ptr(), new_state.data_ptr(), T, N, HQ, HK, HV, D,
+        int(bool(use_qk_l2norm)),
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        C.stream_handle(dev))
+    check("gdn_prefill_launch", status)
+    return output, new_state
+
+
+def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+    """flashinfer-bench DPS entry point (12 parameters, no normalisation)."""
+    return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                       new_state)

@@ -1,0 +1,99 @@
+"""CPU: the C-ABI library loads, exports what include/*.h declares, and rejects bad
+arguments before touching a GPU; the host mirror validates like the reference."""
+import ctypes
+import re
+
+import pytest
+import torch
+
+from conftest import REPO, load_pkg
+
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w\s\*]*?\b(gdn_\w+)\s*\(", text, flags=re.M):
+            names.append(m.group(1))
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for required in ("gdn_decode_launch", "gdn_prefill_launch", "gdn_prefill_workspace_size"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    pkg = load_pkg()
+    lib = ctypes.CDLL(str(pkg.LIB_PATH))
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    # and the Python binding knows every one of them
+    from importlib import import_module
+    binding = import_module(pkg.__name__ + "._lib")
+    assert set(binding.SIGNATURES) == set(declared_functions())
+
+
+def test_status_strings():
+    pkg = load_pkg()
+    assert pkg.LIB.gdn_b200_version() >= 100
+    assert pkg.LIB.gdn_status_string(0) == b"GDN_OK"
+    assert pkg.LIB.gdn_status_string(-4) == b"GDN_ERR_WORKSPACE"
+
+
+def _decode_call(lib, **kw):
+    args = dict(q=None, k=None, v=None, state=None, A_log=None, a=None, dt_bias=None, b=None,
+                scale=0.0, out=None, ns=None, batch=1, hq=16, hk=16, hv=32, d=128, l2=0,
+                stream=None)
+    args.update(kw)
+    return lib.gdn_decode_launch(*args.values())
+
+
+def test_decode_argument_checks_return_before_launch():
+    lib = load_pkg().LIB
+    assert _decode_call(lib, batch=0) == 0                      # no-op
+    assert _decode_call(lib, d=64) == -2                        # unsupported head size
+    assert _decode_call(lib, hk=8) == -2                        # HK != HQ
+    assert _decode_call(lib, hv=24) == -2                       # HV % HQ != 0
+    assert _decode_call(lib, batch=-1) == -1
+    assert _decode_call(lib) == -1                              # null pointers
+    fake = 0x1000
+    assert _decode_call(lib, q=fake + 2, k=fake, v=fake, A_log=fake, a=fake, dt_bias=fake,
+                        b=fake, out=fake, ns=fake) == -1        # misaligned q
+
+
+def test_prefill_argument_checks_return_before_launch():
+    lib = load_pkg().LIB
+    call = lambda **kw: lib.gdn_prefill_launch(*{**dict(  # noqa: E731
+        q=None, k=None, v=None, state=None, A_log=None, a=None, dt_bias=None, b=None, cu=None,
+        cu64=0, scale=0.0, out=None, ns=None, T=10, N=1, hq=16, hk=16, hv=32, d=128, l2=0,
+        ws=None, wsb=0, stream=None), **kw}.values())
+    assert call(N=0) == 0
+    assert call(d=256) == -2
+    assert call() == -1
+    assert call(T=-1) == -1
+
+
+def test_host_rejects_cpu_tensors_and_bad_dtypes():
+    pkg = load_pkg()
+    W = pkg.workloads
+    inp = W.decode_inputs(1, hq=1, hv=2)
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.gdn_decode(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"],
+                       inp["dt_bias"], inp["b"], inp["scale"])
+    with pytest.raises(TypeError):
+        pkg.gdn_decode([1], inp["k"], inp["v"], None, inp["A_log"], inp["a"], inp["dt_bias"],
+                       inp["b"], 0.0)
+
+
+def test_dps_entry_point_arity_matches_reference():
+    """flashinfer-bench checks the DPS parameter count: 11 (decode) / 12 (prefill)."""
+    import inspect
+    pkg = load_pkg()
+    assert len(inspect.signature(pkg.decode_kernel).parameters) == 11
+    assert len(inspect.signature(pkg.prefill_kernel).parameters) == 12
+    assert list(inspect.signature(pkg.prefill_kernel).parameters)[8] == "cu_seqlens"

@@ -1,0 +1,81 @@
+"""CPU: the oracle reproduces the reference's golden vectors (no GPU needed)."""
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import gdn_oracle as O
+
+pytestmark = pytest.mark.filterwarnings("ignore")
+
+
+def test_decode_matches_definition_and_reference_triton():
+    d, m = load_golden("decode_gva")
+    o, s = O.decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
+                    d["b"], m["scale"])
+    # definition reference (flashinfer) -- fp32 on both sides
+    assert O.state_rel_err(s, d["new_state"]) < 1e-6
+    assert (s - d["new_state"]).abs().max().item() < 1e-5
+    assert (o.float() - d["out"].float()).abs().max().item() <= 0.0 + 1e-6
+    # the reference repository's own Triton kernel (run by the Triton interpreter)
+    assert O.state_rel_err(s, d["new_state_triton"]) < 1e-6
+    ok, frac, _, _ = O.flashinfer_allclose(o, d["out_triton"], 1e-2, 1e-2)
+    assert ok and frac == 1.0
+
+
+def test_decode_defaults_and_l2norm():
+    d, m = load_golden("decode_nostate_l2")
+    q = O.l2norm(d["q"])
+    k = O.l2norm(d["k"])
+    o, s = O.decode(q, k, d["v"], None, d["A_log"], d["a"], d["dt_bias"], d["b"], m["scale"])
+    assert m["scale"] == 0.0  # exercised the 1/sqrt(D) default
+    assert O.state_rel_err(s, d["new_state"]) < 1e-6
+    assert (o.float() - d["out"].float()).abs().max().item() < 1e-6
+
+
+def test_prefill_varlen_with_empty_sequence():
+    d, m = load_golden("prefill_varlen_l2")
+    o, s = O.prefill(O.l2norm(d["q"]), O.l2norm(d["k"]), d["v"], d["state"], d["A_log"], d["a"],
+                     d["dt_bias"], d["b"], d["cu_seqlens"], m["scale"])
+    assert O.state_rel_err(s, d["new_state"]) < 1e-6
+    ok, frac, _, _ = O.flashinfer_allclose(o, d["out"], 1e-3, 1e-3)
+    assert ok
+    # the empty middle sequence leaves a zero state slice (definition semantics)
+    assert d["cu_seqlens"][1] == d["cu_seqlens"][2]
+    assert s[1].abs().max().item() == 0.0 and d["new_state"][1].abs().max().item() == 0.0
+
+
+def test_prefill_zero_state_raw_qk():
+    d, m = load_golden("prefill_nostate_raw")
+    o, s = O.prefill(d["q"], d["k"], d["v"], None, d["A_log"], d["a"], d["dt_bias"], d["b"],
+                     d["cu_seqlens"], None)
+    assert O.state_rel_err(s, d["new_state"]) < 1e-5
+    ok, _, _, _ = O.flashinfer_allclose(o, d["out"], 1e-2, 1e-2)
+    assert ok
+
+
+def test_oracle_fp32_vs_fp64():
+    """The fp32 oracle is itself accurate: compare with its float64 evaluation."""
+    d, m = load_golden("prefill_varlen_l2")
+    args = (O.l2norm(d["q"]), O.l2norm(d["k"]), d["v"], d["state"], d["A_log"], d["a"],
+            d["dt_bias"], d["b"], d["cu_seqlens"], m["scale"])
+    o32, s32 = O.prefill(*args)
+    o64, s64 = O.prefill(*args, dtype=torch.float64)
+    assert O.state_rel_err(s32, s64) < 1e-6
+
+
+def test_tolerance_rule_semantics():
+    """flashinfer rule: fail only if BOTH abs and rel error exceed their bounds."""
+    ref = torch.tensor([1.0, 100.0, 0.001])
+    act = torch.tensor([1.015, 101.0, 0.0105])
+    ok, frac, _, _ = O.flashinfer_allclose(act, ref, 1e-2, 1e-2)
+    # 1.015: abs .015>.01 and rel .015>.01 -> fail; 101: rel .01 ok; .0105: abs ok
+    assert not ok and abs(frac - 2 / 3) < 1e-6
+
+
+def test_planted_mistake_is_caught():
+    """A deliberately wrong gate (planted in a copy of the oracle's inputs) fails the check."""
+    d, m = load_golden("decode_gva")
+    wrong_dt = d["dt_bias"] + 0.5
+    o, s = O.decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], wrong_dt, d["b"],
+                    m["scale"])
+    assert O.state_rel_err(s, d["new_state"]) > 1e-3
