@@ -79,8 +79,6 @@ int gdn_decode_launch(const void* q, const void* k, const void* v, const float* 
 
 /*
  * Bytes of device workspace gdn_prefill_launch needs for this problem (may be 0).
- * `max_seqlen` is an upper bound on any single sequence length (total_tokens is
- * always a valid bound).
  */
 size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
                                   int num_v_heads, int head_size);
@@ -111,6 +109,31 @@ int gdn_prefill_launch(const void* q, const void* k, const void* v, const float*
                        int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
                        int use_qk_l2norm, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/*
+ * Same contract as gdn_prefill_launch, but always runs the token-serial
+ * recurrent CUDA-core kernel (the definition's per-token recurrence, exact to
+ * fp32 rounding) instead of the chunked tensor-core kernel.  For validation
+ * and for callers whose buffers do not meet the chunked kernel's 16-byte
+ * alignment.  Same reference interface as gdn_prefill_launch.
+ */
+int gdn_prefill_launch_recurrent(const void* q, const void* k, const void* v, const float* state,
+                                 const float* A_log, const void* a, const float* dt_bias,
+                                 const void* b, const void* cu_seqlens, int cu_seqlens_int64,
+                                 float scale, void* output, float* new_state, int total_tokens,
+                                 int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+                                 int head_size, int use_qk_l2norm, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
+ * Diagnostics: synchronises the current device and returns the device-side
+ * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
+ * wait ran out, 2 = a tensor-core wait ran out; -1 = the device reported an
+ * error).  Every wait inside the kernels is bounded; a wait that runs out sets
+ * a bit, the kernel releases its resources and returns instead of hanging.
+ * The bits are cleared when `clear` != 0.  No counterpart in the reference.
+ */
+int gdn_device_error(int clear);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -14,10 +14,12 @@ in the in-tree CUDA library ``libgdn_b200.so`` through its C ABI
 The directory name is not a Python identifier; import it with
 ``importlib.import_module("mlsys26-flashinfer-ai-kernel-generation-contest_b200")``.
 """
-from ._lib import LIB, LIB_PATH, GDNError  # noqa: F401
+from ._lib import LIB, LIB_PATH, GDNError, device_error  # noqa: F401
 from .decode import gdn_decode, kernel as decode_kernel  # noqa: F401
-from .prefill import gdn_prefill, kernel as prefill_kernel, workspace_bytes  # noqa: F401
+from .prefill import (gdn_prefill, gdn_prefill_recurrent, kernel as prefill_kernel,  # noqa: F401
+                      workspace_bytes)
 from . import decode, prefill, workloads  # noqa: F401
 
-__all__ = ["gdn_decode", "gdn_prefill", "decode_kernel", "prefill_kernel", "workloads",
-           "GDNError", "LIB", "LIB_PATH", "workspace_bytes"]
+__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "decode_kernel",
+           "prefill_kernel", "workloads", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
+           "device_error"]

@@ -27,6 +27,9 @@ SIGNATURES = {
     "gdn_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "gdn_prefill_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp,
                                 _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_prefill_launch_recurrent": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
+                                          _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_device_error": (_i, [_i]),
 }
 
 
@@ -58,3 +61,9 @@ class GDNError(RuntimeError):
 def check(where: str, status: int) -> None:
     if status != GDN_OK:
         raise GDNError(where, status)
+
+
+def device_error(clear: bool = True) -> int:
+    """Synchronise the current device and return the kernels' device-side error bits
+    (0 = none; 1 = a TMA wait ran out; 2 = a tensor-core wait ran out)."""
+    return int(LIB.gdn_device_error(int(bool(clear))))

@@ -24,7 +24,10 @@ extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int
   return 0;
 }
 
-extern "C" int gdn_prefill_launch(const void* q, const void* k, const void* v, const float* state,
+namespace {
+enum class PrefillPath { kAuto, kRecurrent };
+
+int prefill_entry(PrefillPath path, const void* q, const void* k, const void* v, const float* state,
                                   const float* A_log, const void* a, const float* dt_bias,
                                   const void* b, const void* cu_seqlens, int cu_seqlens_int64,
                                   float scale, void* output, float* new_state, int total_tokens,
@@ -53,6 +56,41 @@ extern "C" int gdn_prefill_launch(const void* q, const void* k, const void* v, c
                 (long long)total_tokens, num_seqs, num_q_heads, num_v_heads,
                 use_qk_l2norm != 0, workspace, workspace_bytes};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t err = launch_prefill_recurrent(p, 0, num_seqs, st);
+  cudaError_t err;
+  if (path == PrefillPath::kAuto && prefill_chunked_supported(p))
+    err = launch_prefill_chunked(p, st);
+  else
+    err = launch_prefill_recurrent(p, 0, num_seqs, st);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+}  // namespace
+
+extern "C" int gdn_prefill_launch(const void* q, const void* k, const void* v, const float* state,
+                                  const float* A_log, const void* a, const float* dt_bias,
+                                  const void* b, const void* cu_seqlens, int cu_seqlens_int64,
+                                  float scale, void* output, float* new_state, int total_tokens,
+                                  int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+                                  int head_size, int use_qk_l2norm, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  return prefill_entry(PrefillPath::kAuto, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                       cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
+                       num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
+                       workspace_bytes, stream);
+}
+
+extern "C" int gdn_prefill_launch_recurrent(
+    const void* q, const void* k, const void* v, const float* state, const float* A_log,
+    const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+    int cu_seqlens_int64, float scale, void* output, float* new_state, int total_tokens,
+    int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+    int use_qk_l2norm, void* workspace, size_t workspace_bytes, void* stream) {
+  return prefill_entry(PrefillPath::kRecurrent, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                       cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
+                       num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
+                       workspace_bytes, stream);
+}
+
+extern "C" int gdn_device_error(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  return (int)gdn::read_device_error(clear != 0);
 }

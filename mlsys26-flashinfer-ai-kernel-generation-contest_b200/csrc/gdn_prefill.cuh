@@ -33,4 +33,12 @@ struct PrefillArgs {
 cudaError_t launch_prefill_recurrent(const PrefillArgs& p, int seq_offset, int nseq,
                                      cudaStream_t st);
 
+// Chunked tcgen05 kernel (all sequences).  Needs T > 0, 16-byte aligned q/k/v/out
+// and the driver's tensor-map encoder.
+bool prefill_chunked_supported(const PrefillArgs& p);
+cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st);
+
+// Device-side error flag set by a bounded wait that ran out (0 = none).
+unsigned read_device_error(bool clear);
+
 }  // namespace gdn

@@ -48,7 +48,24 @@ def launches_per_call(total_tokens: int, num_seqs: int) -> int:
 
 def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
                 new_state=None, *, use_qk_l2norm: bool = False):
-    """Varlen prefill; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32)."""
+    """Varlen prefill; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32).
+
+    Runs the chunked tensor-core kernel (``gdn_prefill_launch``)."""
+    return _prefill(LIB.gdn_prefill_launch, "gdn_prefill_launch", q, k, v, state, A_log, a,
+                    dt_bias, b, cu_seqlens, scale, output, new_state, use_qk_l2norm)
+
+
+def gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
+                          new_state=None, *, use_qk_l2norm: bool = False):
+    """Same contract as :func:`gdn_prefill` through the token-serial CUDA-core kernel
+    (``gdn_prefill_launch_recurrent``): the definition's recurrence step by step."""
+    return _prefill(LIB.gdn_prefill_launch_recurrent, "gdn_prefill_launch_recurrent", q, k, v,
+                    state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                    use_qk_l2norm)
+
+
+def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+             new_state, use_qk_l2norm):
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 3, dev)
     C.tensor("k", k, torch.bfloat16, 3, dev)
@@ -95,7 +112,7 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=
         return output, new_state
     ws_n = workspace_bytes(T, N, HQ, HV, D)
     ws = _workspace(dev, ws_n) if ws_n > 0 else None
-    status = LIB.gdn_prefill_launch(
+    status = launch(
         q.data_ptr(), k.data_ptr(), v.data_ptr(),
         state.data_ptr() if state is not None else None,
         A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
@@ -104,7 +121,7 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=
         int(bool(use_qk_l2norm)),
         ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         C.stream_handle(dev))
-    check("gdn_prefill_launch", status)
+    check(name, status)
     return output, new_state
 
 

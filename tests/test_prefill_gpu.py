@@ -123,3 +123,32 @@ def test_p2_split_sequence_property(cuda):
     assert O.state_rel_err(s2.cpu(), s.cpu()) < 1e-3
     ok, *_ = O.flashinfer_allclose(torch.cat([o1, o2]).cpu(), o.cpu(), 2e-2, 2e-2)
     assert ok
+
+
+def test_chunked_matches_recurrent_p2_full(cuda):
+    """P2 at full size (32768 tokens, initial state): the chunked tensor-core kernel
+    and the token-serial CUDA-core kernel agree (state rel <= 1e-3, outputs within
+    the bf16 bar), and no bounded wait ran out."""
+    pkg = load_pkg()
+    inp = pkg.workloads.prefill_config_inputs("P2", seed=0, device="cuda")
+    args = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+            inp["b"], inp["cu_seqlens"], inp["scale"])
+    o1, s1 = pkg.gdn_prefill(*args, use_qk_l2norm=True)
+    o2, s2 = pkg.gdn_prefill_recurrent(*args, use_qk_l2norm=True)
+    assert pkg.device_error() == 0
+    assert O.state_rel_err(s1.cpu(), s2.cpu()) < 1e-3
+    ok, frac, mabs, _ = O.flashinfer_allclose(o1.cpu(), o2.cpu(), 2e-2, 2e-2)
+    assert ok, (frac, mabs)
+
+
+def test_recurrent_kernel_vs_oracle(cuda):
+    """The token-serial kernel (second opinion above) itself matches the oracle."""
+    pkg = load_pkg()
+    inp = pkg.workloads.prefill_inputs([1, 70, 0, 129], seed=31)
+    d = to(inp, cuda)
+    o, s = pkg.gdn_prefill_recurrent(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
+                                     d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"],
+                                     use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    ro, rs = oracle_prefill(inp, True)
+    assert_parity(o, s, ro, rs, what="recurrent")
