@@ -9,8 +9,8 @@
 //
 //   A[t,j] = beta_t exp(Lam_t - Lam_j) rk_t rk_j (k_t . k_j)      j < t
 //   T      = (I + A)^-1                          (unit lower triangular, fp32)
-//   W      = T diag(beta gamma rk) K,   U0 = T diag(beta) V,   gamma_t = exp(Lam_t)
-//   U      = U0 - W S^T                          (per-token corrected values)
+//   T1     = T diag(beta gamma rk),  T2 = T diag(beta),  gamma_t = exp(Lam_t)
+//   U      = T2 V - T1 (K S^T)                   (per-token corrected values)
 //   O      = scale [ diag(gamma rq) Q S^T + P U ],  P[t,j] = exp(Lam_t-Lam_j) rq_t rk_j (q_t.k_j), j<=t
 //   S     <- G S + U~^T K,  U~ = diag(rk exp(Lam_end - Lam_t)) U,  G = exp(Lam_end)
 //
@@ -22,24 +22,33 @@
 // log-gamma to [-88, 88], kernel.py:166, corrupts gamma ratios under strong decay).
 //
 // Precision: every MMA operand is bf16.  q, k, v are bf16 inputs (exact).  The
-// fp32 quantities on the state path are split x = hi + lo (two bf16) and their
-// products expanded: T diag(.) -> 2 MMAs, S W^T -> 3 MMAs (hi.hi + lo.hi + hi.lo),
-// U~ -> 2 MMAs, all accumulated in fp32 in TMEM, so the fp32 state keeps ~16
-// mantissa bits per step instead of bf16's 8.  Output-only terms (S Q^T, P U)
-// use the hi part only.
+// fp32 quantities on the state path are split x = hi + lo (two bf16: hi the
+// truncation, lo the rounded residual; integer ops, not cvt) and their
+// products expanded, accumulated in fp32 in TMEM: S K^T -> 2 MMAs (S_hi, S_lo),
+// T2 V -> 2, T1 (K S^T) -> 3 (hi.hi + lo.hi + hi.lo), U~^T K -> 2, so the fp32
+// state keeps ~16 mantissa bits per step instead of bf16's 8.  Output terms
+// use the hi parts, except P U for raw (un-normalised) q/k, which is split too.
 //
 // Orientation: the tensor-core D tiles are kept "v-major" (v = 128 TMEM lanes),
-// so S (128 x 128), U^T, O^T and the state update all use M = 128 MMAs:
-//   [Skk;Sqk] = [K;Q] K^T        M128 N64  K128   (A, B K-major, TMA tiles)
-//   W^T       = K^T  T1^T        M128 N64  K64    (A = K tile MN-major)
-//   U0^T      = V^T  T2^T        M128 N64  K64    (A = V tile MN-major)
-//   O^T       = S_hi Q~^T        M128 N64  K128
-//   U^T      -= S W^T            M128 N64  K128   (B = W^T MN-major, negated A)
-//   dS        = U~^T K           M128 N128 K64    (B = K tile MN-major)
-//   O^T      += U_hi^T P^T       M128 N64  K64    (+ U_lo P_hi, U_hi P_lo for raw q/k)
+// so S (128 x 128), U^T, O^T and the state update are M = 128 MMAs.  Per chunk
+// three MMA groups, each ended by one commit:
+//   group 1 (needs only this chunk's tiles and S):
+//     [Skk;Sqk] = [K;Q] K^T      M128 N64  K128   (A, B: TMA tiles, K-major)
+//     (S K^T)   = S_hi K^T + S_lo K^T   M128 N64 K128
+//     Oi        = S_hi Q^T              M128 N64 K128
+//   group 2 (after the triangular inverse on the CUDA cores):
+//     U^T = V^T T2^T - (S K^T) T1^T     M128 N64 K64  (A = V tile MN-major; negated A)
+//   group 3:
+//     dS  = U~^T K                      M128 N128 K64 (B = K tile MN-major)
+//     Ot  = U^T P^T                     M128 N64 K64
+// and O = scale (diag(gamma rq) Oi + Ot), S <- G S + dS on the CUDA cores.
+// The next chunk's Q, V and K tiles are fetched as soon as the current ones
+// are consumed (after groups 1, 2 and 3 respectively) and its gates are
+// computed during group 2, so only the inverse and the MMA round trips remain
+// on the serial path.
 //
-// One CTA (8 warps) owns one (sequence, v-head); warp w serves TMEM lanes
-// 32*(w%4).. and column half w/4.  Thread 0 issues TMA and UMMA; completion is
+// One CTA (16 warps) owns one (sequence, v-head); warp w serves TMEM lanes
+// 32*(w%4).. and column quarter w/4.  Thread 0 issues TMA and UMMA; completion is
 // tracked by two mbarriers whose waits are bounded: a wait that runs out sets a
 // device error flag (read by gdn_device_error) and the CTA releases TMEM and exits.
 #include <cudaTypedefs.h>
@@ -56,47 +65,46 @@ namespace {
 using namespace sm100;
 
 constexpr int kC = 64;          // chunk length
-constexpr int kThreads = 256;   // 8 warps
+constexpr int kThreads = 512;   // 16 warps
 constexpr int kLdA = 65;        // padded row stride of the fp32 A matrix (bank-conflict free)
+constexpr int kLdT = 68;        // padded row stride of the fp32 T matrix (16-byte rows)
 
-// ---- shared memory map (byte offsets from a 1024-byte aligned base) ----
+// ---- shared memory map (byte offsets from the 1024-byte aligned dynamic base) ----
 constexpr uint32_t OFF_K0 = 0;        // K tile, d 0..63   [t][d]  (TMA, 128B swizzle)
 constexpr uint32_t OFF_Q0 = 8192;     // Q tile, d 0..63
 constexpr uint32_t OFF_K1 = 16384;    // K tile, d 64..127
 constexpr uint32_t OFF_Q1 = 24576;    // Q tile, d 64..127
-constexpr uint32_t OFF_V = 32768;     // V tile [t][v] 2 x 8 KB; then O staging [t][v] bf16
+constexpr uint32_t OFF_V = 32768;     // V tile [t][v] 2 x 8 KB
 constexpr uint32_t OFF_SHI = 49152;   // S hi [v][k] K-major, 2 k-blocks of 16 KB
 constexpr uint32_t OFF_SLO = 81920;   // S lo
-constexpr uint32_t OFF_WHI = 114688;  // W^T hi [d][t] (MN-major B operand) 16 KB
-constexpr uint32_t OFF_WLO = 131072;  // W^T lo
+constexpr uint32_t OFF_SKHI = 114688; // (S K^T) hi [v][t] K-major 16 KB; then O staging [t][v]
+constexpr uint32_t OFF_SKLO = 131072; // (S K^T) lo
 constexpr uint32_t OFF_U = 147456;    // 64 KB, phase-dependent:
-//   A: Tmat f32[64][64] @16K, E scratch @32K,
-//      then T1hi @32K, T1lo @40K, T2hi @48K, T2lo @56K (each [t][j] K-major 8 KB)
-//   (the fp32 A matrix, [64][kLdA], lives in the W^T buffers, free until step 6)
-//   B: U~hi [v][t] @0, U~lo @16K, Uhi @32K, Ulo @48K (K-major A operands, 16 KB each)
-constexpr uint32_t OFF_P = 212992;    // P [t][j] K-major 8 KB
-constexpr uint32_t OFF_VEC = 221184;  // fp32[64] vectors + barriers
-constexpr uint32_t SMEM_USED = OFF_VEC + 2048;
-constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;  // + alignment slack
+//   before group 2: Tmat f32[64][kLdT] @0, E scratch @17K, A f32[64][kLdA] @21K,
+//                   then (A dead) T1hi @32K, T1lo @40K, T2hi @48K, T2lo @56K  [t][j] K-major
+//   after group 2:  U~hi [v][t] @0, U~lo @16K, Uhi @32K, Ulo @48K (K-major A operands)
+constexpr uint32_t OFF_P = 212992;    // P hi [t][j] K-major 8 KB
+constexpr uint32_t OFF_PLO = 221184;  // P lo (raw q/k only)
+constexpr uint32_t OFF_VEC = 229376;  // fp32[64] vectors + barriers
+constexpr uint32_t VEC_BAR = 2304;    // 2 x (Lam, beta, gamma) + rk, rq, us = 9 x 256 B
+constexpr uint32_t SMEM_ALLOC = OFF_VEC + VEC_BAR + 64;
+static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 
-constexpr uint32_t U_TMAT = 16384, U_E = 32768;
-constexpr uint32_t OFF_AMAT = OFF_WHI;  // 64 x 65 fp32 = 16.25 KB of the 32 KB W^T hi/lo region
+constexpr uint32_t U_TMAT = 0, U_E = 17408, U_AMAT = 21504;
 constexpr uint32_t U_T1HI = 32768, U_T1LO = 40960, U_T2HI = 49152, U_T2LO = 57344;
 constexpr uint32_t U_UTHI = 0, U_UTLO = 16384, U_UHI = 32768, U_ULO = 49152;
-// Raw (un-normalised) q/k: |P| can reach |q||k| ~ 1e2 with heavy cancellation in
-// P U, so that product is split too (P_hi U_hi + P_lo U_hi + P_hi U_lo).  P_lo is
-// written into the W^T lo buffer once the S W^T MMAs that read it have completed.
-constexpr uint32_t OFF_PLO = OFF_WLO;
+constexpr uint32_t OFF_OST = OFF_SKHI;  // output staging, once group 2 has read S K^T
 
-// TMEM columns (512 allocated)
+// TMEM columns (512 allocated, 448 used)
 constexpr uint32_t TM_DS = 0;     // dS  128 lanes (v) x 128 (k)
 constexpr uint32_t TM_UT = 128;   // U^T 128 (v) x 64 (t)
-constexpr uint32_t TM_OT = 192;   // O^T 128 (v) x 64 (t)
-constexpr uint32_t TM_WT = 256;   // W^T 128 (d) x 64 (t)
-constexpr uint32_t TM_KQ = 320;   // lanes 0..63: Skk rows, 64..127: Sqk rows; 64 cols
+constexpr uint32_t TM_OT = 192;   // U^T P^T
+constexpr uint32_t TM_OI = 256;   // S_hi Q^T
+constexpr uint32_t TM_SK = 320;   // S K^T
+constexpr uint32_t TM_KQ = 384;   // lanes 0..63: Skk rows, 64..127: Sqk rows; 64 cols
 constexpr uint32_t TM_COLS = 512;
 
-enum : unsigned { ERR_TMA_TIMEOUT = 1u, ERR_MMA_TIMEOUT = 2u };
+enum : unsigned { ERR_TMA_TIMEOUT = 1u, ERR_MMA_TIMEOUT = 2u, ERR_SMEM_ALIGN = 4u };
 
 struct ChunkedParams {
   const __nv_bfloat16* a;
@@ -114,29 +122,51 @@ struct ChunkedParams {
   float scale;
 };
 
+// bf16 conversions with integer operations (ALU pipe) rather than cvt (which
+// shares the XU pipe with exp/rsqrt and was the kernel's busiest pipe).
+// Round-to-nearest-even of a finite fp32 bit pattern to bf16, kept in the high half.
+__device__ __forceinline__ uint32_t rn_bf16_bits(uint32_t xb) {
+  return (xb + 0x7FFFu + ((xb >> 16) & 1u)) & 0xFFFF0000u;
+}
+// Two bf16 values held in the high halves of a and b -> one packed word (a low, b high).
+__device__ __forceinline__ uint32_t pack_hi16(uint32_t a, uint32_t b) {
+  return __byte_perm(a, b, 0x7632);
+}
 __device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
-  return *reinterpret_cast<uint32_t*>(&v);
+  return pack_hi16(rn_bf16_bits(__float_as_uint(x)), rn_bf16_bits(__float_as_uint(y)));
 }
-__device__ __forceinline__ float bf16_round(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
-// 8 floats -> (hi, lo) bf16 chunks with x ~= hi + lo.
+// 8 floats -> (hi, lo) bf16 chunks with x ~= hi + lo: hi is x truncated to bf16
+// (exact residual x - hi, |x - hi| < 2^-7 |x|), lo is that residual rounded to
+// bf16, so hi + lo carries ~16 significant bits.
 __device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
-  float h[8], l[8];
+  uint32_t hb[8], lb[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    h[i] = bf16_round(x[i]);
-    l[i] = x[i] - h[i];
+    hb[i] = __float_as_uint(x[i]) & 0xFFFF0000u;
+    lb[i] = rn_bf16_bits(__float_as_uint(x[i] - __uint_as_float(hb[i])));
   }
-  hi = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
-                  pack_bf16(h[6], h[7]));
-  lo = make_uint4(pack_bf16(l[0], l[1]), pack_bf16(l[2], l[3]), pack_bf16(l[4], l[5]),
-                  pack_bf16(l[6], l[7]));
+  hi = make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]), pack_hi16(hb[4], hb[5]),
+                  pack_hi16(hb[6], hb[7]));
+  lo = make_uint4(pack_hi16(lb[0], lb[1]), pack_hi16(lb[2], lb[3]), pack_hi16(lb[4], lb[5]),
+                  pack_hi16(lb[6], lb[7]));
 }
 __device__ __forceinline__ uint4 pack8(const float* x) {
   return make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
                     pack_bf16(x[6], x[7]));
+}
+// 16 consecutive fp32 TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void st_v4(uint32_t addr, uint4 v) {
   st_shared_v4(addr, v.x, v.y, v.z, v.w);
@@ -151,89 +181,104 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity, unsigne
 }
 
 // T = (I + A)^-1 for a strictly lower triangular fp32 A[64][kLdA] (row stride kLdA),
-// by 16x16 diagonal-block forward substitution and two levels of block merges:
-//   [[L11, 0], [L21, L22]]^-1 = [[T11, 0], [-T22 L21 T11, T22]].
-// Called by all 256 threads (contains __syncthreads).
+// written to Tm[64][kLdT].  Eight 8x8 diagonal blocks by forward substitution (one
+// column per thread, the block's A entries held in registers), then three levels of
+// block merges, each two small products:
+//   [[L11, 0], [L21, L22]]^-1 = [[T11, 0], [-T22 (L21 T11), T22]].
+// The padded strides keep the shared-memory access patterns conflict-free.
+// Called by all kThreads (= 512) threads (contains __syncthreads).
 __device__ __forceinline__ void invert_unit_lower64(const float* __restrict__ A,
                                                     float* __restrict__ Tm,
                                                     float* __restrict__ E) {
   const int tid = threadIdx.x;
-  // ---- level 1: four 16x16 diagonal blocks, one column per thread ----
+  // ---- level 1: 8x8 diagonal blocks ----
   if (tid < 64) {
-    const int blk = tid >> 4, col = tid & 15, o = 16 * blk;
-    float x[16];
+    const int o = 8 * (tid >> 3), col = tid & 7;
+    float a[8][8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 1; r < 8; ++r)
+#pragma unroll
+      for (int j = 0; j < r; ++j) a[r][j] = A[(o + r) * kLdA + o + j];
+    float x[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
       float acc = 0.f;
 #pragma unroll
-      for (int j = 0; j < r; ++j) acc = fmaf(A[(o + r) * kLdA + o + j], x[j], acc);
+      for (int j = 0; j < r; ++j) acc = fmaf(a[r][j], x[j], acc);
       x[r] = (r < col) ? 0.f : ((r == col) ? 1.f : -acc);
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Tm[(o + r) * 64 + o + col] = x[r];
+    for (int r = 0; r < 8; ++r) Tm[(o + r) * kLdT + o + col] = x[r];
   } else {
-    // zero the blocks above the diagonal: rows 0..31 x cols 32..63, block (0,1), block (2,3)
-    for (int u = tid - 64; u < 1536; u += kThreads - 64) {
-      int r, c;
-      if (u < 1024) { r = u >> 5; c = 32 + (u & 31); }
-      else if (u < 1280) { r = (u - 1024) >> 4; c = 16 + ((u - 1024) & 15); }
-      else { r = 32 + ((u - 1280) >> 4); c = 48 + ((u - 1280) & 15); }
-      Tm[r * 64 + c] = 0.f;
+    // zero everything above the 8x8 block diagonal
+    for (int u = tid - 64; u < 64 * 64; u += kThreads - 64) {
+      const int r = u >> 6, c = u & 63;
+      if (c >= 8 * ((r >> 3) + 1)) Tm[r * kLdT + c] = 0.f;
     }
   }
   __syncthreads();
-  // ---- level 2: blocks (1,0) and (3,2): T_ij = -D_i A_ij D_j ----
+  // ---- level 2 (8 -> 16): pairs p = 0..3, rows bi = 16p + 8, cols bj = 16p ----
   {
-    const int c = tid & 15, g = tid >> 4;  // 16 groups x 2 rows each
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int pr = g * 2 + rr;  // 0..31
-      const int p = pr >> 4, r = pr & 15;
-      const int bi = 16 * (2 * p + 1), bj = 16 * (2 * p);
+    const int p = (tid >> 6) & 3, r = (tid >> 3) & 7, c = tid & 7;
+    const int bi = 16 * p + 8, bj = 16 * p;
+    if (tid < 256) {
       float acc = 0.f;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc = fmaf(A[(bi + r) * kLdA + bj + k], Tm[(bj + k) * 64 + bj + c], acc);
-      E[p * 256 + r * 16 + c] = acc;
+      for (int k = 0; k < 8; ++k)
+        acc = fmaf(A[(bi + r) * kLdA + bj + k], Tm[(bj + k) * kLdT + bj + c], acc);
+      E[p * 64 + r * 8 + c] = acc;
+    }
+    __syncthreads();
+    if (tid < 256) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc = fmaf(Tm[(bi + r) * kLdT + bi + k], E[p * 64 + k * 8 + c], acc);
+      Tm[(bi + r) * kLdT + bj + c] = -acc;
     }
   }
   __syncthreads();
+  // ---- level 3 (16 -> 32): pairs p = 0..1, rows bi = 32p + 16, cols bj = 32p ----
   {
-    const int c = tid & 15, g = tid >> 4;
+    const int p = tid >> 8, r = (tid >> 4) & 15, c = tid & 15;
+    const int bi = 32 * p + 16, bj = 32 * p;
+    float acc = 0.f;
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int pr = g * 2 + rr;
-      const int p = pr >> 4, r = pr & 15;
-      const int bi = 16 * (2 * p + 1), bj = 16 * (2 * p);
-      float acc = 0.f;
+    for (int k = 0; k < 16; ++k)
+      acc = fmaf(A[(bi + r) * kLdA + bj + k], Tm[(bj + k) * kLdT + bj + c], acc);
+    E[p * 256 + r * 16 + c] = acc;
+    __syncthreads();
+    acc = 0.f;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc = fmaf(Tm[(bi + r) * 64 + bi + k], E[p * 256 + k * 16 + c], acc);
-      Tm[(bi + r) * 64 + bj + c] = -acc;
-    }
+    for (int k = 0; k < 16; ++k) acc = fmaf(Tm[(bi + r) * kLdT + bi + k], E[p * 256 + k * 16 + c], acc);
+    Tm[(bi + r) * kLdT + bj + c] = -acc;
   }
   __syncthreads();
-  // ---- level 3: rows 32..63 x cols 0..31: -T22 A21 T11 ----
+  // ---- level 4 (32 -> 64): rows 32..63 x cols 0..31, 1x2 outputs per thread ----
   {
-    const int c = tid & 31, r0 = tid >> 5;  // rows r0, r0+8, r0+16, r0+24
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = r0 + 8 * i;
-      float acc = 0.f;
+    const int r = tid >> 4, c = 2 * (tid & 15);
+    float e0 = 0.f, e1 = 0.f;
 #pragma unroll 8
-      for (int k = 0; k < 32; ++k) acc = fmaf(A[(32 + r) * kLdA + k], Tm[k * 64 + c], acc);
-      E[r * 32 + c] = acc;
+    for (int k = 0; k < 32; ++k) {
+      const float a0 = A[(32 + r) * kLdA + k];
+      const float2 t = *reinterpret_cast<const float2*>(Tm + k * kLdT + c);
+      e0 = fmaf(a0, t.x, e0);
+      e1 = fmaf(a0, t.y, e1);
     }
-  }
-  __syncthreads();
-  {
-    const int c = tid & 31, r0 = tid >> 5;
+    *reinterpret_cast<float2*>(E + r * 32 + c) = make_float2(e0, e1);
+    __syncthreads();
+    e0 = e1 = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < 32; k += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(Tm + (32 + r) * kLdT + 32 + k);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = r0 + 8 * i;
-      float acc = 0.f;
-#pragma unroll 8
-      for (int k = 0; k < 32; ++k) acc = fmaf(Tm[(32 + r) * 64 + 32 + k], E[k * 32 + c], acc);
-      Tm[(32 + r) * 64 + c] = -acc;
+      for (int kk = 0; kk < 4; ++kk) {
+        const float2 t = *reinterpret_cast<const float2*>(E + (k + kk) * 32 + c);
+        e0 = fmaf(av[kk], t.x, e0);
+        e1 = fmaf(av[kk], t.y, e1);
+      }
     }
+    *reinterpret_cast<float2*>(Tm + (32 + r) * kLdT + c) = make_float2(-e0, -e1);
   }
   __syncthreads();
 }
@@ -243,13 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const ChunkedParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sb = smem_u32(smem);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int sp = warp & 3, half = warp >> 2;
+  const int sp = warp & 3, qtr = warp >> 2;  // TMEM subpartition, column quarter
   const int row = sp * 32 + lane;  // TMEM lane owned by this thread
   const int HV = p.HV;
   const int n = blockIdx.x / HV;
@@ -259,25 +302,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long s1 = min(max((long long)cu[n + 1], 0LL), p.T);
   const long long s0 = min(max((long long)cu[n], 0LL), s1);
   const long long L = s1 - s0;
-  float* nsrow = p.new_state + (((size_t)n * HV + h) * kHeadDim + row) * kHeadDim + 64 * half;
+  float* nsrow = p.new_state + (((size_t)n * HV + h) * kHeadDim + row) * kHeadDim + 32 * qtr;
 
   if (L <= 0) {  // empty sequence: zero final state (definition semantics)
 #pragma unroll
-    for (int i = 0; i < 16; ++i) st_stream_f4(nsrow + 4 * i, make_float4(0.f, 0.f, 0.f, 0.f));
+    for (int i = 0; i < 8; ++i) st_stream_f4(nsrow + 4 * i, make_float4(0.f, 0.f, 0.f, 0.f));
+    return;
+  }
+  if ((sb & 1023u) != 0) {  // the swizzled layouts need a 1024-byte aligned base
+    if (tid == 0) atomicOr(&g_prefill_device_error, ERR_SMEM_ALIGN);
     return;
   }
 
+  // gate vectors are double-buffered: chunk c uses set (c & 1) while set (c + 1) & 1
+  // is filled for the next chunk
   float* vec = reinterpret_cast<float*>(smem + OFF_VEC);
   float* Lam = vec;         // cumulative log decay within the chunk
   float* beta = vec + 64;
   float* gam = vec + 128;   // exp(Lam)
-  float* rk = vec + 192;
-  float* rq = vec + 256;
-  float* us = vec + 320;    // rk exp(Lam_end - Lam)
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_VEC + 1536);
+  float* rk = vec + 384;
+  float* rq = vec + 448;
+  float* us = vec + 512;    // rk exp(Lam_end - Lam)
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_VEC + VEC_BAR);
   uint64_t* bar_mma = bar_tma + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_VEC + 1552);
-  float* Amat = reinterpret_cast<float*>(smem + OFF_AMAT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_VEC + VEC_BAR + 16);
+  float* Amat = reinterpret_cast<float*>(smem + OFF_U + U_AMAT);
   float* Tmat = reinterpret_cast<float*>(smem + OFF_U + U_TMAT);
   float* Escr = reinterpret_cast<float*>(smem + OFF_U + U_E);
 
@@ -286,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   if (tid == 32) {
-    mbar_init(bar_tma, 1);
+    mbar_init(bar_tma, 3);  // three arrivals per chunk: the Q, V and K tiles
     mbar_init(bar_mma, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -299,50 +348,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);  // this warp's lane base
 
-  // ---- initial state: this thread keeps S[v=row][64*half .. +64) in fp32 registers ----
-  float s[64];
+  // ---- initial state: this thread keeps S[v=row][32*qtr .. +32) in fp32 registers ----
+  float s[32];
   if constexpr (HAS_STATE) {
-    const float* srow = p.state + (((size_t)n * HV + h) * kHeadDim + row) * kHeadDim + 64 * half;
+    const float* srow = p.state + (((size_t)n * HV + h) * kHeadDim + row) * kHeadDim + 32 * qtr;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const float4 v4 = ld_stream_f4(srow + 4 * i);
       s[4 * i] = v4.x; s[4 * i + 1] = v4.y; s[4 * i + 2] = v4.z; s[4 * i + 3] = v4.w;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) s[i] = 0.f;
+    for (int i = 0; i < 32; ++i) s[i] = 0.f;
   }
-  // S hi / lo -> shared (K-major [v][k], k-block = half)
+  // S hi / lo -> shared (K-major [v][k]: k-block qtr/2, 16-byte chunks 4*(qtr&1)..+3)
   auto write_state_split = [&]() {
-    const uint32_t bhi = sb + OFF_SHI + 16384u * half, blo = sb + OFF_SLO + 16384u * half;
+    const uint32_t kb = 16384u * (qtr >> 1), c0 = 4u * (qtr & 1);
+    const uint32_t bhi = sb + OFF_SHI + kb, blo = sb + OFF_SLO + kb;
 #pragma unroll
-    for (int cidx = 0; cidx < 8; ++cidx) {
+    for (int q4 = 0; q4 < 4; ++q4) {
       uint4 hi, lo;
-      split8(&s[8 * cidx], hi, lo);
-      st_v4(bhi + sw128(row, cidx), hi);
-      st_v4(blo + sw128(row, cidx), lo);
+      split8(&s[8 * q4], hi, lo);
+      st_v4(bhi + sw128(row, c0 + q4), hi);
+      st_v4(blo + sw128(row, c0 + q4), lo);
     }
   };
   write_state_split();
-
-  // P[t][j] = exp(Lam_t - Lam_j) rq_t rk_j Sqk[t][j] (j <= t) for this thread's row
-  // t = row - 64 and 32-column half, as bf16 hi (or, with lo_part, the lo residual).
-  auto write_p = [&](const float (&kq)[32], bool lo_part) {
-    const int t = row - 64;
-    const float qt = rq[t], lt = Lam[t];
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      float pv[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = 32 * half + 8 * q4 + e;
-        pv[e] = (j <= t) ? expf(lt - Lam[j]) * qt * rk[j] * kq[8 * q4 + e] : 0.f;
-      }
-      uint4 hi, lo;
-      split8(pv, hi, lo);
-      st_v4(sb + (lo_part ? OFF_PLO : OFF_P) + sw128(t, 4 * half + q4), lo_part ? lo : hi);
-    }
-  };
 
   const float nexpA = -expf(__ldg(p.A_log + h));
   const float dtb = __ldg(p.dt_bias + h);
@@ -352,65 +383,106 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = true;
   bool mma_pending = false, tma_pending = false;
 
+  // Gates, by one warp (two tokens per lane): the raw a/b values of chunk cc are
+  // loaded one chunk ahead (load_gates) and turned into log decay, its inclusive
+  // prefix sum Lam, exp(Lam) and beta in vector set `buf` (finish_gates).
+  // Padding tokens get decay 1 and beta 0.
+  float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+  auto load_gates = [&](int cc) {
+    const long long tc0 = s0 + (long long)kC * cc;
+    const int Lcc = (int)min((long long)kC, s1 - tc0);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 2 * lane + e;
+      if (t < Lcc) {
+        const size_t ti = (size_t)(tc0 + t) * HV + h;
+        ga[e] = bf2f(p.a[ti]);
+        gb[e] = bf2f(p.b[ti]);
+      }
+    }
+  };
+  auto finish_gates = [&](int cc, int buf) {
+    const long long tc0 = s0 + (long long)kC * cc;
+    const int Lcc = (int)min((long long)kC, s1 - tc0);
+    float* Lm = vec + 192 * buf;
+    float lg[2], bb[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const bool valid = 2 * lane + e < Lcc;
+      lg[e] = valid ? nexpA * softplus_f(ga[e] + dtb) : 0.f;
+      bb[e] = valid ? sigmoid_f(gb[e]) : 0.f;
+    }
+    float x = lg[0] + lg[1];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    const float x0 = x - lg[1];
+    Lm[2 * lane] = x0;
+    Lm[2 * lane + 1] = x;
+    Lm[64 + 2 * lane] = bb[0];
+    Lm[64 + 2 * lane + 1] = bb[1];
+    Lm[128 + 2 * lane] = expf(x0);
+    Lm[128 + 2 * lane + 1] = expf(x);
+  };
+  // TMA of chunk cc, one arrival each: the Q tile, the V tile, the K tile
+  auto issue_tiles = [&](int cc, uint32_t off0, uint32_t off1, const CUtensorMap* m, int head) {
+    const int y = (int)(s0 + (long long)kC * cc);
+    fence_proxy_async();
+    mbar_arrive_expect_tx(bar_tma, 2 * 8192);
+    tma_load_2d(smem + off0, m, bar_tma, head * 128, y);
+    tma_load_2d(smem + off1, m, bar_tma, head * 128 + 64, y);
+  };
+  if (tid == 0) {
+    issue_tiles(0, OFF_Q0, OFF_Q1, &tm_q, qh);
+    issue_tiles(0, OFF_V, OFF_V + 8192, &tm_v, h);
+    issue_tiles(0, OFF_K0, OFF_K1, &tm_k, qh);
+  }
+  tma_pending = true;
+  if (warp == 1) {
+    load_gates(0);
+    finish_gates(0, 0);
+  }
+
   for (int c = 0; c < nchunks; ++c) {
     const long long t0 = s0 + (long long)kC * c;
     const int Lc = (int)min((long long)kC, s1 - t0);
+    const bool more = c + 1 < nchunks;
+    Lam = vec + 192 * (c & 1);
+    beta = Lam + 64;
+    gam = Lam + 128;
 
-    // (1) TMA: K, Q (GVA q/k head) and V tiles of this chunk
+    // (1) wait for this chunk's K, Q and V tiles (issued during the previous chunk)
     fence_proxy_async();
     __syncthreads();
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_tma, 6 * 8192);
-      const int y = (int)t0;
-      tma_load_2d(smem + OFF_K0, &tm_k, bar_tma, qh * 128, y);
-      tma_load_2d(smem + OFF_K1, &tm_k, bar_tma, qh * 128 + 64, y);
-      tma_load_2d(smem + OFF_Q0, &tm_q, bar_tma, qh * 128, y);
-      tma_load_2d(smem + OFF_Q1, &tm_q, bar_tma, qh * 128 + 64, y);
-      tma_load_2d(smem + OFF_V, &tm_v, bar_tma, h * 128, y);
-      tma_load_2d(smem + OFF_V + 8192, &tm_v, bar_tma, h * 128 + 64, y);
-    }
-    tma_pending = true;
-    // gates of the chunk (padding tokens: decay 1, beta 0), inclusive scan of log decay
-    if (tid < 64) {
-      float lg = 0.f, bt = 0.f;
-      if (tid < Lc) {
-        const size_t ti = (size_t)(t0 + tid) * HV + h;
-        lg = nexpA * softplus_f(bf2f(p.a[ti]) + dtb);
-        bt = sigmoid_f(bf2f(p.b[ti]));
-      }
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, lg, off);
-        if (lane >= off) lg += y;
-      }
-      Lam[tid] = lg;
-      beta[tid] = bt;
-    }
-    __syncthreads();
-    if (tid >= 32 && tid < 64) Lam[tid] += Lam[31];
     if (!cta_wait(bar_tma, ph_tma, ERR_TMA_TIMEOUT)) { ok = false; break; }
     ph_tma ^= 1;
     tma_pending = false;
+    if (warp == 1 && more) load_gates(c + 1);  // consumed during group 2
 
-    // (2) [Skk; Sqk] = [K; Q] K^T  (M128 N64 K128)
+    // (2) MMA group 1: [Skk;Sqk] = [K;Q] K^T,  S K^T (hi + lo),  Oi = S_hi Q^T
     if (tid == 0) {
       tc_fence_after();
       const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
-        umma_bf16(tmem + TM_KQ, umma_desc_k(sb + OFF_K0 + off), umma_desc_k(sb + OFF_K0 + off),
-                  idesc, ks > 0);
+        const uint64_t kdesc = umma_desc_k(sb + OFF_K0 + off);
+        umma_bf16(tmem + TM_KQ, kdesc, kdesc, idesc, ks > 0);
+        umma_bf16(tmem + TM_SK, umma_desc_k(sb + OFF_SHI + off), kdesc, idesc, ks > 0);
+        umma_bf16(tmem + TM_SK, umma_desc_k(sb + OFF_SLO + off), kdesc, idesc, 1);
+        umma_bf16(tmem + TM_OI, umma_desc_k(sb + OFF_SHI + off),
+                  umma_desc_k(sb + ((ks >> 2) ? OFF_Q1 : OFF_Q0) + 32u * (ks & 3)), idesc, ks > 0);
       }
       umma_commit(bar_mma);
     }
     mma_pending = true;
-    // meanwhile: gamma, q/k L2-norm factors
-    if (tid < 64) gam[tid] = expf(Lam[tid]);
+    // meanwhile: q/k L2-norm factors
     if constexpr (L2NORM) {
-      if (tid >= 64 && tid < 192) {
-        const int t = (tid - 64) & 63;
-        const bool isq = tid < 128;
+      if (tid >= 256 && tid < 384) {
+        const int t = tid & 63;
+        const bool isq = tid < 320;
         const uint32_t b0 = sb + (isq ? OFF_Q0 : OFF_K0) + 128u * t;
         float ss = 0.f;
 #pragma unroll
@@ -437,61 +509,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     ph_mma ^= 1;
     mma_pending = false;
     tc_fence_after();
+    if (more) {  // the Q tile is consumed: fetch the next one
+      if (tid == 0) issue_tiles(c + 1, OFF_Q0, OFF_Q1, &tm_q, qh);
+      tma_pending = true;
+    }
 
-    // (3) A (from Skk) -> Amat;  P (from Sqk) -> bf16 [t][j];  Q~ = gamma rq Q in place
+    // (3) A (from Skk) -> Amat;  P (from Sqk) -> bf16 [t][j] (hi, and lo for raw q/k);
+    //     S K^T -> hi/lo K-major [v][t]
     {
-      float kq[32];
-      tmem_ld32(tl + TM_KQ + 32u * half, kq);
+      float kq[16];
+      tmem_ld16(tl + TM_KQ + 16u * qtr, kq);
+      float sk[16];
+      tmem_ld16(tl + TM_SK + 16u * qtr, sk);
+      // all shared-memory operands first (the stores below would otherwise order
+      // every later load behind them)
+      const int t = row & 63;
+      const bool is_k = row < 64;
+      const float lt = Lam[t];
+      const float ft = is_k ? beta[t] * rk[t] : rq[t];
+      float lv[16], rv[16];
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 lj = *reinterpret_cast<const float4*>(Lam + 16 * qtr + i);
+        const float4 rj = *reinterpret_cast<const float4*>(rk + 16 * qtr + i);
+        lv[i] = lj.x; lv[i + 1] = lj.y; lv[i + 2] = lj.z; lv[i + 3] = lj.w;
+        rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
+      }
       tmem_wait_ld();
-      if (row < 64) {
-        const int t = row;
-        const float bt = beta[t] * rk[t], lt = Lam[t];
+      float ej[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = 32 * half + i;
-          Amat[t * kLdA + j] = (j < t) ? bt * expf(lt - Lam[j]) * rk[j] * kq[i] : 0.f;
-        }
+      for (int i = 0; i < 16; ++i) {
+        const int j = 16 * qtr + i;
+        // A: strictly lower (j < t); P: lower incl. diagonal (j <= t)
+        const bool keep = is_k ? (j < t) : (j <= t);
+        ej[i] = keep ? ft * rv[i] * kq[i] * __expf(lt - lv[i]) : 0.f;
+      }
+      if (is_k) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Amat[t * kLdA + 16 * qtr + i] = ej[i];
       } else {
-        const int t = row - 64;
-        const float qt = rq[t];
-        write_p(kq, false);
-        // scale this thread's half of Q row t
-        const float f = gam[t] * qt;
-        const uint32_t qb = sb + (half ? OFF_Q1 : OFF_Q0);
 #pragma unroll
-        for (int ci = 0; ci < 8; ++ci) {
-          const int ch = (ci + t) & 7;
-          const uint32_t addr = qb + 128u * t + 16u * ch;
-          const uint4 u = ld_shared_v4(addr);
-          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-          float x[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f2 = bf2x2_to_f2(w4[e]);
-            x[2 * e] = f2.x * f;
-            x[2 * e + 1] = f2.y * f;
-          }
-          st_v4(addr, pack8(x));
+        for (int q2 = 0; q2 < 2; ++q2) {
+          uint4 hi, lo;
+          split8(&ej[8 * q2], hi, lo);
+          st_v4(sb + OFF_P + sw128(t, 2 * qtr + q2), hi);
+          if constexpr (!L2NORM) st_v4(sb + OFF_PLO + sw128(t, 2 * qtr + q2), lo);
         }
+      }
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        uint4 hi, lo;
+        split8(&sk[8 * q2], hi, lo);
+        st_v4(sb + OFF_SKHI + sw128(row, 2 * qtr + q2), hi);
+        st_v4(sb + OFF_SKLO + sw128(row, 2 * qtr + q2), lo);
       }
     }
     __syncthreads();
 
     // (4) T = (I + A)^-1;  T1 = T diag(beta gamma rk), T2 = T diag(beta) -> hi/lo bf16
     invert_unit_lower64(Amat, Tmat, Escr);
-#pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2) {
-      const int u = tid + kThreads * k2;  // 512 (row, 16B chunk) units
-      const int t = u >> 3, cidx = u & 7;
-      float w1[8], w2[8];
-      const float4 ta = *reinterpret_cast<const float4*>(Tmat + t * 64 + 8 * cidx);
-      const float4 tb = *reinterpret_cast<const float4*>(Tmat + t * 64 + 8 * cidx + 4);
-      const float tv8[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+    {
+      // thread -> 16-byte column chunk cidx of row t
+      const int cidx = tid & 7, t = tid >> 3;
+      float cb[8], cg[8], tv[8];
+      const float* tr = Tmat + t * kLdT + 8 * cidx;
+      const float4 ta = *reinterpret_cast<const float4*>(tr);
+      const float4 tb = *reinterpret_cast<const float4*>(tr + 4);
+      tv[0] = ta.x; tv[1] = ta.y; tv[2] = ta.z; tv[3] = ta.w;
+      tv[4] = tb.x; tv[5] = tb.y; tv[6] = tb.z; tv[7] = tb.w;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int j = 8 * cidx + e;
-        w2[e] = tv8[e] * beta[j];
-        w1[e] = w2[e] * gam[j] * rk[j];
+        cb[e] = beta[j];
+        cg[e] = beta[j] * gam[j] * rk[j];
+      }
+      float w1[8], w2[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        w1[e] = tv[e] * cg[e];
+        w2[e] = tv[e] * cb[e];
       }
       uint4 hi, lo;
       split8(w1, hi, lo);
@@ -506,112 +602,70 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
 
-    // (5) W^T = K^T T1^T,  U0^T = V^T T2^T,  O^T = S_hi Q~^T
+    // (5) MMA group 2: U^T = V^T T2^T - (S K^T) T1^T
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t id_w = umma_idesc_bf16(128, 64, true, false);
+      const uint32_t id_v = umma_idesc_bf16(128, 64, true, false);
+      const uint32_t id_x = umma_idesc_bf16(128, 64, false, false, true);
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
-        const uint32_t t1 = sb + OFF_U + (part ? U_T1LO : U_T1HI);
         const uint32_t t2 = sb + OFF_U + (part ? U_T2LO : U_T2HI);
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          umma_bf16(tmem + TM_WT, umma_desc_mn(sb + OFF_K0 + 2048u * ks, 16384),
-                    umma_desc_k(t1 + 32u * ks), id_w, (part | ks) != 0);
+        for (int ks = 0; ks < 4; ++ks)
           umma_bf16(tmem + TM_UT, umma_desc_mn(sb + OFF_V + 2048u * ks, 8192),
-                    umma_desc_k(t2 + 32u * ks), id_w, (part | ks) != 0);
-        }
+                    umma_desc_k(t2 + 32u * ks), id_v, (part | ks) != 0);
       }
-      const uint32_t id_o = umma_idesc_bf16(128, 64, false, false);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t kb = 32u * (ks & 3);
-        umma_bf16(tmem + TM_OT, umma_desc_k(sb + OFF_SHI + 16384u * (ks >> 2) + kb),
-                  umma_desc_k(sb + ((ks >> 2) ? OFF_Q1 : OFF_Q0) + kb), id_o, ks > 0);
-      }
-      umma_commit(bar_mma);
-    }
-    mma_pending = true;
-    if (!cta_wait(bar_mma, ph_mma, ERR_MMA_TIMEOUT)) { ok = false; break; }
-    ph_mma ^= 1;
-    mma_pending = false;
-    tc_fence_after();
-
-    // (6) W^T -> hi/lo, MN-major [d][t]
-    {
-      float wv[32];
-      tmem_ld32(tl + TM_WT + 32u * half, wv);
-      tmem_wait_ld();
+      for (int term = 0; term < 3; ++term) {  // (SK_hi,T1_hi) (SK_lo,T1_hi) (SK_hi,T1_lo)
+        const uint32_t a = sb + (term == 1 ? OFF_SKLO : OFF_SKHI);
+        const uint32_t b = sb + OFF_U + (term == 2 ? U_T1LO : U_T1HI);
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint4 hi, lo;
-        split8(&wv[8 * q4], hi, lo);
-        st_v4(sb + OFF_WHI + sw128(row, 4 * half + q4), hi);
-        st_v4(sb + OFF_WLO + sw128(row, 4 * half + q4), lo);
-      }
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-
-    // (7) U^T -= S W^T  (hi.hi + lo.hi + hi.lo)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t id_x = umma_idesc_bf16(128, 64, false, true, true);
-#pragma unroll
-      for (int term = 0; term < 3; ++term) {
-        const uint32_t sa = sb + (term == 1 ? OFF_SLO : OFF_SHI);
-        const uint32_t wb = sb + (term == 2 ? OFF_WLO : OFF_WHI);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tmem + TM_UT, umma_desc_k(sa + 16384u * (ks >> 2) + 32u * (ks & 3)),
-                    umma_desc_mn(wb + 2048u * ks, 8192), id_x, 1);
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + TM_UT, umma_desc_k(a + 32u * ks), umma_desc_k(b + 32u * ks), id_x, 1);
       }
       umma_commit(bar_mma);
     }
     mma_pending = true;
+    if (warp == 1 && more) finish_gates(c + 1, (c + 1) & 1);
     if (!cta_wait(bar_mma, ph_mma, ERR_MMA_TIMEOUT)) { ok = false; break; }
     ph_mma ^= 1;
     mma_pending = false;
     tc_fence_after();
+    if (more) {  // the V tile is consumed
+      if (tid == 0) issue_tiles(c + 1, OFF_V, OFF_V + 8192, &tm_v, h);
+      tma_pending = true;
+    }
 
-    // (8) U -> U~ = diag(us) U (hi/lo) and U hi, K-major [v][t]
+    // (6) U -> U~ = diag(us) U (hi/lo) and U hi (lo), K-major [v][t]
     {
-      float uv[32];
-      tmem_ld32(tl + TM_UT + 32u * half, uv);
+      float uv[16], uw[16];
+      tmem_ld16(tl + TM_UT + 16u * qtr, uv);
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(us + 16 * qtr + i);
+        uw[i] = w4.x; uw[i + 1] = w4.y; uw[i + 2] = w4.z; uw[i + 3] = w4.w;
+      }
       tmem_wait_ld();
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         float x[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = uv[8 * q4 + e] * us[32 * half + 8 * q4 + e];
+        for (int e = 0; e < 8; ++e) x[e] = uv[8 * q2 + e] * uw[8 * q2 + e];
         uint4 hi, lo;
         split8(x, hi, lo);
-        const uint32_t o = sw128(row, 4 * half + q4);
+        const uint32_t o = sw128(row, 2 * qtr + q2);
         st_v4(sb + OFF_U + U_UTHI + o, hi);
         st_v4(sb + OFF_U + U_UTLO + o, lo);
-        split8(&uv[8 * q4], hi, lo);
+        split8(&uv[8 * q2], hi, lo);
         st_v4(sb + OFF_U + U_UHI + o, hi);
         if constexpr (!L2NORM) st_v4(sb + OFF_U + U_ULO + o, lo);
       }
-      if constexpr (!L2NORM) {
-        if (row >= 64) {  // P lo residual from Sqk, still resident in TMEM
-          float kq[32];
-          tmem_ld32(tl + TM_KQ + 32u * half, kq);
-          tmem_wait_ld();
-          write_p(kq, true);
-        } else {
-          float kq[32];  // keep the warp-collective load uniform across warps
-          tmem_ld32(tl + TM_KQ + 32u * half, kq);
-          tmem_wait_ld();
-        }
-      }
     }
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
 
-    // (9) dS = U~^T K (hi + lo);  O^T += U_hi^T P^T
+    // (7) MMA group 3: dS = U~^T K (hi + lo);  Ot = U^T P^T
     if (tid == 0) {
       tc_fence_after();
       const uint32_t id_s = umma_idesc_bf16(128, 128, false, true);
@@ -630,7 +684,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t pb = sb + (term == 2 ? OFF_PLO : OFF_P);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_bf16(tmem + TM_OT, umma_desc_k(ua + 32u * ks), umma_desc_k(pb + 32u * ks), id_p, 1);
+          umma_bf16(tmem + TM_OT, umma_desc_k(ua + 32u * ks), umma_desc_k(pb + 32u * ks), id_p,
+                    (term | ks) != 0);
       }
       umma_commit(bar_mma);
     }
@@ -639,43 +694,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     ph_mma ^= 1;
     mma_pending = false;
     tc_fence_after();
+    if (more && tid == 0) issue_tiles(c + 1, OFF_K0, OFF_K1, &tm_k, qh);  // K consumed
 
-    // (10) S <- G S + dS ; O^T -> staging [t][v] bf16 ; new S hi/lo
+    // (8) S <- G S + dS ;  O = scale (diag(gamma rq) Oi + Ot) -> staging [t][v] ; S hi/lo
     {
       const float G = expf(Lam[63]);
+      float dv[32];
+      tmem_ld32(tl + TM_DS + 32u * qtr, dv);
+      float oi[16], ot[16], fo[16];
+      tmem_ld16(tl + TM_OI + 16u * qtr, oi);
+      tmem_ld16(tl + TM_OT + 16u * qtr, ot);
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        float dv[32];
-        tmem_ld32(tl + TM_DS + 64u * half + 32u * part, dv);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 * part + i] = fmaf(G, s[32 * part + i], dv[i]);
+      for (int i = 0; i < 16; i += 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gam + 16 * qtr + i);
+        const float4 q4 = *reinterpret_cast<const float4*>(rq + 16 * qtr + i);
+        fo[i] = g4.x * q4.x; fo[i + 1] = g4.y * q4.y; fo[i + 2] = g4.z * q4.z; fo[i + 3] = g4.w * q4.w;
       }
-      float ov[32];
-      tmem_ld32(tl + TM_OT + 32u * half, ov);
       tmem_wait_ld();
-      __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(smem + OFF_V);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        ostage[(32 * half + i) * kHeadDim + row] = __float2bfloat16_rn(scale * ov[i]);
-      if (c + 1 < nchunks) write_state_split();
+      for (int i = 0; i < 32; ++i) s[i] = fmaf(G, s[i], dv[i]);
+      uint16_t* ostage = reinterpret_cast<uint16_t*>(smem + OFF_OST);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        ostage[(16 * qtr + i) * kHeadDim + row] = (uint16_t)(
+            rn_bf16_bits(__float_as_uint(scale * fmaf(fo[i], oi[i], ot[i]))) >> 16);
+      if (more) write_state_split();
     }
     tc_fence_before();
     __syncthreads();
     // coalesced output rows (t < Lc): 16 x 16-byte pieces per 256-byte row
     {
       __nv_bfloat16* obase = p.out + ((size_t)t0 * HV + h) * kHeadDim;
-      for (int u = tid; u < Lc * 16; u += kThreads) {
-        const int t = u >> 4, ch = u & 15;
-        const uint4 v4 = ld_shared_v4(sb + OFF_V + 256u * t + 16u * ch);
-        *reinterpret_cast<uint4*>(obase + (size_t)t * HV * kHeadDim + 8 * ch) = v4;
+      constexpr int kUnits = 64 * 16 / kThreads;  // 16-byte pieces per thread
+      uint4 v4[kUnits];
+#pragma unroll
+      for (int k4 = 0; k4 < kUnits; ++k4) {
+        const int u = tid + kThreads * k4;
+        v4[k4] = ld_shared_v4(sb + OFF_OST + 256u * (u >> 4) + 16u * (u & 15));
+      }
+#pragma unroll
+      for (int k4 = 0; k4 < kUnits; ++k4) {
+        const int u = tid + kThreads * k4, t = u >> 4;
+        if (t < Lc)
+          *reinterpret_cast<uint4*>(obase + (size_t)t * HV * kHeadDim + 8 * (u & 15)) = v4[k4];
       }
     }
   }
 
   if (ok) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < 8; ++i)
       st_stream_f4(nsrow + 4 * i, make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]));
   } else {
     // a wait ran out: give in-flight copies / MMAs one more bounded chance to land
