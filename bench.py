@@ -181,17 +181,6 @@ class Dist:
             self.pg.destroy_process_group()
 
 
-def lpt_shard(lengths, n):
-    """Longest-processing-time bin packing of sequence indices onto n ranks."""
-    bins = [[] for _ in range(n)]
-    load = [0] * n
-    for i in sorted(range(len(lengths)), key=lambda i: -lengths[i]):
-        j = min(range(n), key=lambda j: load[j])
-        bins[j].append(i)
-        load[j] += lengths[i]
-    return [sorted(b) for b in bins]
-
-
 # --------------------------------------------------------------------------- workloads
 class DecodeWork:
     """One decode step over `batch` sequences; state ping-pongs between two buffers."""
@@ -244,22 +233,9 @@ class PrefillWork:
         W = pkg.workloads
         self.pkg, self.dev = pkg, dev
         inp = W.prefill_config_inputs(cfg_name, seed=seed, device="cpu")
-        cu = inp["cu_seqlens"].tolist()
-        lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
-        if shard is not None:
-            idx = shard
-            parts = [(cu[i], cu[i + 1]) for i in idx]
-            take = torch.cat([torch.arange(a, b) for a, b in parts]) if parts else \
-                torch.zeros(0, dtype=torch.long)
-            lens = [lens[i] for i in idx]
-            for k_ in ("q", "k", "v", "a", "b"):
-                inp[k_] = inp[k_][take].contiguous()
-            if inp["state"] is not None:
-                inp["state"] = inp["state"][idx].contiguous()
-            c = torch.zeros(len(lens) + 1, dtype=torch.int32)
-            if lens:
-                c[1:] = torch.tensor(lens).cumsum(0)
-            inp["cu_seqlens"] = c
+        if shard is not None:  # this rank's sequences, re-packed (no collective)
+            inp = pkg.sharding.prefill_shard(inp, shard)
+        lens = pkg.sharding.seqlens_from_cu(inp["cu_seqlens"])
         self.lens = lens
         self.inp = {k_: (v_.to(dev) if isinstance(v_, torch.Tensor) else v_) for k_, v_ in inp.items()}
         self.cpu_inp = inp
@@ -466,7 +442,7 @@ def run_ours(args, dist):
             W = pkg.workloads
             cfg = W.PREFILL_CONFIGS[param]
             lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
-            shard = lpt_shard(lens, dist.world)[dist.rank]
+            shard = pkg.sharding.lpt_assign(lens, dist.world)[dist.rank]
         r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
         line.update({
             "metric": "prefill tokens/s", "value": round(r["value"], 1), "unit": "tokens/s",
@@ -491,7 +467,8 @@ def run_ours(args, dist):
             if dist.world > 1:
                 W = pkg.workloads
                 cfg = W.PREFILL_CONFIGS[nm]
-                shard = lpt_shard(W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0), dist.world)[dist.rank]
+                shard = pkg.sharding.lpt_assign(W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0),
+                                                dist.world)[dist.rank]
             r = measure_prefill(pkg, dist, nm, max(3, min(args.steps, 10)), 3, dev, shard=shard,
                                 with_e2e=False)
             extra[nm] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),

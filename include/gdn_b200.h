@@ -96,7 +96,10 @@ size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_head
  *   output   bf16 [total_tokens, max(num_q_heads, num_v_heads), 128]  (written)
  *   new_state fp32 [num_seqs, max(num_q_heads, num_v_heads), 128, 128] (written)
  *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes
- *              (may be NULL when that size is 0)
+ *              (may be NULL when that size is 0).  Scratch only: it holds the
+ *              longest-first order in which the sequences are scheduled, is
+ *              rewritten by every call, and must not be shared by calls that
+ *              overlap on the GPU.
  * A sequence of length 0 gets an all-zero new_state slice (as the
  * flashinfer-bench definition reference does).
  * Replaces gdn_prefill_chunk_kernel (gdn_prefill/solution/triton/kernel.py:28-250)
@@ -115,7 +118,8 @@ int gdn_prefill_launch(const void* q, const void* k, const void* v, const float*
  * recurrent CUDA-core kernel (the definition's per-token recurrence, exact to
  * fp32 rounding) instead of the chunked tensor-core kernel.  For validation
  * and for callers whose buffers do not meet the chunked kernel's 16-byte
- * alignment.  Same reference interface as gdn_prefill_launch.
+ * alignment.  `workspace` is ignored.  Same reference interface as
+ * gdn_prefill_launch.
  */
 int gdn_prefill_launch_recurrent(const void* q, const void* k, const void* v, const float* state,
                                  const float* A_log, const void* a, const float* dt_bias,

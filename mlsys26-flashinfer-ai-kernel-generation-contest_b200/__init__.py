@@ -18,8 +18,8 @@ from ._lib import LIB, LIB_PATH, GDNError, device_error  # noqa: F401
 from .decode import gdn_decode, kernel as decode_kernel  # noqa: F401
 from .prefill import (gdn_prefill, gdn_prefill_recurrent, kernel as prefill_kernel,  # noqa: F401
                       workspace_bytes)
-from . import decode, prefill, workloads  # noqa: F401
+from . import decode, prefill, sharding, workloads  # noqa: F401
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "decode_kernel",
-           "prefill_kernel", "workloads", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
+           "prefill_kernel", "workloads", "sharding", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
            "device_error"]

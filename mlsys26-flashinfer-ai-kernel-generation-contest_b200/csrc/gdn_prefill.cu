@@ -16,12 +16,11 @@ inline bool misaligned(const void* p, uintptr_t n) {
 
 extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
                                              int num_v_heads, int head_size) {
-  (void)total_tokens;
-  (void)num_seqs;
   (void)num_q_heads;
   (void)num_v_heads;
   (void)head_size;
-  return 0;
+  if (total_tokens <= 0) return 0;
+  return gdn::prefill_chunked_workspace(num_seqs);  // longest-first sequence order
 }
 
 namespace {
@@ -49,7 +48,8 @@ int prefill_entry(PrefillPath path, const void* q, const void* k, const void* v,
   if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
   const size_t need =
       gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads, num_v_heads, head_size);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
+  if (path == PrefillPath::kAuto && need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return GDN_ERR_WORKSPACE;  // (the recurrent kernel uses no workspace)
 
   PrefillArgs p{q,        k,     v,      state,      A_log,        a,           dt_bias,
                 b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,

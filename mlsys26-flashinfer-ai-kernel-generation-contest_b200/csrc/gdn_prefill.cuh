@@ -36,6 +36,8 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs& p, int seq_offset, int n
 // Chunked tcgen05 kernel (all sequences).  Needs T > 0, 16-byte aligned q/k/v/out
 // and the driver's tensor-map encoder.
 bool prefill_chunked_supported(const PrefillArgs& p);
+// Scratch bytes the chunked path uses for its longest-first sequence order.
+size_t prefill_chunked_workspace(int num_seqs);
 cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st);
 
 // Device-side error flag set by a bounded wait that ran out (0 = none).

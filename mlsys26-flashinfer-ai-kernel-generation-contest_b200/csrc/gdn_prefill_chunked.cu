@@ -115,6 +115,7 @@ struct ChunkedParams {
   const float* state;
   float* new_state;
   __nv_bfloat16* out;
+  const int* order;  // longest-first sequence order (may be null: natural order)
   long long T;
   int cu64;
   int HV;
@@ -149,10 +150,6 @@ __device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
                   pack_hi16(hb[6], hb[7]));
   lo = make_uint4(pack_hi16(lb[0], lb[1]), pack_hi16(lb[2], lb[3]), pack_hi16(lb[4], lb[5]),
                   pack_hi16(lb[6], lb[7]));
-}
-__device__ __forceinline__ uint4 pack8(const float* x) {
-  return make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
-                    pack_bf16(x[6], x[7]));
 }
 // 16 consecutive fp32 TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -295,8 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int sp = warp & 3, qtr = warp >> 2;  // TMEM subpartition, column quarter
   const int row = sp * 32 + lane;  // TMEM lane owned by this thread
   const int HV = p.HV;
-  const int n = blockIdx.x / HV;
-  const int h = blockIdx.x - n * HV;
+  const int wi = blockIdx.x / HV;  // work item: the wi-th longest sequence
+  const int h = blockIdx.x - wi * HV;
+  const int n = p.order ? p.order[wi] : wi;
   const int qh = h / p.ratio;
   const CuT* cu = static_cast<const CuT*>(p.cu);
   const long long s1 = min(max((long long)cu[n + 1], 0LL), p.T);
@@ -755,6 +753,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, TM_COLS);
 }
 
+// ---------------------------------------------------------------- LPT order
+// CTAs are scheduled roughly in blockIdx order and one CTA fills an SM, so
+// handing out the longest sequences first (longest-processing-time) keeps the
+// last wave short.  One CTA bitonic-sorts (length desc, index asc) keys in
+// shared memory and writes the permutation.
+constexpr int kLptMaxSeqs = 8192;
+
+template <typename CuT>
+__global__ void __launch_bounds__(1024) lpt_order_kernel(const CuT* __restrict__ cu, int N,
+                                                         long long T, int* __restrict__ order) {
+  extern __shared__ unsigned long long keys[];
+  int P = 1;
+  while (P < N) P <<= 1;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    unsigned long long key = 0ull;  // padding sorts last
+    if (i < N) {
+      const long long a = min(max((long long)cu[i], 0LL), T);
+      const long long b = min(max((long long)cu[i + 1], 0LL), T);
+      const unsigned long long len = (unsigned long long)max(b - a, 0LL);
+      key = (len << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int l = i ^ j;
+        if (l > i) {
+          const unsigned long long x = keys[i], y = keys[l];
+          const bool desc = (i & k) == 0;  // descending overall
+          if (desc ? (x < y) : (x > y)) {
+            keys[i] = y;
+            keys[l] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < N; i += blockDim.x)
+    order[i] = (int)(0xFFFFFFFFu - (unsigned)(keys[i] & 0xFFFFFFFFull));
+}
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -815,6 +857,11 @@ cudaError_t launch_chunked_cu(const CUtensorMap& mq, const CUtensorMap& mk, cons
 
 }  // namespace
 
+size_t prefill_chunked_workspace(int num_seqs) {
+  if (num_seqs <= 1 || num_seqs > kLptMaxSeqs) return 0;
+  return ((size_t)num_seqs * sizeof(int) + 255) & ~(size_t)255;
+}
+
 bool prefill_chunked_supported(const PrefillArgs& p) {
   const auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   return p.T > 0 && p.T < (1LL << 31) && a16(p.q) && a16(p.k) && a16(p.v) && a16(p.out) &&
@@ -826,9 +873,34 @@ cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st) {
   if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
       !make_tile_map(&mv, p.v, p.HV, p.T))
     return cudaErrorInvalidValue;
+  int* order = nullptr;
+  if (p.N > 1 && p.N <= kLptMaxSeqs && p.workspace != nullptr &&
+      p.workspace_bytes >= (size_t)p.N * sizeof(int)) {
+    order = static_cast<int*>(p.workspace);
+    int P = 1;
+    while (P < p.N) P <<= 1;
+    const size_t sm = (size_t)P * sizeof(unsigned long long);
+    static bool lpt_configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !lpt_configured[dev]) {
+      cudaFuncSetAttribute(lpt_order_kernel<int>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kLptMaxSeqs * 8);
+      cudaFuncSetAttribute(lpt_order_kernel<long long>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, kLptMaxSeqs * 8);
+      if (dev >= 0 && dev < 64) lpt_configured[dev] = true;
+    }
+    if (p.cu_int64)
+      lpt_order_kernel<long long><<<1, 1024, sm, st>>>(static_cast<const long long*>(p.cu), p.N,
+                                                        p.T, order);
+    else
+      lpt_order_kernel<int><<<1, 1024, sm, st>>>(static_cast<const int*>(p.cu), p.N, p.T, order);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   ChunkedParams cp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
                    p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
-                   static_cast<__nv_bfloat16*>(p.out), p.T, p.cu_int64 ? 1 : 0, p.HV,
+                   static_cast<__nv_bfloat16*>(p.out), order, p.T, p.cu_int64 ? 1 : 0, p.HV,
                    p.HV / p.HQ, p.scale};
   if (p.cu_int64)
     return launch_chunked_cu<long long>(mq, mk, mv, cp, p.l2norm, p.state != nullptr, p.N, st);

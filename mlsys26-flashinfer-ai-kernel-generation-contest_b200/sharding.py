@@ -1,0 +1,96 @@
+"""Multi-GPU partitioning of the GDN workloads (one process per GPU, no collective).
+
+Every unit of GDN work is independent of every other one:
+
+* decode: each (batch row, v-head) state is updated from that row's own q/k/v,
+  so a batch splits into contiguous row ranges, one per rank;
+* prefill: each sequence's scan touches only its own tokens and state slice,
+  so whole sequences are dealt to ranks; the packed token ranges of a rank's
+  sequences are gathered into a rank-local packed layout with re-based
+  ``cu_seqlens`` (0, len0, len0+len1, ...).
+
+Load balance for prefill uses longest-processing-time bin packing on token
+counts.  There is no exchange step on the data path, so there is no NCCL
+call in the timed region; results are gathered (to the host, outside timing)
+only for verification.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Sequence, Tuple
+
+import torch
+
+
+def batch_range(batch: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [lo, hi) row range of `rank` when `batch` rows are split over `world`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    base, extra = divmod(batch, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def lpt_assign(lengths: Sequence[int], world: int) -> List[List[int]]:
+    """Longest-first greedy bin packing: sequence indices per rank (each sorted).
+
+    Every index appears in exactly one bin; ties go to the lowest rank, so the
+    plan is deterministic.
+    """
+    if world <= 0:
+        raise ValueError("world must be positive")
+    bins: List[List[int]] = [[] for _ in range(world)]
+    load = [0] * world
+    for i in sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i)):
+        j = min(range(world), key=lambda r: (load[r], r))
+        bins[j].append(i)
+        load[j] += int(lengths[i])
+    return [sorted(b) for b in bins]
+
+
+def seqlens_from_cu(cu_seqlens: torch.Tensor) -> List[int]:
+    cu = [int(x) for x in cu_seqlens.tolist()]
+    return [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
+
+
+def prefill_shard(inp: Dict[str, torch.Tensor], seq_ids: Sequence[int]) -> Dict[str, torch.Tensor]:
+    """The rank-local prefill problem for sequences `seq_ids` (host or device tensors).
+
+    Token-indexed tensors (q, k, v, a, b) are gathered, the initial state (if
+    any) is sliced, and cu_seqlens is re-based.  Per-head parameters and
+    scale are shared.
+    """
+    cu = [int(x) for x in inp["cu_seqlens"].tolist()]
+    dev = inp["q"].device
+    idx = [torch.arange(cu[i], cu[i + 1], device=dev) for i in seq_ids]
+    take = torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long, device=dev)
+    out = dict(inp)
+    for key in ("q", "k", "v", "a", "b"):
+        out[key] = inp[key].index_select(0, take).contiguous()
+    if inp.get("state") is not None:
+        sel = torch.tensor(list(seq_ids), dtype=torch.long, device=inp["state"].device)
+        out["state"] = inp["state"].index_select(0, sel).contiguous()
+    lens = [cu[i + 1] - cu[i] for i in seq_ids]
+    c = torch.zeros(len(lens) + 1, dtype=inp["cu_seqlens"].dtype)
+    if lens:
+        c[1:] = torch.tensor(lens, dtype=torch.int64).cumsum(0).to(c.dtype)
+    out["cu_seqlens"] = c.to(inp["cu_seqlens"].device)
+    return out
+
+
+def prefill_unshard(full_tokens: int, num_seqs: int, cu_seqlens: torch.Tensor,
+                    plan: Sequence[Sequence[int]],
+                    outputs: Sequence[torch.Tensor], states: Sequence[torch.Tensor]
+                    ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Reassemble per-rank (output, new_state) into the unsharded layout."""
+    cu = [int(x) for x in cu_seqlens.tolist()]
+    o0, s0 = outputs[0], states[0]
+    out = torch.zeros((full_tokens,) + tuple(o0.shape[1:]), dtype=o0.dtype)
+    st = torch.zeros((num_seqs,) + tuple(s0.shape[1:]), dtype=s0.dtype)
+    for ids, o, s in zip(plan, outputs, states):
+        pos = 0
+        for j, i in enumerate(ids):
+            n = cu[i + 1] - cu[i]
+            out[cu[i]:cu[i + 1]] = o[pos:pos + n].cpu()
+            st[i] = s[j].cpu()
+            pos += n
+    return out, st

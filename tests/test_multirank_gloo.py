@@ -1,0 +1,125 @@
+"""CPU, world_size 2 over gloo: the one-process-per-GPU driver's host logic.
+
+* sharded decode and prefill (oracle as the per-rank compute) reassemble into
+  the unsharded result, and the max-over-ranks timing reduction works;
+* failure detection on the host: a rank that dies before the barrier makes
+  the surviving rank's next collective end with an error within the process
+  group's short timeout instead of hanging.
+"""
+import datetime
+import os
+import socket
+import sys
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG_NAME, REPO
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker_sharded(rank, world, port, q):
+    try:
+        sys.path.insert(0, str(REPO))
+        import importlib
+        pkg = importlib.import_module(PKG_NAME)
+        from oracle import gdn_oracle as O
+        _init(rank, world, port, 60)
+        S, W = pkg.sharding, pkg.workloads
+        # decode: batch-sharded
+        inp = W.decode_inputs(5, hq=1, hv=2, seed=7)
+        lo, hi = S.batch_range(5, world, rank)
+        o, s = O.decode(inp["q"][lo:hi], inp["k"][lo:hi], inp["v"][lo:hi], inp["state"][lo:hi],
+                        inp["A_log"], inp["a"][lo:hi], inp["dt_bias"], inp["b"][lo:hi],
+                        inp["scale"])
+        dec = [None] * world
+        dist.all_gather_object(dec, (o, s))
+        # prefill: longest-first sequence sharding
+        lens = [4, 11, 0, 7, 2]
+        pinp = W.prefill_inputs(lens, hq=1, hv=2, seed=8)
+        plan = S.lpt_assign(lens, world)
+        sh = S.prefill_shard(pinp, plan[rank])
+        po, ps = O.prefill(sh["q"], sh["k"], sh["v"], sh["state"], sh["A_log"], sh["a"],
+                           sh["dt_bias"], sh["b"], sh["cu_seqlens"], sh["scale"])
+        pre = [None] * world
+        dist.all_gather_object(pre, (po, ps))
+        # max-over-ranks reduction used for the bench timing
+        t = torch.tensor([float(rank + 1)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            full_o, full_s = O.decode(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"],
+                                      inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+            ok_dec = torch.equal(torch.cat([d[0] for d in dec]), full_o) and \
+                O.state_rel_err(torch.cat([d[1] for d in dec]), full_s) < 1e-6
+            ro, rs = O.prefill(pinp["q"], pinp["k"], pinp["v"], pinp["state"], pinp["A_log"],
+                               pinp["a"], pinp["dt_bias"], pinp["b"], pinp["cu_seqlens"],
+                               pinp["scale"])
+            uo, us = S.prefill_unshard(sum(lens), len(lens), pinp["cu_seqlens"], plan,
+                                       [x[0] for x in pre], [x[1] for x in pre])
+            ok_pre = torch.equal(uo, ro) and O.state_rel_err(us, rs) < 1e-6
+            q.put(("ok", ok_dec, ok_pre, float(t.item())))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
+def _worker_failing(rank, world, port, q):
+    try:
+        _init(rank, world, port, 3)
+        if rank == 1:
+            os._exit(0)  # leaves between steps, without joining the next collective
+        try:
+            dist.barrier()
+            q.put(("no-error",))
+        except Exception as e:  # the surviving rank learns of it on the host
+            q.put(("detected", type(e).__name__))
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
+def _run(fn, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("worker did not finish")
+    items = []
+    while not q.empty():
+        items.append(q.get())
+    return items
+
+
+def test_two_rank_sharded_results_match_unsharded():
+    items = _run(_worker_sharded)
+    assert items, "no result from rank 0"
+    assert all(i[0] == "ok" for i in items), items
+    _, ok_dec, ok_pre, tmax = items[0]
+    assert ok_dec and ok_pre
+    assert tmax == 2.0
+
+
+def test_dead_rank_is_detected_not_hung():
+    items = _run(_worker_failing)
+    assert ("detected",) == items[0][:1], items

@@ -1,0 +1,59 @@
+"""CPU: multi-GPU partitioning plans (batch ranges, longest-first sequence packing)
+and the shard -> unshard round trip, checked with the oracle on small problems."""
+import pytest
+import torch
+
+from conftest import load_pkg
+from oracle import gdn_oracle as O
+
+
+def test_batch_ranges_cover_exactly():
+    S = load_pkg().sharding
+    for batch in (0, 1, 7, 128, 1024):
+        for world in (1, 2, 3, 8):
+            rs = [S.batch_range(batch, world, r) for r in range(world)]
+            assert rs[0][0] == 0 and rs[-1][1] == batch
+            assert all(a[1] == b[0] for a, b in zip(rs, rs[1:]))
+            sizes = [hi - lo for lo, hi in rs]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        S.batch_range(4, 2, 2)
+
+
+def test_lpt_assign_partition_and_balance():
+    pkg = load_pkg()
+    S, W = pkg.sharding, pkg.workloads
+    cfg = W.PREFILL_CONFIGS["P3"]
+    lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
+    for world in (1, 2, 4, 8):
+        plan = S.lpt_assign(lens, world)
+        flat = sorted(i for b in plan for i in b)
+        assert flat == list(range(len(lens)))
+        loads = [sum(lens[i] for i in b) for b in plan]
+        # LPT bound: max load <= mean + longest item
+        assert max(loads) <= sum(lens) / world + max(lens)
+    assert S.lpt_assign([5, 0, 9], 2) == S.lpt_assign([5, 0, 9], 2)  # deterministic
+
+
+def test_prefill_shard_roundtrip_matches_unsharded_oracle():
+    pkg = load_pkg()
+    S, W = pkg.sharding, pkg.workloads
+    lens = [5, 0, 9, 3, 12]
+    inp = W.prefill_inputs(lens, hq=1, hv=2, seed=3)
+    full_o, full_s = O.prefill(O.l2norm(inp["q"]), O.l2norm(inp["k"]), inp["v"], inp["state"],
+                               inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                               inp["cu_seqlens"], inp["scale"])
+    plan = S.lpt_assign(lens, 3)
+    outs, states = [], []
+    for ids in plan:
+        sh = S.prefill_shard(inp, ids)
+        assert int(sh["cu_seqlens"][-1]) == sh["q"].shape[0] == sum(lens[i] for i in ids)
+        o, s = O.prefill(O.l2norm(sh["q"]), O.l2norm(sh["k"]), sh["v"], sh["state"],
+                         sh["A_log"], sh["a"], sh["dt_bias"], sh["b"], sh["cu_seqlens"],
+                         sh["scale"])
+        outs.append(o)
+        states.append(s)
+    o, s = S.prefill_unshard(sum(lens), len(lens), inp["cu_seqlens"], plan, outs, states)
+    assert torch.equal(o, full_o)
+    # same recurrence per sequence; the batched einsum may only reorder fp32 sums
+    assert O.state_rel_err(s, full_s) < 1e-6
