@@ -51,6 +51,7 @@ extern "C" {
 #define GDN_ERR_UNSUPPORTED (-2)      /* head_size != 128, bad head ratio, ...    */
 #define GDN_ERR_LAUNCH (-3)           /* the CUDA launch itself reported an error */
 #define GDN_ERR_WORKSPACE (-4)        /* workspace missing or too small           */
+#define GDN_ERR_TOO_LARGE (-5)        /* beyond a fixed capacity (no-alloc entry) */
 
 /* Library version, e.g. 100 for 0.1.0. */
 int gdn_b200_version(void);
@@ -128,6 +129,29 @@ int gdn_prefill_launch_recurrent(const void* q, const void* k, const void* v, co
                                  int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
                                  int head_size, int use_qk_l2norm, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/*
+ * Allocation-free variant of gdn_prefill_launch (no counterpart in the
+ * reference).  For callers that cannot allocate device memory where they
+ * launch -- inside an allocator or memory-pool callback, under a runtime
+ * whose device memory is fully pre-reserved, or in a plugin host that hands
+ * the kernel only its inputs and outputs -- it takes no workspace and uses a
+ * 16 KiB scratch array compiled into the library instead.
+ *   - Same arguments and results as gdn_prefill_launch, minus the workspace.
+ *   - num_seqs is limited to 4096; larger requests return GDN_ERR_TOO_LARGE
+ *     and launch nothing.
+ *   - The first call on each device looks up the scratch array's device
+ *     address (cudaGetSymbolAddress); make that first call before capturing
+ *     a stream.  No call allocates or frees memory.
+ *   - All calls on a device share the scratch array: calls that overlap on
+ *     the GPU (e.g. on two streams) race and must not be issued that way.
+ */
+int gdn_prefill_launch_noalloc(const void* q, const void* k, const void* v, const float* state,
+                               const float* A_log, const void* a, const float* dt_bias,
+                               const void* b, const void* cu_seqlens, int cu_seqlens_int64,
+                               float scale, void* output, float* new_state, int total_tokens,
+                               int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+                               int head_size, int use_qk_l2norm, void* stream);
 
 /*
  * Diagnostics: synchronises the current device and returns the device-side

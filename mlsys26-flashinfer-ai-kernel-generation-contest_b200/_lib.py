@@ -16,6 +16,7 @@ GDN_ERR_INVALID_ARGUMENT = -1
 GDN_ERR_UNSUPPORTED = -2
 GDN_ERR_LAUNCH = -3
 GDN_ERR_WORKSPACE = -4
+GDN_ERR_TOO_LARGE = -5
 
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
 _vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
@@ -29,6 +30,8 @@ SIGNATURES = {
                                 _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_prefill_launch_recurrent": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
                                           _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_prefill_launch_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
+                                        _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_device_error": (_i, [_i]),
 }
 

@@ -10,6 +10,7 @@ extern "C" const char* gdn_status_string(int status) {
     case GDN_ERR_UNSUPPORTED: return "GDN_ERR_UNSUPPORTED";
     case GDN_ERR_LAUNCH: return "GDN_ERR_LAUNCH";
     case GDN_ERR_WORKSPACE: return "GDN_ERR_WORKSPACE";
+    case GDN_ERR_TOO_LARGE: return "GDN_ERR_TOO_LARGE";
     default: return "GDN_ERR_UNKNOWN";
   }
 }
