@@ -753,6 +753,746 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, TM_COLS);
 }
 
+// ---------------------------------------------------------------- pipelined kernel
+// Warp-specialised variant for L2-normalised q/k.  The chunk's work splits into
+//   prep  (depends only on the chunk's own q/k/gates): KQ MMA, A and P, the 64x64
+//         inverse, T hi/lo, Q~ = diag(gamma rq) Q, the vectors;
+//   state (depends on S): S K^T and S_hi Q~^T MMAs, R = diag(beta)(V - diag(gamma rk) K S^T),
+//         U^T = R^T T^T, U~ and the state update dS = U~^T K, O += U^T P^T.
+// Warps 8..15 ("prep group") run chunk c+1's prep while warps 0..7 ("state group")
+// run chunk c's state work; they hand over through mbarriers (prep -> state: T(c)
+// ready; state -> prep: T consumed, chunk done).  S is kept in TMEM: fp32 as the
+// accumulator of the state update (pre-scaled by the chunk decay), and as bf16
+// hi/lo pairs that are the A operand of the S K^T and S Q~^T MMAs, so no shared
+// memory holds the state.  U = T R is the "right-hand side" form of the same
+// algebra: T is split hi/lo once, and R (fp32) is split hi/lo by the state group.
+namespace pl {
+constexpr int kThreads = 512;
+constexpr uint32_t kGroup = 256;        // threads per warp group
+constexpr uint32_t kBarState = 1, kBarPrep = 2;
+constexpr int kLd = 68;                 // row stride of the in-place A / T matrix
+// shared memory
+constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // per buffer: K0 | Q0 | K1 | Q1 (8 KB each)
+constexpr uint32_t V = 65536;             // V0 | V1
+constexpr uint32_t RHI = 81920, RLO = 98304;  // R^T hi/lo [v][j]; RHI also stages the output
+constexpr uint32_t UTHI = 114688, UTLO = 131072, UHI = 147456;
+constexpr uint32_t THI = 163840, TLO = 172032;  // T hi/lo [t][j]
+constexpr uint32_t P0 = 180224, P1 = 188416;    // P hi [t][j], one per chunk parity
+constexpr uint32_t AT = 196608;                 // fp32 [64][kLd], A then T in place
+constexpr uint32_t E = 214016;                  // fp32 scratch of the block merges
+constexpr uint32_t VEC = 218112;                // per parity: Lam beta gam rk rq us (6 x 64 f32)
+constexpr uint32_t BARS = VEC + 2 * 6 * 256;
+constexpr uint32_t SMEM = BARS + 256;
+static_assert(SMEM <= 232448, "shared memory budget");
+// TMEM columns
+constexpr uint32_t TS = 0, TSH = 128, TSL = 192, TUT = 256, TO = 320, TSK = 384, TKQ = 448;
+
+struct Bars {
+  uint64_t kqtma[2], vtma, kq, g1, g2, g3, t_ready, t_free, b_done[2];
+};
+
+// bounded wait by every thread of a group; false on all of them if any ran out or
+// the other group has given up
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint32_t gid,
+                                           volatile int* abort_flag, unsigned code) {
+  bool ok = false;
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (mbar_try_wait(bar, parity)) { ok = true; break; }
+    if ((i & 1023u) == 1023u && *abort_flag) break;
+  }
+  const bool bad = group_or(gid, kGroup, !ok);
+  if (bad && (threadIdx.x & (kGroup - 1)) == 0) {
+    atomicOr(&g_prefill_device_error, code);
+    *abort_flag = 1;
+  }
+  return !bad;
+}
+
+// In-place T = (I + A)^-1 for the strictly lower triangular A in M[64][kLd], by
+// the 256 threads of the prep group (local index u): 8x8 diagonal blocks by
+// forward substitution, then 8->16, 16->32, 32->64 block merges
+// T21 = -T22 (A21 T11), each A21 block overwritten by T21 once it has been read.
+__device__ __forceinline__ void invert_in_place(float* __restrict__ M, float* __restrict__ Es,
+                                                int u) {
+  if (u < 64) {
+    const int o = 8 * (u >> 3), col = u & 7;
+    float a[8][8];
+#pragma unroll
+    for (int r = 1; r < 8; ++r)
+#pragma unroll
+      for (int j = 0; j < r; ++j) a[r][j] = M[(o + r) * kLd + o + j];
+    __syncwarp();  // the block's 8 threads share this warp: all reads before any write
+    float x[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) acc = fmaf(a[r][j], x[j], acc);
+      x[r] = (r < col) ? 0.f : ((r == col) ? 1.f : -acc);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) M[(o + r) * kLd + o + col] = x[r];
+  }
+  group_sync(kBarPrep, kGroup);
+  {  // 8 -> 16: pairs p = 0..3, rows bi = 16p + 8, cols bj = 16p
+    const int p = u >> 6, r = (u >> 3) & 7, c = u & 7;
+    const int bi = 16 * p + 8, bj = 16 * p;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc = fmaf(M[(bi + r) * kLd + bj + k], M[(bj + k) * kLd + bj + c], acc);
+    Es[p * 64 + r * 8 + c] = acc;
+    group_sync(kBarPrep, kGroup);
+    acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc = fmaf(M[(bi + r) * kLd + bi + k], Es[p * 64 + k * 8 + c], acc);
+    M[(bi + r) * kLd + bj + c] = -acc;
+  }
+  group_sync(kBarPrep, kGroup);
+  {  // 16 -> 32: pairs p = 0..1, rows bi = 32p + 16, cols bj = 32p; 2 outputs per thread
+    const int r = (u >> 4) & 15, c = u & 15;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int bi = 32 * p + 16, bj = 32 * p;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        acc = fmaf(M[(bi + r) * kLd + bj + k], M[(bj + k) * kLd + bj + c], acc);
+      Es[p * 256 + r * 16 + c] = acc;
+    }
+    group_sync(kBarPrep, kGroup);
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int bi = 32 * p + 16, bj = 32 * p;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        acc = fmaf(M[(bi + r) * kLd + bi + k], Es[p * 256 + k * 16 + c], acc);
+      M[(bi + r) * kLd + bj + c] = -acc;
+    }
+  }
+  group_sync(kBarPrep, kGroup);
+  {  // 32 -> 64: rows 32..63 x cols 0..31, 2x2 outputs per thread
+    const int r = 2 * (u >> 4), c = 2 * (u & 15);
+    float e00 = 0.f, e01 = 0.f, e10 = 0.f, e11 = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < 32; k += 4) {
+      const float4 a0 = *reinterpret_cast<const float4*>(M + (32 + r) * kLd + k);
+      const float4 a1 = *reinterpret_cast<const float4*>(M + (33 + r) * kLd + k);
+      const float a0v[4] = {a0.x, a0.y, a0.z, a0.w}, a1v[4] = {a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float2 t = *reinterpret_cast<const float2*>(M + (k + kk) * kLd + c);
+        e00 = fmaf(a0v[kk], t.x, e00); e01 = fmaf(a0v[kk], t.y, e01);
+        e10 = fmaf(a1v[kk], t.x, e10); e11 = fmaf(a1v[kk], t.y, e11);
+      }
+    }
+    *reinterpret_cast<float2*>(Es + r * 32 + c) = make_float2(e00, e01);
+    *reinterpret_cast<float2*>(Es + (r + 1) * 32 + c) = make_float2(e10, e11);
+    group_sync(kBarPrep, kGroup);
+    e00 = e01 = e10 = e11 = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < 32; k += 4) {
+      const float4 a0 = *reinterpret_cast<const float4*>(M + (32 + r) * kLd + 32 + k);
+      const float4 a1 = *reinterpret_cast<const float4*>(M + (33 + r) * kLd + 32 + k);
+      const float a0v[4] = {a0.x, a0.y, a0.z, a0.w}, a1v[4] = {a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float2 t = *reinterpret_cast<const float2*>(Es + (k + kk) * 32 + c);
+        e00 = fmaf(a0v[kk], t.x, e00); e01 = fmaf(a0v[kk], t.y, e01);
+        e10 = fmaf(a1v[kk], t.x, e10); e11 = fmaf(a1v[kk], t.y, e11);
+      }
+    }
+    *reinterpret_cast<float2*>(M + (32 + r) * kLd + c) = make_float2(-e00, -e01);
+    *reinterpret_cast<float2*>(M + (33 + r) * kLd + c) = make_float2(-e10, -e11);
+  }
+  group_sync(kBarPrep, kGroup);
+}
+}  // namespace pl
+
+template <bool HAS_STATE, typename CuT>
+__global__ void __launch_bounds__(pl::kThreads, 1)
+    prefill_pipelined_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const ChunkedParams p) {
+  using namespace pl;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sb = smem_u32(smem);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool prep = warp >= 8;
+  const int u = tid & (kGroup - 1);          // index within the group
+  const int sp = warp & 3, half = (warp >> 2) & 1;
+  const int row = sp * 32 + lane;            // TMEM lane of this thread
+  const int HV = p.HV;
+  const int wi = blockIdx.x / HV;
+  const int h = blockIdx.x - wi * HV;
+  const int n = p.order ? p.order[wi] : wi;
+  const int qh = h / p.ratio;
+  const CuT* cu = static_cast<const CuT*>(p.cu);
+  const long long s1 = min(max((long long)cu[n + 1], 0LL), p.T);
+  const long long s0 = min(max((long long)cu[n], 0LL), s1);
+  const long long L = s1 - s0;
+  float* nsbase = p.new_state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
+
+  if (L <= 0) {  // empty sequence: zero final state (definition semantics)
+    for (int i = tid; i < kHeadDim * kHeadDim / 4; i += pl::kThreads)
+      st_stream_f4(nsbase + 4 * i, make_float4(0.f, 0.f, 0.f, 0.f));
+    return;
+  }
+  if ((sb & 1023u) != 0) {
+    if (tid == 0) atomicOr(&g_prefill_device_error, ERR_SMEM_ALIGN);
+    return;
+  }
+  Bars* bars = reinterpret_cast<Bars*>(smem + BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + sizeof(Bars));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + BARS + sizeof(Bars) + 4);
+  auto vecp = [&](int par, int which) {  // which: 0 Lam 1 beta 2 gam 3 rk 4 rq 5 us
+    return reinterpret_cast<float*>(smem + VEC + 1536u * par + 256u * which);
+  };
+
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    uint64_t* b = reinterpret_cast<uint64_t*>(bars);
+    for (int i = 0; i < (int)(sizeof(Bars) / 8); ++i) mbar_init(b + i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+  const int nchunks = (int)((L + kC - 1) / kC);
+  const float nexpA = -expf(__ldg(p.A_log + h));
+  const float dtb = __ldg(p.dt_bias + h);
+  bool ok = true;
+  // async work issued but not yet waited for (drained, boundedly, if a wait runs out)
+  uint64_t* pend_bar[2] = {nullptr, nullptr};
+  uint32_t pend_par[2] = {0, 0};
+
+  if (prep) {
+    // =========================== prep group: chunk c one ahead of the state group
+    float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    auto load_gates = [&](int cc) {
+      const long long tc0 = s0 + (long long)kC * cc;
+      const int Lcc = (int)min((long long)kC, s1 - tc0);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * lane + e;
+        if (t < Lcc) {
+          const size_t ti = (size_t)(tc0 + t) * HV + h;
+          ga[e] = bf2f(p.a[ti]);
+          gb[e] = bf2f(p.b[ti]);
+        }
+      }
+    };
+    if (warp == 8) load_gates(0);
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int par = c & 1;
+      const long long t0 = s0 + (long long)kC * c;
+      const int Lc = (int)min((long long)kC, s1 - t0);
+      const uint32_t kqb = par ? KQ1 : KQ0;
+      float* Lam = vecp(par, 0);
+      float* beta = vecp(par, 1);
+      float* gam = vecp(par, 2);
+      float* rk = vecp(par, 3);
+      float* rq = vecp(par, 4);
+      float* us = vecp(par, 5);
+      // buffers of this parity are free once the state group finished chunk c-2
+      if (c >= 2 && !group_wait(&bars->b_done[par], ((c - 2) >> 1) & 1, kBarPrep, abort_flag,
+                                ERR_MMA_TIMEOUT)) { ok = false; break; }
+      pend_bar[0] = &bars->kqtma[par];
+      pend_par[0] = (c >> 1) & 1;
+      if (u == 0) {
+        const int y = (int)t0;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&bars->kqtma[par], 4 * 8192);
+        tma_load_2d(smem + kqb, &tm_k, &bars->kqtma[par], qh * 128, y);
+        tma_load_2d(smem + kqb + 16384, &tm_k, &bars->kqtma[par], qh * 128 + 64, y);
+        tma_load_2d(smem + kqb + 8192, &tm_q, &bars->kqtma[par], qh * 128, y);
+        tma_load_2d(smem + kqb + 24576, &tm_q, &bars->kqtma[par], qh * 128 + 64, y);
+      }
+      if (warp == 8) {  // gates of chunk c (loaded one chunk ahead), then prefetch c+1
+        float lg[2], bb[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool valid = 2 * lane + e < Lc;
+          lg[e] = valid ? nexpA * softplus_f(ga[e] + dtb) : 0.f;
+          bb[e] = valid ? sigmoid_f(gb[e]) : 0.f;
+        }
+        float x = lg[0] + lg[1];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, x, off);
+          if (lane >= off) x += y;
+        }
+        const float x0 = x - lg[1];
+        Lam[2 * lane] = x0;
+        Lam[2 * lane + 1] = x;
+        beta[2 * lane] = bb[0];
+        beta[2 * lane + 1] = bb[1];
+        gam[2 * lane] = expf(x0);
+        gam[2 * lane + 1] = expf(x);
+        if (c + 1 < nchunks) load_gates(c + 1);
+      }
+      if (!group_wait(&bars->kqtma[par], (c >> 1) & 1, kBarPrep, abort_flag, ERR_TMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[0] = &bars->kq;
+      pend_par[0] = c & 1;
+      if (u == 0) {  // [Skk; Sqk] = [K; Q] K^T
+        tc_fence_after();
+        const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
+          const uint64_t kd = umma_desc_k(sb + kqb + off);
+          umma_bf16(tmem + TKQ, kd, kd, idesc, ks > 0);
+        }
+        umma_commit(&bars->kq);
+      }
+      if (u >= 64 && u < 192) {  // q/k row norms
+        const int t = u & 63;
+        const bool isq = u < 128;
+        const uint32_t b0 = sb + kqb + (isq ? 8192u : 0u) + 128u * t;
+        float ss = 0.f;
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+          for (int ci = 0; ci < 8; ++ci) {
+            const int ch = (ci + t) & 7;
+            const uint4 w = ld_shared_v4(b0 + 16384u * blk + 16u * ch);
+            const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = bf2x2_to_f2(w4[e]);
+              ss = fmaf(f.x, f.x, ss);
+              ss = fmaf(f.y, f.y, ss);
+            }
+          }
+        const float r = rsqrtf(ss + kL2NormEps);
+        if (isq) rq[t] = r; else rk[t] = r;
+      }
+      if (!group_wait(&bars->kq, c & 1, kBarPrep, abort_flag, ERR_MMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[0] = nullptr;
+      tc_fence_after();
+      // A (from Skk) -> AT in place; P hi (from Sqk) -> P[par]; Q~ = gamma rq Q in place
+      {
+        float kq[32];
+        tmem_ld32(tl + TKQ + 32u * half, kq);
+        const int t = row & 63;
+        const bool is_k = row < 64;
+        const float lt = Lam[t];
+        const float ft = is_k ? beta[t] * rk[t] : rq[t];
+        float lv[32], rv[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 lj = *reinterpret_cast<const float4*>(Lam + 32 * half + i);
+          const float4 rj = *reinterpret_cast<const float4*>(rk + 32 * half + i);
+          lv[i] = lj.x; lv[i + 1] = lj.y; lv[i + 2] = lj.z; lv[i + 3] = lj.w;
+          rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
+        }
+        tmem_wait_ld();
+        float ej[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j = 32 * half + i;
+          const bool keep = is_k ? (j < t) : (j <= t);
+          ej[i] = keep ? ft * rv[i] * kq[i] * __expf(lt - lv[i]) : 0.f;
+        }
+        if (is_k) {
+          float* Arow = reinterpret_cast<float*>(smem + AT) + t * kLd + 32 * half;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(Arow + i) = make_float4(ej[i], ej[i + 1], ej[i + 2], ej[i + 3]);
+        } else {
+          const uint32_t pb = sb + (par ? P1 : P0);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t hb[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) hb[e] = rn_bf16_bits(__float_as_uint(ej[8 * q4 + e]));
+            st_v4(pb + sw128(t, 4 * half + q4),
+                  make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
+                             pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+          }
+          // Q~ row t, d-block `half` (the KQ MMA that read Q has completed)
+          const float f = gam[t] * rq[t];
+          const uint32_t qb = sb + kqb + 8192u + 16384u * half + 128u * t;
+#pragma unroll
+          for (int ci = 0; ci < 8; ++ci) {
+            const int ch = (ci + t) & 7;
+            const uint4 w = ld_shared_v4(qb + 16u * ch);
+            const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+            uint32_t hb[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f2 = bf2x2_to_f2(w4[e]);
+              hb[2 * e] = rn_bf16_bits(__float_as_uint(f2.x * f));
+              hb[2 * e + 1] = rn_bf16_bits(__float_as_uint(f2.y * f));
+            }
+            st_v4(qb + 16u * ch, make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
+                                            pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+          }
+        }
+        if (u < 64) us[u] = (u < Lc) ? rk[u] * expf(Lam[63] - Lam[u]) : 0.f;
+      }
+      tc_fence_before();
+      group_sync(kBarPrep, kGroup);
+      invert_in_place(reinterpret_cast<float*>(smem + AT), reinterpret_cast<float*>(smem + E), u);
+      // T hi/lo once the state group has consumed the previous chunk's T
+      if (c >= 1 && !group_wait(&bars->t_free, (c - 1) & 1, kBarPrep, abort_flag,
+                                ERR_MMA_TIMEOUT)) { ok = false; break; }
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int unit = u + 256 * k2;
+        const int t = unit >> 3, cidx = unit & 7;
+        const float* tr = reinterpret_cast<const float*>(smem + AT) + t * kLd + 8 * cidx;
+        const float4 ta = *reinterpret_cast<const float4*>(tr);
+        const float4 tb = *reinterpret_cast<const float4*>(tr + 4);
+        const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+        uint4 hi, lo;
+        split8(tv, hi, lo);
+        st_v4(sb + THI + sw128(t, cidx), hi);
+        st_v4(sb + TLO + sw128(t, cidx), lo);
+      }
+      fence_proxy_async();
+      group_sync(kBarPrep, kGroup);
+      if (u == 0) mbar_arrive(&bars->t_ready);
+    }
+  } else {
+    // =========================== state group
+    const float scale = default_scale(p.scale);
+    // initial state -> TMEM: fp32 (TS) and bf16 hi/lo (TSH / TSL), row v = row, k-half
+    {
+      float sv[64];
+      if constexpr (HAS_STATE) {
+        const float* srow = p.state + (((size_t)n * HV + h) * kHeadDim + row) * kHeadDim + 64 * half;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 v4 = ld_stream_f4(srow + 4 * i);
+          sv[4 * i] = v4.x; sv[4 * i + 1] = v4.y; sv[4 * i + 2] = v4.z; sv[4 * i + 3] = v4.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) sv[i] = 0.f;
+      }
+      uint32_t w[32], whi[32], wlo[32];
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(sv[32 * part + i]);
+        tmem_st32(tl + TS + 64u * half + 32u * part, w);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t b0 = __float_as_uint(sv[2 * i]), b1 = __float_as_uint(sv[2 * i + 1]);
+        const uint32_t h0 = b0 & 0xFFFF0000u, h1 = b1 & 0xFFFF0000u;
+        whi[i] = pack_hi16(h0, h1);
+        wlo[i] = pack_hi16(rn_bf16_bits(__float_as_uint(sv[2 * i] - __uint_as_float(h0))),
+                           rn_bf16_bits(__float_as_uint(sv[2 * i + 1] - __uint_as_float(h1))));
+      }
+      tmem_st32(tl + TSH + 32u * half, whi);
+      tmem_st32(tl + TSL + 32u * half, wlo);
+      tmem_wait_st();
+    }
+    if (tid == 0) {
+      fence_proxy_async();
+      mbar_arrive_expect_tx(&bars->vtma, 2 * 8192);
+      tma_load_2d(smem + V, &tm_v, &bars->vtma, h * 128, (int)s0);
+      tma_load_2d(smem + V + 8192, &tm_v, &bars->vtma, h * 128 + 64, (int)s0);
+    }
+    tc_fence_before();
+    group_sync(kBarState, kGroup);
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int par = c & 1;
+      const long long t0 = s0 + (long long)kC * c;
+      const int Lc = (int)min((long long)kC, s1 - t0);
+      const uint32_t kqb = par ? KQ1 : KQ0;
+      const float* Lam = vecp(par, 0);
+      const float* beta = vecp(par, 1);
+      const float* gam = vecp(par, 2);
+      const float* rk = vecp(par, 3);
+      const float* us = vecp(par, 5);
+      pend_bar[1] = &bars->vtma;
+      pend_par[1] = c & 1;
+      if (!group_wait(&bars->t_ready, c & 1, kBarState, abort_flag, ERR_MMA_TIMEOUT) ||
+          !group_wait(&bars->vtma, c & 1, kBarState, abort_flag, ERR_TMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[1] = nullptr;
+      // G1: S K^T (S hi + S lo) and O = S_hi Q~^T, A operands from TMEM
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
+          const uint64_t kd = umma_desc_k(sb + kqb + off);
+          umma_bf16_tmem_a(tmem + TSK, tmem + TSH + 8u * ks, kd, idesc, ks > 0);
+          umma_bf16_tmem_a(tmem + TSK, tmem + TSL + 8u * ks, kd, idesc, 1);
+          umma_bf16_tmem_a(tmem + TO, tmem + TSH + 8u * ks, umma_desc_k(sb + kqb + 8192u + off),
+                           idesc, ks > 0);
+        }
+        umma_commit(&bars->g1);
+      }
+      pend_bar[0] = &bars->g1;
+      pend_par[0] = c & 1;
+      // meanwhile: pre-scale the fp32 state by this chunk's decay (the G3 MMA accumulates on it)
+      {
+        const float G = expf(Lam[63]);
+        float sv[32];
+        uint32_t w[32];
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          tmem_ld32(tl + TS + 64u * half + 32u * part, sv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(G * sv[i]);
+          tmem_st32(tl + TS + 64u * half + 32u * part, w);
+        }
+        tmem_wait_st();
+      }
+      if (!group_wait(&bars->g1, c & 1, kBarState, abort_flag, ERR_MMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[0] = nullptr;
+      tc_fence_after();
+      // R^T[v][j] = beta_j (V[j][v] - gamma_j rk_j (S K^T)[v][j]) -> hi/lo K-major [v][j]
+      {
+        float sk[32], bj[32], gj[32];
+        tmem_ld32(tl + TSK + 32u * half, sk);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(beta + 32 * half + i);
+          const float4 g4 = *reinterpret_cast<const float4*>(gam + 32 * half + i);
+          const float4 r4 = *reinterpret_cast<const float4*>(rk + 32 * half + i);
+          bj[i] = b4.x; bj[i + 1] = b4.y; bj[i + 2] = b4.z; bj[i + 3] = b4.w;
+          gj[i] = g4.x * r4.x; gj[i + 1] = g4.y * r4.y; gj[i + 2] = g4.z * r4.z; gj[i + 3] = g4.w * r4.w;
+        }
+        // V tile element (t, v): box v/64, row t, 16-byte chunk ((v%64)/8) swizzled, 2-byte lane v%8
+        const uint16_t* vt = reinterpret_cast<const uint16_t*>(smem + V + 8192u * (row >> 6));
+        const int vc = (row & 63) >> 3, ve = row & 7;
+        float vv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = 32 * half + i;
+          const uint16_t bits = vt[t * 64 + ((vc ^ (t & 7)) << 3) + ve];
+          vv[i] = __uint_as_float((uint32_t)bits << 16);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int i = 8 * q4 + e;
+            x[e] = bj[i] * (vv[i] - gj[i] * sk[i]);
+          }
+          uint4 hi, lo;
+          split8(x, hi, lo);
+          st_v4(sb + RHI + sw128(row, 4 * half + q4), hi);
+          st_v4(sb + RLO + sw128(row, 4 * half + q4), lo);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      group_sync(kBarState, kGroup);
+      // G2: U^T = R^T T^T  (R_hi T_hi + R_lo T_hi + R_hi T_lo)
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+          const uint32_t a = sb + (term == 1 ? RLO : RHI);
+          const uint32_t b = sb + (term == 2 ? TLO : THI);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + TUT, umma_desc_k(a + 32u * ks), umma_desc_k(b + 32u * ks), idesc,
+                      (term | ks) != 0);
+        }
+        umma_commit(&bars->g2);
+      }
+      pend_bar[0] = &bars->g2;
+      pend_par[0] = c & 1;
+      if (!group_wait(&bars->g2, c & 1, kBarState, abort_flag, ERR_MMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[0] = nullptr;
+      tc_fence_after();
+      if (tid == 0) {
+        mbar_arrive(&bars->t_free);  // T consumed: the prep group may write the next one
+        if (c + 1 < nchunks) {       // V consumed (read into registers above)
+          pend_bar[1] = &bars->vtma;
+          pend_par[1] = (c + 1) & 1;
+          fence_proxy_async();
+          mbar_arrive_expect_tx(&bars->vtma, 2 * 8192);
+          tma_load_2d(smem + V, &tm_v, &bars->vtma, h * 128, (int)(t0 + kC));
+          tma_load_2d(smem + V + 8192, &tm_v, &bars->vtma, h * 128 + 64, (int)(t0 + kC));
+        }
+      }
+      // U -> U~ = diag(us) U (hi/lo) and U hi, K-major [v][t]
+      {
+        float uv[32], uw[32];
+        tmem_ld32(tl + TUT + 32u * half, uv);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(us + 32 * half + i);
+          uw[i] = w4.x; uw[i + 1] = w4.y; uw[i + 2] = w4.z; uw[i + 3] = w4.w;
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float x[8];
+          uint32_t hb[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            x[e] = uv[8 * q4 + e] * uw[8 * q4 + e];
+            hb[e] = rn_bf16_bits(__float_as_uint(uv[8 * q4 + e]));
+          }
+          uint4 hi, lo;
+          split8(x, hi, lo);
+          const uint32_t o = sw128(row, 4 * half + q4);
+          st_v4(sb + UTHI + o, hi);
+          st_v4(sb + UTLO + o, lo);
+          st_v4(sb + UHI + o, make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
+                                         pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      group_sync(kBarState, kGroup);
+      // G3: S += U~^T K (on the decay-scaled S);  O += U^T P^T
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t id_s = umma_idesc_bf16(128, 128, false, true);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + TS, umma_desc_k(sb + (part ? UTLO : UTHI) + 32u * ks),
+                      umma_desc_mn(sb + kqb + 2048u * ks, 16384), id_s, 1);
+        const uint32_t id_p = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + TO, umma_desc_k(sb + UHI + 32u * ks),
+                    umma_desc_k(sb + (par ? P1 : P0) + 32u * ks), id_p, 1);
+        umma_commit(&bars->g3);
+      }
+      pend_bar[0] = &bars->g3;
+      pend_par[0] = c & 1;
+      if (!group_wait(&bars->g3, c & 1, kBarState, abort_flag, ERR_MMA_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      pend_bar[0] = nullptr;
+      tc_fence_after();
+      // epilogue: S(c+1) -> bf16 hi/lo in TMEM (or the final state to global); O -> staging
+      const bool last = c + 1 == nchunks;
+      {
+        float sv[32];
+        uint32_t whi[32], wlo[32];
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          tmem_ld32(tl + TS + 64u * half + 32u * part, sv);
+          tmem_wait_ld();
+          if (last) {
+            float* dst = nsbase + (size_t)row * kHeadDim + 64 * half + 32 * part;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_stream_f4(dst + i, make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint32_t b0 = __float_as_uint(sv[2 * i]), b1 = __float_as_uint(sv[2 * i + 1]);
+              const uint32_t h0 = b0 & 0xFFFF0000u, h1 = b1 & 0xFFFF0000u;
+              whi[16 * part + i] = pack_hi16(h0, h1);
+              wlo[16 * part + i] =
+                  pack_hi16(rn_bf16_bits(__float_as_uint(sv[2 * i] - __uint_as_float(h0))),
+                            rn_bf16_bits(__float_as_uint(sv[2 * i + 1] - __uint_as_float(h1))));
+            }
+          }
+        }
+        if (!last) {
+          tmem_st32(tl + TSH + 32u * half, whi);
+          tmem_st32(tl + TSL + 32u * half, wlo);
+        }
+        float ov[32];
+        tmem_ld32(tl + TO + 32u * half, ov);
+        tmem_wait_ld();
+        uint16_t* ostage = reinterpret_cast<uint16_t*>(smem + RHI);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          ostage[(32 * half + i) * kHeadDim + row] =
+              (uint16_t)(rn_bf16_bits(__float_as_uint(scale * ov[i])) >> 16);
+        if (!last) tmem_wait_st();
+      }
+      tc_fence_before();
+      group_sync(kBarState, kGroup);
+      {
+        __nv_bfloat16* obase = p.out + ((size_t)t0 * HV + h) * kHeadDim;
+        uint4 v4[4];
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int unit = u + 256 * k4;
+          v4[k4] = ld_shared_v4(sb + RHI + 256u * (unit >> 4) + 16u * (unit & 15));
+        }
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int unit = u + 256 * k4, t = unit >> 4;
+          if (t < Lc)
+            *reinterpret_cast<uint4*>(obase + (size_t)t * HV * kHeadDim + 8 * (unit & 15)) = v4[k4];
+        }
+      }
+      group_sync(kBarState, kGroup);
+      if (tid == 0) mbar_arrive(&bars->b_done[par]);
+    }
+  }
+  // a wait ran out: tell the other group, give our in-flight copies / MMAs one more
+  // bounded chance to land, then release TMEM
+  if (!ok) {
+    *abort_flag = 1;
+    if (u == 0)
+      for (int i = 0; i < 2; ++i)
+        if (pend_bar[i]) mbar_wait(pend_bar[i], pend_par[i], 1u << 20);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+template <bool HS, typename CuT>
+cudaError_t launch_pipelined_t(const CUtensorMap& mq, const CUtensorMap& mk,
+                               const CUtensorMap& mv, const ChunkedParams& cp, int nseq,
+                               cudaStream_t st) {
+  auto kern = prefill_pipelined_kernel<HS, CuT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl::SMEM);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  kern<<<dim3((unsigned)((long long)nseq * cp.HV)), dim3(pl::kThreads), pl::SMEM, st>>>(mq, mk,
+                                                                                         mv, cp);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- LPT order
 // CTAs are scheduled roughly in blockIdx order and one CTA fills an SM, so
 // handing out the longest sequences first (longest-processing-time) keeps the
@@ -902,6 +1642,14 @@ cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st) {
                    p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
                    static_cast<__nv_bfloat16*>(p.out), order, p.T, p.cu_int64 ? 1 : 0, p.HV,
                    p.HV / p.HQ, p.scale};
+  if (p.l2norm) {  // warp-specialised, pipelined kernel
+    const bool hs = p.state != nullptr;
+    if (p.cu_int64)
+      return hs ? launch_pipelined_t<true, long long>(mq, mk, mv, cp, p.N, st)
+                : launch_pipelined_t<false, long long>(mq, mk, mv, cp, p.N, st);
+    return hs ? launch_pipelined_t<true, int>(mq, mk, mv, cp, p.N, st)
+              : launch_pipelined_t<false, int>(mq, mk, mv, cp, p.N, st);
+  }
   if (p.cu_int64)
     return launch_chunked_cu<long long>(mq, mk, mv, cp, p.l2norm, p.state != nullptr, p.N, st);
   return launch_chunked_cu<int>(mq, mk, mv, cp, p.l2norm, p.state != nullptr, p.N, st);
