@@ -133,23 +133,26 @@ __device__ __forceinline__ uint32_t rn_bf16_bits(uint32_t xb) {
 __device__ __forceinline__ uint32_t pack_hi16(uint32_t a, uint32_t b) {
   return __byte_perm(a, b, 0x7632);
 }
-__device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
-  return pack_hi16(rn_bf16_bits(__float_as_uint(x)), rn_bf16_bits(__float_as_uint(y)));
-}
 // 8 floats -> (hi, lo) bf16 chunks with x ~= hi + lo: hi is x truncated to bf16
-// (exact residual x - hi, |x - hi| < 2^-7 |x|), lo is that residual rounded to
-// bf16, so hi + lo carries ~16 significant bits.
+// (exact residual x - hi, |x - hi| < 2^-7 |x|) and lo that residual truncated, so
+// hi + lo keeps ~15 significant bits (relative error < 2^-15) for three ALU
+// operations per element (mask, subtract, byte-permute).
 __device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
-  uint32_t hb[8], lb[8];
+  uint32_t xb[8], lb[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    hb[i] = __float_as_uint(x[i]) & 0xFFFF0000u;
-    lb[i] = rn_bf16_bits(__float_as_uint(x[i] - __uint_as_float(hb[i])));
+    xb[i] = __float_as_uint(x[i]);
+    lb[i] = __float_as_uint(x[i] - __uint_as_float(xb[i] & 0xFFFF0000u));
   }
-  hi = make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]), pack_hi16(hb[4], hb[5]),
-                  pack_hi16(hb[6], hb[7]));
+  hi = make_uint4(pack_hi16(xb[0], xb[1]), pack_hi16(xb[2], xb[3]), pack_hi16(xb[4], xb[5]),
+                  pack_hi16(xb[6], xb[7]));
   lo = make_uint4(pack_hi16(lb[0], lb[1]), pack_hi16(lb[2], lb[3]), pack_hi16(lb[4], lb[5]),
                   pack_hi16(lb[6], lb[7]));
+}
+// Round-to-nearest bf16 pair (one cvt per two elements), low element first.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo_elem, float hi_elem) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 // 16 consecutive fp32 TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -761,7 +764,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //         U^T = R^T T^T, U~ and the state update dS = U~^T K, O += U^T P^T.
 // Warps 8..15 ("prep group") run chunk c+1's prep while warps 0..7 ("state group")
 // run chunk c's state work; they hand over through mbarriers (prep -> state: T(c)
-// ready; state -> prep: T consumed, chunk done).  S is kept in TMEM: fp32 as the
+// ready; state -> prep: T consumed; the state group also refills a K/Q buffer as
+// soon as it has finished the chunk that used it).  S is kept in TMEM: fp32 as the
 // accumulator of the state update (pre-scaled by the chunk decay), and as bf16
 // hi/lo pairs that are the A operand of the S K^T and S Q~^T MMAs, so no shared
 // memory holds the state.  U = T R is the "right-hand side" form of the same
@@ -779,8 +783,8 @@ constexpr uint32_t UTHI = 114688, UTLO = 131072, UHI = 147456;
 constexpr uint32_t THI = 163840, TLO = 172032;  // T hi/lo [t][j]
 constexpr uint32_t P0 = 180224, P1 = 188416;    // P hi [t][j], one per chunk parity
 constexpr uint32_t AT = 196608;                 // fp32 [64][kLd], A then T in place
-constexpr uint32_t E = 214016;                  // fp32 scratch of the block merges
-constexpr uint32_t VEC = 218112;                // per parity: Lam beta gam rk rq us (6 x 64 f32)
+constexpr uint32_t E = 214016;                  // fp32 scratch of the block merges (32 x 36)
+constexpr uint32_t VEC = 218624;                // per parity: Lam beta gam rk rq us (6 x 64 f32)
 constexpr uint32_t BARS = VEC + 2 * 6 * 256;
 constexpr uint32_t SMEM = BARS + 256;
 static_assert(SMEM <= 232448, "shared memory budget");
@@ -788,7 +792,7 @@ static_assert(SMEM <= 232448, "shared memory budget");
 constexpr uint32_t TS = 0, TSH = 128, TSL = 192, TUT = 256, TO = 320, TSK = 384, TKQ = 448;
 
 struct Bars {
-  uint64_t kqtma[2], vtma, kq, g1, g2, g3, t_ready, t_free, b_done[2];
+  uint64_t kqtma[2], vtma, kq, g1, g2, g3, t_ready, t_free;
 };
 
 // bounded wait by every thread of a group; false on all of them if any ran out or
@@ -808,10 +812,59 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint3
   return !bad;
 }
 
+// ---- warp-level tensor-core products for the inverse's block merges ----
+// D(16x8) = X(16xK) * Y(Kx8), fp32 operands as 3xTF32 (hi.hi + hi.lo + lo.hi;
+// hi = the top 10 mantissa bits, lo = the exact residual), so the result carries
+// ~21 significant bits.  Fragment layout of mma.m16n8k8 (tf32): g = lane/4,
+// t = lane%4; A: (g, t) (g+8, t) (g, t+4) (g+8, t+4); B: (t, g) (t+4, g);
+// C: (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1).
+constexpr int kLdE3 = 20, kLdE4 = 36;  // scratch strides (2-way bank conflicts at most)
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ void mma_tile_tf32x3(const float* X, int ldx, const float* Y, int ldy,
+                                                int K, float (&c)[4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  c[0] = c[1] = c[2] = c[3] = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const float af[4] = {X[g * ldx + k0 + t], X[(g + 8) * ldx + k0 + t],
+                         X[g * ldx + k0 + t + 4], X[(g + 8) * ldx + k0 + t + 4]};
+    const float bf[2] = {Y[(k0 + t) * ldy + g], Y[(k0 + t + 4) * ldy + g]};
+    uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ah[i] = __float_as_uint(af[i]) & 0xFFFFE000u;
+      al[i] = __float_as_uint(af[i] - __uint_as_float(ah[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      bh[i] = __float_as_uint(bf[i]) & 0xFFFFE000u;
+      bl[i] = __float_as_uint(bf[i] - __uint_as_float(bh[i]));
+    }
+    mma_tf32(c, al, bh);
+    mma_tf32(c, ah, bl);
+    mma_tf32(c, ah, bh);
+  }
+}
+__device__ __forceinline__ void store_tile(float* D, int ldd, const float (&c)[4], float sgn) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  D[g * ldd + 2 * t] = sgn * c[0];
+  D[g * ldd + 2 * t + 1] = sgn * c[1];
+  D[(g + 8) * ldd + 2 * t] = sgn * c[2];
+  D[(g + 8) * ldd + 2 * t + 1] = sgn * c[3];
+}
+
 // In-place T = (I + A)^-1 for the strictly lower triangular A in M[64][kLd], by
 // the 256 threads of the prep group (local index u): 8x8 diagonal blocks by
-// forward substitution, then 8->16, 16->32, 32->64 block merges
-// T21 = -T22 (A21 T11), each A21 block overwritten by T21 once it has been read.
+// forward substitution, then 8->16 (CUDA cores), 16->32 and 32->64 (warp-level
+// tensor cores, 3xTF32) block merges T21 = -T22 (A21 T11), each A21 block
+// overwritten by T21 once it has been read.
 __device__ __forceinline__ void invert_in_place(float* __restrict__ M, float* __restrict__ Es,
                                                 int u) {
   if (u < 64) {
@@ -848,62 +901,34 @@ __device__ __forceinline__ void invert_in_place(float* __restrict__ M, float* __
     M[(bi + r) * kLd + bj + c] = -acc;
   }
   group_sync(kBarPrep, kGroup);
-  {  // 16 -> 32: pairs p = 0..1, rows bi = 32p + 16, cols bj = 32p; 2 outputs per thread
-    const int r = (u >> 4) & 15, c = u & 15;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int bi = 32 * p + 16, bj = 32 * p;
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        acc = fmaf(M[(bi + r) * kLd + bj + k], M[(bj + k) * kLd + bj + c], acc);
-      Es[p * 256 + r * 16 + c] = acc;
+  const int wg = u >> 5;  // warp within the group
+  {  // 16 -> 32 on the tensor cores: pairs p = 0..1 (rows bi = 32p+16, cols bj = 32p),
+     // two 8-wide column tiles each -> warps 0..3
+    if (wg < 4) {
+      const int pr = wg >> 1, nt = wg & 1;
+      const int bi = 32 * pr + 16, bj = 32 * pr;
+      float c[4];
+      mma_tile_tf32x3(M + bi * kLd + bj, kLd, M + bj * kLd + bj + 8 * nt, kLd, 16, c);
+      store_tile(Es + pr * 16 * kLdE3 + 8 * nt, kLdE3, c, 1.f);
     }
     group_sync(kBarPrep, kGroup);
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int bi = 32 * p + 16, bj = 32 * p;
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        acc = fmaf(M[(bi + r) * kLd + bi + k], Es[p * 256 + k * 16 + c], acc);
-      M[(bi + r) * kLd + bj + c] = -acc;
+    if (wg < 4) {
+      const int pr = wg >> 1, nt = wg & 1;
+      const int bi = 32 * pr + 16, bj = 32 * pr;
+      float c[4];
+      mma_tile_tf32x3(M + bi * kLd + bi, kLd, Es + pr * 16 * kLdE3 + 8 * nt, kLdE3, 16, c);
+      store_tile(M + bi * kLd + bj + 8 * nt, kLd, c, -1.f);
     }
   }
   group_sync(kBarPrep, kGroup);
-  {  // 32 -> 64: rows 32..63 x cols 0..31, 2x2 outputs per thread
-    const int r = 2 * (u >> 4), c = 2 * (u & 15);
-    float e00 = 0.f, e01 = 0.f, e10 = 0.f, e11 = 0.f;
-#pragma unroll 2
-    for (int k = 0; k < 32; k += 4) {
-      const float4 a0 = *reinterpret_cast<const float4*>(M + (32 + r) * kLd + k);
-      const float4 a1 = *reinterpret_cast<const float4*>(M + (33 + r) * kLd + k);
-      const float a0v[4] = {a0.x, a0.y, a0.z, a0.w}, a1v[4] = {a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float2 t = *reinterpret_cast<const float2*>(M + (k + kk) * kLd + c);
-        e00 = fmaf(a0v[kk], t.x, e00); e01 = fmaf(a0v[kk], t.y, e01);
-        e10 = fmaf(a1v[kk], t.x, e10); e11 = fmaf(a1v[kk], t.y, e11);
-      }
-    }
-    *reinterpret_cast<float2*>(Es + r * 32 + c) = make_float2(e00, e01);
-    *reinterpret_cast<float2*>(Es + (r + 1) * 32 + c) = make_float2(e10, e11);
+  {  // 32 -> 64 on the tensor cores: rows 32..63 x cols 0..31 = 2 x 4 tiles of 16 x 8
+    const int mt = wg >> 2, nt = wg & 3;
+    float c[4];
+    mma_tile_tf32x3(M + (32 + 16 * mt) * kLd, kLd, M + 8 * nt, kLd, 32, c);
+    store_tile(Es + 16 * mt * kLdE4 + 8 * nt, kLdE4, c, 1.f);
     group_sync(kBarPrep, kGroup);
-    e00 = e01 = e10 = e11 = 0.f;
-#pragma unroll 2
-    for (int k = 0; k < 32; k += 4) {
-      const float4 a0 = *reinterpret_cast<const float4*>(M + (32 + r) * kLd + 32 + k);
-      const float4 a1 = *reinterpret_cast<const float4*>(M + (33 + r) * kLd + 32 + k);
-      const float a0v[4] = {a0.x, a0.y, a0.z, a0.w}, a1v[4] = {a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float2 t = *reinterpret_cast<const float2*>(Es + (k + kk) * 32 + c);
-        e00 = fmaf(a0v[kk], t.x, e00); e01 = fmaf(a0v[kk], t.y, e01);
-        e10 = fmaf(a1v[kk], t.x, e10); e11 = fmaf(a1v[kk], t.y, e11);
-      }
-    }
-    *reinterpret_cast<float2*>(M + (32 + r) * kLd + c) = make_float2(-e00, -e01);
-    *reinterpret_cast<float2*>(M + (33 + r) * kLd + c) = make_float2(-e10, -e11);
+    mma_tile_tf32x3(M + (32 + 16 * mt) * kLd + 32, kLd, Es + 8 * nt, kLdE4, 32, c);
+    store_tile(M + (32 + 16 * mt) * kLd + 8 * nt, kLd, c, -1.f);
   }
   group_sync(kBarPrep, kGroup);
 }
@@ -975,6 +1000,24 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
   // async work issued but not yet waited for (drained, boundedly, if a wait runs out)
   uint64_t* pend_bar[2] = {nullptr, nullptr};
   uint32_t pend_par[2] = {0, 0};
+  // K and Q tiles of chunk cc into buffer cc & 1 (one arrival on kqtma[cc & 1]).  Chunks 0
+  // and 1 are fetched here; chunk c + 2 by the state group as soon as it has finished
+  // chunk c, i.e. as soon as that buffer (and the P / vector set of that parity) is free.
+  auto issue_kq = [&](int cc) {
+    const int bpar = cc & 1;
+    const uint32_t dst = bpar ? KQ1 : KQ0;
+    const int y = (int)(s0 + (long long)kC * cc);
+    fence_proxy_async();
+    mbar_arrive_expect_tx(&bars->kqtma[bpar], 4 * 8192);
+    tma_load_2d(smem + dst, &tm_k, &bars->kqtma[bpar], qh * 128, y);
+    tma_load_2d(smem + dst + 16384, &tm_k, &bars->kqtma[bpar], qh * 128 + 64, y);
+    tma_load_2d(smem + dst + 8192, &tm_q, &bars->kqtma[bpar], qh * 128, y);
+    tma_load_2d(smem + dst + 24576, &tm_q, &bars->kqtma[bpar], qh * 128 + 64, y);
+  };
+  if (tid == 0) {
+    issue_kq(0);
+    if (nchunks > 1) issue_kq(1);
+  }
 
   if (prep) {
     // =========================== prep group: chunk c one ahead of the state group
@@ -1004,20 +1047,10 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       float* rk = vecp(par, 3);
       float* rq = vecp(par, 4);
       float* us = vecp(par, 5);
-      // buffers of this parity are free once the state group finished chunk c-2
-      if (c >= 2 && !group_wait(&bars->b_done[par], ((c - 2) >> 1) & 1, kBarPrep, abort_flag,
-                                ERR_MMA_TIMEOUT)) { ok = false; break; }
+      // this chunk's K/Q tiles (their arrival also means the state group has finished
+      // chunk c - 2, so the P buffer and vector set of this parity are free)
       pend_bar[0] = &bars->kqtma[par];
       pend_par[0] = (c >> 1) & 1;
-      if (u == 0) {
-        const int y = (int)t0;
-        fence_proxy_async();
-        mbar_arrive_expect_tx(&bars->kqtma[par], 4 * 8192);
-        tma_load_2d(smem + kqb, &tm_k, &bars->kqtma[par], qh * 128, y);
-        tma_load_2d(smem + kqb + 16384, &tm_k, &bars->kqtma[par], qh * 128 + 64, y);
-        tma_load_2d(smem + kqb + 8192, &tm_q, &bars->kqtma[par], qh * 128, y);
-        tma_load_2d(smem + kqb + 24576, &tm_q, &bars->kqtma[par], qh * 128 + 64, y);
-      }
       if (warp == 8) {  // gates of chunk c (loaded one chunk ahead), then prefetch c+1
         float lg[2], bb[2];
 #pragma unroll
@@ -1088,61 +1121,60 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       tc_fence_after();
       // A (from Skk) -> AT in place; P hi (from Sqk) -> P[par]; Q~ = gamma rq Q in place
       {
-        float kq[32];
-        tmem_ld32(tl + TKQ + 32u * half, kq);
         const int t = row & 63;
         const bool is_k = row < 64;
         const float lt = Lam[t];
         const float ft = is_k ? beta[t] * rk[t] : rq[t];
-        float lv[32], rv[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 lj = *reinterpret_cast<const float4*>(Lam + 32 * half + i);
-          const float4 rj = *reinterpret_cast<const float4*>(rk + 32 * half + i);
-          lv[i] = lj.x; lv[i + 1] = lj.y; lv[i + 2] = lj.z; lv[i + 3] = lj.w;
-          rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
-        }
-        tmem_wait_ld();
-        float ej[32];
+        for (int pass = 0; pass < 2; ++pass) {  // 16 columns per pass keeps registers low
+          const int j0 = 32 * half + 16 * pass;
+          float kq[16], lv[16], rv[16];
+          tmem_ld16(tl + TKQ + (uint32_t)j0, kq);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = 32 * half + i;
-          const bool keep = is_k ? (j < t) : (j <= t);
-          ej[i] = keep ? ft * rv[i] * kq[i] * __expf(lt - lv[i]) : 0.f;
-        }
-        if (is_k) {
-          float* Arow = reinterpret_cast<float*>(smem + AT) + t * kLd + 32 * half;
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(Arow + i) = make_float4(ej[i], ej[i + 1], ej[i + 2], ej[i + 3]);
-        } else {
-          const uint32_t pb = sb + (par ? P1 : P0);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint32_t hb[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) hb[e] = rn_bf16_bits(__float_as_uint(ej[8 * q4 + e]));
-            st_v4(pb + sw128(t, 4 * half + q4),
-                  make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
-                             pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+          for (int i = 0; i < 16; i += 4) {
+            const float4 lj = *reinterpret_cast<const float4*>(Lam + j0 + i);
+            const float4 rj = *reinterpret_cast<const float4*>(rk + j0 + i);
+            lv[i] = lj.x; lv[i + 1] = lj.y; lv[i + 2] = lj.z; lv[i + 3] = lj.w;
+            rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
           }
-          // Q~ row t, d-block `half` (the KQ MMA that read Q has completed)
-          const float f = gam[t] * rq[t];
+          tmem_wait_ld();
+          float ej[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = j0 + i;
+            const bool keep = is_k ? (j < t) : (j <= t);
+            ej[i] = keep ? ft * rv[i] * kq[i] * __expf(lt - lv[i]) : 0.f;
+          }
+          if (is_k) {
+            float* Arow = reinterpret_cast<float*>(smem + AT) + t * kLd + j0;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(Arow + i) =
+                  make_float4(ej[i], ej[i + 1], ej[i + 2], ej[i + 3]);
+          } else {
+            const uint32_t pb = sb + (par ? P1 : P0);
+#pragma unroll
+            for (int q2 = 0; q2 < 2; ++q2) {
+              const float* e8 = &ej[8 * q2];
+              st_v4(pb + sw128(t, (j0 >> 3) + q2),
+                    make_uint4(cvt_bf16x2(e8[0], e8[1]), cvt_bf16x2(e8[2], e8[3]),
+                               cvt_bf16x2(e8[4], e8[5]), cvt_bf16x2(e8[6], e8[7])));
+            }
+          }
+        }
+        if (!is_k) {
+          // Q~ row t, d-block `half` (the KQ MMA that read Q has completed);
+          // bf16x2 multiplies: this term only feeds the bf16 output
+          const __nv_bfloat162 f2 = __float2bfloat162_rn(gam[t] * rq[t]);
           const uint32_t qb = sb + kqb + 8192u + 16384u * half + 128u * t;
 #pragma unroll
           for (int ci = 0; ci < 8; ++ci) {
             const int ch = (ci + t) & 7;
-            const uint4 w = ld_shared_v4(qb + 16u * ch);
-            const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
-            uint32_t hb[8];
+            uint4 w = ld_shared_v4(qb + 16u * ch);
+            __nv_bfloat162* w2 = reinterpret_cast<__nv_bfloat162*>(&w);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f2 = bf2x2_to_f2(w4[e]);
-              hb[2 * e] = rn_bf16_bits(__float_as_uint(f2.x * f));
-              hb[2 * e + 1] = rn_bf16_bits(__float_as_uint(f2.y * f));
-            }
-            st_v4(qb + 16u * ch, make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
-                                            pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+            for (int e = 0; e < 4; ++e) w2[e] = __hmul2(w2[e], f2);
+            st_v4(qb + 16u * ch, w);
           }
         }
         if (u < 64) us[u] = (u < Lc) ? rk[u] * expf(Lam[63] - Lam[u]) : 0.f;
@@ -1187,23 +1219,23 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) sv[i] = 0.f;
       }
-      uint32_t w[32], whi[32], wlo[32];
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
+        uint32_t w[32], whi[16], wlo[16];
 #pragma unroll
         for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(sv[32 * part + i]);
         tmem_st32(tl + TS + 64u * half + 32u * part, w);
-      }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint32_t b0 = __float_as_uint(sv[2 * i]), b1 = __float_as_uint(sv[2 * i + 1]);
-        const uint32_t h0 = b0 & 0xFFFF0000u, h1 = b1 & 0xFFFF0000u;
-        whi[i] = pack_hi16(h0, h1);
-        wlo[i] = pack_hi16(rn_bf16_bits(__float_as_uint(sv[2 * i] - __uint_as_float(h0))),
-                           rn_bf16_bits(__float_as_uint(sv[2 * i + 1] - __uint_as_float(h1))));
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = sv[32 * part + 2 * i], x1 = sv[32 * part + 2 * i + 1];
+          const uint32_t b0 = __float_as_uint(x0), b1 = __float_as_uint(x1);
+          whi[i] = pack_hi16(b0, b1);
+          wlo[i] = pack_hi16(__float_as_uint(x0 - __uint_as_float(b0 & 0xFFFF0000u)),
+                             __float_as_uint(x1 - __uint_as_float(b1 & 0xFFFF0000u)));
+        }
+        tmem_st16(tl + TSH + 32u * half + 16u * part, whi);
+        tmem_st16(tl + TSL + 32u * half + 16u * part, wlo);
       }
-      tmem_st32(tl + TSH + 32u * half, whi);
-      tmem_st32(tl + TSL + 32u * half, wlo);
       tmem_wait_st();
     }
     if (tid == 0) {
@@ -1357,19 +1389,16 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           float x[8];
-          uint32_t hb[8];
+          const float* u8 = &uv[8 * q4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            x[e] = uv[8 * q4 + e] * uw[8 * q4 + e];
-            hb[e] = rn_bf16_bits(__float_as_uint(uv[8 * q4 + e]));
-          }
+          for (int e = 0; e < 8; ++e) x[e] = u8[e] * uw[8 * q4 + e];
           uint4 hi, lo;
           split8(x, hi, lo);
           const uint32_t o = sw128(row, 4 * half + q4);
           st_v4(sb + UTHI + o, hi);
           st_v4(sb + UTLO + o, lo);
-          st_v4(sb + UHI + o, make_uint4(pack_hi16(hb[0], hb[1]), pack_hi16(hb[2], hb[3]),
-                                         pack_hi16(hb[4], hb[5]), pack_hi16(hb[6], hb[7])));
+          st_v4(sb + UHI + o, make_uint4(cvt_bf16x2(u8[0], u8[1]), cvt_bf16x2(u8[2], u8[3]),
+                                         cvt_bf16x2(u8[4], u8[5]), cvt_bf16x2(u8[6], u8[7])));
         }
       }
       fence_proxy_async();
@@ -1403,10 +1432,9 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       // epilogue: S(c+1) -> bf16 hi/lo in TMEM (or the final state to global); O -> staging
       const bool last = c + 1 == nchunks;
       {
-        float sv[32];
-        uint32_t whi[32], wlo[32];
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
+          float sv[32];
           tmem_ld32(tl + TS + 64u * half + 32u * part, sv);
           tmem_wait_ld();
           if (last) {
@@ -1415,29 +1443,28 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
             for (int i = 0; i < 32; i += 4)
               st_stream_f4(dst + i, make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]));
           } else {
+            uint32_t whi[16], wlo[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const uint32_t b0 = __float_as_uint(sv[2 * i]), b1 = __float_as_uint(sv[2 * i + 1]);
-              const uint32_t h0 = b0 & 0xFFFF0000u, h1 = b1 & 0xFFFF0000u;
-              whi[16 * part + i] = pack_hi16(h0, h1);
-              wlo[16 * part + i] =
-                  pack_hi16(rn_bf16_bits(__float_as_uint(sv[2 * i] - __uint_as_float(h0))),
-                            rn_bf16_bits(__float_as_uint(sv[2 * i + 1] - __uint_as_float(h1))));
+              whi[i] = pack_hi16(b0, b1);
+              wlo[i] = pack_hi16(__float_as_uint(sv[2 * i] - __uint_as_float(b0 & 0xFFFF0000u)),
+                                 __float_as_uint(sv[2 * i + 1] - __uint_as_float(b1 & 0xFFFF0000u)));
             }
+            tmem_st16(tl + TSH + 32u * half + 16u * part, whi);
+            tmem_st16(tl + TSL + 32u * half + 16u * part, wlo);
           }
-        }
-        if (!last) {
-          tmem_st32(tl + TSH + 32u * half, whi);
-          tmem_st32(tl + TSL + 32u * half, wlo);
         }
         float ov[32];
         tmem_ld32(tl + TO + 32u * half, ov);
         tmem_wait_ld();
         uint16_t* ostage = reinterpret_cast<uint16_t*>(smem + RHI);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          ostage[(32 * half + i) * kHeadDim + row] =
-              (uint16_t)(rn_bf16_bits(__float_as_uint(scale * ov[i])) >> 16);
+        for (int i = 0; i < 32; i += 2) {
+          const uint32_t pr = cvt_bf16x2(scale * ov[i], scale * ov[i + 1]);
+          ostage[(32 * half + i) * kHeadDim + row] = (uint16_t)(pr & 0xFFFFu);
+          ostage[(32 * half + i + 1) * kHeadDim + row] = (uint16_t)(pr >> 16);
+        }
         if (!last) tmem_wait_st();
       }
       tc_fence_before();
@@ -1458,7 +1485,7 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         }
       }
       group_sync(kBarState, kGroup);
-      if (tid == 0) mbar_arrive(&bars->b_done[par]);
+      if (tid == 0 && c + 2 < nchunks) issue_kq(c + 2);  // buffer `par` is free again
     }
   }
   // a wait ran out: tell the other group, give our in-flight copies / MMAs one more
