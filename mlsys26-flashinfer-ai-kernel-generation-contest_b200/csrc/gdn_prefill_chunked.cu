@@ -784,9 +784,14 @@ constexpr uint32_t THI = 163840, TLO = 172032;  // T hi/lo [t][j]
 constexpr uint32_t P0 = 180224, P1 = 188416;    // P hi [t][j], one per chunk parity
 constexpr uint32_t AT = 196608;                 // fp32 [64][kLd], A then T in place
 constexpr uint32_t E = 214016;                  // fp32 scratch of the block merges (32 x 36)
-constexpr uint32_t VEC = 218624;                // per parity: Lam beta gam rk rq us (6 x 64 f32)
-constexpr uint32_t BARS = VEC + 2 * 6 * 256;
-constexpr uint32_t SMEM = BARS + 256;
+constexpr uint32_t VEC = 218624;                // per chunk mod 3: Lam beta gam rk rq us (6 x 64 f32)
+constexpr uint32_t BARS = VEC + 3 * 6 * 256;
+// decay factors exp(Lam_t - Lam_j) of one chunk, built by the prep group before A and P:
+constexpr uint32_t DEF = BARS + 256;            // fp32 [4][16][kLdDE]: inside the diagonal 16x16 blocks
+constexpr uint32_t ROWF = DEF + 4 * 16 * 20 * 4;  // fp32 [4][64]: exp(Lam_t - Lam_{16b+15}), b < t/16
+constexpr uint32_t COLF = ROWF + 4 * 64 * 4;    // fp32 [64]:    exp(Lam_{j|15} - Lam_j)
+constexpr uint32_t SMEM = COLF + 64 * 4;
+constexpr int kLdDE = 20;  // row stride of DEF (floats): conflict-free float4 rows
 static_assert(SMEM <= 232448, "shared memory budget");
 // TMEM columns
 constexpr uint32_t TS = 0, TSH = 128, TSL = 192, TUT = 256, TO = 320, TSK = 384, TKQ = 448;
@@ -971,8 +976,10 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + sizeof(Bars));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + BARS + sizeof(Bars) + 4);
-  auto vecp = [&](int par, int which) {  // which: 0 Lam 1 beta 2 gam 3 rk 4 rq 5 us
-    return reinterpret_cast<float*>(smem + VEC + 1536u * par + 256u * which);
+  // vector set of chunk c is c % 3: the gates of chunk c + 1 are written while the state
+  // group still reads the set of chunk c - 1
+  auto vecp = [&](int set, int which) {  // which: 0 Lam 1 beta 2 gam 3 rk 4 rq 5 us
+    return reinterpret_cast<float*>(smem + VEC + 1536u * set + 256u * which);
   };
 
   if (warp == 0) {
@@ -1021,59 +1028,96 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
 
   if (prep) {
     // =========================== prep group: chunk c one ahead of the state group
-    float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    // raw bf16 bits, converted where they are used one chunk later (so that nothing
+    // waits for these loads while the current chunk is processed)
+    uint32_t ga[2] = {0u, 0u}, gb[2] = {0u, 0u};
     auto load_gates = [&](int cc) {
       const long long tc0 = s0 + (long long)kC * cc;
       const int Lcc = (int)min((long long)kC, s1 - tc0);
+      const unsigned short* ra = reinterpret_cast<const unsigned short*>(p.a);
+      const unsigned short* rb = reinterpret_cast<const unsigned short*>(p.b);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int t = 2 * lane + e;
         if (t < Lcc) {
           const size_t ti = (size_t)(tc0 + t) * HV + h;
-          ga[e] = bf2f(p.a[ti]);
-          gb[e] = bf2f(p.b[ti]);
+          ga[e] = ra[ti];
+          gb[e] = rb[ti];
         }
       }
     };
-    if (warp == 8) load_gates(0);
+    // log decays (inclusive cumsum), beta and gamma of chunk cc into its vector set
+    auto compute_gates = [&](int cc) {
+      const long long tc0 = s0 + (long long)kC * cc;
+      const int Lcc = (int)min((long long)kC, s1 - tc0);
+      float* Lam = vecp(cc % 3, 0);
+      float* beta = vecp(cc % 3, 1);
+      float* gam = vecp(cc % 3, 2);
+      float lg[2], bb[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = 2 * lane + e < Lcc;
+        lg[e] = valid ? nexpA * softplus_f(__uint_as_float(ga[e] << 16) + dtb) : 0.f;
+        bb[e] = valid ? sigmoid_f(__uint_as_float(gb[e] << 16)) : 0.f;
+      }
+      float x = lg[0] + lg[1];
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+      }
+      const float x0 = x - lg[1];
+      Lam[2 * lane] = x0;
+      Lam[2 * lane + 1] = x;
+      beta[2 * lane] = bb[0];
+      beta[2 * lane + 1] = bb[1];
+      gam[2 * lane] = expf(x0);
+      gam[2 * lane + 1] = expf(x);
+    };
+    if (warp == 9) {
+      load_gates(0);
+      compute_gates(0);
+      if (nchunks > 1) load_gates(1);
+    }
+    group_sync(kBarPrep, kGroup);
     for (int c = 0; c < nchunks && ok; ++c) {
       const int par = c & 1;
       const long long t0 = s0 + (long long)kC * c;
       const int Lc = (int)min((long long)kC, s1 - t0);
       const uint32_t kqb = par ? KQ1 : KQ0;
-      float* Lam = vecp(par, 0);
-      float* beta = vecp(par, 1);
-      float* gam = vecp(par, 2);
-      float* rk = vecp(par, 3);
-      float* rq = vecp(par, 4);
-      float* us = vecp(par, 5);
+      const int set = c % 3;
+      const float* Lam = vecp(set, 0);
+      const float* beta = vecp(set, 1);
+      const float* gam = vecp(set, 2);
+      float* rk = vecp(set, 3);
+      float* rq = vecp(set, 4);
+      float* us = vecp(set, 5);
+      // decay factors exp(Lam_t - Lam_j), j <= t, with no positive exponent anywhere:
+      // directly inside the diagonal 16x16 blocks; across blocks through the last
+      // token e of j's block, exp(Lam_t - Lam_e) * exp(Lam_e - Lam_j).  (This chunk's
+      // gates were computed during the previous chunk.)
+      {
+        float* DE = reinterpret_cast<float*>(smem + DEF);
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int idx = u + 256 * k4;
+          const int blk = idx >> 8, r = (idx >> 4) & 15, jj = idx & 15;
+          DE[(16 * blk + r) * kLdDE + jj] =
+              (jj <= r) ? __expf(Lam[16 * blk + r] - Lam[16 * blk + jj]) : 0.f;
+        }
+        if (u < 64) {
+          float* RF = reinterpret_cast<float*>(smem + ROWF);
+          reinterpret_cast<float*>(smem + COLF)[u] = __expf(Lam[u | 15] - Lam[u]);
+#pragma unroll
+          for (int blk = 0; blk < 3; ++blk)
+            RF[64 * blk + u] = (16 * blk + 15 < u) ? __expf(Lam[u] - Lam[16 * blk + 15]) : 0.f;
+        }
+      }
       // this chunk's K/Q tiles (their arrival also means the state group has finished
-      // chunk c - 2, so the P buffer and vector set of this parity are free)
+      // chunk c - 2, so the P buffer of this parity and the vector set of chunk c + 1
+      // are free)
       pend_bar[0] = &bars->kqtma[par];
       pend_par[0] = (c >> 1) & 1;
-      if (warp == 8) {  // gates of chunk c (loaded one chunk ahead), then prefetch c+1
-        float lg[2], bb[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const bool valid = 2 * lane + e < Lc;
-          lg[e] = valid ? nexpA * softplus_f(ga[e] + dtb) : 0.f;
-          bb[e] = valid ? sigmoid_f(gb[e]) : 0.f;
-        }
-        float x = lg[0] + lg[1];
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, x, off);
-          if (lane >= off) x += y;
-        }
-        const float x0 = x - lg[1];
-        Lam[2 * lane] = x0;
-        Lam[2 * lane + 1] = x;
-        beta[2 * lane] = bb[0];
-        beta[2 * lane + 1] = bb[1];
-        gam[2 * lane] = expf(x0);
-        gam[2 * lane + 1] = expf(x);
-        if (c + 1 < nchunks) load_gates(c + 1);
-      }
       if (!group_wait(&bars->kqtma[par], (c >> 1) & 1, kBarPrep, abort_flag, ERR_TMA_TIMEOUT)) {
         ok = false;
         break;
@@ -1090,6 +1134,11 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
           umma_bf16(tmem + TKQ, kd, kd, idesc, ks > 0);
         }
         umma_commit(&bars->kq);
+      }
+      // while the MMA runs: gates (warp 9) and q/k row norms (warps 10-13)
+      if (warp == 9 && c + 1 < nchunks) {  // gates of chunk c + 1, then prefetch c + 2
+        compute_gates(c + 1);
+        if (c + 2 < nchunks) load_gates(c + 2);
       }
       if (u >= 64 && u < 192) {  // q/k row norms
         const int t = u & 63;
@@ -1113,6 +1162,8 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         const float r = rsqrtf(ss + kL2NormEps);
         if (isq) rq[t] = r; else rk[t] = r;
       }
+      group_sync(kBarPrep, kGroup);
+      if (u < 64) us[u] = (u < Lc) ? rk[u] * expf(Lam[63] - Lam[u]) : 0.f;
       if (!group_wait(&bars->kq, c & 1, kBarPrep, abort_flag, ERR_MMA_TIMEOUT)) {
         ok = false;
         break;
@@ -1121,29 +1172,39 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       tc_fence_after();
       // A (from Skk) -> AT in place; P hi (from Sqk) -> P[par]; Q~ = gamma rq Q in place
       {
-        const int t = row & 63;
+        const int t = row & 63, bt = t >> 4;
         const bool is_k = row < 64;
-        const float lt = Lam[t];
         const float ft = is_k ? beta[t] * rk[t] : rq[t];
+        const float* DE = reinterpret_cast<const float*>(smem + DEF) + t * kLdDE;
+        const float* RF = reinterpret_cast<const float*>(smem + ROWF);
+        const float* CF = reinterpret_cast<const float*>(smem + COLF);
 #pragma unroll
-        for (int pass = 0; pass < 2; ++pass) {  // 16 columns per pass keeps registers low
-          const int j0 = 32 * half + 16 * pass;
-          float kq[16], lv[16], rv[16];
-          tmem_ld16(tl + TKQ + (uint32_t)j0, kq);
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 lj = *reinterpret_cast<const float4*>(Lam + j0 + i);
-            const float4 rj = *reinterpret_cast<const float4*>(rk + j0 + i);
-            lv[i] = lj.x; lv[i + 1] = lj.y; lv[i + 2] = lj.z; lv[i + 3] = lj.w;
-            rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
-          }
-          tmem_wait_ld();
+        for (int pass = 0; pass < 2; ++pass) {  // one 16-token block of columns per pass
+          const int j0 = 32 * half + 16 * pass, bj = j0 >> 4;
           float ej[16];
+          if ((t | 31) < j0) {  // whole warp above the diagonal (warp-uniform)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int j = j0 + i;
-            const bool keep = is_k ? (j < t) : (j <= t);
-            ej[i] = keep ? ft * rv[i] * kq[i] * __expf(lt - lv[i]) : 0.f;
+            for (int i = 0; i < 16; ++i) ej[i] = 0.f;
+          } else {
+            float kq[16], rv[16], fv[16];
+            tmem_ld16(tl + TKQ + (uint32_t)j0, kq);
+            // factor row: diagonal block from DE, earlier blocks RF x CF, later ones 0
+            const float rowf = ft * ((bj < bt) ? RF[64 * bj + t] : (bj == bt ? 1.f : 0.f));
+            const float* fsrc = (bj == bt) ? DE : (CF + j0);
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 rj = *reinterpret_cast<const float4*>(rk + j0 + i);
+              const float4 f4 = *reinterpret_cast<const float4*>(fsrc + i);
+              rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
+              fv[i] = f4.x; fv[i + 1] = f4.y; fv[i + 2] = f4.z; fv[i + 3] = f4.w;
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int j = j0 + i;
+              const bool keep = is_k ? (j < t) : (j <= t);
+              ej[i] = keep ? rowf * fv[i] * rv[i] * kq[i] : 0.f;
+            }
           }
           if (is_k) {
             float* Arow = reinterpret_cast<float*>(smem + AT) + t * kLd + j0;
@@ -1177,7 +1238,6 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
             st_v4(qb + 16u * ch, w);
           }
         }
-        if (u < 64) us[u] = (u < Lc) ? rk[u] * expf(Lam[63] - Lam[u]) : 0.f;
       }
       tc_fence_before();
       group_sync(kBarPrep, kGroup);
@@ -1251,11 +1311,11 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       const long long t0 = s0 + (long long)kC * c;
       const int Lc = (int)min((long long)kC, s1 - t0);
       const uint32_t kqb = par ? KQ1 : KQ0;
-      const float* Lam = vecp(par, 0);
-      const float* beta = vecp(par, 1);
-      const float* gam = vecp(par, 2);
-      const float* rk = vecp(par, 3);
-      const float* us = vecp(par, 5);
+      const float* Lam = vecp(c % 3, 0);
+      const float* beta = vecp(c % 3, 1);
+      const float* gam = vecp(c % 3, 2);
+      const float* rk = vecp(c % 3, 3);
+      const float* us = vecp(c % 3, 5);
       pend_bar[1] = &bars->vtma;
       pend_par[1] = c & 1;
       if (!group_wait(&bars->t_ready, c & 1, kBarState, abort_flag, ERR_MMA_TIMEOUT) ||
