@@ -12,8 +12,9 @@ line also carries a ``prefill`` object with the P1 (8 varlen sequences) and P2
 N > 1 (torchrun, one process per GPU): weak scaling -- every rank runs the
 same per-GPU workload on its own data (decode: 128 sequences per GPU, so N=8
 is the 1024-sequence configuration sharded by batch; prefill: the 64-sequence
-P3 set sharded by sequence with longest-first bin packing); there is no
-collective on the data path.  Time is the max over ranks of the device time.
+P3 set sharded by sequence with longest-first bin packing, and the single
+sequence of P2 sharded by q/k-head group); there is no collective on the data
+path.  Time is the max over ranks of the device time.
 
 Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
 the launching stream, barrier + synchronize on both sides.  Inputs are larger
@@ -228,13 +229,39 @@ class DecodeWork:
         self.h_ns.copy_(self.d_ns, non_blocking=True)
 
 
+def prefill_plan(pkg, name, dist):
+    """This rank's part of prefill config `name`: None at N=1; whole sequences
+    (longest-first packing) when there are at least as many sequences as ranks;
+    else a q/k-head group with its v-heads.  No collective either way."""
+    if dist.world == 1:
+        return None
+    W = pkg.workloads
+    cfg = W.PREFILL_CONFIGS[name]
+    if cfg.n >= dist.world:
+        lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
+        return ("seqs", pkg.sharding.lpt_assign(lens, dist.world)[dist.rank])
+    return ("heads",) + tuple(pkg.sharding.head_range(W.HQ, dist.world, dist.rank))
+
+
+def plan_text(plan, world):
+    if plan is None:
+        return "single GPU"
+    if plan[0] == "seqs":
+        return f"sequence-sharded x{world} (LPT), no collective"
+    return f"q/k-head-group-sharded x{world}, no collective"
+
+
 class PrefillWork:
     def __init__(self, pkg, cfg_name, dev, seed, shard=None):
         W = pkg.workloads
         self.pkg, self.dev = pkg, dev
         inp = W.prefill_config_inputs(cfg_name, seed=seed, device="cpu")
-        if shard is not None:  # this rank's sequences, re-packed (no collective)
-            inp = pkg.sharding.prefill_shard(inp, shard)
+        head_frac = 1.0
+        if shard is not None and shard[0] == "seqs":  # this rank's sequences, re-packed
+            inp = pkg.sharding.prefill_shard(inp, shard[1])
+        elif shard is not None:  # this rank's q/k heads and their v-heads
+            inp = pkg.sharding.prefill_head_shard(inp, shard[1], shard[2])
+            head_frac = inp["v"].shape[1] / W.HV
         lens = pkg.sharding.seqlens_from_cu(inp["cu_seqlens"])
         self.lens = lens
         self.inp = {k_: (v_.to(dev) if isinstance(v_, torch.Tensor) else v_) for k_, v_ in inp.items()}
@@ -243,8 +270,9 @@ class PrefillWork:
         N = len(lens)
         self.out = torch.empty(T, self.inp["v"].shape[1], 128, dtype=torch.bfloat16, device=dev)
         self.ns = torch.empty(N, self.inp["v"].shape[1], 128, 128, dtype=torch.float32, device=dev)
-        self.tokens = T
-        self.flops = T * W.prefill_flops_per_token()
+        # whole-sequence tokens this rank completes (a head group does a share of each)
+        self.tokens = T * head_frac
+        self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
         self.launches = pkg.prefill.launches_per_call(T, N)
 
     def step(self):
@@ -380,7 +408,7 @@ def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2
     if dist.pg:
         t = torch.tensor([w.tokens], dtype=torch.float64, device=dev)
         dist.pg.all_reduce(t)
-        tokens_all = int(t.item())
+        tokens_all = int(round(t.item()))
     res = {"ms": ms, "kern_ms": kern_ms, "value": tokens_all / (ms * 1e-3),
            "tflops": tokens_all * pkg.workloads.prefill_flops_per_token() / (ms * 1e-3) / 1e12,
            "achieved": w.flops / (kern_ms * 1e-3) / 1e12, "clocks": clk.summary(),
@@ -437,12 +465,7 @@ def run_ours(args, dist):
             "kernel_ms": round(r["kern_ms"], 5),
         })
     else:
-        shard = None
-        if dist.world > 1:
-            W = pkg.workloads
-            cfg = W.PREFILL_CONFIGS[param]
-            lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
-            shard = pkg.sharding.lpt_assign(lens, dist.world)[dist.rank]
+        shard = prefill_plan(pkg, param, dist)
         r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
         line.update({
             "metric": "prefill tokens/s", "value": round(r["value"], 1), "unit": "tokens/s",
@@ -451,7 +474,7 @@ def run_ours(args, dist):
             "scaling": "strong" if dist.world > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
             "config": {"workload": f"GDN prefill {param}", "tokens": r["tokens_all"],
-                       "parallelism": f"sequence-sharded x{dist.world} (LPT), no collective",
+                       "parallelism": plan_text(shard, dist.world),
                        "l2": "inputs > L2"},
             "tflops": round(r["tflops"], 2),
             "roofline": roofline("tensor", r["achieved"], args.workload, pk, src),
@@ -461,18 +484,14 @@ def run_ours(args, dist):
     # secondary: the prefill configurations next to the decode headline
     if kind == "decode" and not args.no_prefill_extra:
         extra = {}
-        names = ["P1", "P2"] if dist.world == 1 else ["P3"]
+        names = ["P1", "P2"] if dist.world == 1 else ["P2", "P3"]
         for nm in names:
-            shard = None
-            if dist.world > 1:
-                W = pkg.workloads
-                cfg = W.PREFILL_CONFIGS[nm]
-                shard = pkg.sharding.lpt_assign(W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0),
-                                                dist.world)[dist.rank]
+            shard = prefill_plan(pkg, nm, dist)
             r = measure_prefill(pkg, dist, nm, max(3, min(args.steps, 10)), 3, dev, shard=shard,
                                 with_e2e=False)
             extra[nm] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
                          "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
+                         "parallelism": plan_text(shard, dist.world),
                          "roofline": roofline("tensor", r["achieved"], "prefill_" + nm.lower(),
                                               pk, src)}
         line["prefill"] = extra

@@ -7,7 +7,10 @@ Every unit of GDN work is independent of every other one:
 * prefill: each sequence's scan touches only its own tokens and state slice,
   so whole sequences are dealt to ranks; the packed token ranges of a rank's
   sequences are gathered into a rank-local packed layout with re-based
-  ``cu_seqlens`` (0, len0, len0+len1, ...).
+  ``cu_seqlens`` (0, len0, len0+len1, ...);
+* prefill with fewer sequences than ranks (one long sequence): each v-head's
+  scan reads only its own q/k head (v-head h uses q/k head h // (HV/HQ)), so
+  q/k-head groups are dealt to ranks together with the v-heads that use them.
 
 Load balance for prefill uses longest-processing-time bin packing on token
 counts.  There is no exchange step on the data path, so there is no NCCL
@@ -93,4 +96,45 @@ def prefill_unshard(full_tokens: int, num_seqs: int, cu_seqlens: torch.Tensor,
             out[cu[i]:cu[i + 1]] = o[pos:pos + n].cpu()
             st[i] = s[j].cpu()
             pos += n
+    return out, st
+
+
+def head_range(num_qk_heads: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [lo, hi) range of q/k heads of `rank` (head-group sharding)."""
+    return batch_range(num_qk_heads, world, rank)
+
+
+def prefill_head_shard(inp: Dict[str, torch.Tensor], qk_lo: int, qk_hi: int
+                       ) -> Dict[str, torch.Tensor]:
+    """The rank-local prefill problem for q/k heads [qk_lo, qk_hi) and their v-heads.
+
+    All sequences and tokens stay; q and k keep heads [qk_lo, qk_hi), and v, a,
+    b, A_log, dt_bias and the initial state keep the v-heads
+    [qk_lo * r, qk_hi * r) with r = HV / HQ, each copied into a contiguous
+    tensor.  cu_seqlens and scale are shared.
+    """
+    HQ, HV = inp["q"].shape[1], inp["v"].shape[1]
+    if HQ <= 0 or HV % HQ != 0:
+        raise ValueError(f"head-group sharding needs HV ({HV}) to be a multiple of HQ ({HQ})")
+    if not 0 <= qk_lo < qk_hi <= HQ:
+        raise ValueError(f"bad q/k head range [{qk_lo}, {qk_hi}) for {HQ} heads")
+    r = HV // HQ
+    v_lo, v_hi = qk_lo * r, qk_hi * r
+    out = dict(inp)
+    for key in ("q", "k"):
+        out[key] = inp[key][:, qk_lo:qk_hi].contiguous()
+    for key in ("v", "a", "b"):
+        out[key] = inp[key][:, v_lo:v_hi].contiguous()
+    for key in ("A_log", "dt_bias"):
+        out[key] = inp[key][v_lo:v_hi].contiguous()
+    if inp.get("state") is not None:
+        out["state"] = inp["state"][:, v_lo:v_hi].contiguous()
+    return out
+
+
+def prefill_head_unshard(outputs: Sequence[torch.Tensor], states: Sequence[torch.Tensor]
+                         ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Reassemble per-rank (output, new_state) of consecutive head ranges (rank order)."""
+    out = torch.cat([o.cpu() for o in outputs], dim=1)
+    st = torch.cat([s.cpu() for s in states], dim=1)
     return out, st

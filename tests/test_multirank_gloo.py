@@ -1,6 +1,7 @@
 """CPU, world_size 2 over gloo: the one-process-per-GPU driver's host logic.
 
-* sharded decode and prefill (oracle as the per-rank compute) reassemble into
+* sharded decode and prefill (by sequence and by q/k-head group; oracle as the
+  per-rank compute) reassemble into
   the unsharded result, and the max-over-ranks timing reduction works;
 * failure detection on the host: a rank that dies before the barrier makes
   the surviving rank's next collective end with an error within the process
@@ -58,6 +59,14 @@ def _worker_sharded(rank, world, port, q):
                            sh["dt_bias"], sh["b"], sh["cu_seqlens"], sh["scale"])
         pre = [None] * world
         dist.all_gather_object(pre, (po, ps))
+        # prefill, one sequence: q/k-head-group sharding
+        hinp = W.prefill_inputs([37], hq=2, hv=4, seed=9)
+        hlo, hhi = S.head_range(2, world, rank)
+        hs = S.prefill_head_shard(hinp, hlo, hhi)
+        ho, hst = O.prefill(hs["q"], hs["k"], hs["v"], hs["state"], hs["A_log"], hs["a"],
+                            hs["dt_bias"], hs["b"], hs["cu_seqlens"], hs["scale"])
+        heads = [None] * world
+        dist.all_gather_object(heads, (ho, hst))
         # max-over-ranks reduction used for the bench timing
         t = torch.tensor([float(rank + 1)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -72,6 +81,11 @@ def _worker_sharded(rank, world, port, q):
             uo, us = S.prefill_unshard(sum(lens), len(lens), pinp["cu_seqlens"], plan,
                                        [x[0] for x in pre], [x[1] for x in pre])
             ok_pre = torch.equal(uo, ro) and O.state_rel_err(us, rs) < 1e-6
+            fo, fs = O.prefill(hinp["q"], hinp["k"], hinp["v"], hinp["state"], hinp["A_log"],
+                               hinp["a"], hinp["dt_bias"], hinp["b"], hinp["cu_seqlens"],
+                               hinp["scale"])
+            ho_all, hs_all = S.prefill_head_unshard([x[0] for x in heads], [x[1] for x in heads])
+            ok_pre = ok_pre and torch.equal(ho_all, fo) and O.state_rel_err(hs_all, fs) < 1e-6
             q.put(("ok", ok_dec, ok_pre, float(t.item())))
         dist.barrier()
         dist.destroy_process_group()

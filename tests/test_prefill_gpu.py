@@ -125,6 +125,29 @@ def test_p2_split_sequence_property(cuda):
     assert ok
 
 
+def test_p2_head_group_shards_reassemble_bitwise(cuda):
+    """P2 sharded by q/k-head group (the multi-GPU plan when there are fewer
+    sequences than GPUs), run shard by shard on one GPU: the reassembled output
+    and final state are bit-identical to the unsharded call, because every
+    (sequence, v-head) scan depends only on its own heads."""
+    pkg = load_pkg()
+    S = pkg.sharding
+    inp = pkg.workloads.prefill_config_inputs("P2", seed=0, device="cuda")
+    keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")
+    o, s = pkg.gdn_prefill(*[inp[k_] for k_ in keys], use_qk_l2norm=True)
+    for world in (2, 8):
+        outs, states = [], []
+        for r in range(world):
+            lo, hi = S.head_range(inp["q"].shape[1], world, r)
+            sh = S.prefill_head_shard(inp, lo, hi)
+            ro, rs = pkg.gdn_prefill(*[sh[k_] for k_ in keys], use_qk_l2norm=True)
+            outs.append(ro)
+            states.append(rs)
+        uo, us = S.prefill_head_unshard(outs, states)
+        assert torch.equal(uo, o.cpu()) and torch.equal(us, s.cpu())
+    assert pkg.device_error() == 0
+
+
 def test_chunked_matches_recurrent_p2_full(cuda):
     """P2 at full size (32768 tokens, initial state): the chunked tensor-core kernel
     and the token-serial CUDA-core kernel agree (state rel <= 1e-3, outputs within

@@ -57,3 +57,33 @@ def test_prefill_shard_roundtrip_matches_unsharded_oracle():
     assert torch.equal(o, full_o)
     # same recurrence per sequence; the batched einsum may only reorder fp32 sums
     assert O.state_rel_err(s, full_s) < 1e-6
+
+
+def test_head_ranges_and_shard_roundtrip_matches_unsharded_oracle():
+    pkg = load_pkg()
+    S, W = pkg.sharding, pkg.workloads
+    lens = [9, 0, 70]
+    inp = W.prefill_inputs(lens, hq=4, hv=8, seed=5)
+    full_o, full_s = O.prefill(O.l2norm(inp["q"]), O.l2norm(inp["k"]), inp["v"], inp["state"],
+                               inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                               inp["cu_seqlens"], inp["scale"])
+    for world in (1, 2, 3, 4):
+        rs = [S.head_range(4, world, r) for r in range(world)]
+        assert rs[0][0] == 0 and rs[-1][1] == 4
+        outs, states = [], []
+        for lo, hi in rs:
+            sh = S.prefill_head_shard(inp, lo, hi)
+            assert sh["q"].shape[1] == hi - lo and sh["v"].shape[1] == 2 * (hi - lo)
+            assert sh["q"].is_contiguous() and sh["state"].is_contiguous()
+            o, s = O.prefill(O.l2norm(sh["q"]), O.l2norm(sh["k"]), sh["v"], sh["state"],
+                             sh["A_log"], sh["a"], sh["dt_bias"], sh["b"], sh["cu_seqlens"],
+                             sh["scale"])
+            outs.append(o)
+            states.append(s)
+        o, s = S.prefill_head_unshard(outs, states)
+        assert torch.equal(o, full_o)
+        assert O.state_rel_err(s, full_s) < 1e-6
+    with pytest.raises(ValueError):
+        S.prefill_head_shard(inp, 2, 2)
+    with pytest.raises(ValueError):
+        S.prefill_head_shard(W.prefill_inputs([3], hq=2, hv=3, seed=1), 0, 1)
