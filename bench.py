@@ -273,7 +273,7 @@ class PrefillWork:
         # whole-sequence tokens this rank completes (a head group does a share of each)
         self.tokens = T * head_frac
         self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
-        self.launches = pkg.prefill.launches_per_call(T, N)
+        self.launches = pkg.prefill.launches_per_call(T, N, self.inp["q"].shape[1], self.inp["v"].shape[1])
 
     def step(self):
         d = self.inp

@@ -98,9 +98,10 @@ size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_head
  *   new_state fp32 [num_seqs, max(num_q_heads, num_v_heads), 128, 128] (written)
  *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes
  *              (may be NULL when that size is 0).  Scratch only: it holds the
- *              longest-first order in which the sequences are scheduled, is
- *              rewritten by every call, and must not be shared by calls that
- *              overlap on the GPU.
+ *              longest-first order in which the sequences are scheduled and,
+ *              for the split kernels, the per-chunk records (34,048 bytes per
+ *              64-token chunk and v-head); it is rewritten by every call and
+ *              must not be shared by calls that overlap on the GPU.
  * A sequence of length 0 gets an all-zero new_state slice (as the
  * flashinfer-bench definition reference does).
  * Replaces gdn_prefill_chunk_kernel (gdn_prefill/solution/triton/kernel.py:28-250)
@@ -129,6 +130,38 @@ int gdn_prefill_launch_recurrent(const void* q, const void* k, const void* v, co
                                  int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
                                  int head_size, int use_qk_l2norm, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/*
+ * Prefill kernel selection (no counterpart in the reference), for validation
+ * and benchmarking of the individual kernels:
+ *   GDN_PREFILL_AUTO       what gdn_prefill_launch runs for these sizes
+ *   GDN_PREFILL_RECURRENT  token-serial CUDA-core kernel (same as
+ *                          gdn_prefill_launch_recurrent; no workspace)
+ *   GDN_PREFILL_FUSED      chunked tensor-core kernel, one CTA per
+ *                          (sequence, v-head) for the whole scan
+ *   GDN_PREFILL_SPLIT      chunk-parallel preparation kernel + sequential
+ *                          state kernel per (sequence, v-head, 64-row v-block)
+ * FUSED and SPLIT need 16-byte aligned q, k, v and output (else
+ * GDN_ERR_UNSUPPORTED); AUTO falls back to RECURRENT in that case.
+ */
+#define GDN_PREFILL_AUTO 0
+#define GDN_PREFILL_RECURRENT 1
+#define GDN_PREFILL_FUSED 2
+#define GDN_PREFILL_SPLIT 3
+
+/* Workspace bytes of gdn_prefill_launch_variant(variant, ...) for this problem. */
+size_t gdn_prefill_workspace_size_variant(int variant, int total_tokens, int num_seqs,
+                                          int num_q_heads, int num_v_heads, int head_size);
+
+/* gdn_prefill_launch with an explicit kernel choice (GDN_PREFILL_*). */
+int gdn_prefill_launch_variant(int variant, const void* q, const void* k, const void* v,
+                               const float* state, const float* A_log, const void* a,
+                               const float* dt_bias, const void* b, const void* cu_seqlens,
+                               int cu_seqlens_int64, float scale, void* output,
+                               float* new_state, int total_tokens, int num_seqs,
+                               int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+                               int use_qk_l2norm, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /*
  * Allocation-free variant of gdn_prefill_launch (no counterpart in the

@@ -32,8 +32,17 @@ SIGNATURES = {
                                           _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_prefill_launch_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
                                         _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_prefill_workspace_size_variant": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "gdn_prefill_launch_variant": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
+                                        _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_device_error": (_i, [_i]),
 }
+
+# Prefill kernel selection (gdn_prefill_launch_variant).
+GDN_PREFILL_AUTO = 0
+GDN_PREFILL_RECURRENT = 1
+GDN_PREFILL_FUSED = 2
+GDN_PREFILL_SPLIT = 3
 
 
 def _load() -> ctypes.CDLL:

@@ -14,26 +14,52 @@ inline bool misaligned(const void* p, uintptr_t n) {
 }
 }  // namespace
 
+namespace {
+// The fused kernel runs one CTA per (sequence, v-head) for the whole scan; with
+// fewer such pairs than B200 has SMs (148), most SMs would idle, and the split
+// kernels (chunk-parallel preparation, then the scan on two CTAs per pair) are
+// faster.  With at least one pair per SM the fused kernel is faster.
+constexpr long long kSplitBelowPairs = 148;
+bool auto_uses_split(long long T, int N, int HV) {
+  return T > 0 && N > 0 && (long long)N * HV < kSplitBelowPairs;
+}
+
+size_t variant_workspace(int variant, long long T, int N, int HV) {
+  if (T <= 0 || N <= 0) return 0;
+  switch (variant) {
+    case GDN_PREFILL_RECURRENT: return 0;
+    case GDN_PREFILL_FUSED: return gdn::prefill_chunked_workspace(N);
+    case GDN_PREFILL_SPLIT: return gdn::prefill_split_workspace(T, N, HV);
+    default:
+      return auto_uses_split(T, N, HV) ? gdn::prefill_split_workspace(T, N, HV)
+                                       : gdn::prefill_chunked_workspace(N);
+  }
+}
+}  // namespace
+
+extern "C" size_t gdn_prefill_workspace_size_variant(int variant, int total_tokens, int num_seqs,
+                                                     int num_q_heads, int num_v_heads,
+                                                     int head_size) {
+  (void)num_q_heads;
+  (void)head_size;
+  return variant_workspace(variant, total_tokens, num_seqs, num_v_heads);
+}
+
 extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
                                              int num_v_heads, int head_size) {
-  (void)num_q_heads;
-  (void)num_v_heads;
-  (void)head_size;
-  if (total_tokens <= 0) return 0;
-  return gdn::prefill_chunked_workspace(num_seqs);  // longest-first sequence order
+  return gdn_prefill_workspace_size_variant(GDN_PREFILL_AUTO, total_tokens, num_seqs,
+                                            num_q_heads, num_v_heads, head_size);
 }
 
 namespace {
-enum class PrefillPath { kAuto, kRecurrent };
-
-int prefill_entry(PrefillPath path, const void* q, const void* k, const void* v, const float* state,
-                                  const float* A_log, const void* a, const float* dt_bias,
-                                  const void* b, const void* cu_seqlens, int cu_seqlens_int64,
-                                  float scale, void* output, float* new_state, int total_tokens,
-                                  int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
-                                  int head_size, int use_qk_l2norm, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+int prefill_entry(int variant, const void* q, const void* k, const void* v, const float* state,
+                  const float* A_log, const void* a, const float* dt_bias, const void* b,
+                  const void* cu_seqlens, int cu_seqlens_int64, float scale, void* output,
+                  float* new_state, int total_tokens, int num_seqs, int num_q_heads,
+                  int num_k_heads, int num_v_heads, int head_size, int use_qk_l2norm,
+                  void* workspace, size_t workspace_bytes, void* stream) {
   using namespace gdn;
+  if (variant < GDN_PREFILL_AUTO || variant > GDN_PREFILL_SPLIT) return GDN_ERR_INVALID_ARGUMENT;
   if (total_tokens < 0 || num_seqs < 0 || num_q_heads <= 0 || num_k_heads <= 0 ||
       num_v_heads <= 0)
     return GDN_ERR_INVALID_ARGUMENT;
@@ -46,18 +72,28 @@ int prefill_entry(PrefillPath path, const void* q, const void* k, const void* v,
       (state && misaligned(state, 16)) || misaligned(cu_seqlens, cu_seqlens_int64 ? 8 : 4))
     return GDN_ERR_INVALID_ARGUMENT;
   if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
-  const size_t need =
-      gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads, num_v_heads, head_size);
-  if (path == PrefillPath::kAuto && need > 0 && (workspace == nullptr || workspace_bytes < need))
-    return GDN_ERR_WORKSPACE;  // (the recurrent kernel uses no workspace)
+  const size_t need = variant_workspace(variant, total_tokens, num_seqs, num_v_heads);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
 
   PrefillArgs p{q,        k,     v,      state,      A_log,        a,           dt_bias,
                 b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,
                 (long long)total_tokens, num_seqs, num_q_heads, num_v_heads,
                 use_qk_l2norm != 0, workspace, workspace_bytes};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool chunked_ok = total_tokens > 0 && prefill_chunked_supported(p);
+  int kind = variant;
+  if (kind == GDN_PREFILL_AUTO)
+    kind = !chunked_ok ? GDN_PREFILL_RECURRENT
+                       : (auto_uses_split(total_tokens, num_seqs, num_v_heads) ? GDN_PREFILL_SPLIT
+                                                                              : GDN_PREFILL_FUSED);
+  if ((kind == GDN_PREFILL_FUSED || kind == GDN_PREFILL_SPLIT) && !chunked_ok) {
+    if (total_tokens > 0) return GDN_ERR_UNSUPPORTED;
+    kind = GDN_PREFILL_RECURRENT;  // no tokens: only the zero final states to write
+  }
   cudaError_t err;
-  if (path == PrefillPath::kAuto && prefill_chunked_supported(p))
+  if (kind == GDN_PREFILL_SPLIT)
+    err = launch_prefill_split(p, st);
+  else if (kind == GDN_PREFILL_FUSED)
     err = launch_prefill_chunked(p, st);
   else
     err = launch_prefill_recurrent(p, 0, num_seqs, st);
@@ -72,7 +108,7 @@ extern "C" int gdn_prefill_launch(const void* q, const void* k, const void* v, c
                                   int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
                                   int head_size, int use_qk_l2norm, void* workspace,
                                   size_t workspace_bytes, void* stream) {
-  return prefill_entry(PrefillPath::kAuto, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+  return prefill_entry(GDN_PREFILL_AUTO, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                        cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
                        num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
                        workspace_bytes, stream);
@@ -84,7 +120,19 @@ extern "C" int gdn_prefill_launch_recurrent(
     int cu_seqlens_int64, float scale, void* output, float* new_state, int total_tokens,
     int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
     int use_qk_l2norm, void* workspace, size_t workspace_bytes, void* stream) {
-  return prefill_entry(PrefillPath::kRecurrent, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+  return prefill_entry(GDN_PREFILL_RECURRENT, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                       cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
+                       num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
+                       workspace_bytes, stream);
+}
+
+extern "C" int gdn_prefill_launch_variant(
+    int variant, const void* q, const void* k, const void* v, const float* state,
+    const float* A_log, const void* a, const float* dt_bias, const void* b,
+    const void* cu_seqlens, int cu_seqlens_int64, float scale, void* output, float* new_state,
+    int total_tokens, int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+    int head_size, int use_qk_l2norm, void* workspace, size_t workspace_bytes, void* stream) {
+  return prefill_entry(variant, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                        cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
                        num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
                        workspace_bytes, stream);
@@ -92,5 +140,8 @@ extern "C" int gdn_prefill_launch_recurrent(
 
 extern "C" int gdn_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  return (int)gdn::read_device_error(clear != 0);
+  const unsigned a = gdn::read_device_error(clear != 0);
+  const unsigned b = gdn::read_split_device_error(clear != 0);
+  if (a == ~0u || b == ~0u) return -1;
+  return (int)(a | b);
 }

@@ -1,6 +1,7 @@
 // Internal interface between the prefill C-ABI entry point and its kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -39,6 +40,17 @@ bool prefill_chunked_supported(const PrefillArgs& p);
 // Scratch bytes the chunked path uses for its longest-first sequence order.
 size_t prefill_chunked_workspace(int num_seqs);
 cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st);
+
+// TMA descriptor of a [rows][heads * 128] bf16 matrix with 64 x 64 boxes and the
+// 128-byte swizzle (false if the driver's encoder is unavailable or refuses it).
+bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows);
+
+// Split path: a chunk-parallel preparation kernel and a sequential state kernel
+// split over v-blocks.  Same requirements as the chunked kernel; the workspace
+// holds the per-chunk records.
+size_t prefill_split_workspace(long long T, int num_seqs, int HV);
+cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t st);
+unsigned read_split_device_error(bool clear);
 
 // Device-side error flag set by a bounded wait that ran out (0 = none).
 unsigned read_device_error(bool clear);

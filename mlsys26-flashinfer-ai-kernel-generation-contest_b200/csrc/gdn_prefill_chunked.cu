@@ -54,6 +54,8 @@
 #include <cudaTypedefs.h>
 
 #include "gdn_common.cuh"
+#include "gdn_chunk_math.cuh"
+#include "gdn_lpt.cuh"
 #include "gdn_prefill.cuh"
 #include "sm100.cuh"
 
@@ -63,6 +65,7 @@ __device__ unsigned int g_prefill_device_error = 0;
 
 namespace {
 using namespace sm100;
+using namespace cm;
 
 constexpr int kC = 64;          // chunk length
 constexpr int kThreads = 512;   // 16 warps
@@ -122,55 +125,6 @@ struct ChunkedParams {
   int ratio;
   float scale;
 };
-
-// bf16 conversions with integer operations (ALU pipe) rather than cvt (which
-// shares the XU pipe with exp/rsqrt and was the kernel's busiest pipe).
-// Round-to-nearest-even of a finite fp32 bit pattern to bf16, kept in the high half.
-__device__ __forceinline__ uint32_t rn_bf16_bits(uint32_t xb) {
-  return (xb + 0x7FFFu + ((xb >> 16) & 1u)) & 0xFFFF0000u;
-}
-// Two bf16 values held in the high halves of a and b -> one packed word (a low, b high).
-__device__ __forceinline__ uint32_t pack_hi16(uint32_t a, uint32_t b) {
-  return __byte_perm(a, b, 0x7632);
-}
-// 8 floats -> (hi, lo) bf16 chunks with x ~= hi + lo: hi is x truncated to bf16
-// (exact residual x - hi, |x - hi| < 2^-7 |x|) and lo that residual truncated, so
-// hi + lo keeps ~15 significant bits (relative error < 2^-15) for three ALU
-// operations per element (mask, subtract, byte-permute).
-__device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
-  uint32_t xb[8], lb[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    xb[i] = __float_as_uint(x[i]);
-    lb[i] = __float_as_uint(x[i] - __uint_as_float(xb[i] & 0xFFFF0000u));
-  }
-  hi = make_uint4(pack_hi16(xb[0], xb[1]), pack_hi16(xb[2], xb[3]), pack_hi16(xb[4], xb[5]),
-                  pack_hi16(xb[6], xb[7]));
-  lo = make_uint4(pack_hi16(lb[0], lb[1]), pack_hi16(lb[2], lb[3]), pack_hi16(lb[4], lb[5]),
-                  pack_hi16(lb[6], lb[7]));
-}
-// Round-to-nearest bf16 pair (one cvt per two elements), low element first.
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo_elem, float hi_elem) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-// 16 consecutive fp32 TMEM columns of this thread's lane (warp-collective).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void st_v4(uint32_t addr, uint4 v) {
-  st_shared_v4(addr, v.x, v.y, v.z, v.w);
-}
 
 // All threads wait on `bar`; returns false on every thread if any thread timed out.
 __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity, unsigned code) {
@@ -774,7 +728,6 @@ namespace pl {
 constexpr int kThreads = 512;
 constexpr uint32_t kGroup = 256;        // threads per warp group
 constexpr uint32_t kBarState = 1, kBarPrep = 2;
-constexpr int kLd = 68;                 // row stride of the in-place A / T matrix
 // shared memory
 constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // per buffer: K0 | Q0 | K1 | Q1 (8 KB each)
 constexpr uint32_t V = 65536;             // V0 | V1
@@ -817,126 +770,6 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint3
   return !bad;
 }
 
-// ---- warp-level tensor-core products for the inverse's block merges ----
-// D(16x8) = X(16xK) * Y(Kx8), fp32 operands as 3xTF32 (hi.hi + hi.lo + lo.hi;
-// hi = the top 10 mantissa bits, lo = the exact residual), so the result carries
-// ~21 significant bits.  Fragment layout of mma.m16n8k8 (tf32): g = lane/4,
-// t = lane%4; A: (g, t) (g+8, t) (g, t+4) (g+8, t+4); B: (t, g) (t+4, g);
-// C: (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1).
-constexpr int kLdE3 = 20, kLdE4 = 36;  // scratch strides (2-way bank conflicts at most)
-
-__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
-                                         const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-__device__ __forceinline__ void mma_tile_tf32x3(const float* X, int ldx, const float* Y, int ldy,
-                                                int K, float (&c)[4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  c[0] = c[1] = c[2] = c[3] = 0.f;
-  for (int k0 = 0; k0 < K; k0 += 8) {
-    const float af[4] = {X[g * ldx + k0 + t], X[(g + 8) * ldx + k0 + t],
-                         X[g * ldx + k0 + t + 4], X[(g + 8) * ldx + k0 + t + 4]};
-    const float bf[2] = {Y[(k0 + t) * ldy + g], Y[(k0 + t + 4) * ldy + g]};
-    uint32_t ah[4], al[4], bh[2], bl[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      ah[i] = __float_as_uint(af[i]) & 0xFFFFE000u;
-      al[i] = __float_as_uint(af[i] - __uint_as_float(ah[i]));
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      bh[i] = __float_as_uint(bf[i]) & 0xFFFFE000u;
-      bl[i] = __float_as_uint(bf[i] - __uint_as_float(bh[i]));
-    }
-    mma_tf32(c, al, bh);
-    mma_tf32(c, ah, bl);
-    mma_tf32(c, ah, bh);
-  }
-}
-__device__ __forceinline__ void store_tile(float* D, int ldd, const float (&c)[4], float sgn) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  D[g * ldd + 2 * t] = sgn * c[0];
-  D[g * ldd + 2 * t + 1] = sgn * c[1];
-  D[(g + 8) * ldd + 2 * t] = sgn * c[2];
-  D[(g + 8) * ldd + 2 * t + 1] = sgn * c[3];
-}
-
-// In-place T = (I + A)^-1 for the strictly lower triangular A in M[64][kLd], by
-// the 256 threads of the prep group (local index u): 8x8 diagonal blocks by
-// forward substitution, then 8->16 (CUDA cores), 16->32 and 32->64 (warp-level
-// tensor cores, 3xTF32) block merges T21 = -T22 (A21 T11), each A21 block
-// overwritten by T21 once it has been read.
-__device__ __forceinline__ void invert_in_place(float* __restrict__ M, float* __restrict__ Es,
-                                                int u) {
-  if (u < 64) {
-    const int o = 8 * (u >> 3), col = u & 7;
-    float a[8][8];
-#pragma unroll
-    for (int r = 1; r < 8; ++r)
-#pragma unroll
-      for (int j = 0; j < r; ++j) a[r][j] = M[(o + r) * kLd + o + j];
-    __syncwarp();  // the block's 8 threads share this warp: all reads before any write
-    float x[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < r; ++j) acc = fmaf(a[r][j], x[j], acc);
-      x[r] = (r < col) ? 0.f : ((r == col) ? 1.f : -acc);
-    }
-#pragma unroll
-    for (int r = 0; r < 8; ++r) M[(o + r) * kLd + o + col] = x[r];
-  }
-  group_sync(kBarPrep, kGroup);
-  {  // 8 -> 16: pairs p = 0..3, rows bi = 16p + 8, cols bj = 16p
-    const int p = u >> 6, r = (u >> 3) & 7, c = u & 7;
-    const int bi = 16 * p + 8, bj = 16 * p;
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc = fmaf(M[(bi + r) * kLd + bj + k], M[(bj + k) * kLd + bj + c], acc);
-    Es[p * 64 + r * 8 + c] = acc;
-    group_sync(kBarPrep, kGroup);
-    acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc = fmaf(M[(bi + r) * kLd + bi + k], Es[p * 64 + k * 8 + c], acc);
-    M[(bi + r) * kLd + bj + c] = -acc;
-  }
-  group_sync(kBarPrep, kGroup);
-  const int wg = u >> 5;  // warp within the group
-  {  // 16 -> 32 on the tensor cores: pairs p = 0..1 (rows bi = 32p+16, cols bj = 32p),
-     // two 8-wide column tiles each -> warps 0..3
-    if (wg < 4) {
-      const int pr = wg >> 1, nt = wg & 1;
-      const int bi = 32 * pr + 16, bj = 32 * pr;
-      float c[4];
-      mma_tile_tf32x3(M + bi * kLd + bj, kLd, M + bj * kLd + bj + 8 * nt, kLd, 16, c);
-      store_tile(Es + pr * 16 * kLdE3 + 8 * nt, kLdE3, c, 1.f);
-    }
-    group_sync(kBarPrep, kGroup);
-    if (wg < 4) {
-      const int pr = wg >> 1, nt = wg & 1;
-      const int bi = 32 * pr + 16, bj = 32 * pr;
-      float c[4];
-      mma_tile_tf32x3(M + bi * kLd + bi, kLd, Es + pr * 16 * kLdE3 + 8 * nt, kLdE3, 16, c);
-      store_tile(M + bi * kLd + bj + 8 * nt, kLd, c, -1.f);
-    }
-  }
-  group_sync(kBarPrep, kGroup);
-  {  // 32 -> 64 on the tensor cores: rows 32..63 x cols 0..31 = 2 x 4 tiles of 16 x 8
-    const int mt = wg >> 2, nt = wg & 3;
-    float c[4];
-    mma_tile_tf32x3(M + (32 + 16 * mt) * kLd, kLd, M + 8 * nt, kLd, 32, c);
-    store_tile(Es + 16 * mt * kLdE4 + 8 * nt, kLdE4, c, 1.f);
-    group_sync(kBarPrep, kGroup);
-    mma_tile_tf32x3(M + (32 + 16 * mt) * kLd + 32, kLd, Es + 8 * nt, kLdE4, 32, c);
-    store_tile(M + (32 + 16 * mt) * kLd + 8 * nt, kLd, c, -1.f);
-  }
-  group_sync(kBarPrep, kGroup);
-}
 }  // namespace pl
 
 template <bool HAS_STATE, typename CuT>
@@ -1241,7 +1074,7 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       }
       tc_fence_before();
       group_sync(kBarPrep, kGroup);
-      invert_in_place(reinterpret_cast<float*>(smem + AT), reinterpret_cast<float*>(smem + E), u);
+      invert_in_place<kBarPrep>(reinterpret_cast<float*>(smem + AT), reinterpret_cast<float*>(smem + E), u);
       // T hi/lo once the state group has consumed the previous chunk's T
       if (c >= 1 && !group_wait(&bars->t_free, (c - 1) & 1, kBarPrep, abort_flag,
                                 ERR_MMA_TIMEOUT)) { ok = false; break; }
@@ -1580,78 +1413,7 @@ cudaError_t launch_pipelined_t(const CUtensorMap& mq, const CUtensorMap& mk,
   return cudaGetLastError();
 }
 
-// ---------------------------------------------------------------- LPT order
-// CTAs are scheduled roughly in blockIdx order and one CTA fills an SM, so
-// handing out the longest sequences first (longest-processing-time) keeps the
-// last wave short.  One CTA bitonic-sorts (length desc, index asc) keys in
-// shared memory and writes the permutation.
-constexpr int kLptMaxSeqs = 8192;
-
-template <typename CuT>
-__global__ void __launch_bounds__(1024) lpt_order_kernel(const CuT* __restrict__ cu, int N,
-                                                         long long T, int* __restrict__ order) {
-  extern __shared__ unsigned long long keys[];
-  int P = 1;
-  while (P < N) P <<= 1;
-  for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    unsigned long long key = 0ull;  // padding sorts last
-    if (i < N) {
-      const long long a = min(max((long long)cu[i], 0LL), T);
-      const long long b = min(max((long long)cu[i + 1], 0LL), T);
-      const unsigned long long len = (unsigned long long)max(b - a, 0LL);
-      key = (len << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
-    }
-    keys[i] = key;
-  }
-  __syncthreads();
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int l = i ^ j;
-        if (l > i) {
-          const unsigned long long x = keys[i], y = keys[l];
-          const bool desc = (i & k) == 0;  // descending overall
-          if (desc ? (x < y) : (x > y)) {
-            keys[i] = y;
-            keys[l] = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (int i = threadIdx.x; i < N; i += blockDim.x)
-    order[i] = (int)(0xFFFFFFFFu - (unsigned)(keys[i] & 0xFFFFFFFFull));
-}
-
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// [rows][heads * 128] bf16 matrix, 64 x 64 boxes, 128-byte swizzle.
-bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)heads * kHeadDim, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)heads * kHeadDim * 2};
-  cuuint32_t box[2] = {64, 64};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <bool L2, bool HS, typename CuT>
 cudaError_t launch_chunked_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const ChunkedParams& cp, int nseq, cudaStream_t st) {
@@ -1683,6 +1445,33 @@ cudaError_t launch_chunked_cu(const CUtensorMap& mq, const CUtensorMap& mk, cons
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [rows][heads * 128] bf16 matrix, 64 x 64 boxes, 128-byte swizzle.
+bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)heads * kHeadDim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)heads * kHeadDim * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 size_t prefill_chunked_workspace(int num_seqs) {
   if (num_seqs <= 1 || num_seqs > kLptMaxSeqs) return 0;

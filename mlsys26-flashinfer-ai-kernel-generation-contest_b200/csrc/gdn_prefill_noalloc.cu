@@ -56,16 +56,25 @@ extern "C" int gdn_prefill_launch_noalloc(const void* q, const void* k, const vo
                                           int num_k_heads, int num_v_heads, int head_size,
                                           int use_qk_l2norm, void* stream) {
   if (num_seqs > kNoAllocMaxSeqs) return GDN_ERR_TOO_LARGE;
-  const size_t need = gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads,
-                                                 num_v_heads, head_size);
+  // the fused chunked kernel: its only scratch is the sequence order (4 bytes each)
+  const size_t need = gdn_prefill_workspace_size_variant(GDN_PREFILL_FUSED, total_tokens,
+                                                         num_seqs, num_q_heads, num_v_heads,
+                                                         head_size);
   if (need > sizeof(int) * (size_t)kNoAllocMaxSeqs) return GDN_ERR_TOO_LARGE;
   void* scratch = nullptr;
   if (need > 0) {
     scratch = noalloc_scratch_address();
     if (scratch == nullptr) return GDN_ERR_LAUNCH;
   }
-  return gdn_prefill_launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_int64,
-                            scale, output, new_state, total_tokens, num_seqs, num_q_heads,
-                            num_k_heads, num_v_heads, head_size, use_qk_l2norm, scratch,
-                            scratch ? sizeof(int) * (size_t)kNoAllocMaxSeqs : 0, stream);
+  const size_t bytes = scratch ? sizeof(int) * (size_t)kNoAllocMaxSeqs : 0;
+  const int rc = gdn_prefill_launch_variant(
+      GDN_PREFILL_FUSED, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_int64,
+      scale, output, new_state, total_tokens, num_seqs, num_q_heads, num_k_heads, num_v_heads,
+      head_size, use_qk_l2norm, scratch, bytes, stream);
+  if (rc != GDN_ERR_UNSUPPORTED) return rc;
+  // buffers the chunked kernel cannot take (alignment): the token-serial kernel
+  return gdn_prefill_launch_variant(GDN_PREFILL_RECURRENT, q, k, v, state, A_log, a, dt_bias, b,
+                                    cu_seqlens, cu_seqlens_int64, scale, output, new_state,
+                                    total_tokens, num_seqs, num_q_heads, num_k_heads, num_v_heads,
+                                    head_size, use_qk_l2norm, nullptr, 0, stream);
 }

@@ -1,0 +1,856 @@
+// GDN prefill, split form for sm_100a: a chunk-parallel preparation kernel and a
+// sequential state kernel split over v-blocks.
+//
+// Same algebra as the fused chunked kernel (reference gdn_prefill/solution/triton/
+// kernel.py:60-79, regrouped per chunk of C = 64 tokens), with k-last state S[v, k]:
+//
+//   A[t,j] = beta_t exp(Lam_t - Lam_j) rk_t rk_j (k_t . k_j)   j < t,   T = (I + A)^-1
+//   P[t,j] = exp(Lam_t - Lam_j) rq_t rk_j (q_t . k_j)          j <= t
+//   R      = diag(beta) (V - diag(gamma rk) K S^T)
+//   U      = T R,   O = scale diag(gamma rq) Q S^T + scale (P T) R
+//   S     <- G S + U~^T K,  U~ = diag(rk exp(Lam_end - Lam_t)) U,  G = exp(Lam_end)
+//
+// Everything that does not depend on the state -- the gates, the q/k norms, A, the
+// triangular inverse T and the product P T -- is computed for every chunk of every
+// sequence at once by the preparation kernel (one CTA per (chunk, v-head), three
+// CTAs per SM), which stores a record per (chunk, v-head):
+//
+//   [T; P T] hi and lo: two 128 x 64 bf16 tiles in the 128-byte-swizzled K-major
+//       image the tensor cores read (rows 0..63 T, rows 64..127 P T), x = hi + lo;
+//   beta, gamma rk, us = rk exp(Lam_end - Lam), scale gamma rq (64 fp32 each), G.
+//
+// The state recurrence is separable in v (row v of S only ever meets column v of
+// V, U and O), so the sequential kernel runs one CTA per (sequence, v-head,
+// 64-row v-block).  It keeps S^T[k][v] (fp32) in TMEM and per chunk issues three
+// M = 128 MMA groups:
+//   G1  [K; Q] S^T              -> rows 0..63 K S^T, rows 64..127 Q S^T  (S hi + S lo)
+//   G2  [T; P T] R              -> rows 0..63 U,     rows 64..127 P U    (3 split terms)
+//   G3  S^T += K^T U~                                                    (U~ hi + lo)
+// with the R / U~ / output / state epilogues on the CUDA cores.  The next two
+// chunks' K/Q tiles, V block and record are in flight while a chunk is processed.
+//
+// Every wait is bounded: a wait that runs out sets a device error flag (read by
+// gdn_device_error), lets its copies and MMAs in flight land (again boundedly),
+// releases TMEM and returns.
+#include <cudaTypedefs.h>
+
+#include "gdn_chunk_math.cuh"
+#include "gdn_common.cuh"
+#include "gdn_lpt.cuh"
+#include "gdn_prefill.cuh"
+#include "sm100.cuh"
+
+namespace gdn {
+
+__device__ unsigned int g_split_device_error = 0;
+
+namespace {
+using namespace sm100;
+using namespace cm;
+
+constexpr int kC = 64;
+enum : unsigned { ERR_TMA_TIMEOUT = 1u, ERR_MMA_TIMEOUT = 2u, ERR_SMEM_ALIGN = 4u };
+
+// ---- per (chunk, v-head) record
+constexpr uint32_t kRecTpHi = 0, kRecTpLo = 16384, kRecVec = 32768;
+constexpr uint32_t kRecVecBytes = 1040;  // beta | gamma rk | us | scale gamma rq (4 x 64 f32), G, pad
+constexpr size_t kRecBytes = 34048;      // 16-byte multiple
+
+struct SplitParams {
+  const __nv_bfloat16* a;
+  const __nv_bfloat16* b;
+  const float* A_log;
+  const float* dt_bias;
+  const void* cu;
+  const float* state;
+  float* new_state;
+  __nv_bfloat16* out;
+  const int* order;       // longest-first sequence order (null: natural order)
+  const int* chunk_base;  // [N + 1] exclusive prefix of chunks per sequence
+  uint8_t* rec;           // records, (chunk, v-head) major
+  long long T;
+  int N;
+  int HV;
+  int ratio;
+  float scale;
+};
+
+template <typename CuT>
+__device__ __forceinline__ void seq_range(const CuT* cu, int n, long long T, long long& s0,
+                                          long long& s1) {
+  s1 = min(max((long long)cu[n + 1], 0LL), T);
+  s0 = min(max((long long)cu[n], 0LL), s1);
+}
+
+// All threads wait on `bar`; false on every thread if any thread's wait ran out.
+__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  const bool ok = mbar_wait(bar, parity);
+  const int bad = __syncthreads_or(ok ? 0 : 1);
+  if (bad && threadIdx.x == 0) atomicOr(&g_split_device_error, code);
+  return bad == 0;
+}
+
+// ------------------------------------------------------------ chunk offsets
+// base[i] = number of 64-token chunks of sequences 0..i-1 (base[N] = total), one CTA.
+template <typename CuT>
+__global__ void __launch_bounds__(1024) chunk_base_kernel(const CuT* __restrict__ cu, int N,
+                                                          long long T, int* __restrict__ base) {
+  __shared__ int part[1024];
+  const int tid = threadIdx.x;
+  const int per = (N + 1023) / 1024;
+  const int i0 = min(tid * per, N), i1 = min(i0 + per, N);
+  auto nch = [&](int i) {
+    long long s0, s1;
+    seq_range(cu, i, T, s0, s1);
+    return (int)((s1 - s0 + kC - 1) / kC);
+  };
+  int sum = 0;
+  for (int i = i0; i < i1; ++i) sum += nch(i);
+  part[tid] = sum;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int add = tid >= off ? part[tid - off] : 0;
+    __syncthreads();
+    part[tid] += add;
+    __syncthreads();
+  }
+  int run = part[tid] - sum;
+  for (int i = i0; i < i1; ++i) {
+    base[i] = run;
+    run += nch(i);
+  }
+  if (tid == 1023) base[N] = part[1023];
+}
+
+// ============================================================ preparation kernel
+namespace prep {
+constexpr int kThreads = 256;
+constexpr uint32_t KQ = 0;        // K0 | Q0 | K1 | Q1 (8 KB each); then [P hi; P lo] (16 KB)
+constexpr uint32_t TIMG = 32768;  // T hi | T lo, K-major [t][j] (8 KB each)
+constexpr uint32_t AT = 49152;    // fp32 [64][kLd]: A, T in place, then (P lo T) partials
+constexpr uint32_t E = AT + 64 * kLd * 4;  // merge scratch; before it the diagonal decay blocks
+constexpr uint32_t ROWF = E + 64 * 20 * 4;  // fp32 [3][64]: exp(Lam_t - Lam_{16b+15}), b < t/16
+constexpr uint32_t COLF = ROWF + 1024;      // fp32 [64]:    exp(Lam_{j|15} - Lam_j)
+constexpr uint32_t VEC = COLF + 256;        // Lam beta gam rk rq (5 x 64 f32)
+constexpr uint32_t BARS = VEC + 5 * 256;
+constexpr uint32_t SMEM = BARS + 64;
+constexpr int kLdDE = 20;
+constexpr uint32_t TKQ = 0, TPT = 64;  // TMEM columns (128 allocated)
+static_assert(64 * 20 * 4 >= 32 * kLdE4 * 4, "merge scratch fits the decay table");
+static_assert(3 * (SMEM + 1024) <= 233472, "three CTAs per SM");
+}  // namespace prep
+
+template <bool L2NORM, typename CuT>
+__global__ void __launch_bounds__(prep::kThreads, 3)
+    split_prep_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k, const SplitParams p) {
+  using namespace prep;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sb = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = warp & 3, half = warp >> 2;
+  const int row = sp * 32 + lane;  // TMEM lane of this thread
+  const int g = blockIdx.x, h = blockIdx.y;
+  const int total = p.chunk_base[p.N];
+  if (g >= total) return;
+  int lo = 0, hi = p.N - 1;  // the sequence of chunk g: largest n with base[n] <= g
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.chunk_base[mid] <= g) lo = mid; else hi = mid - 1;
+  }
+  const int n = lo, c = g - p.chunk_base[n];
+  long long s0, s1;
+  seq_range(static_cast<const CuT*>(p.cu), n, p.T, s0, s1);
+  const long long t0 = s0 + (long long)kC * c;
+  const int Lc = (int)min((long long)kC, s1 - t0);
+  const int qh = h / p.ratio;
+  uint8_t* rec = p.rec + ((size_t)g * p.HV + h) * kRecBytes;
+  if ((sb & 1023u) != 0) {
+    if (tid == 0) atomicOr(&g_split_device_error, ERR_SMEM_ALIGN);
+    return;
+  }
+  float* Lam = reinterpret_cast<float*>(smem + VEC);
+  float* beta = Lam + 64;
+  float* gam = Lam + 128;
+  float* rk = Lam + 192;
+  float* rq = Lam + 256;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BARS);  // kqtma, kq, pt
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + 32);
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int i = 0; i < 3; ++i) mbar_init(bars + i, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], 4 * 8192);
+    tma_load_2d(smem + KQ, &tm_k, &bars[0], qh * 128, (int)t0);
+    tma_load_2d(smem + KQ + 16384, &tm_k, &bars[0], qh * 128 + 64, (int)t0);
+    tma_load_2d(smem + KQ + 8192, &tm_q, &bars[0], qh * 128, (int)t0);
+    tma_load_2d(smem + KQ + 24576, &tm_q, &bars[0], qh * 128 + 64, (int)t0);
+  }
+  if (warp == 1) {  // gates: cumulative log decay, beta, gamma
+    const float nexpA = -expf(__ldg(p.A_log + h));
+    const float dtb = __ldg(p.dt_bias + h);
+    float lg[2], bb[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 2 * lane + e;
+      const bool valid = t < Lc;
+      const size_t ti = (size_t)(t0 + (valid ? t : 0)) * p.HV + h;
+      lg[e] = valid ? nexpA * softplus_f(bf2f(p.a[ti]) + dtb) : 0.f;
+      bb[e] = valid ? sigmoid_f(bf2f(p.b[ti])) : 0.f;
+    }
+    float x = lg[0] + lg[1];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    const float x0 = x - lg[1];
+    Lam[2 * lane] = x0;
+    Lam[2 * lane + 1] = x;
+    beta[2 * lane] = bb[0];
+    beta[2 * lane + 1] = bb[1];
+    gam[2 * lane] = expf(x0);
+    gam[2 * lane + 1] = expf(x);
+  }
+  bool ok = true;
+  uint64_t* pend = nullptr;  // copy or MMA group in flight
+  do {
+    pend = &bars[0];
+    if (!(ok = cta_wait(&bars[0], 0, ERR_TMA_TIMEOUT))) break;
+    pend = nullptr;
+    if (tid == 0) {  // [Skk; Sqk] = [K; Q] K^T
+      tc_fence_after();
+      const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
+        const uint64_t kd = umma_desc_k(sb + KQ + off);
+        umma_bf16(tmem + TKQ, kd, kd, idesc, ks > 0);
+      }
+      umma_commit(&bars[1]);
+    }
+    pend = &bars[1];
+    if constexpr (L2NORM) {
+      if (tid >= 64 && tid < 192) {  // q/k row norms
+        const int t = tid & 63;
+        const bool isq = tid < 128;
+        const uint32_t b0 = sb + KQ + (isq ? 8192u : 0u) + 128u * t;
+        float ss = 0.f;
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk)
+#pragma unroll
+          for (int ci = 0; ci < 8; ++ci) {
+            const int ch = (ci + t) & 7;
+            const uint4 w = ld_shared_v4(b0 + 16384u * blk + 16u * ch);
+            const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = bf2x2_to_f2(w4[e]);
+              ss = fmaf(f.x, f.x, ss);
+              ss = fmaf(f.y, f.y, ss);
+            }
+          }
+        const float r = rsqrtf(ss + kL2NormEps);
+        if (isq) rq[t] = r; else rk[t] = r;
+      }
+    } else {
+      if (tid < 64) {
+        rk[tid] = 1.f;
+        rq[tid] = 1.f;
+      }
+    }
+    __syncthreads();
+    // decay factors exp(Lam_t - Lam_j), j <= t, with no positive exponent: directly
+    // inside the diagonal 16x16 blocks; across blocks through the last token e of j's
+    // block, exp(Lam_t - Lam_e) exp(Lam_e - Lam_j)
+    {
+      float* DE = reinterpret_cast<float*>(smem + E);
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int idx = tid + 256 * k4;
+        const int blk = idx >> 8, r = (idx >> 4) & 15, jj = idx & 15;
+        DE[(16 * blk + r) * kLdDE + jj] =
+            (jj <= r) ? __expf(Lam[16 * blk + r] - Lam[16 * blk + jj]) : 0.f;
+      }
+      if (tid < 64) {
+        float* RF = reinterpret_cast<float*>(smem + ROWF);
+        reinterpret_cast<float*>(smem + COLF)[tid] = __expf(Lam[tid | 15] - Lam[tid]);
+#pragma unroll
+        for (int blk = 0; blk < 3; ++blk)
+          RF[64 * blk + tid] = (16 * blk + 15 < tid) ? __expf(Lam[tid] - Lam[16 * blk + 15]) : 0.f;
+      }
+    }
+    if (!(ok = cta_wait(&bars[1], 0, ERR_MMA_TIMEOUT))) break;
+    pend = nullptr;
+    tc_fence_after();
+    // A (from Skk) -> AT; P (from Sqk) -> [P hi; P lo] image over the consumed K/Q tiles
+    {
+      const int t = row & 63, bt = t >> 4;
+      const bool is_k = row < 64;
+      const float ft = is_k ? beta[t] * rk[t] : rq[t];
+      const float* DE = reinterpret_cast<const float*>(smem + E) + t * kLdDE;
+      const float* RF = reinterpret_cast<const float*>(smem + ROWF);
+      const float* CF = reinterpret_cast<const float*>(smem + COLF);
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int j0 = 32 * half + 16 * pass, bj = j0 >> 4;
+        float ej[16];
+        if ((t | 31) < j0) {  // whole warp above the diagonal (warp-uniform)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ej[i] = 0.f;
+        } else {
+          float kq[16], rv[16], fv[16];
+          tmem_ld16(tl + TKQ + (uint32_t)j0, kq);
+          const float rowf = ft * ((bj < bt) ? RF[64 * bj + t] : (bj == bt ? 1.f : 0.f));
+          const float* fsrc = (bj == bt) ? DE : (CF + j0);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 rj = *reinterpret_cast<const float4*>(rk + j0 + i);
+            const float4 f4 = *reinterpret_cast<const float4*>(fsrc + i);
+            rv[i] = rj.x; rv[i + 1] = rj.y; rv[i + 2] = rj.z; rv[i + 3] = rj.w;
+            fv[i] = f4.x; fv[i + 1] = f4.y; fv[i + 2] = f4.z; fv[i + 3] = f4.w;
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = j0 + i;
+            const bool keep = is_k ? (j < t) : (j <= t);
+            ej[i] = keep ? rowf * fv[i] * rv[i] * kq[i] : 0.f;
+          }
+        }
+        if (is_k) {
+          float* Arow = reinterpret_cast<float*>(smem + AT) + t * kLd + j0;
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(Arow + i) = make_float4(ej[i], ej[i + 1], ej[i + 2], ej[i + 3]);
+        } else {
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            uint4 phi, plo;
+            split8(&ej[8 * q2], phi, plo);
+            st_v4(sb + KQ + sw128(t, (j0 >> 3) + q2), phi);
+            st_v4(sb + KQ + 8192u + sw128(t, (j0 >> 3) + q2), plo);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < 64) {  // the record's row vectors
+      float* rv = reinterpret_cast<float*>(rec + kRecVec);
+      const int t = tid;
+      const float lend = Lam[63];
+      rv[t] = beta[t];
+      rv[64 + t] = gam[t] * rk[t];
+      rv[128 + t] = (t < Lc) ? rk[t] * expf(lend - Lam[t]) : 0.f;
+      rv[192 + t] = default_scale(p.scale) * gam[t] * rq[t];
+      if (t < 4) rv[256 + t] = (t == 0) ? expf(lend) : 0.f;
+    }
+    invert_in_place<1>(reinterpret_cast<float*>(smem + AT), reinterpret_cast<float*>(smem + E), tid);
+    // T -> hi/lo: the B operand of P T here, rows 0..63 of the record
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+      const int unit = tid + 256 * k2;
+      const int t = unit >> 3, cidx = unit & 7;
+      const float* tr = reinterpret_cast<const float*>(smem + AT) + t * kLd + 8 * cidx;
+      const float4 ta = *reinterpret_cast<const float4*>(tr);
+      const float4 tb = *reinterpret_cast<const float4*>(tr + 4);
+      const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+      uint4 thi, tlo;
+      split8(tv, thi, tlo);
+      const uint32_t o = sw128(t, cidx);
+      st_v4(sb + TIMG + o, thi);
+      st_v4(sb + TIMG + 8192u + o, tlo);
+      *reinterpret_cast<uint4*>(rec + kRecTpHi + o) = thi;
+      *reinterpret_cast<uint4*>(rec + kRecTpLo + o) = tlo;
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // [P hi; P lo] T  (T hi + T lo; B = T as MN-major [s][j])
+      tc_fence_after();
+      const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int term = 0; term < 2; ++term)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + TPT, umma_desc_k(sb + KQ + 32u * ks),
+                    umma_desc_mn(sb + TIMG + 8192u * term + 2048u * ks, 8192), idesc,
+                    (term | ks) != 0);
+      umma_commit(&bars[2]);
+    }
+    pend = &bars[2];
+    if (!(ok = cta_wait(&bars[2], 0, ERR_MMA_TIMEOUT))) break;
+    pend = nullptr;
+    tc_fence_after();
+    // P T = (P hi T) + (P lo T): lanes 64..127 hand their part over through AT
+    if (sp >= 2) {
+      float v[32];
+      tmem_ld32(tl + TPT + 32u * half, v);
+      tmem_wait_ld();
+      float* dst = reinterpret_cast<float*>(smem + AT) + (row - 64) * kLd + 32 * half;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+    __syncthreads();
+    if (sp < 2) {
+      float v[32];
+      tmem_ld32(tl + TPT + 32u * half, v);
+      tmem_wait_ld();
+      const float* src = reinterpret_cast<const float*>(smem + AT) + row * kLd + 32 * half;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(src + i);
+        v[i] += a4.x; v[i + 1] += a4.y; v[i + 2] += a4.z; v[i + 3] += a4.w;
+      }
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 xhi, xlo;
+        split8(&v[8 * q4], xhi, xlo);
+        const uint32_t o = sw128(64 + row, 4 * half + q4);
+        *reinterpret_cast<uint4*>(rec + kRecTpHi + o) = xhi;
+        *reinterpret_cast<uint4*>(rec + kRecTpLo + o) = xlo;
+      }
+    }
+  } while (0);
+  if (!ok && tid == 0 && pend != nullptr) {  // let the copy / MMA in flight land
+    mbar_wait(pend, 0, 1u << 20);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// ============================================================ sequential state kernel
+namespace st {
+constexpr int kThreads = 256;
+constexpr int kVB = 64;  // v-rows per CTA
+constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // K0 | Q0 | K1 | Q1 (8 KB each), per buffer
+constexpr uint32_t V0 = 65536, V1 = 73728;  // V block [t][64 v] (8 KB), per buffer
+constexpr uint32_t TP0 = 81920, TP1 = 114688;  // record tiles: hi (16 KB) | lo (16 KB)
+constexpr uint32_t SHI = 147456, SLO = 163840;  // S image [k][v] (MN-major B of G1)
+constexpr uint32_t RHI = 180224, RLO = 188416;  // R image [j][v] (MN-major B of G2)
+constexpr uint32_t UHI = 196608, ULO = 204800;  // U~ image [t][v] (MN-major B of G3)
+constexpr uint32_t VEC0 = 212992, VEC1 = 214272;  // record vectors (1040 B), per buffer
+constexpr uint32_t BARS = 215552;
+constexpr uint32_t SMEM = BARS + 128;
+constexpr uint32_t TST = 0, TG1 = 64, TG2 = 128;  // TMEM columns (256 allocated)
+static_assert(SMEM <= 232448, "shared memory budget");
+struct Bars {
+  uint64_t kq[2], vt[2], g1, g2, g3;
+};
+}  // namespace st
+
+template <bool HAS_STATE, typename CuT>
+__global__ void __launch_bounds__(st::kThreads, 1)
+    split_state_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const SplitParams p) {
+  using namespace st;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sb = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = warp & 3, half = warp >> 2;
+  const int row = sp * 32 + lane;  // TMEM lane: k for the state, token for G1 / G2 rows
+  const int HV = p.HV;
+  const int per = 2 * HV;
+  const int wi = blockIdx.x / per;
+  const int rem = blockIdx.x - wi * per;
+  const int h = rem >> 1, vb = rem & 1;
+  const int n = p.order ? p.order[wi] : wi;
+  const int qh = h / p.ratio;
+  long long s0, s1;
+  seq_range(static_cast<const CuT*>(p.cu), n, p.T, s0, s1);
+  const long long L = s1 - s0;
+  // this thread's state elements: S[v][k], k = row, v = v_lo + i (i < 32)
+  const int v_lo = kVB * vb + 32 * half;
+  float* ns = p.new_state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
+  if (L <= 0) {  // empty sequence: zero final state (definition semantics)
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = 0.f;
+    return;
+  }
+  if ((sb & 1023u) != 0) {
+    if (tid == 0) atomicOr(&g_split_device_error, ERR_SMEM_ALIGN);
+    return;
+  }
+  const int nchunks = (int)((L + kC - 1) / kC);
+  const size_t rstride = (size_t)HV * kRecBytes;
+  const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * kRecBytes;
+  const float scale = default_scale(p.scale);
+  Bars* bars = reinterpret_cast<Bars*>(smem + BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + sizeof(Bars));
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    uint64_t* b = reinterpret_cast<uint64_t*>(bars);
+    for (int i = 0; i < (int)(sizeof(Bars) / 8); ++i) mbar_init(b + i, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+
+  // copies in flight, per buffer (-1: none); identical on every thread
+  int pend_kq[2] = {-1, -1}, pend_vt[2] = {-1, -1};
+  auto issue = [&](int cc) {  // K/Q tiles, V block and record of chunk cc -> buffer cc & 1
+    const int bf = cc & 1;
+    const int y = (int)(s0 + (long long)kC * cc);
+    pend_kq[bf] = (cc >> 1) & 1;
+    pend_vt[bf] = (cc >> 1) & 1;
+    if (tid != 0) return;
+    fence_proxy_async();
+    const uint32_t kq = bf ? KQ1 : KQ0;
+    mbar_arrive_expect_tx(&bars->kq[bf], 4 * 8192);
+    tma_load_2d(smem + kq, &tm_k, &bars->kq[bf], qh * 128, y);
+    tma_load_2d(smem + kq + 16384, &tm_k, &bars->kq[bf], qh * 128 + 64, y);
+    tma_load_2d(smem + kq + 8192, &tm_q, &bars->kq[bf], qh * 128, y);
+    tma_load_2d(smem + kq + 24576, &tm_q, &bars->kq[bf], qh * 128 + 64, y);
+    const uint8_t* r = rec0 + (size_t)cc * rstride;
+    mbar_arrive_expect_tx(&bars->vt[bf], 8192 + 32768 + kRecVecBytes);
+    tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
+    bulk_load(smem + (bf ? TP1 : TP0), r, 32768, &bars->vt[bf]);
+    bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecVec, kRecVecBytes, &bars->vt[bf]);
+  };
+  issue(0);
+  if (nchunks > 1) issue(1);
+
+  // initial state: S^T[k][v] -> TMEM (fp32) and the hi/lo image of G1's B operand
+  {
+    float sv[32];
+    if constexpr (HAS_STATE) {
+      const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sv[i] = __ldg(src + (size_t)(v_lo + i) * kHeadDim + row);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sv[i] = 0.f;
+    }
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(sv[i]);
+    tmem_st32(tl + TST + 32u * half, w);
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      uint4 xhi, xlo;
+      split8(&sv[8 * q4], xhi, xlo);
+      st_v4(sb + SHI + sw128(row, 4 * half + q4), xhi);
+      st_v4(sb + SLO + sw128(row, 4 * half + q4), xlo);
+    }
+    tmem_wait_st();
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+
+  bool ok = true;
+  uint64_t* mma_bar = nullptr;  // MMA group in flight
+  uint32_t mma_par = 0;
+  for (int c = 0; c < nchunks && ok; ++c) {
+    const int bf = c & 1;
+    const uint32_t par2 = (c >> 1) & 1;
+    const long long t0 = s0 + (long long)kC * c;
+    const int Lc = (int)min((long long)kC, s1 - t0);
+    const uint32_t kqb = bf ? KQ1 : KQ0;
+    const uint32_t tpb = bf ? TP1 : TP0;
+    const float* vec = reinterpret_cast<const float*>(smem + (bf ? VEC1 : VEC0));
+    if (!(ok = cta_wait(&bars->kq[bf], par2, ERR_TMA_TIMEOUT))) break;
+    pend_kq[bf] = -1;
+    if (!(ok = cta_wait(&bars->vt[bf], par2, ERR_TMA_TIMEOUT))) break;
+    pend_vt[bf] = -1;
+    // G1: [K; Q] S^T  (S hi + S lo)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = umma_desc_k(sb + kqb + 16384u * (ks >> 2) + 32u * (ks & 3));
+        umma_bf16(tmem + TG1, ad, umma_desc_mn(sb + SHI + 2048u * ks, 8192), idesc, ks > 0);
+        umma_bf16(tmem + TG1, ad, umma_desc_mn(sb + SLO + 2048u * ks, 8192), idesc, 1);
+      }
+      umma_commit(&bars->g1);
+    }
+    mma_bar = &bars->g1;
+    mma_par = c & 1;
+    {  // meanwhile: decay the fp32 state (G3 accumulates onto it)
+      const float G = vec[256];
+      float sv[32];
+      uint32_t w[32];
+      tmem_ld32(tl + TST + 32u * half, sv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(G * sv[i]);
+      tmem_st32(tl + TST + 32u * half, w);
+      tmem_wait_st();
+    }
+    if (!(ok = cta_wait(&bars->g1, c & 1, ERR_MMA_TIMEOUT))) break;
+    mma_bar = nullptr;
+    tc_fence_after();
+    // R[j][v] = beta_j (V[j][v] - gamma_j rk_j (K S^T)[j][v])  (lanes 0..63: j = row)
+    if (sp < 2) {
+      float sk[32];
+      tmem_ld32(tl + TG1 + 32u * half, sk);
+      const float bj = vec[row], cj = vec[64 + row];
+      const uint32_t vt = sb + (bf ? V1 : V0);
+      uint4 vw[4];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) vw[q4] = ld_shared_v4(vt + sw128(row, 4 * half + q4));
+      tmem_wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const uint32_t w4[4] = {vw[q4].x, vw[q4].y, vw[q4].z, vw[q4].w};
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = bf2x2_to_f2(w4[e]);
+          x[2 * e] = bj * (f.x - cj * sk[8 * q4 + 2 * e]);
+          x[2 * e + 1] = bj * (f.y - cj * sk[8 * q4 + 2 * e + 1]);
+        }
+        uint4 xhi, xlo;
+        split8(x, xhi, xlo);
+        st_v4(sb + RHI + sw128(row, 4 * half + q4), xhi);
+        st_v4(sb + RLO + sw128(row, 4 * half + q4), xlo);
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    // G2: [T; P T] R  (TP hi R hi + TP lo R hi + TP hi R lo)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int term = 0; term < 3; ++term) {
+        const uint32_t a = tpb + (term == 1 ? 16384u : 0u);
+        const uint32_t b = term == 2 ? RLO : RHI;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + TG2, umma_desc_k(sb + a + 32u * ks),
+                    umma_desc_mn(sb + b + 2048u * ks, 8192), idesc, (term | ks) != 0);
+      }
+      umma_commit(&bars->g2);
+    }
+    mma_bar = &bars->g2;
+    mma_par = c & 1;
+    if (!(ok = cta_wait(&bars->g2, c & 1, ERR_MMA_TIMEOUT))) break;
+    mma_bar = nullptr;
+    tc_fence_after();
+    if (sp < 2) {  // U~ = diag(us) U -> hi/lo image [t][v]
+      float uv[32];
+      tmem_ld32(tl + TG2 + 32u * half, uv);
+      const float ut = vec[128 + row];
+      tmem_wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = ut * uv[8 * q4 + e];
+        uint4 xhi, xlo;
+        split8(x, xhi, xlo);
+        st_v4(sb + UHI + sw128(row, 4 * half + q4), xhi);
+        st_v4(sb + ULO + sw128(row, 4 * half + q4), xlo);
+      }
+    } else {  // O = scale gamma rq (Q S^T) + scale (P T) R  (lanes 64..127: t = row - 64)
+      const int t = row - 64;
+      float qs[32], pu[32];
+      tmem_ld32(tl + TG1 + 32u * half, qs);
+      tmem_ld32(tl + TG2 + 32u * half, pu);
+      const float ct = vec[192 + t];
+      tmem_wait_ld();
+      if (t < Lc) {
+        __nv_bfloat16* dst = p.out + ((size_t)(t0 + t) * HV + h) * kHeadDim + v_lo;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * q4 + 2 * e;
+            w[e] = cvt_bf16x2(ct * qs[i] + scale * pu[i], ct * qs[i + 1] + scale * pu[i + 1]);
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * q4) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    // G3: S^T += K^T U~  (A = K tile as MN-major [t][k]; U~ hi + lo)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = umma_idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int term = 0; term < 2; ++term)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + TST, umma_desc_mn(sb + kqb + 2048u * ks, 16384),
+                    umma_desc_mn(sb + (term ? ULO : UHI) + 2048u * ks, 8192), idesc, 1);
+      umma_commit(&bars->g3);
+    }
+    mma_bar = &bars->g3;
+    mma_par = c & 1;
+    if (!(ok = cta_wait(&bars->g3, c & 1, ERR_MMA_TIMEOUT))) break;
+    mma_bar = nullptr;
+    tc_fence_after();
+    if (c + 2 < nchunks) issue(c + 2);  // buffer bf fully consumed
+    // epilogue: S^T -> next chunk's hi/lo image, or the final state
+    {
+      float sv[32];
+      tmem_ld32(tl + TST + 32u * half, sv);
+      tmem_wait_ld();
+      if (c + 1 == nchunks) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = sv[i];
+      } else {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 xhi, xlo;
+          split8(&sv[8 * q4], xhi, xlo);
+          st_v4(sb + SHI + sw128(row, 4 * half + q4), xhi);
+          st_v4(sb + SLO + sw128(row, 4 * half + q4), xlo);
+        }
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (!ok && tid == 0) {  // let the copies and the MMA group in flight land
+    if (mma_bar) mbar_wait(mma_bar, mma_par, 1u << 20);
+    for (int i = 0; i < 2; ++i) {
+      if (pend_kq[i] >= 0) mbar_wait(&bars->kq[i], (uint32_t)pend_kq[i], 1u << 20);
+      if (pend_vt[i] >= 0) mbar_wait(&bars->vt[i], (uint32_t)pend_vt[i], 1u << 20);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------ host side
+struct SplitLayout {
+  size_t order, base, rec, total;
+  long long slots;
+};
+SplitLayout split_layout(long long T, int N, int HV) {
+  SplitLayout l{};
+  const auto up = [](size_t x, size_t a) { return (x + a - 1) / a * a; };
+  l.order = 0;
+  l.base = up((size_t)N * sizeof(int), 256);
+  l.rec = up(l.base + (size_t)(N + 1) * sizeof(int), 1024);
+  l.slots = (T + kC - 1) / kC + N;
+  l.total = l.rec + (size_t)l.slots * HV * kRecBytes;
+  return l;
+}
+
+template <auto kern>
+bool configure(uint32_t smem) {  // once per (kernel, device)
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return false;
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return true;
+}
+
+template <bool L2, bool HS, typename CuT>
+cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                           const SplitParams& sp, long long slots, cudaStream_t s) {
+  constexpr auto ka = split_prep_kernel<L2, CuT>;
+  constexpr auto kb = split_state_kernel<HS, CuT>;
+  if (!configure<ka>(prep::SMEM) || !configure<kb>(st::SMEM)) return cudaErrorInvalidValue;
+  chunk_base_kernel<CuT><<<1, 1024, 0, s>>>(static_cast<const CuT*>(sp.cu), sp.N, sp.T,
+                                            const_cast<int*>(sp.chunk_base));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ka<<<dim3((unsigned)slots, (unsigned)sp.HV), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk, sp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  kb<<<dim3((unsigned)((long long)sp.N * sp.HV * 2)), dim3(st::kThreads), st::SMEM, s>>>(mq, mk,
+                                                                                        mv, sp);
+  return cudaGetLastError();
+}
+
+template <typename CuT>
+cudaError_t launch_split_cu(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                            const SplitParams& sp, bool l2, bool hs, long long slots,
+                            cudaStream_t s) {
+  if (l2) return hs ? launch_split_t<true, true, CuT>(mq, mk, mv, sp, slots, s)
+                    : launch_split_t<true, false, CuT>(mq, mk, mv, sp, slots, s);
+  return hs ? launch_split_t<false, true, CuT>(mq, mk, mv, sp, slots, s)
+            : launch_split_t<false, false, CuT>(mq, mk, mv, sp, slots, s);
+}
+
+}  // namespace
+
+size_t prefill_split_workspace(long long T, int num_seqs, int HV) {
+  if (T <= 0 || num_seqs <= 0) return 0;
+  return split_layout(T, num_seqs, HV).total;
+}
+
+cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
+  const SplitLayout lay = split_layout(p.T, p.N, p.HV);
+  if (p.workspace == nullptr || p.workspace_bytes < lay.total) return cudaErrorInvalidValue;
+  if (lay.slots > 0x7fffffffLL || (long long)p.N * p.HV * 2 > 0x7fffffffLL)
+    return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv;
+  if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
+      !make_tile_map(&mv, p.v, p.HV, p.T))
+    return cudaErrorInvalidValue;
+  uint8_t* ws = static_cast<uint8_t*>(p.workspace);
+  int* order = nullptr;
+  if (p.N > 1 && p.N <= kLptMaxSeqs) {
+    order = reinterpret_cast<int*>(ws + lay.order);
+    int P = 1;
+    while (P < p.N) P <<= 1;
+    const size_t sm = (size_t)P * sizeof(unsigned long long);
+    if (!configure<lpt_order_kernel<int>>(kLptMaxSeqs * 8) ||
+        !configure<lpt_order_kernel<long long>>(kLptMaxSeqs * 8))
+      return cudaErrorInvalidValue;
+    if (p.cu_int64)
+      lpt_order_kernel<long long><<<1, 1024, sm, s>>>(static_cast<const long long*>(p.cu), p.N,
+                                                       p.T, order);
+    else
+      lpt_order_kernel<int><<<1, 1024, sm, s>>>(static_cast<const int*>(p.cu), p.N, p.T, order);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  SplitParams sp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
+                 p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
+                 static_cast<__nv_bfloat16*>(p.out), order,
+                 reinterpret_cast<const int*>(ws + lay.base), ws + lay.rec, p.T, p.N, p.HV,
+                 p.HV / p.HQ, p.scale};
+  if (p.cu_int64)
+    return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
+  return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
+}
+
+unsigned read_split_device_error(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_split_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+  if (clear) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(g_split_device_error, &zero, sizeof(zero));
+  }
+  return v;
+}
+
+}  // namespace gdn

@@ -17,7 +17,13 @@ import threading
 import torch
 
 from . import _checks as C
-from ._lib import LIB, check
+from ._lib import (GDN_PREFILL_AUTO, GDN_PREFILL_FUSED, GDN_PREFILL_RECURRENT, GDN_PREFILL_SPLIT,
+                   LIB, check)
+
+# kernel= choices of gdn_prefill (see gdn_prefill_launch_variant in include/gdn_b200.h)
+KERNELS = {"auto": GDN_PREFILL_AUTO, "recurrent": GDN_PREFILL_RECURRENT,
+           "fused": GDN_PREFILL_FUSED, "split": GDN_PREFILL_SPLIT}
+_LPT_MAX_SEQS = 8192  # the longest-first ordering kernel's capacity
 
 _ws_lock = threading.Lock()
 _ws_cache = {}
@@ -36,23 +42,56 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def workspace_bytes(total_tokens: int, num_seqs: int, num_q_heads: int, num_v_heads: int,
-                    head_size: int = 128) -> int:
-    return int(LIB.gdn_prefill_workspace_size(total_tokens, num_seqs, num_q_heads, num_v_heads,
-                                              head_size))
+                    head_size: int = 128, kernel: str = "auto") -> int:
+    return int(LIB.gdn_prefill_workspace_size_variant(KERNELS[kernel], total_tokens, num_seqs,
+                                                      num_q_heads, num_v_heads, head_size))
 
 
-def launches_per_call(total_tokens: int, num_seqs: int) -> int:
+def resolved_kernel(total_tokens: int, num_seqs: int, num_q_heads: int, num_v_heads: int,
+                    kernel: str = "auto") -> str:
+    """The kernel family `kernel` runs for these sizes (16-byte aligned buffers)."""
+    if kernel != "auto" or total_tokens <= 0 or num_seqs <= 0:
+        return kernel if total_tokens > 0 else "recurrent"
+    split = LIB.gdn_prefill_workspace_size_variant(GDN_PREFILL_SPLIT, total_tokens, num_seqs,
+                                                   num_q_heads, num_v_heads, 128)
+    auto = LIB.gdn_prefill_workspace_size_variant(GDN_PREFILL_AUTO, total_tokens, num_seqs,
+                                                  num_q_heads, num_v_heads, 128)
+    return "split" if auto == split else "fused"
+
+
+def launches_per_call(total_tokens: int, num_seqs: int, num_q_heads: int = 16,
+                      num_v_heads: int = 32, kernel: str = "auto") -> int:
     """Number of this library's kernels one prefill call launches."""
-    return 1 if num_seqs > 0 else 0
+    if num_seqs <= 0:
+        return 0
+    kind = resolved_kernel(total_tokens, num_seqs, num_q_heads, num_v_heads, kernel)
+    lpt = 1 if 1 < num_seqs <= _LPT_MAX_SEQS else 0
+    if kind == "split":  # order, chunk offsets, preparation, state
+        return lpt + 3
+    if kind == "fused":
+        return lpt + 1
+    return 1
 
 
 def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
-                new_state=None, *, use_qk_l2norm: bool = False):
+                new_state=None, *, use_qk_l2norm: bool = False, kernel: str = "auto"):
     """Varlen prefill; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32).
 
-    Runs the chunked tensor-core kernel (``gdn_prefill_launch``)."""
-    return _prefill(LIB.gdn_prefill_launch, "gdn_prefill_launch", q, k, v, state, A_log, a,
-                    dt_bias, b, cu_seqlens, scale, output, new_state, use_qk_l2norm)
+    ``kernel="auto"`` calls ``gdn_prefill_launch`` (the reference-facing entry
+    point); "split", "fused" and "recurrent" force one kernel family through
+    ``gdn_prefill_launch_variant``."""
+    if kernel not in KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(KERNELS)}, got {kernel!r}")
+    if kernel == "auto":
+        launch, name = LIB.gdn_prefill_launch, "gdn_prefill_launch"
+    else:
+        variant = KERNELS[kernel]
+        name = f"gdn_prefill_launch_variant({kernel})"
+
+        def launch(*args):
+            return LIB.gdn_prefill_launch_variant(variant, *args)
+    return _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+                    output, new_state, use_qk_l2norm, kernel)
 
 
 def gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
@@ -61,11 +100,11 @@ def gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scal
     (``gdn_prefill_launch_recurrent``): the definition's recurrence step by step."""
     return _prefill(LIB.gdn_prefill_launch_recurrent, "gdn_prefill_launch_recurrent", q, k, v,
                     state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                    use_qk_l2norm)
+                    use_qk_l2norm, "recurrent")
 
 
 def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-             new_state, use_qk_l2norm):
+             new_state, use_qk_l2norm, kernel):
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 3, dev)
     C.tensor("k", k, torch.bfloat16, 3, dev)
@@ -110,7 +149,7 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
         C.shape("new_state", new_state, (N, H, D, D))
     if N == 0:
         return output, new_state
-    ws_n = workspace_bytes(T, N, HQ, HV, D)
+    ws_n = workspace_bytes(T, N, HQ, HV, D, kernel)
     ws = _workspace(dev, ws_n) if ws_n > 0 else None
     status = launch(
         q.data_ptr(), k.data_ptr(), v.data_ptr(),

@@ -8,8 +8,11 @@ from oracle import gdn_oracle as O
 
 pytestmark = pytest.mark.gpu
 
+# both tensor-core kernel families (auto picks one of them)
+KERNELS = ["split", "fused"]
 
-def run(pkg, inp, l2, dev, *, cu64=False, inplace=False):
+
+def run(pkg, inp, l2, dev, *, cu64=False, inplace=False, kernel="auto"):
     d = to(inp, dev)
     if cu64:
         d["cu_seqlens"] = d["cu_seqlens"].to(torch.int64)
@@ -21,18 +24,19 @@ def run(pkg, inp, l2, dev, *, cu64=False, inplace=False):
         torch.empty(N, HV, D, D, dtype=torch.float32, device=dev)
     o, s = pkg.gdn_prefill(d["q"], d["k"], d["v"], d.get("state"), d["A_log"], d["a"],
                            d["dt_bias"], d["b"], d["cu_seqlens"], d.get("scale"), out, ns,
-                           use_qk_l2norm=l2)
+                           use_qk_l2norm=l2, kernel=kernel)
     torch.cuda.synchronize()
     assert o.data_ptr() == out.data_ptr() and s.data_ptr() == ns.data_ptr()
     return o, s
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("name,l2", [("prefill_varlen_l2", True), ("prefill_nostate_raw", False)])
-def test_golden(cuda, name, l2):
+def test_golden(cuda, name, l2, kernel):
     pkg = load_pkg()
     d, m = load_golden(name)
     d["scale"] = m["scale"]
-    o, s = run(pkg, d, l2, cuda)
+    o, s = run(pkg, d, l2, cuda, kernel=kernel)
     assert_parity(o, s, d["out"], d["new_state"], what=name)
 
 
@@ -40,11 +44,12 @@ def test_golden(cuda, name, l2):
 RAGGED = [1, 5, 63, 64, 65, 0, 127, 128, 129, 200]
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("with_state", [True, False])
-def test_ragged_varlen_l2(cuda, with_state):
+def test_ragged_varlen_l2(cuda, with_state, kernel):
     pkg = load_pkg()
     inp = pkg.workloads.prefill_inputs(RAGGED, seed=21, with_state=with_state)
-    o, s = run(pkg, inp, True, cuda)
+    o, s = run(pkg, inp, True, cuda, kernel=kernel)
     ro, rs = oracle_prefill(inp, True)
     assert_parity(o, s, ro, rs, what=f"ragged state={with_state}")
     assert s[5].abs().max().item() == 0.0  # empty sequence -> zero state slice
@@ -63,19 +68,30 @@ def test_raw_qk_short(cuda):
     assert_parity(o, s, ro, rs, what="raw")
 
 
-def test_int64_cu_seqlens_and_in_place(cuda):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_raw_qk_short_each_kernel(cuda, kernel):
+    pkg = load_pkg()
+    inp = pkg.workloads.prefill_inputs([3, 17, 40, 64, 65], seed=25)
+    o, s = run(pkg, inp, False, cuda, kernel=kernel)
+    ro, rs = oracle_prefill(inp, False)
+    assert_parity(o, s, ro, rs, what=f"raw {kernel}")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_int64_cu_seqlens_and_in_place(cuda, kernel):
     pkg = load_pkg()
     inp = pkg.workloads.prefill_inputs([70, 9], seed=23)
     ro, rs = oracle_prefill(inp, True)
-    o, s = run(pkg, inp, True, cuda, cu64=True, inplace=True)
+    o, s = run(pkg, inp, True, cuda, cu64=True, inplace=True, kernel=kernel)
     assert_parity(o, s, ro, rs, what="int64+inplace")
 
 
-@pytest.mark.parametrize("hq,hv", [(4, 8), (1, 1)])
-def test_head_layouts(cuda, hq, hv):
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("hq,hv", [(4, 8), (1, 1), (2, 8)])
+def test_head_layouts(cuda, hq, hv, kernel):
     pkg = load_pkg()
     inp = pkg.workloads.prefill_inputs([33, 100], hq=hq, hv=hv, seed=hq + hv)
-    o, s = run(pkg, inp, True, cuda)
+    o, s = run(pkg, inp, True, cuda, kernel=kernel)
     ro, rs = oracle_prefill(inp, True)
     assert_parity(o, s, ro, rs, what=f"hq={hq} hv={hv}")
 
@@ -87,12 +103,13 @@ def test_all_sequences_empty(cuda):
     assert s.abs().max().item() == 0.0 and o.numel() == 0
 
 
-def test_p1_config_full_vs_oracle(cuda):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_p1_config_full_vs_oracle(cuda, kernel):
     """P1: 8 sequences, lengths U[256, 4096] (T = 19,762 at seed 0), zero initial state."""
     pkg = load_pkg()
     inp = pkg.workloads.prefill_config_inputs("P1", seed=0)
     assert inp["q"].shape[0] == 19762
-    o, s = run(pkg, inp, True, cuda)
+    o, s = run(pkg, inp, True, cuda, kernel=kernel)
     ro, rs = oracle_prefill(inp, True)
     err, _ = assert_parity(o, s, ro, rs, what="P1")
     ok, *_ = O.flashinfer_allclose(o.cpu(), ro, 1e-2, 1e-2)
@@ -148,15 +165,16 @@ def test_p2_head_group_shards_reassemble_bitwise(cuda):
     assert pkg.device_error() == 0
 
 
-def test_chunked_matches_recurrent_p2_full(cuda):
-    """P2 at full size (32768 tokens, initial state): the chunked tensor-core kernel
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_chunked_matches_recurrent_p2_full(cuda, kernel):
+    """P2 at full size (32768 tokens, initial state): each chunked tensor-core kernel
     and the token-serial CUDA-core kernel agree (state rel <= 1e-3, outputs within
     the bf16 bar), and no bounded wait ran out."""
     pkg = load_pkg()
     inp = pkg.workloads.prefill_config_inputs("P2", seed=0, device="cuda")
     args = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
             inp["b"], inp["cu_seqlens"], inp["scale"])
-    o1, s1 = pkg.gdn_prefill(*args, use_qk_l2norm=True)
+    o1, s1 = pkg.gdn_prefill(*args, use_qk_l2norm=True, kernel=kernel)
     o2, s2 = pkg.gdn_prefill_recurrent(*args, use_qk_l2norm=True)
     assert pkg.device_error() == 0
     assert O.state_rel_err(s1.cpu(), s2.cpu()) < 1e-3
