@@ -44,6 +44,9 @@ cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st);
 // TMA descriptor of a [rows][heads * 128] bf16 matrix with 64 x 64 boxes and the
 // 128-byte swizzle (false if the driver's encoder is unavailable or refuses it).
 bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows);
+// Same with `box_x` (<= 64) columns per box, 128-byte swizzle or none.
+bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows, int box_x,
+                       bool swizzle128);
 
 // Split path: a chunk-parallel preparation kernel and a sequential state kernel
 // split over v-blocks.  Same requirements as the chunked kernel; the workspace

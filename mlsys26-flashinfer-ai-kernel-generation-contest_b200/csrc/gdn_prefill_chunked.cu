@@ -1460,17 +1460,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // [rows][heads * 128] bf16 matrix, 64 x 64 boxes, 128-byte swizzle.
-bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows) {
+bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows, int box_x,
+                       bool swizzle128) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return false;
   cuuint64_t dims[2] = {(cuuint64_t)heads * kHeadDim, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)heads * kHeadDim * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {(cuuint32_t)box_x, 64};
   cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows) {
+  return make_tile_map_box(m, base, heads, rows, 64, true);
 }
 
 size_t prefill_chunked_workspace(int num_seqs) {

@@ -21,11 +21,14 @@
 //
 // The state recurrence is separable in v (row v of S only ever meets column v of
 // V, U and O), so the sequential kernel runs one CTA per (sequence, v-head,
-// 64-row v-block).  It keeps S^T[k][v] (fp32) in TMEM and per chunk issues three
+// 32-row v-block).  It keeps S^T[k][v] (fp32) in TMEM and per chunk issues three
 // M = 128 MMA groups:
 //   G1  [K; Q] S^T              -> rows 0..63 K S^T, rows 64..127 Q S^T  (S hi + S lo)
-//   G2  [T; P T] R              -> rows 0..63 U,     rows 64..127 P U    (3 split terms)
+//   G2  [T; P T] R              -> rows 0..63 U,     rows 64..127 P U    ((hi + lo)(hi + lo))
 //   G3  S^T += K^T U~                                                    (U~ hi + lo)
+// each split operand read as one N = 64 tile [hi | lo] into two accumulator halves.
+// Warp 16 issues the MMAs, warp 17 the copies, and warps 0..15 the TMEM epilogues;
+// they hand over through mbarriers.
 // with the R / U~ / output / state epilogues on the CUDA cores.  The next two
 // chunks' K/Q tiles, V block and record are in flight while a chunk is processed.
 //
@@ -433,22 +436,65 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 
 // ============================================================ sequential state kernel
 namespace st {
-constexpr int kThreads = 256;
-constexpr int kVB = 64;  // v-rows per CTA
+constexpr int kCompute = 512;             // warps 0..15: TMEM epilogues on the CUDA cores
+constexpr int kMmaWarp = kCompute / 32;   // warp 16 issues the MMA groups
+constexpr int kTmaWarp = kMmaWarp + 1;    // warp 17 issues the copies
+constexpr int kThreads = kCompute + 64;
+constexpr int kVB = 32;                   // v-rows per CTA (four CTAs per v-head)
+constexpr int kSplitV = kHeadDim / kVB;
 constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // K0 | Q0 | K1 | Q1 (8 KB each), per buffer
-constexpr uint32_t V0 = 65536, V1 = 73728;  // V block [t][64 v] (8 KB), per buffer
-constexpr uint32_t TP0 = 81920, TP1 = 114688;  // record tiles: hi (16 KB) | lo (16 KB)
-constexpr uint32_t SHI = 147456, SLO = 163840;  // S image [k][v] (MN-major B of G1)
-constexpr uint32_t RHI = 180224, RLO = 188416;  // R image [j][v] (MN-major B of G2)
-constexpr uint32_t UHI = 196608, ULO = 204800;  // U~ image [t][v] (MN-major B of G3)
-constexpr uint32_t VEC0 = 212992, VEC1 = 214272;  // record vectors (1040 B), per buffer
-constexpr uint32_t BARS = 215552;
-constexpr uint32_t SMEM = BARS + 128;
-constexpr uint32_t TST = 0, TG1 = 64, TG2 = 128;  // TMEM columns (256 allocated)
+constexpr uint32_t TP0 = 65536, TP1 = 98304;  // record tiles: hi (16 KB) | lo (16 KB), per buffer
+// MMA B images, 128-byte rows [hi (32 v) | lo (32 v)] in the 128-byte swizzle, MN-major:
+constexpr uint32_t SIMG = 131072;  // S [k][v]   (G1)
+constexpr uint32_t RIMG = 147456;  // R [j][v]   (G2)
+constexpr uint32_t UIMG = 155648;  // U~ [t][v]  (G3)
+constexpr uint32_t V0 = 163840, V1 = 167936;  // V block [t][32 v], 64-byte rows, per buffer
+constexpr uint32_t VEC0 = 172032, VEC1 = 173312;  // record vectors (1040 B), per buffer
+constexpr uint32_t BARS = 174592;
+constexpr uint32_t SMEM = BARS + 256;
+// TMEM columns (256 allocated).  Each MMA reads its split operand as one N = 64 B
+// tile [hi | lo], so each D tile holds two 32-column halves whose sum is the product:
+//   TST: state S^T = (cols 0..31) + (cols 32..63), both decayed; G3 adds U~ hi / U~ lo
+//   TG1: [K; Q] S_hi^T | [K; Q] S_lo^T       TG2: [T; P T] R_hi | [T; P T] R_lo
+constexpr uint32_t TST = 0, TG1 = 64, TG2 = 128;
 static_assert(SMEM <= 232448, "shared memory budget");
 struct Bars {
-  uint64_t kq[2], vt[2], g1, g2, g3;
+  uint64_t kq[2], vt[2];          // copies landed (transaction counts)
+  uint64_t kq_free[2], vt_free[2];  // buffers consumed (MMA commit / + 16 compute warps)
+  uint64_t g1, g2, g3;            // MMA groups completed (commit)
+  uint64_t s_ready;               // 16 compute warps: S images written
+  uint64_t r_ready, u_ready;      // 8 warps of TMEM lanes 0..63: R / U~ images written
+  uint64_t o_done;                // 8 warps of TMEM lanes 64..127: outputs read out
 };
+
+// Bounded wait that gives up early once another thread has aborted; a wait that
+// runs out records `code` and raises the abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, unsigned code) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  atomicOr(&g_split_device_error, code);
+  *abort_flag = 1;
+  return false;
+}
+// One arrival per warp, after every lane's shared-memory and TMEM accesses are
+// ordered for the async proxy / tensor cores.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  fence_proxy_async();
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+// 8 fp32 values of columns 8q.. -> row r of a [hi | lo] image: hi in 16-byte chunk q,
+// lo in chunk 4 + q (128-byte swizzle).
+__device__ __forceinline__ void store_split8(uint32_t base, int r, int q, const float* x) {
+  uint4 xhi, xlo;
+  split8(x, xhi, xlo);
+  st_v4(base + sw128(r, q), xhi);
+  st_v4(base + sw128(r, 4 + q), xlo);
+}
 }  // namespace st
 
 template <bool HAS_STATE, typename CuT>
@@ -460,24 +506,27 @@ __global__ void __launch_bounds__(st::kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sb = smem_u32(smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int sp = warp & 3, half = warp >> 2;
+  const int sp = warp & 3, qc = (warp >> 2) & 3;  // TMEM lane quarter, 16-column quarter
   const int row = sp * 32 + lane;  // TMEM lane: k for the state, token for G1 / G2 rows
   const int HV = p.HV;
-  const int per = 2 * HV;
+  const int per = kSplitV * HV;
   const int wi = blockIdx.x / per;
   const int rem = blockIdx.x - wi * per;
-  const int h = rem >> 1, vb = rem & 1;
+  const int h = rem / kSplitV, vb = rem % kSplitV;
   const int n = p.order ? p.order[wi] : wi;
   const int qh = h / p.ratio;
   long long s0, s1;
   seq_range(static_cast<const CuT*>(p.cu), n, p.T, s0, s1);
   const long long L = s1 - s0;
-  // this thread's state elements: S[v][k], k = row, v = v_lo + i (i < 32)
-  const int v_lo = kVB * vb + 32 * half;
+  // a compute thread's state elements: S[v][k], k = row, v = v_lo + i (i < 8)
+  const int vq = 8 * qc;  // column offset inside the v-block
+  const int v_lo = kVB * vb + vq;
   float* ns = p.new_state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
   if (L <= 0) {  // empty sequence: zero final state (definition semantics)
-#pragma unroll 4
-    for (int i = 0; i < 32; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = 0.f;
+    if (tid < kCompute) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = 0.f;
+    }
     return;
   }
   if ((sb & 1023u) != 0) {
@@ -485,261 +534,264 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     return;
   }
   const int nchunks = (int)((L + kC - 1) / kC);
-  const size_t rstride = (size_t)HV * kRecBytes;
-  const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * kRecBytes;
-  const float scale = default_scale(p.scale);
   Bars* bars = reinterpret_cast<Bars*>(smem + BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + sizeof(Bars));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + BARS + sizeof(Bars) + 4);
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   if (tid == 32) {
-    uint64_t* b = reinterpret_cast<uint64_t*>(bars);
-    for (int i = 0; i < (int)(sizeof(Bars) / 8); ++i) mbar_init(b + i, 1);
+    mbar_init(&bars->kq[0], 1);
+    mbar_init(&bars->kq[1], 1);
+    mbar_init(&bars->vt[0], 1);
+    mbar_init(&bars->vt[1], 1);
+    mbar_init(&bars->kq_free[0], 1);
+    mbar_init(&bars->kq_free[1], 1);
+    mbar_init(&bars->vt_free[0], kCompute / 32 + 1);
+    mbar_init(&bars->vt_free[1], kCompute / 32 + 1);
+    mbar_init(&bars->g1, 1);
+    mbar_init(&bars->g2, 1);
+    mbar_init(&bars->g3, 1);
+    mbar_init(&bars->s_ready, kCompute / 32);
+    mbar_init(&bars->r_ready, kCompute / 64);
+    mbar_init(&bars->u_ready, kCompute / 64);
+    mbar_init(&bars->o_done, kCompute / 64);
+    *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
-
-  // copies in flight, per buffer (-1: none); identical on every thread
-  int pend_kq[2] = {-1, -1}, pend_vt[2] = {-1, -1};
-  auto issue = [&](int cc) {  // K/Q tiles, V block and record of chunk cc -> buffer cc & 1
-    const int bf = cc & 1;
-    const int y = (int)(s0 + (long long)kC * cc);
-    pend_kq[bf] = (cc >> 1) & 1;
-    pend_vt[bf] = (cc >> 1) & 1;
-    if (tid != 0) return;
-    fence_proxy_async();
-    const uint32_t kq = bf ? KQ1 : KQ0;
-    mbar_arrive_expect_tx(&bars->kq[bf], 4 * 8192);
-    tma_load_2d(smem + kq, &tm_k, &bars->kq[bf], qh * 128, y);
-    tma_load_2d(smem + kq + 16384, &tm_k, &bars->kq[bf], qh * 128 + 64, y);
-    tma_load_2d(smem + kq + 8192, &tm_q, &bars->kq[bf], qh * 128, y);
-    tma_load_2d(smem + kq + 24576, &tm_q, &bars->kq[bf], qh * 128 + 64, y);
-    const uint8_t* r = rec0 + (size_t)cc * rstride;
-    mbar_arrive_expect_tx(&bars->vt[bf], 8192 + 32768 + kRecVecBytes);
-    tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
-    bulk_load(smem + (bf ? TP1 : TP0), r, 32768, &bars->vt[bf]);
-    bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecVec, kRecVecBytes, &bars->vt[bf]);
-  };
-  issue(0);
-  if (nchunks > 1) issue(1);
-
-  // initial state: S^T[k][v] -> TMEM (fp32) and the hi/lo image of G1's B operand
-  {
-    float sv[32];
-    if constexpr (HAS_STATE) {
-      const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = __ldg(src + (size_t)(v_lo + i) * kHeadDim + row);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = 0.f;
-    }
-    uint32_t w[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(sv[i]);
-    tmem_st32(tl + TST + 32u * half, w);
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      uint4 xhi, xlo;
-      split8(&sv[8 * q4], xhi, xlo);
-      st_v4(sb + SHI + sw128(row, 4 * half + q4), xhi);
-      st_v4(sb + SLO + sw128(row, 4 * half + q4), xlo);
-    }
-    tmem_wait_st();
-  }
-  fence_proxy_async();
-  tc_fence_before();
-  __syncthreads();
-
-  bool ok = true;
-  uint64_t* mma_bar = nullptr;  // MMA group in flight
+  int kq_issued = 0, vt_issued = 0;  // copy warp: chunks whose copies were issued
+  uint64_t* mma_bar = nullptr;       // MMA warp: group in flight when a wait ran out
   uint32_t mma_par = 0;
-  for (int c = 0; c < nchunks && ok; ++c) {
-    const int bf = c & 1;
-    const uint32_t par2 = (c >> 1) & 1;
-    const long long t0 = s0 + (long long)kC * c;
-    const int Lc = (int)min((long long)kC, s1 - t0);
-    const uint32_t kqb = bf ? KQ1 : KQ0;
-    const uint32_t tpb = bf ? TP1 : TP0;
-    const float* vec = reinterpret_cast<const float*>(smem + (bf ? VEC1 : VEC0));
-    if (!(ok = cta_wait(&bars->kq[bf], par2, ERR_TMA_TIMEOUT))) break;
-    pend_kq[bf] = -1;
-    if (!(ok = cta_wait(&bars->vt[bf], par2, ERR_TMA_TIMEOUT))) break;
-    pend_vt[bf] = -1;
-    // G1: [K; Q] S^T  (S hi + S lo)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint64_t ad = umma_desc_k(sb + kqb + 16384u * (ks >> 2) + 32u * (ks & 3));
-        umma_bf16(tmem + TG1, ad, umma_desc_mn(sb + SHI + 2048u * ks, 8192), idesc, ks > 0);
-        umma_bf16(tmem + TG1, ad, umma_desc_mn(sb + SLO + 2048u * ks, 8192), idesc, 1);
-      }
-      umma_commit(&bars->g1);
-    }
-    mma_bar = &bars->g1;
-    mma_par = c & 1;
-    {  // meanwhile: decay the fp32 state (G3 accumulates onto it)
-      const float G = vec[256];
-      float sv[32];
-      uint32_t w[32];
-      tmem_ld32(tl + TST + 32u * half, sv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(G * sv[i]);
-      tmem_st32(tl + TST + 32u * half, w);
-      tmem_wait_st();
-    }
-    if (!(ok = cta_wait(&bars->g1, c & 1, ERR_MMA_TIMEOUT))) break;
-    mma_bar = nullptr;
-    tc_fence_after();
-    // R[j][v] = beta_j (V[j][v] - gamma_j rk_j (K S^T)[j][v])  (lanes 0..63: j = row)
-    if (sp < 2) {
-      float sk[32];
-      tmem_ld32(tl + TG1 + 32u * half, sk);
-      const float bj = vec[row], cj = vec[64 + row];
-      const uint32_t vt = sb + (bf ? V1 : V0);
-      uint4 vw[4];
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) vw[q4] = ld_shared_v4(vt + sw128(row, 4 * half + q4));
-      tmem_wait_ld();
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const uint32_t w4[4] = {vw[q4].x, vw[q4].y, vw[q4].z, vw[q4].w};
-        float x[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = bf2x2_to_f2(w4[e]);
-          x[2 * e] = bj * (f.x - cj * sk[8 * q4 + 2 * e]);
-          x[2 * e + 1] = bj * (f.y - cj * sk[8 * q4 + 2 * e + 1]);
-        }
-        uint4 xhi, xlo;
-        split8(x, xhi, xlo);
-        st_v4(sb + RHI + sw128(row, 4 * half + q4), xhi);
-        st_v4(sb + RLO + sw128(row, 4 * half + q4), xlo);
+
+  if (warp == kTmaWarp) {
+    // =========================================================== copy warp
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const size_t rstride = (size_t)HV * kRecBytes;
+      const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * kRecBytes;
+      for (int cc = 0; cc < nchunks; ++cc) {
+        const int bf = cc & 1;
+        const uint32_t free_par = ((cc >> 1) + 1) & 1;  // phase cc/2 - 1 of the free barrier
+        const int y = (int)(s0 + (long long)kC * cc);
+        if (cc >= 2 && !wait_or_abort(&bars->kq_free[bf], free_par, abort_flag, ERR_MMA_TIMEOUT))
+          break;
+        const uint32_t kq = bf ? KQ1 : KQ0;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&bars->kq[bf], 4 * 8192);
+        tma_load_2d(smem + kq, &tm_k, &bars->kq[bf], qh * 128, y);
+        tma_load_2d(smem + kq + 16384, &tm_k, &bars->kq[bf], qh * 128 + 64, y);
+        tma_load_2d(smem + kq + 8192, &tm_q, &bars->kq[bf], qh * 128, y);
+        tma_load_2d(smem + kq + 24576, &tm_q, &bars->kq[bf], qh * 128 + 64, y);
+        kq_issued = cc + 1;
+        if (cc >= 2 && !wait_or_abort(&bars->vt_free[bf], free_par, abort_flag, ERR_MMA_TIMEOUT))
+          break;
+        const uint8_t* r = rec0 + (size_t)cc * rstride;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&bars->vt[bf], 64 * kVB * 2 + 32768 + kRecVecBytes);
+        tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
+        bulk_load(smem + (bf ? TP1 : TP0), r, 32768, &bars->vt[bf]);
+        bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecVec, kRecVecBytes, &bars->vt[bf]);
+        vt_issued = cc + 1;
       }
     }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    // G2: [T; P T] R  (TP hi R hi + TP lo R hi + TP hi R lo)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
+  } else if (warp == kMmaWarp) {
+    // =========================================================== MMA warp
+    if (lane == 0) {
+      const uint32_t id_nn = umma_idesc_bf16(128, 64, false, true);  // A K-major, B MN-major
+      const uint32_t id_mm = umma_idesc_bf16(128, 64, true, true);   // A and B MN-major
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int bf = c & 1;
+        const uint32_t par = c & 1, par2 = (c >> 1) & 1;
+        const uint32_t kqb = bf ? KQ1 : KQ0, tpb = bf ? TP1 : TP0;
+        if (!(ok = wait_or_abort(&bars->kq[bf], par2, abort_flag, ERR_TMA_TIMEOUT))) break;
+        if (!(ok = wait_or_abort(&bars->vt[bf], par2, abort_flag, ERR_TMA_TIMEOUT))) break;
+        if (!(ok = wait_or_abort(&bars->s_ready, par, abort_flag, ERR_MMA_TIMEOUT))) break;
+        if (c > 0 && !(ok = wait_or_abort(&bars->o_done, par ^ 1u, abort_flag, ERR_MMA_TIMEOUT)))
+          break;
+        tc_fence_after();
+        // G1: [K; Q] [S_hi | S_lo]^T
 #pragma unroll
-      for (int term = 0; term < 3; ++term) {
-        const uint32_t a = tpb + (term == 1 ? 16384u : 0u);
-        const uint32_t b = term == 2 ? RLO : RHI;
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem + TG1, umma_desc_k(sb + kqb + 16384u * (ks >> 2) + 32u * (ks & 3)),
+                    umma_desc_mn(sb + SIMG + 2048u * ks, 8192), id_nn, ks > 0);
+        umma_commit(&bars->g1);
+        mma_bar = &bars->g1;
+        mma_par = par;
+        if (!(ok = wait_or_abort(&bars->r_ready, par, abort_flag, ERR_MMA_TIMEOUT))) break;
+        tc_fence_after();
+        // G2: ([T; P T] hi + lo) [R_hi | R_lo]
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma_bf16(tmem + TG2, umma_desc_k(sb + a + 32u * ks),
-                    umma_desc_mn(sb + b + 2048u * ks, 8192), idesc, (term | ks) != 0);
-      }
-      umma_commit(&bars->g2);
-    }
-    mma_bar = &bars->g2;
-    mma_par = c & 1;
-    if (!(ok = cta_wait(&bars->g2, c & 1, ERR_MMA_TIMEOUT))) break;
-    mma_bar = nullptr;
-    tc_fence_after();
-    if (sp < 2) {  // U~ = diag(us) U -> hi/lo image [t][v]
-      float uv[32];
-      tmem_ld32(tl + TG2 + 32u * half, uv);
-      const float ut = vec[128 + row];
-      tmem_wait_ld();
+        for (int term = 0; term < 2; ++term)
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float x[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = ut * uv[8 * q4 + e];
-        uint4 xhi, xlo;
-        split8(x, xhi, xlo);
-        st_v4(sb + UHI + sw128(row, 4 * half + q4), xhi);
-        st_v4(sb + ULO + sw128(row, 4 * half + q4), xlo);
-      }
-    } else {  // O = scale gamma rq (Q S^T) + scale (P T) R  (lanes 64..127: t = row - 64)
-      const int t = row - 64;
-      float qs[32], pu[32];
-      tmem_ld32(tl + TG1 + 32u * half, qs);
-      tmem_ld32(tl + TG2 + 32u * half, pu);
-      const float ct = vec[192 + t];
-      tmem_wait_ld();
-      if (t < Lc) {
-        __nv_bfloat16* dst = p.out + ((size_t)(t0 + t) * HV + h) * kHeadDim + v_lo;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 8 * q4 + 2 * e;
-            w[e] = cvt_bf16x2(ct * qs[i] + scale * pu[i], ct * qs[i + 1] + scale * pu[i + 1]);
-          }
-          *reinterpret_cast<uint4*>(dst + 8 * q4) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    // G3: S^T += K^T U~  (A = K tile as MN-major [t][k]; U~ hi + lo)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t idesc = umma_idesc_bf16(128, 64, true, true);
-#pragma unroll
-      for (int term = 0; term < 2; ++term)
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + TG2, umma_desc_k(sb + tpb + 16384u * term + 32u * ks),
+                      umma_desc_mn(sb + RIMG + 2048u * ks, 8192), id_nn, (term | ks) != 0);
+        umma_commit(&bars->g2);
+        umma_commit(&bars->vt_free[bf]);  // record tiles consumed once G2 completes
+        mma_bar = &bars->g2;
+        if (!(ok = wait_or_abort(&bars->u_ready, par, abort_flag, ERR_MMA_TIMEOUT))) break;
+        tc_fence_after();
+        // G3: S^T += K^T [U~_hi | U~_lo]  (A = K tile as MN-major [t][k])
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma_bf16(tmem + TST, umma_desc_mn(sb + kqb + 2048u * ks, 16384),
-                    umma_desc_mn(sb + (term ? ULO : UHI) + 2048u * ks, 8192), idesc, 1);
-      umma_commit(&bars->g3);
-    }
-    mma_bar = &bars->g3;
-    mma_par = c & 1;
-    if (!(ok = cta_wait(&bars->g3, c & 1, ERR_MMA_TIMEOUT))) break;
-    mma_bar = nullptr;
-    tc_fence_after();
-    if (c + 2 < nchunks) issue(c + 2);  // buffer bf fully consumed
-    // epilogue: S^T -> next chunk's hi/lo image, or the final state
-    {
-      float sv[32];
-      tmem_ld32(tl + TST + 32u * half, sv);
-      tmem_wait_ld();
-      if (c + 1 == nchunks) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = sv[i];
-      } else {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 xhi, xlo;
-          split8(&sv[8 * q4], xhi, xlo);
-          st_v4(sb + SHI + sw128(row, 4 * half + q4), xhi);
-          st_v4(sb + SLO + sw128(row, 4 * half + q4), xlo);
+                    umma_desc_mn(sb + UIMG + 2048u * ks, 8192), id_mm, 1);
+        umma_commit(&bars->g3);
+        umma_commit(&bars->kq_free[bf]);  // K (G3) and Q (G1) consumed once G3 completes
+        mma_bar = &bars->g3;
+      }
+      if (ok) {
+        // the buffer-free arrivals of the last two chunks are waited by nobody else:
+        // let them land before the CTA's shared memory is released
+        mma_bar = nullptr;
+        for (int c = max(nchunks - 2, 0); c < nchunks; ++c) {
+          mbar_wait(&bars->kq_free[c & 1], (c >> 1) & 1, 1u << 20);
+          mbar_wait(&bars->vt_free[c & 1], (c >> 1) & 1, 1u << 20);
         }
       }
     }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-  }
-  if (!ok && tid == 0) {  // let the copies and the MMA group in flight land
-    if (mma_bar) mbar_wait(mma_bar, mma_par, 1u << 20);
-    for (int i = 0; i < 2; ++i) {
-      if (pend_kq[i] >= 0) mbar_wait(&bars->kq[i], (uint32_t)pend_kq[i], 1u << 20);
-      if (pend_vt[i] >= 0) mbar_wait(&bars->vt[i], (uint32_t)pend_vt[i], 1u << 20);
+  } else {
+    // =========================================================== compute warps
+    const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+    const float scale = default_scale(p.scale);
+    // initial state: S^T[k][v] -> TMEM (fp32; second half 0) and G1's [hi | lo] image
+    {
+      float sv[8];
+      if constexpr (HAS_STATE) {
+        const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sv[i] = __ldg(src + (size_t)(v_lo + i) * kHeadDim + row);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sv[i] = 0.f;
+      }
+      const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      tmem_st8(tl + TST + vq, sv);
+      tmem_st8(tl + TST + 32u + vq, zero);
+      store_split8(sb + SIMG, row, qc, sv);
+      tmem_wait_st();
+      warp_arrive(&bars->s_ready);
+    }
+    for (int c = 0; c < nchunks; ++c) {
+      const int bf = c & 1;
+      const uint32_t par = c & 1, par2 = (c >> 1) & 1;
+      const long long t0 = s0 + (long long)kC * c;
+      const int Lc = (int)min((long long)kC, s1 - t0);
+      const float* vec = reinterpret_cast<const float*>(smem + (bf ? VEC1 : VEC0));
+      if (!wait_or_abort(&bars->vt[bf], par2, abort_flag, ERR_TMA_TIMEOUT)) break;
+      {  // decay both halves of the fp32 state while G1 runs (G3 accumulates onto them)
+        const float G = vec[256];
+        float sa[8], sc[8];
+        tmem_ld8(tl + TST + vq, sa);
+        tmem_ld8(tl + TST + 32u + vq, sc);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          sa[i] *= G;
+          sc[i] *= G;
+        }
+        tmem_st8(tl + TST + vq, sa);
+        tmem_st8(tl + TST + 32u + vq, sc);
+        tmem_wait_st();
+      }
+      if (!wait_or_abort(&bars->g1, par, abort_flag, ERR_MMA_TIMEOUT)) break;
+      tc_fence_after();
+      if (sp < 2) {
+        // R[j][v] = beta_j (V[j][v] - gamma_j rk_j (K S^T)[j][v])  (j = row)
+        float sk[8], sk2[8];
+        tmem_ld8(tl + TG1 + vq, sk);
+        tmem_ld8(tl + TG1 + 32u + vq, sk2);
+        const float bj = vec[row], cj = vec[64 + row];
+        const uint4 va = ld_shared_v4(sb + (bf ? V1 : V0) + row * (2 * kVB) + 16 * qc);
+        tmem_wait_ld();
+        const uint32_t vw[4] = {va.x, va.y, va.z, va.w};
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = bf2x2_to_f2(vw[e]);
+          x[2 * e] = bj * (f.x - cj * (sk[2 * e] + sk2[2 * e]));
+          x[2 * e + 1] = bj * (f.y - cj * (sk[2 * e + 1] + sk2[2 * e + 1]));
+        }
+        store_split8(sb + RIMG, row, qc, x);
+        warp_arrive(&bars->r_ready);
+        if (!wait_or_abort(&bars->g2, par, abort_flag, ERR_MMA_TIMEOUT)) break;
+        tc_fence_after();
+        // U~ = diag(us) U -> [hi | lo] image [t][v]
+        float uv[8], uv2[8];
+        tmem_ld8(tl + TG2 + vq, uv);
+        tmem_ld8(tl + TG2 + 32u + vq, uv2);
+        const float ut = vec[128 + row];
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = ut * (uv[i] + uv2[i]);
+        store_split8(sb + UIMG, row, qc, x);
+        warp_arrive(&bars->u_ready);
+      } else {
+        // O = scale gamma rq (Q S^T) + scale (P T) R  (t = row - 64)
+        if (!wait_or_abort(&bars->g2, par, abort_flag, ERR_MMA_TIMEOUT)) break;
+        tc_fence_after();
+        const int t = row - 64;
+        float qs[8], q2[8], pu[8], p2[8];
+        tmem_ld8(tl + TG1 + vq, qs);
+        tmem_ld8(tl + TG1 + 32u + vq, q2);
+        tmem_ld8(tl + TG2 + vq, pu);
+        tmem_ld8(tl + TG2 + 32u + vq, p2);
+        const float ct = vec[192 + t];
+        tmem_wait_ld();
+        warp_arrive(&bars->o_done);  // TG1 / TG2 read out: the next G1 / G2 may overwrite
+        if (t < Lc) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 2 * e;
+            w[e] = cvt_bf16x2(ct * (qs[i] + q2[i]) + scale * (pu[i] + p2[i]),
+                              ct * (qs[i + 1] + q2[i + 1]) + scale * (pu[i + 1] + p2[i + 1]));
+          }
+          *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + t) * HV + h) * kHeadDim + v_lo) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      warp_arrive(&bars->vt_free[bf]);  // this warp's V / vector reads of buffer bf are done
+      if (!wait_or_abort(&bars->g3, par, abort_flag, ERR_MMA_TIMEOUT)) break;
+      tc_fence_after();
+      // epilogue: S^T -> next chunk's [hi | lo] image, or the final state
+      {
+        float sv[8], s2[8];
+        tmem_ld8(tl + TST + vq, sv);
+        tmem_ld8(tl + TST + 32u + vq, s2);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sv[i] += s2[i];
+        if (c + 1 == nchunks) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = sv[i];
+        } else {
+          store_split8(sb + SIMG, row, qc, sv);
+          warp_arrive(&bars->s_ready);
+        }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {  // a wait ran out: copies and MMAs still in flight land first (bounded)
+    if (warp == kTmaWarp && lane == 0) {
+      for (int cc = max(kq_issued - 2, 0); cc < kq_issued; ++cc)
+        mbar_wait(&bars->kq[cc & 1], (cc >> 1) & 1, 1u << 20);
+      for (int cc = max(vt_issued - 2, 0); cc < vt_issued; ++cc)
+        mbar_wait(&bars->vt[cc & 1], (cc >> 1) & 1, 1u << 20);
+    }
+    if (warp == kMmaWarp && lane == 0 && mma_bar != nullptr) mbar_wait(mma_bar, mma_par, 1u << 20);
+    __syncthreads();
+  }
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
@@ -784,8 +836,8 @@ cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const C
   ka<<<dim3((unsigned)slots, (unsigned)sp.HV), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk, sp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  kb<<<dim3((unsigned)((long long)sp.N * sp.HV * 2)), dim3(st::kThreads), st::SMEM, s>>>(mq, mk,
-                                                                                        mv, sp);
+  kb<<<dim3((unsigned)((long long)sp.N * sp.HV * st::kSplitV)), dim3(st::kThreads), st::SMEM,
+       s>>>(mq, mk, mv, sp);
   return cudaGetLastError();
 }
 
@@ -809,11 +861,11 @@ size_t prefill_split_workspace(long long T, int num_seqs, int HV) {
 cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   const SplitLayout lay = split_layout(p.T, p.N, p.HV);
   if (p.workspace == nullptr || p.workspace_bytes < lay.total) return cudaErrorInvalidValue;
-  if (lay.slots > 0x7fffffffLL || (long long)p.N * p.HV * 2 > 0x7fffffffLL)
+  if (lay.slots > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
     return cudaErrorInvalidValue;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv;  // V in [64 tokens][32 v] boxes, unswizzled (read by the CUDA cores)
   if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
-      !make_tile_map(&mv, p.v, p.HV, p.T))
+      !make_tile_map_box(&mv, p.v, p.HV, p.T, st::kVB, false))
     return cudaErrorInvalidValue;
   uint8_t* ws = static_cast<uint8_t*>(p.workspace);
   int* order = nullptr;
