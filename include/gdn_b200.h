@@ -99,7 +99,7 @@ size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_head
  *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes
  *              (may be NULL when that size is 0).  Scratch only: it holds the
  *              longest-first order in which the sequences are scheduled and,
- *              for the split kernels, the per-chunk records (34,048 bytes per
+ *              for the split kernels, the per-chunk records (33,808 bytes per
  *              64-token chunk and v-head); it is rewritten by every call and
  *              must not be shared by calls that overlap on the GPU.
  * A sequence of length 0 gets an all-zero new_state slice (as the

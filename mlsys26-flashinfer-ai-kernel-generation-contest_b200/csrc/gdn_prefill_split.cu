@@ -15,8 +15,9 @@
 // sequence at once by the preparation kernel (one CTA per (chunk, v-head), three
 // CTAs per SM), which stores a record per (chunk, v-head):
 //
-//   [T; P T] hi and lo: two 128 x 64 bf16 tiles in the 128-byte-swizzled K-major
-//       image the tensor cores read (rows 0..63 T, rows 64..127 P T), x = hi + lo;
+//   [T; P T]: a 128 x 64 bf16 tile in the 128-byte-swizzled K-major image the
+//       tensor cores read (rows 0..63 T, rows 64..127 P T), and the lo image of T
+//       (T = hi + lo; P T only feeds the output and is rounded to bf16);
 //   beta, gamma rk, us = rk exp(Lam_end - Lam), scale gamma rq (64 fp32 each), G.
 //
 // The state recurrence is separable in v (row v of S only ever meets column v of
@@ -55,9 +56,17 @@ constexpr int kC = 64;
 enum : unsigned { ERR_TMA_TIMEOUT = 1u, ERR_MMA_TIMEOUT = 2u, ERR_SMEM_ALIGN = 4u };
 
 // ---- per (chunk, v-head) record
-constexpr uint32_t kRecTpHi = 0, kRecTpLo = 16384, kRecVec = 32768;
-constexpr uint32_t kRecVecBytes = 1040;  // beta | gamma rk | us | scale gamma rq (4 x 64 f32), G, pad
-constexpr size_t kRecBytes = 34048;      // 16-byte multiple
+//   [0, 16 KB)   hi image of [T; P T] (rows 0..63 T, rows 64..127 P T)
+//   [16 KB, ..)  lo image: rows 0..63 (T) with normalised q/k, where P T only
+//                feeds the bf16 output and is rounded to bf16; all 128 rows with
+//                raw q/k, whose P T entries span a far wider range
+//   then         beta | gamma rk | us | scale gamma rq (4 x 64 f32), G, pad (1040 B)
+constexpr uint32_t kRecTpHi = 0, kRecTpLo = 16384;
+constexpr uint32_t kRecVecBytes = 1040;
+__host__ __device__ constexpr uint32_t rec_lo_bytes(bool l2) { return l2 ? 8192u : 16384u; }
+__host__ __device__ constexpr uint32_t rec_vec(bool l2) { return kRecTpLo + rec_lo_bytes(l2); }
+__host__ __device__ constexpr uint32_t rec_bytes(bool l2) { return rec_vec(l2) + kRecVecBytes; }
+constexpr size_t kRecBytesMax = rec_bytes(false);  // workspace sizing (16-byte multiple)
 
 struct SplitParams {
   const __nv_bfloat16* a;
@@ -71,6 +80,8 @@ struct SplitParams {
   const int* order;       // longest-first sequence order (null: natural order)
   const int* chunk_base;  // [N + 1] exclusive prefix of chunks per sequence
   uint8_t* rec;           // records, (chunk, v-head) major
+  uint32_t rec_stride;    // bytes per record (rec_bytes(l2norm))
+  uint32_t rec_lo;        // bytes of the record's lo image (rec_lo_bytes(l2norm))
   long long T;
   int N;
   int HV;
@@ -153,7 +164,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int row = sp * 32 + lane;  // TMEM lane of this thread
-  const int g = blockIdx.x, h = blockIdx.y;
+  // v-head fastest: the two v-heads of a q/k head fetch the same K/Q tiles back to back
+  const int g = blockIdx.x / p.HV, h = blockIdx.x - g * p.HV;
   const int total = p.chunk_base[p.N];
   if (g >= total) return;
   int lo = 0, hi = p.N - 1;  // the sequence of chunk g: largest n with base[n] <= g
@@ -167,7 +179,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   const long long t0 = s0 + (long long)kC * c;
   const int Lc = (int)min((long long)kC, s1 - t0);
   const int qh = h / p.ratio;
-  uint8_t* rec = p.rec + ((size_t)g * p.HV + h) * kRecBytes;
+  uint8_t* rec = p.rec + ((size_t)g * p.HV + h) * rec_bytes(L2NORM);
   if ((sb & 1023u) != 0) {
     if (tid == 0) atomicOr(&g_split_device_error, ERR_SMEM_ALIGN);
     return;
@@ -349,7 +361,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     }
     __syncthreads();
     if (tid < 64) {  // the record's row vectors
-      float* rv = reinterpret_cast<float*>(rec + kRecVec);
+      float* rv = reinterpret_cast<float*>(rec + rec_vec(L2NORM));
       const int t = tid;
       const float lend = Lam[63];
       rv[t] = beta[t];
@@ -418,11 +430,18 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
       }
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
-        uint4 xhi, xlo;
-        split8(&v[8 * q4], xhi, xlo);
+        const float* x = &v[8 * q4];
         const uint32_t o = sw128(64 + row, 4 * half + q4);
-        *reinterpret_cast<uint4*>(rec + kRecTpHi + o) = xhi;
-        *reinterpret_cast<uint4*>(rec + kRecTpLo + o) = xlo;
+        if constexpr (L2NORM) {
+          *reinterpret_cast<uint4*>(rec + kRecTpHi + o) =
+              make_uint4(cvt_bf16x2(x[0], x[1]), cvt_bf16x2(x[2], x[3]), cvt_bf16x2(x[4], x[5]),
+                         cvt_bf16x2(x[6], x[7]));
+        } else {
+          uint4 xhi, xlo;
+          split8(x, xhi, xlo);
+          *reinterpret_cast<uint4*>(rec + kRecTpHi + o) = xhi;
+          *reinterpret_cast<uint4*>(rec + kRecTpLo + o) = xlo;
+        }
       }
     }
   } while (0);
@@ -443,7 +462,8 @@ constexpr int kThreads = kCompute + 64;
 constexpr int kVB = 32;                   // v-rows per CTA (four CTAs per v-head)
 constexpr int kSplitV = kHeadDim / kVB;
 constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // K0 | Q0 | K1 | Q1 (8 KB each), per buffer
-constexpr uint32_t TP0 = 65536, TP1 = 98304;  // record tiles: hi (16 KB) | lo (16 KB), per buffer
+constexpr uint32_t TP0 = 65536, TP1 = 98304;  // record tiles: hi (16 KB) | lo (16 KB; rows
+                                              // 64..127 stay zero), per buffer
 // MMA B images, 128-byte rows [hi (32 v) | lo (32 v)] in the 128-byte swizzle, MN-major:
 constexpr uint32_t SIMG = 131072;  // S [k][v]   (G1)
 constexpr uint32_t RIMG = 147456;  // R [j][v]   (G2)
@@ -574,8 +594,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      const size_t rstride = (size_t)HV * kRecBytes;
-      const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * kRecBytes;
+      const size_t rstride = (size_t)HV * p.rec_stride;
+      const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * p.rec_stride;
       for (int cc = 0; cc < nchunks; ++cc) {
         const int bf = cc & 1;
         const uint32_t free_par = ((cc >> 1) + 1) & 1;  // phase cc/2 - 1 of the free barrier
@@ -594,10 +614,10 @@ __global__ void __launch_bounds__(st::kThreads, 1)
           break;
         const uint8_t* r = rec0 + (size_t)cc * rstride;
         fence_proxy_async();
-        mbar_arrive_expect_tx(&bars->vt[bf], 64 * kVB * 2 + 32768 + kRecVecBytes);
+        mbar_arrive_expect_tx(&bars->vt[bf], 64 * kVB * 2 + p.rec_stride);
         tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
-        bulk_load(smem + (bf ? TP1 : TP0), r, 32768, &bars->vt[bf]);
-        bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecVec, kRecVecBytes, &bars->vt[bf]);
+        bulk_load(smem + (bf ? TP1 : TP0), r, kRecTpLo + p.rec_lo, &bars->vt[bf]);  // hi | lo
+        bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecTpLo + p.rec_lo, kRecVecBytes, &bars->vt[bf]);
         vt_issued = cc + 1;
       }
     }
@@ -662,6 +682,14 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     // =========================================================== compute warps
     const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
     const float scale = default_scale(p.scale);
+    // records without a P T lo part: rows 64..127 of both lo tiles stay zero
+    if (p.rec_lo < 16384u) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t a = (i ? TP1 : TP0) + 16384u + 8192u + 16u * (uint32_t)tid;
+        st_shared_v4(sb + a, 0u, 0u, 0u, 0u);
+      }
+    }
     // initial state: S^T[k][v] -> TMEM (fp32; second half 0) and G1's [hi | lo] image
     {
       float sv[8];
@@ -807,7 +835,7 @@ SplitLayout split_layout(long long T, int N, int HV) {
   l.base = up((size_t)N * sizeof(int), 256);
   l.rec = up(l.base + (size_t)(N + 1) * sizeof(int), 1024);
   l.slots = (T + kC - 1) / kC + N;
-  l.total = l.rec + (size_t)l.slots * HV * kRecBytes;
+  l.total = l.rec + (size_t)l.slots * HV * kRecBytesMax;
   return l;
 }
 
@@ -833,7 +861,7 @@ cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const C
                                             const_cast<int*>(sp.chunk_base));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  ka<<<dim3((unsigned)slots, (unsigned)sp.HV), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk, sp);
+  ka<<<dim3((unsigned)(slots * sp.HV)), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk, sp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   kb<<<dim3((unsigned)((long long)sp.N * sp.HV * st::kSplitV)), dim3(st::kThreads), st::SMEM,
@@ -861,7 +889,7 @@ size_t prefill_split_workspace(long long T, int num_seqs, int HV) {
 cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   const SplitLayout lay = split_layout(p.T, p.N, p.HV);
   if (p.workspace == nullptr || p.workspace_bytes < lay.total) return cudaErrorInvalidValue;
-  if (lay.slots > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
+  if (lay.slots * p.HV > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
     return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv;  // V in [64 tokens][32 v] boxes, unswizzled (read by the CUDA cores)
   if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
@@ -888,8 +916,9 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   SplitParams sp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
                  p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
                  static_cast<__nv_bfloat16*>(p.out), order,
-                 reinterpret_cast<const int*>(ws + lay.base), ws + lay.rec, p.T, p.N, p.HV,
-                 p.HV / p.HQ, p.scale};
+                 reinterpret_cast<const int*>(ws + lay.base), ws + lay.rec,
+                 rec_bytes(p.l2norm), rec_lo_bytes(p.l2norm), p.T, p.N, p.HV, p.HV / p.HQ,
+                 p.scale};
   if (p.cu_int64)
     return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
   return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
