@@ -218,13 +218,15 @@ class DecodeWork:
         return h2d, d2h
 
     def e2e_step(self):
-        """Host inputs -> device -> the DPS entry point -> host outputs."""
+        """Host inputs -> device -> the C-ABI entry point (gdn_decode_launch, same flags as
+        the device-timed step) -> host outputs."""
         di = self.d_in
         for k_, t in self.h.items():
             di[k_].copy_(t, non_blocking=True)
         d = self.inp
-        self.pkg.decode_kernel(di["q"], di["k"], di["v"], di["state"], d["A_log"], di["a"],
-                               d["dt_bias"], di["b"], d["scale"], self.out, self.d_ns)
+        self.pkg.gdn_decode(di["q"], di["k"], di["v"], di["state"], d["A_log"], di["a"],
+                            d["dt_bias"], di["b"], d["scale"], self.out, self.d_ns,
+                            use_qk_l2norm=True)
         self.h_out.copy_(self.out, non_blocking=True)
         self.h_ns.copy_(self.d_ns, non_blocking=True)
 
@@ -293,13 +295,15 @@ class PrefillWork:
         return h2d, d2h
 
     def e2e_step(self):
+        """Host inputs -> device -> the C-ABI entry point (gdn_prefill_launch, same flags as
+        the device-timed step) -> host outputs."""
         di = self.d_in
         for k_, t in self.h.items():
             di[k_].copy_(t, non_blocking=True)
         d = self.inp
-        self.pkg.prefill_kernel(di["q"], di["k"], di["v"], di.get("state"), d["A_log"], di["a"],
-                                d["dt_bias"], di["b"], di["cu_seqlens"], d["scale"], self.out,
-                                self.ns)
+        self.pkg.gdn_prefill(di["q"], di["k"], di["v"], di.get("state"), d["A_log"], di["a"],
+                             d["dt_bias"], di["b"], di["cu_seqlens"], d["scale"], self.out,
+                             self.ns, use_qk_l2norm=True)
         self.h_out.copy_(self.out, non_blocking=True)
         self.h_ns.copy_(self.ns, non_blocking=True)
 
