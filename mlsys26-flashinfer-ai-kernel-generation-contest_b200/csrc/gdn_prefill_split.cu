@@ -847,6 +847,11 @@ bool configure(uint32_t smem) {  // once per (kernel, device)
   if (dev >= 0 && dev < 64 && done[dev]) return true;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return false;
+  // all of the unified L1 / shared storage as shared memory (the preparation kernel
+  // relies on three CTAs per SM)
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return false;
   if (dev >= 0 && dev < 64) done[dev] = true;
   return true;
 }
