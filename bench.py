@@ -1,7 +1,8 @@
 """Benchmark of the GDN decode / prefill hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_b128|decode_b4|decode_b1024|prefill_p1|prefill_p2|prefill_p3]
+                    [--workload decode_b128|decode_b4|decode_b1024|prefill_p1|prefill_p2|prefill_p3|
+                                mtp_b128_t4]
 
 Prints ONE JSON line (rank 0).  Default workload: one GDN decode step over
 batch 128 (state 128 x 32 x 128 x 128 fp32 = 268 MB read + 268 MB written per
@@ -231,6 +232,58 @@ class DecodeWork:
         self.h_ns.copy_(self.d_ns, non_blocking=True)
 
 
+class MtpWork:
+    """One multi-token decode call: `batch` rows of MTP_T draft tokens against a resident
+    state pool (one slot per row, updated in place), with the rollback buffer that
+    receives the state after every token."""
+
+    def __init__(self, pkg, batch, dev, seed):
+        W = pkg.workloads
+        self.pkg, self.batch, self.dev = pkg, batch, dev
+        self.inp = W.mtp_inputs(batch, MTP_T, batch, seed=seed, device=str(dev))
+        d = self.inp
+        self.inter = torch.empty((batch, MTP_T) + tuple(d["state"].shape[1:]),
+                                 dtype=torch.float32, device=dev)
+        self.out = torch.empty_like(d["v"])
+        self.units = W.mtp_state_bytes(batch, MTP_T, intermediate=True)
+        self.launches = 1
+
+    def step(self):
+        d = self.inp
+        self.pkg.gdn_mtp(d["q"], d["k"], d["v"], d["state"], d["state_indices"], d["A_log"],
+                         d["a"], d["dt_bias"], d["b"], d["scale"], self.out, None, self.inter,
+                         use_qk_l2norm=True)
+
+    def host_copies(self):
+        d = self.inp
+        keys = ("q", "k", "v", "state", "state_indices", "a", "b")
+        self.h = {k_: d[k_].cpu().pin_memory() for k_ in keys}
+        self.d_in = {k_: torch.empty_like(d[k_]) for k_ in keys}
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h_state = torch.empty(d["state"].shape, dtype=torch.float32).pin_memory()
+        self.h_inter = torch.empty(self.inter.shape, dtype=torch.float32).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in self.h.values())
+        d2h = (self.h_out.numel() * 2 + self.h_state.numel() * 4 + self.h_inter.numel() * 4)
+        return h2d, d2h
+
+    def e2e_step(self):
+        """Host inputs and pool -> device -> gdn_mtp_launch -> output, pool and rollback
+        buffer back to the host."""
+        di = self.d_in
+        for k_, t in self.h.items():
+            di[k_].copy_(t, non_blocking=True)
+        d = self.inp
+        self.pkg.gdn_mtp(di["q"], di["k"], di["v"], di["state"], di["state_indices"],
+                         d["A_log"], di["a"], d["dt_bias"], di["b"], d["scale"], self.out, None,
+                         self.inter, use_qk_l2norm=True)
+        self.h_out.copy_(self.out, non_blocking=True)
+        self.h_state.copy_(di["state"], non_blocking=True)
+        self.h_inter.copy_(self.inter, non_blocking=True)
+
+
+MTP_T = 4  # draft tokens verified per row (speculative decoding)
+
+
 def prefill_plan(pkg, name, dist):
     """This rank's part of prefill config `name`: None at N=1; whole sequences
     (longest-first packing) when there are at least as many sequences as ranks;
@@ -404,6 +457,48 @@ def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True):
     return res
 
 
+def measure_mtp(pkg, dist, batch, steps, warmup, dev, with_e2e=True):
+    w = MtpWork(pkg, batch, dev, seed=dist.rank)
+    with ClockSampler(dev.index) as clk:
+        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+    total_bytes = w.units * dist.world
+    res = {"ms": ms, "kern_ms": kern_ms, "value": total_bytes / (ms * 1e-3) / 1e9,
+           "achieved": w.units / (kern_ms * 1e-3) / 1e9, "clocks": clk.summary(),
+           "launches": w.launches * steps, "units": w.units}
+    if with_e2e:
+        h2d, d2h = w.host_copies()
+        e2e_steps = max(3, min(steps, 10))
+        e_ms, _ = time_steps(w.e2e_step, e2e_steps, 2, dist, per_launch_events=False)
+        res["e2e"] = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "ms_per_step": e_ms, "steps": e2e_steps}
+    return res
+
+
+def cpu_baseline_mtp(batch, budget_s=10.0):
+    from oracle import gdn_oracle as O
+    pkg = importlib.import_module(PKG_NAME)
+    W = pkg.workloads
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = min(batch, 16)  # bounded sample: `rows` rows of the same workload
+    inp = W.mtp_inputs(rows, MTP_T, rows, seed=0)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+    reps, t_start = 0, time.perf_counter()
+    while True:
+        O.mtp(q, k, inp["v"], inp["state"], inp["state_indices"], inp["A_log"], inp["a"],
+              inp["dt_bias"], inp["b"], inp["scale"], intermediate=True)
+        reps += 1
+        el = time.perf_counter() - t_start
+        if el > budget_s or reps >= 5:
+            break
+    per = el / reps
+    gbs = W.mtp_state_bytes(rows, MTP_T, intermediate=True) / per / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} call(s) of {rows} rows x {MTP_T} tokens (oracle, fp32 torch CPU)",
+            "sec_per_step": per * batch / rows}
+
+
 def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True):
     w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard)
     with ClockSampler(dev.index) as clk:
@@ -442,6 +537,7 @@ WORKLOADS = {
     "decode_b4": ("decode", 4), "decode_b128": ("decode", 128), "decode_b1024": ("decode", 1024),
     "prefill_p1": ("prefill", "P1"), "prefill_p2": ("prefill", "P2"),
     "prefill_p3": ("prefill", "P3"),
+    "mtp_b128_t4": ("mtp", 128),
 }
 
 
@@ -464,6 +560,24 @@ def run_ours(args, dist):
                        "batch_per_gpu": param, "global_batch": param * dist.world,
                        "parallelism": f"batch-sharded x{dist.world}, no collective",
                        "l2": "inputs > L2: 537 MB state traffic per step, state ping-pong"},
+            "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
+            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
+            "kernel_ms": round(r["kern_ms"], 5),
+        })
+    elif kind == "mtp":
+        r = measure_mtp(pkg, dist, param, args.steps, args.warmup, dev)
+        line.update({
+            "metric": "mtp state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+            "config": {"workload": f"GDN multi-token decode, {param} rows x {MTP_T} tokens per "
+                                   f"GPU, 16 q/k + 32 v heads, fp32 k-last state pool updated "
+                                   f"in place, rollback buffer written per token, q/k "
+                                   f"L2-normalised in-kernel",
+                       "batch_per_gpu": param, "draft_tokens": MTP_T,
+                       "parallelism": f"batch-sharded x{dist.world}, no collective",
+                       "l2": f"inputs > L2: {r['units'] / 1e9:.2f} GB state traffic per step"},
             "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
             "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_ms": round(r["kern_ms"], 5),
@@ -501,6 +615,7 @@ def run_ours(args, dist):
         line["prefill"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = (cpu_baseline_decode(param) if kind == "decode"
+                                else cpu_baseline_mtp(param) if kind == "mtp"
                                 else cpu_baseline_prefill(param))
     return line
 
@@ -516,6 +631,12 @@ def run_reference(args, dist):
             steps.append(cpu_baseline_decode(param, budget_s=5.0))
         v = statistics.median(s["value"] for s in steps)
         metric, unit = "decode state-traffic GB/s", "GB/s"
+        ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3
+    elif kind == "mtp":
+        for _ in range(max(1, min(args.steps, 3))):
+            steps.append(cpu_baseline_mtp(param, budget_s=5.0))
+        v = statistics.median(s["value"] for s in steps)
+        metric, unit = "mtp state-traffic GB/s", "GB/s"
         ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3
     else:
         for _ in range(max(1, min(args.steps, 2))):

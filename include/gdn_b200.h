@@ -79,6 +79,34 @@ int gdn_decode_launch(const void* q, const void* k, const void* v, const float* 
                       int use_qk_l2norm, void* stream);
 
 /*
+ * Multi-token decode (speculative-decoding verification): `seq_len` tokens per batch
+ * row applied in order to the row's state in a pool, as the flashinfer-bench
+ * definition `_gdn_mtp_reference` does (flashinfer/trace/templates/gdn.py:379-466;
+ * FlashInfer's GPU API gated_delta_rule_mtp, flashinfer/gdn_decode.py:557).
+ *   q, k          bf16 [batch, seq_len, num_q_heads, 128]
+ *   v             bf16 [batch, seq_len, num_v_heads, 128]
+ *   initial_state fp32 [pool_size, num_v_heads, 128 (v), 128 (k)] (k-last pool)
+ *   state_indices int32 (state_indices_int64 == 0) or int64 [batch]: pool slot of each
+ *                 row; a slot outside [0, pool_size) marks a padding row (zero
+ *                 output, no state read or written)
+ *   A_log, dt_bias fp32 [num_v_heads];  a, b bf16 [batch, seq_len, num_v_heads]
+ *   output        bf16 [batch, seq_len, num_v_heads, 128]                 (written)
+ *   final_state   fp32 [pool_size, num_v_heads, 128, 128]: slot state_indices[i]
+ *                 receives row i's state after the last token; other slots are not
+ *                 touched.  May be initial_state (in-place pool update).
+ *   intermediate_states  fp32 [pool_size, seq_len, num_v_heads, 128, 128] or NULL:
+ *                 slot state_indices[i], token t receives the state after token t
+ * Rows must reference distinct slots (rows sharing a slot race on its final state).
+ * Each slot is read once and written once; q/k/v/gates are read once.
+ */
+int gdn_mtp_launch(const void* q, const void* k, const void* v, const float* initial_state,
+                   const void* state_indices, int state_indices_int64, const float* A_log,
+                   const void* a, const float* dt_bias, const void* b, float scale,
+                   void* output, float* final_state, float* intermediate_states, int batch,
+                   int seq_len, int pool_size, int num_q_heads, int num_k_heads,
+                   int num_v_heads, int head_size, int use_qk_l2norm, void* stream);
+
+/*
  * Bytes of device workspace gdn_prefill_launch needs for this problem (may be 0).
  */
 size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,

@@ -7,7 +7,9 @@ MLSys26 FlashInfer contest GDN track:
 * ``gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)``
 
 (``decode_kernel`` / ``prefill_kernel`` are the exact-arity DPS forms, also
-exposed as ``decode.kernel`` / ``prefill.kernel``).  All compute runs
+exposed as ``decode.kernel`` / ``prefill.kernel``), plus the multi-token decode of
+the ``gdn_mtp`` definition (``gdn_mtp`` / ``mtp_kernel``) for speculative-decoding
+verification over a state pool.  All compute runs
 in the in-tree CUDA library ``libgdn_b200.so`` through its C ABI
 (``include/gdn_b200.h``); importing this package fails if it is not built.
 
@@ -18,8 +20,10 @@ from ._lib import LIB, LIB_PATH, GDNError, device_error  # noqa: F401
 from .decode import gdn_decode, kernel as decode_kernel  # noqa: F401
 from .prefill import (gdn_prefill, gdn_prefill_recurrent, kernel as prefill_kernel,  # noqa: F401
                       workspace_bytes)
-from . import decode, prefill, sharding, workloads  # noqa: F401
+from .mtp import gdn_mtp, kernel as mtp_kernel  # noqa: F401
+from . import decode, mtp, prefill, sharding, workloads  # noqa: F401
 
-__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "decode_kernel",
+__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "gdn_mtp", "decode_kernel",
+           "mtp_kernel",
            "prefill_kernel", "workloads", "sharding", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
            "device_error"]

@@ -25,6 +25,8 @@ SIGNATURES = {
     "gdn_status_string": (ctypes.c_char_p, [_i]),
     "gdn_decode_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
                                _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_mtp_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp,
+                            _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "gdn_prefill_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp,
                                 _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),

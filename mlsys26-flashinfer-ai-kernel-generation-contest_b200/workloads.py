@@ -55,6 +55,43 @@ def decode_inputs(batch: int, *, hq: int = HQ, hv: int = HV, d: int = D, seed: i
     return out
 
 
+def mtp_inputs(batch: int, seq_len: int, pool_size: int, *, hq: int = HQ, hv: int = HV,
+               d: int = D, seed: int = 0, indices: Optional[Sequence[int]] = None,
+               index_dtype: torch.dtype = torch.int32,
+               device: str = "cpu") -> Dict[str, torch.Tensor]:
+    """Inputs of one multi-token decode (speculative verification) call: T tokens per
+    batch row and a k-last state pool [pool_size, HV, D, D].  ``indices`` maps batch rows
+    to pool slots (default: a seeded permutation of distinct slots, pool_size >= batch)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = {
+        "q": _randn((batch, seq_len, hq, d), g, torch.bfloat16, device),
+        "k": _randn((batch, seq_len, hq, d), g, torch.bfloat16, device),
+        "v": _randn((batch, seq_len, hv, d), g, torch.bfloat16, device),
+        "state": _randn((pool_size, hv, d, d), g, torch.float32, device, std=0.02),
+    }
+    u = torch.rand((hv,), generator=g, dtype=torch.float32, device=device)
+    out["A_log"] = torch.log(1.0 + 15.0 * u)
+    out["dt_bias"] = _randn((hv,), g, torch.float32, device, std=0.5)
+    out["a"] = _randn((batch, seq_len, hv), g, torch.bfloat16, device)
+    out["b"] = _randn((batch, seq_len, hv), g, torch.bfloat16, device)
+    if indices is None:
+        if pool_size < batch:
+            raise ValueError("default indices need pool_size >= batch")
+        perm = torch.randperm(pool_size, generator=torch.Generator().manual_seed(seed + 1))
+        indices = perm[:batch].tolist()
+    out["state_indices"] = torch.tensor(list(indices), dtype=index_dtype).to(device)
+    out["scale"] = 1.0 / math.sqrt(d)
+    return out
+
+
+def mtp_state_bytes(batch: int, seq_len: int, hv: int = HV, d: int = D,
+                    intermediate: bool = False) -> int:
+    """State bytes one multi-token decode call moves: each slot read and written once,
+    plus one state write per token with the intermediate-state buffer."""
+    per = hv * d * d * 4
+    return batch * per * (2 + (seq_len if intermediate else 0))
+
+
 def draw_seqlens(n: int, lo: int, hi: int, seed: int = 0) -> List[int]:
     """Sequence lengths ~ U[lo, hi] (inclusive), the first draw of a prefill config."""
     g = torch.Generator().manual_seed(seed)

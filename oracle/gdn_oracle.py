@@ -134,6 +134,47 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, *, dtype=torch.float32):
 
 
 @torch.no_grad()
+def mtp(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b, scale, *,
+        intermediate=False, dtype=torch.float32):
+    """Multi-token decode (speculative-decoding verification): the recurrence of
+    ``_gdn_mtp_reference`` (``flashinfer/trace/templates/gdn.py:379-466``), shapes as
+    ``gdn.py:469-560``, one decode step per token (:func:`decode`), batched over rows.
+
+    q/k [B,T,HQ,D], v [B,T,HV,D], initial_state [P,HV,D,D] fp32 k-last pool,
+    state_indices [B] int (pool slot of each row), A_log/dt_bias [HV], a/b [B,T,HV].
+    Returns (output [B,T,HV,D] bf16, final_state [P,HV,D,D] fp32 = the pool with the
+    rows' slots replaced by their state after T tokens, intermediate [P,T,HV,D,D] fp32
+    with the state after every token in the rows' slots (zeros elsewhere) or None).
+
+    Every row starts from the initial pool, as in the definition.  A row whose index
+    lies outside [0, P) is padding: zero output and no state change (the definition
+    would index the pool with Python's negative-index wrap; the kernels skip such rows).
+    """
+    B, T = q.shape[:2]
+    HV, D = v.shape[2], v.shape[3]
+    P = initial_state.shape[0]
+    final = initial_state.clone().float()
+    inter = torch.zeros((P, T) + tuple(initial_state.shape[1:]), dtype=torch.float32) \
+        if intermediate else None
+    out = torch.zeros(B, T, HV, D, dtype=torch.bfloat16)
+    idx = [int(i) for i in state_indices.tolist()]
+    rows = [r for r in range(B) if 0 <= idx[r] < P]
+    if not rows or T == 0:
+        return out, final, inter
+    sel = torch.tensor(rows, dtype=torch.long)
+    slots = torch.tensor([idx[r] for r in rows], dtype=torch.long)
+    S = initial_state[slots].float()
+    for t in range(T):
+        o, S = decode(q[sel, t:t + 1], k[sel, t:t + 1], v[sel, t:t + 1], S, A_log,
+                      a[sel, t:t + 1], dt_bias, b[sel, t:t + 1], scale, dtype=dtype)
+        out[sel, t] = o[:, 0]
+        if inter is not None:
+            inter[slots, t] = S
+    final[slots] = S
+    return out, final, inter
+
+
+@torch.no_grad()
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
             dtype=torch.float32):
     """Variable-length prefill.  Shapes as ``gdn.py:303-363``.

@@ -103,7 +103,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", required=True, type=pathlib.Path)
     args = ap.parse_args()
-    from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_prefill_reference
+    from flashinfer.trace.templates.gdn import (_gdn_decode_reference, _gdn_mtp_reference,
+                                                 _gdn_prefill_reference)
 
     W = _pkg_workloads()
     ref_triton = _reference_triton_decode(args.reference_root)
@@ -156,6 +157,31 @@ def main():
                                   "out": o, "new_state": s},
           {"scale": 0.0, "use_qk_l2norm": 0,
            "source": "flashinfer 0.6.11.post2 _gdn_prefill_reference"})
+
+    # ---- multi-token decode: GVA 1 -> 2, pool of 4, three rows, raw q/k, rollback buffer ----
+    inp = W.mtp_inputs(3, 3, 4, hq=1, hv=2, seed=15, indices=[3, 0, 2])
+    inter = torch.zeros(4, 3, 2, 128, 128, dtype=torch.float32)
+    o, s = _gdn_mtp_reference(inp["q"], inp["k"], inp["v"], inp["state"], inp["state_indices"],
+                              inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"],
+                              intermediate_states_buffer=inter)
+    _save("mtp_gva_inter", {**{k_: v_ for k_, v_ in inp.items() if k_ != "scale"},
+                            "out": o, "final_state": s, "intermediate": inter},
+          {"scale": inp["scale"], "use_qk_l2norm": 0,
+           "source": "flashinfer 0.6.11.post2 _gdn_mtp_reference"})
+
+    # ---- multi-token decode: int64 indices, default scale, host-normalised q/k ----
+    inp = W.mtp_inputs(2, 3, 2, hq=1, hv=2, seed=16, indices=[1, 0],
+                       index_dtype=torch.int64)
+    qn = inp["q"].float()
+    qn = qn * torch.rsqrt((qn * qn).sum(-1, keepdim=True) + 1e-6)
+    kn = inp["k"].float()
+    kn = kn * torch.rsqrt((kn * kn).sum(-1, keepdim=True) + 1e-6)
+    o, s = _gdn_mtp_reference(qn, kn, inp["v"], inp["state"], inp["state_indices"],
+                              inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], 0.0)
+    _save("mtp_l2", {**{k_: v_ for k_, v_ in inp.items() if k_ != "scale"},
+                     "out": o, "final_state": s},
+          {"scale": 0.0, "use_qk_l2norm": 1,
+           "source": "flashinfer 0.6.11.post2 _gdn_mtp_reference on host-normalised q/k"})
 
 
 if __name__ == "__main__":

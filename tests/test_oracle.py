@@ -53,6 +53,34 @@ def test_prefill_zero_state_raw_qk():
     assert ok
 
 
+@pytest.mark.parametrize("name,l2,inter", [("mtp_gva_inter", False, True), ("mtp_l2", True, False)])
+def test_mtp_matches_definition(name, l2, inter):
+    """Multi-token decode (pool slots, rollback buffer) against _gdn_mtp_reference."""
+    d, m = load_golden(name)
+    q, k = (O.l2norm(d["q"]), O.l2norm(d["k"])) if l2 else (d["q"], d["k"])
+    o, s, it = O.mtp(q, k, d["v"], d["state"], d["state_indices"], d["A_log"], d["a"],
+                     d["dt_bias"], d["b"], float(m["scale"]), intermediate=inter)
+    assert torch.equal(o, d["out"])
+    assert O.state_rel_err(s, d["final_state"]) < 1e-6
+    if inter:
+        assert O.state_rel_err(it, d["intermediate"]) < 1e-6
+        # slots no row references stay zero in the rollback buffer and initial in the pool
+        assert it[1].abs().max().item() == 0.0
+        assert torch.equal(s[1], d["state"][1])
+
+
+def test_mtp_padding_rows_and_single_token_equals_decode():
+    W = __import__("conftest").load_pkg().workloads
+    inp = W.mtp_inputs(3, 1, 4, hq=1, hv=2, seed=21, indices=[2, -1, 7])
+    o, s, _ = O.mtp(inp["q"], inp["k"], inp["v"], inp["state"], inp["state_indices"],
+                    inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+    assert o[1].abs().max().item() == 0.0 and o[2].abs().max().item() == 0.0
+    assert torch.equal(s[[0, 1, 3]], inp["state"][[0, 1, 3]])  # padding rows touch nothing
+    od, sd = O.decode(inp["q"][:1], inp["k"][:1], inp["v"][:1], inp["state"][2:3], inp["A_log"],
+                      inp["a"][:1], inp["dt_bias"], inp["b"][:1], inp["scale"])
+    assert torch.equal(o[:1], od) and torch.equal(s[2:3], sd)
+
+
 def test_oracle_fp32_vs_fp64():
     """The fp32 oracle is itself accurate: compare with its float64 evaluation."""
     d, m = load_golden("prefill_varlen_l2")
