@@ -192,6 +192,38 @@ int gdn_prefill_launch_variant(int variant, const void* q, const void* k, const 
                                void* stream);
 
 /*
+ * Prefill with the options of FlashInfer's chunk_gated_delta_rule
+ * (flashinfer/gdn_prefill.py:99-185), otherwise the gdn_prefill_launch_variant
+ * contract:
+ *   gate_mode 0: gates from A_log, a, dt_bias, b as in gdn_prefill_launch (g, beta
+ *                ignored);
+ *   gate_mode 1: precomputed fp32 [total_tokens, num_v_heads] decay g (alpha in [0, 1],
+ *                the forget gate itself) and beta; NULL means all ones; A_log, a,
+ *                dt_bias, b are ignored (may be NULL).
+ *   checkpoint_every_n_tokens = N > 0 (a multiple of 64): the state after every N tokens
+ *                of sequence i goes to state_checkpoints[checkpoint_cu_starts[i] + j]
+ *                (fp32 [num_v_heads, 128, 128] each, j < len_i / N); entries at or beyond
+ *                checkpoint_capacity are not written.  N = 0: no checkpoints (the three
+ *                checkpoint pointers may be NULL).
+ * With raw (un-normalised) q/k and either option, GDN_PREFILL_AUTO runs the split
+ * kernels and GDN_PREFILL_FUSED returns GDN_ERR_UNSUPPORTED.
+ */
+size_t gdn_prefill_workspace_size_ext(int variant, int total_tokens, int num_seqs,
+                                      int num_q_heads, int num_v_heads, int head_size,
+                                      int use_qk_l2norm, int gate_mode,
+                                      int checkpoint_every_n_tokens);
+int gdn_prefill_launch_ext(int variant, const void* q, const void* k, const void* v,
+                           const float* state, int gate_mode, const float* A_log, const void* a,
+                           const float* dt_bias, const void* b, const float* g,
+                           const float* beta, const void* cu_seqlens, int cu_seqlens_int64,
+                           float scale, void* output, float* new_state, float* state_checkpoints,
+                           const long long* checkpoint_cu_starts, long long checkpoint_capacity,
+                           int checkpoint_every_n_tokens, int total_tokens, int num_seqs,
+                           int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+                           int use_qk_l2norm, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
  * Allocation-free variant of gdn_prefill_launch (no counterpart in the
  * reference).  For callers that cannot allocate device memory where they
  * launch -- inside an allocator or memory-pool callback, under a runtime

@@ -9,7 +9,8 @@ MLSys26 FlashInfer contest GDN track:
 (``decode_kernel`` / ``prefill_kernel`` are the exact-arity DPS forms, also
 exposed as ``decode.kernel`` / ``prefill.kernel``), plus the multi-token decode of
 the ``gdn_mtp`` definition (``gdn_mtp`` / ``mtp_kernel``) for speculative-decoding
-verification over a state pool.  All compute runs
+verification over a state pool, and ``chunk_gated_delta_rule`` (FlashInfer's prefill
+argument order: precomputed gates, state checkpoints every N tokens).  All compute runs
 in the in-tree CUDA library ``libgdn_b200.so`` through its C ABI
 (``include/gdn_b200.h``); importing this package fails if it is not built.
 
@@ -18,12 +19,12 @@ The directory name is not a Python identifier; import it with
 """
 from ._lib import LIB, LIB_PATH, GDNError, device_error  # noqa: F401
 from .decode import gdn_decode, kernel as decode_kernel  # noqa: F401
-from .prefill import (gdn_prefill, gdn_prefill_recurrent, kernel as prefill_kernel,  # noqa: F401
-                      workspace_bytes)
+from .prefill import (chunk_gated_delta_rule, gdn_prefill, gdn_prefill_recurrent,  # noqa: F401
+                      kernel as prefill_kernel, workspace_bytes)
 from .mtp import gdn_mtp, kernel as mtp_kernel  # noqa: F401
 from . import decode, mtp, prefill, sharding, workloads  # noqa: F401
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "gdn_mtp", "decode_kernel",
-           "mtp_kernel",
+           "mtp_kernel", "chunk_gated_delta_rule",
            "prefill_kernel", "workloads", "sharding", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
            "device_error"]

@@ -37,6 +37,10 @@ SIGNATURES = {
     "gdn_prefill_workspace_size_variant": (_sz, [_i, _i, _i, _i, _i, _i]),
     "gdn_prefill_launch_variant": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
                                         _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_prefill_workspace_size_ext": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i, _i]),
+    "gdn_prefill_launch_ext": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    _vp, _i, _f, _vp, _vp, _vp, _vp, ctypes.c_longlong, _i, _i,
+                                    _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_device_error": (_i, [_i]),
 }
 

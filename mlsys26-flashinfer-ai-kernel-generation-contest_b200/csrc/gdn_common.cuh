@@ -31,6 +31,19 @@ __device__ __forceinline__ float gate_log_g(float A_log, float a, float dt_bias)
   return -expf(A_log) * softplus_f(a + dt_bias);
 }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// log of a precomputed decay alpha in [0, 1]; alpha = 0 (full forget) maps to
+// log(1e-38) ~ -87.5, whose exponential is 0 in fp32
+__device__ __forceinline__ float log_alpha(float alpha) { return logf(fmaxf(alpha, 1e-38f)); }
+
+// Slot of the checkpoint after `tokens` tokens of sequence n (every `every` tokens),
+// or -1 when none is due or it falls outside [0, capacity).
+__device__ __forceinline__ long long checkpoint_slot(const long long* starts, int n,
+                                                     long long tokens, int every,
+                                                     long long capacity) {
+  if (every <= 0 || tokens <= 0 || tokens % every != 0) return -1;
+  const long long ci = starts[n] + tokens / every - 1;
+  return (ci >= 0 && ci < capacity) ? ci : -1;
+}
 
 // Streaming 128-bit global accesses: the state is touched exactly once.
 __device__ __forceinline__ float4 ld_stream_f4(const float* p) {

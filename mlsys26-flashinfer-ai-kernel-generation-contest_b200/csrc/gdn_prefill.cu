@@ -24,8 +24,12 @@ bool auto_uses_split(long long T, int N, int HV) {
   return T > 0 && N > 0 && (long long)N * HV < kSplitBelowPairs;
 }
 
-size_t variant_workspace(int variant, long long T, int N, int HV) {
+// Precomputed gates or checkpoints with raw q/k: only the split kernels have both.
+bool ext_needs_split(bool l2norm, bool ext) { return ext && !l2norm; }
+
+size_t variant_workspace(int variant, long long T, int N, int HV, bool force_split = false) {
   if (T <= 0 || N <= 0) return 0;
+  if (force_split && variant == GDN_PREFILL_AUTO) variant = GDN_PREFILL_SPLIT;
   switch (variant) {
     case GDN_PREFILL_RECURRENT: return 0;
     case GDN_PREFILL_FUSED: return gdn::prefill_chunked_workspace(N);
@@ -45,6 +49,17 @@ extern "C" size_t gdn_prefill_workspace_size_variant(int variant, int total_toke
   return variant_workspace(variant, total_tokens, num_seqs, num_v_heads);
 }
 
+extern "C" size_t gdn_prefill_workspace_size_ext(int variant, int total_tokens, int num_seqs,
+                                                 int num_q_heads, int num_v_heads, int head_size,
+                                                 int use_qk_l2norm, int gate_mode,
+                                                 int checkpoint_every_n_tokens) {
+  (void)num_q_heads;
+  (void)head_size;
+  const bool ext = gate_mode != 0 || checkpoint_every_n_tokens > 0;
+  return variant_workspace(variant, total_tokens, num_seqs, num_v_heads,
+                           ext_needs_split(use_qk_l2norm != 0, ext));
+}
+
 extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,
                                              int num_v_heads, int head_size) {
   return gdn_prefill_workspace_size_variant(GDN_PREFILL_AUTO, total_tokens, num_seqs,
@@ -52,12 +67,23 @@ extern "C" size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int
 }
 
 namespace {
+struct PrefillExt {
+  bool gates_pre = false;
+  const float* g_alpha = nullptr;
+  const float* g_beta = nullptr;
+  float* ckpt = nullptr;
+  const long long* ckpt_starts = nullptr;
+  long long ckpt_capacity = 0;
+  int ckpt_every = 0;
+};
+
 int prefill_entry(int variant, const void* q, const void* k, const void* v, const float* state,
                   const float* A_log, const void* a, const float* dt_bias, const void* b,
                   const void* cu_seqlens, int cu_seqlens_int64, float scale, void* output,
                   float* new_state, int total_tokens, int num_seqs, int num_q_heads,
                   int num_k_heads, int num_v_heads, int head_size, int use_qk_l2norm,
-                  void* workspace, size_t workspace_bytes, void* stream) {
+                  void* workspace, size_t workspace_bytes, void* stream,
+                  const PrefillExt& ext = PrefillExt{}) {
   using namespace gdn;
   if (variant < GDN_PREFILL_AUTO || variant > GDN_PREFILL_SPLIT) return GDN_ERR_INVALID_ARGUMENT;
   if (total_tokens < 0 || num_seqs < 0 || num_q_heads <= 0 || num_k_heads <= 0 ||
@@ -66,26 +92,47 @@ int prefill_entry(int variant, const void* q, const void* k, const void* v, cons
   if (head_size != kHeadDim || num_k_heads != num_q_heads || num_v_heads % num_q_heads != 0)
     return GDN_ERR_UNSUPPORTED;
   if (num_seqs == 0) return GDN_OK;
-  if (!cu_seqlens || !A_log || !dt_bias || !new_state) return GDN_ERR_INVALID_ARGUMENT;
-  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !output)) return GDN_ERR_INVALID_ARGUMENT;
+  if (!cu_seqlens || !new_state) return GDN_ERR_INVALID_ARGUMENT;
+  if (!ext.gates_pre && (!A_log || !dt_bias)) return GDN_ERR_INVALID_ARGUMENT;
+  if (total_tokens > 0 && (!q || !k || !v || !output || (!ext.gates_pre && (!a || !b))))
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (ext.ckpt_every < 0 || (ext.ckpt_every > 0 && (ext.ckpt_every % 64 != 0 || !ext.ckpt ||
+                                                    !ext.ckpt_starts || ext.ckpt_capacity < 0)))
+    return GDN_ERR_INVALID_ARGUMENT;
+  if ((ext.g_alpha && misaligned(ext.g_alpha, 4)) || (ext.g_beta && misaligned(ext.g_beta, 4)) ||
+      (ext.ckpt && misaligned(ext.ckpt, 16)) || (ext.ckpt_starts && misaligned(ext.ckpt_starts, 8)))
+    return GDN_ERR_INVALID_ARGUMENT;
+  const bool has_ext = ext.gates_pre || ext.ckpt_every > 0;
+  const bool need_split = ext_needs_split(use_qk_l2norm != 0, has_ext);
+  if (need_split && variant == GDN_PREFILL_FUSED) return GDN_ERR_UNSUPPORTED;
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(new_state, 16) ||
       (state && misaligned(state, 16)) || misaligned(cu_seqlens, cu_seqlens_int64 ? 8 : 4))
     return GDN_ERR_INVALID_ARGUMENT;
   if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
-  const size_t need = variant_workspace(variant, total_tokens, num_seqs, num_v_heads);
+  const size_t need = variant_workspace(variant, total_tokens, num_seqs, num_v_heads, need_split);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
 
   PrefillArgs p{q,        k,     v,      state,      A_log,        a,           dt_bias,
                 b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,
                 (long long)total_tokens, num_seqs, num_q_heads, num_v_heads,
                 use_qk_l2norm != 0, workspace, workspace_bytes};
+  p.gates_pre = ext.gates_pre;
+  p.g_alpha = ext.g_alpha;
+  p.g_beta = ext.g_beta;
+  if (ext.ckpt_every > 0) {
+    p.ckpt = ext.ckpt;
+    p.ckpt_starts = ext.ckpt_starts;
+    p.ckpt_capacity = ext.ckpt_capacity;
+    p.ckpt_every = ext.ckpt_every;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool chunked_ok = total_tokens > 0 && prefill_chunked_supported(p);
   int kind = variant;
   if (kind == GDN_PREFILL_AUTO)
     kind = !chunked_ok ? GDN_PREFILL_RECURRENT
-                       : (auto_uses_split(total_tokens, num_seqs, num_v_heads) ? GDN_PREFILL_SPLIT
-                                                                              : GDN_PREFILL_FUSED);
+                       : ((need_split || auto_uses_split(total_tokens, num_seqs, num_v_heads))
+                              ? GDN_PREFILL_SPLIT
+                              : GDN_PREFILL_FUSED);
   if ((kind == GDN_PREFILL_FUSED || kind == GDN_PREFILL_SPLIT) && !chunked_ok) {
     if (total_tokens > 0) return GDN_ERR_UNSUPPORTED;
     kind = GDN_PREFILL_RECURRENT;  // no tokens: only the zero final states to write
@@ -136,6 +183,29 @@ extern "C" int gdn_prefill_launch_variant(
                        cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
                        num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
                        workspace_bytes, stream);
+}
+
+extern "C" int gdn_prefill_launch_ext(
+    int variant, const void* q, const void* k, const void* v, const float* state, int gate_mode,
+    const float* A_log, const void* a, const float* dt_bias, const void* b, const float* g,
+    const float* beta, const void* cu_seqlens, int cu_seqlens_int64, float scale, void* output,
+    float* new_state, float* state_checkpoints, const long long* checkpoint_cu_starts,
+    long long checkpoint_capacity, int checkpoint_every_n_tokens, int total_tokens, int num_seqs,
+    int num_q_heads, int num_k_heads, int num_v_heads, int head_size, int use_qk_l2norm,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  if (gate_mode != 0 && gate_mode != 1) return GDN_ERR_INVALID_ARGUMENT;
+  PrefillExt ext;
+  ext.gates_pre = gate_mode == 1;
+  ext.g_alpha = g;
+  ext.g_beta = beta;
+  ext.ckpt = state_checkpoints;
+  ext.ckpt_starts = checkpoint_cu_starts;
+  ext.ckpt_capacity = checkpoint_capacity;
+  ext.ckpt_every = checkpoint_every_n_tokens;
+  return prefill_entry(variant, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                       cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
+                       num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
+                       workspace_bytes, stream, ext);
 }
 
 extern "C" int gdn_device_error(int clear) {

@@ -28,6 +28,18 @@ struct PrefillArgs {
   bool l2norm;
   void* workspace;
   size_t workspace_bytes;
+  // precomputed gates instead of (A_log, a, b, dt_bias): fp32 [T, HV] decay alpha = g
+  // and beta, a null pointer meaning all ones
+  bool gates_pre = false;
+  const float* g_alpha = nullptr;
+  const float* g_beta = nullptr;
+  // state after every ckpt_every tokens of each sequence (0 = off) into
+  // ckpt[ckpt_starts[n] + i] (fp32 [HV, 128, 128] each), i < len_n / ckpt_every;
+  // indices outside [0, ckpt_capacity) are not written
+  float* ckpt = nullptr;
+  const long long* ckpt_starts = nullptr;
+  long long ckpt_capacity = 0;
+  int ckpt_every = 0;
 };
 
 // Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).

@@ -124,6 +124,16 @@ struct ChunkedParams {
   int HV;
   int ratio;
   float scale;
+  // precomputed gates (fp32 [T, HV] decay and beta, null = 1) instead of a / b
+  // (pipelined kernel only)
+  bool gates_pre;
+  const float* g_alpha;
+  const float* g_beta;
+  // state checkpoints every ckpt_every tokens (0 = off; pipelined kernel only)
+  float* ckpt;
+  const long long* ckpt_starts;
+  long long ckpt_cap;
+  int ckpt_every;
 };
 
 // All threads wait on `bar`; returns false on every thread if any thread timed out.
@@ -834,8 +844,8 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
   const int nchunks = (int)((L + kC - 1) / kC);
-  const float nexpA = -expf(__ldg(p.A_log + h));
-  const float dtb = __ldg(p.dt_bias + h);
+  const float nexpA = p.gates_pre ? 0.f : -expf(__ldg(p.A_log + h));
+  const float dtb = p.gates_pre ? 0.f : __ldg(p.dt_bias + h);
   bool ok = true;
   // async work issued but not yet waited for (drained, boundedly, if a wait runs out)
   uint64_t* pend_bar[2] = {nullptr, nullptr};
@@ -874,8 +884,13 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         const int t = 2 * lane + e;
         if (t < Lcc) {
           const size_t ti = (size_t)(tc0 + t) * HV + h;
-          ga[e] = ra[ti];
-          gb[e] = rb[ti];
+          if (p.gates_pre) {  // fp32 bits of the precomputed decay and beta
+            ga[e] = p.g_alpha ? __float_as_uint(p.g_alpha[ti]) : 0x3F800000u;
+            gb[e] = p.g_beta ? __float_as_uint(p.g_beta[ti]) : 0x3F800000u;
+          } else {            // bf16 bits of a and b
+            ga[e] = ra[ti];
+            gb[e] = rb[ti];
+          }
         }
       }
     };
@@ -890,8 +905,13 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const bool valid = 2 * lane + e < Lcc;
-        lg[e] = valid ? nexpA * softplus_f(__uint_as_float(ga[e] << 16) + dtb) : 0.f;
-        bb[e] = valid ? sigmoid_f(__uint_as_float(gb[e] << 16)) : 0.f;
+        if (p.gates_pre) {
+          lg[e] = valid ? log_alpha(__uint_as_float(ga[e])) : 0.f;
+          bb[e] = valid ? __uint_as_float(gb[e]) : 0.f;
+        } else {
+          lg[e] = valid ? nexpA * softplus_f(__uint_as_float(ga[e] << 16) + dtb) : 0.f;
+          bb[e] = valid ? sigmoid_f(__uint_as_float(gb[e] << 16)) : 0.f;
+        }
       }
       float x = lg[0] + lg[1];
 #pragma unroll
@@ -1324,12 +1344,23 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       tc_fence_after();
       // epilogue: S(c+1) -> bf16 hi/lo in TMEM (or the final state to global); O -> staging
       const bool last = c + 1 == nchunks;
+      // state checkpoint after this chunk, when one is due
+      const long long ci = p.ckpt == nullptr ? -1
+          : checkpoint_slot(p.ckpt_starts, n, min((long long)kC * (c + 1), L), p.ckpt_every,
+                            p.ckpt_cap);
       {
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           float sv[32];
           tmem_ld32(tl + TS + 64u * half + 32u * part, sv);
           tmem_wait_ld();
+          if (ci >= 0) {
+            float* cp = p.ckpt + (((size_t)ci * HV + h) * kHeadDim + row) * kHeadDim +
+                        64 * half + 32 * part;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_stream_f4(cp + i, make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]));
+          }
           if (last) {
             float* dst = nsbase + (size_t)row * kHeadDim + 64 * half + 32 * part;
 #pragma unroll
@@ -1523,7 +1554,11 @@ cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st) {
   ChunkedParams cp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
                    p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
                    static_cast<__nv_bfloat16*>(p.out), order, p.T, p.cu_int64 ? 1 : 0, p.HV,
-                   p.HV / p.HQ, p.scale};
+                   p.HV / p.HQ, p.scale, p.gates_pre, p.g_alpha, p.g_beta, p.ckpt,
+                   p.ckpt_starts, p.ckpt_capacity, p.ckpt_every};
+  if (!p.l2norm && (p.gates_pre || p.ckpt != nullptr))
+    return cudaErrorInvalidValue;  // the raw-q/k fused kernel has neither (the entry routes
+                                   // such calls to the split kernels)
   if (p.l2norm) {  // warp-specialised, pipelined kernel
     const bool hs = p.state != nullptr;
     if (p.cu_int64)

@@ -23,9 +23,19 @@ struct TokIn {
   float v, a, b;
 };
 
+// Per-token gate inputs: the raw projections (a, b) or precomputed decay / beta (fp32,
+// null = 1).  `a`/`b` then hold alpha and beta themselves.
+struct GateSrc {
+  const __nv_bfloat16* a;
+  const __nv_bfloat16* b;
+  const float* alpha;
+  const float* beta;
+  bool pre;
+};
+
 __device__ __forceinline__ void load_tok(TokIn& t, const __nv_bfloat16* q, const __nv_bfloat16* k,
-                                         const __nv_bfloat16* v, const __nv_bfloat16* a,
-                                         const __nv_bfloat16* b, long long tok, int HQ, int HV,
+                                         const __nv_bfloat16* v, const GateSrc& gs,
+                                         long long tok, int HQ, int HV,
                                          int qh, int h, int row, int j) {
   const __nv_bfloat16* qp = q + ((size_t)tok * HQ + qh) * kHeadDim + 4 * j;
   const __nv_bfloat16* kp = k + ((size_t)tok * HQ + qh) * kHeadDim + 4 * j;
@@ -35,8 +45,14 @@ __device__ __forceinline__ void load_tok(TokIn& t, const __nv_bfloat16* q, const
     t.k[m] = __ldg(reinterpret_cast<const uint2*>(kp + 32 * m));
   }
   t.v = bf2f(v[((size_t)tok * HV + h) * kHeadDim + row]);
-  t.a = bf2f(a[(size_t)tok * HV + h]);
-  t.b = bf2f(b[(size_t)tok * HV + h]);
+  const size_t ti = (size_t)tok * HV + h;
+  if (gs.pre) {
+    t.a = gs.alpha ? __ldg(gs.alpha + ti) : 1.f;
+    t.b = gs.beta ? __ldg(gs.beta + ti) : 1.f;
+  } else {
+    t.a = bf2f(gs.a[ti]);
+    t.b = bf2f(gs.b[ti]);
+  }
 }
 
 template <bool L2NORM, bool HAS_STATE, typename CuT>
@@ -48,7 +64,11 @@ __global__ void __launch_bounds__(128)
                              const float* __restrict__ dt_bias,
                              const __nv_bfloat16* __restrict__ b, const CuT* __restrict__ cu,
                              float scale, __nv_bfloat16* __restrict__ out, float* new_state,
-                             long long T, int HQ, int HV, int ratio, int seq_offset) {
+                             long long T, int HQ, int HV, int ratio, int seq_offset,
+                             const float* __restrict__ g_alpha, const float* __restrict__ g_beta,
+                             bool gates_pre, float* __restrict__ ckpt,
+                             const long long* __restrict__ ckpt_starts, long long ckpt_cap,
+                             int ckpt_every) {
   constexpr int VT = kHeadDim / kRecRows;
   const int cta = blockIdx.x;
   const int vt = cta % VT;
@@ -73,14 +93,15 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int m = 0; m < 4; ++m) S[m] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  const float nexpA = -expf(__ldg(A_log + h));
-  const float dtb = __ldg(dt_bias + h);
+  const float nexpA = gates_pre ? 0.f : -expf(__ldg(A_log + h));
+  const float dtb = gates_pre ? 0.f : __ldg(dt_bias + h);
   scale = default_scale(scale);
+  const GateSrc gs{a, b, g_alpha, g_beta, gates_pre};
 
   TokIn cur, nxt;
-  if (s1 > s0) load_tok(cur, q, k, v, a, b, s0, HQ, HV, qh, h, row, j);
+  if (s1 > s0) load_tok(cur, q, k, v, gs, s0, HQ, HV, qh, h, row, j);
   for (long long t = s0; t < s1; ++t) {
-    if (t + 1 < s1) load_tok(nxt, q, k, v, a, b, t + 1, HQ, HV, qh, h, row, j);
+    if (t + 1 < s1) load_tok(nxt, q, k, v, gs, t + 1, HQ, HV, qh, h, row, j);
     float kf[16], qf[16];
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -90,8 +111,8 @@ __global__ void __launch_bounds__(128)
       f = bf2x2_to_f2(cur.q[m].x); qf[4 * m] = f.x; qf[4 * m + 1] = f.y;
       f = bf2x2_to_f2(cur.q[m].y); qf[4 * m + 2] = f.x; qf[4 * m + 3] = f.y;
     }
-    const float g = expf(nexpA * softplus_f(cur.a + dtb));
-    const float beta = sigmoid_f(cur.b);
+    const float g = gates_pre ? cur.a : expf(nexpA * softplus_f(cur.a + dtb));
+    const float beta = gates_pre ? cur.b : sigmoid_f(cur.b);
     float kq = 0.f, sk = 0.f, sq = 0.f, ssk = 0.f, ssq = 0.f;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -133,6 +154,14 @@ __global__ void __launch_bounds__(128)
     if (j == 0)
       out[((size_t)t * HV + h) * kHeadDim + row] =
           __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
+    if (ckpt != nullptr) {
+      const long long ci = checkpoint_slot(ckpt_starts, n, t - s0 + 1, ckpt_every, ckpt_cap);
+      if (ci >= 0) {
+        float* cp = ckpt + ((size_t)ci * HV + h) * kHeadDim * kHeadDim + (size_t)row * kHeadDim + 4 * j;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) st_stream_f4(cp + 32 * m, S[m]);
+      }
+    }
     cur = nxt;
   }
 #pragma unroll
@@ -153,7 +182,8 @@ cudaError_t launch_rec_t(const PrefillArgs& p, const CuT* cu, int seq_offset, in
 #define GDN_REC_LAUNCH(L2, HS)                                                              \
   prefill_recurrent_kernel<L2, HS, CuT><<<grid, block, 0, st>>>(                            \
       Q, K, V, p.state, p.A_log, A, p.dt_bias, Bt, cu, p.scale, O, p.new_state, p.T, p.HQ,    \
-      p.HV, ratio, seq_offset)
+      p.HV, ratio, seq_offset, p.g_alpha, p.g_beta, p.gates_pre, p.ckpt, p.ckpt_starts,        \
+      p.ckpt_capacity, p.ckpt_every)
   if (p.state) {
     if (p.l2norm) GDN_REC_LAUNCH(true, true); else GDN_REC_LAUNCH(false, true);
   } else {

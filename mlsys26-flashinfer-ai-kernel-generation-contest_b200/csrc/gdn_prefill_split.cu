@@ -87,6 +87,15 @@ struct SplitParams {
   int HV;
   int ratio;
   float scale;
+  // precomputed gates (fp32 [T, HV] decay and beta, null = 1) instead of a / b
+  bool gates_pre;
+  const float* g_alpha;
+  const float* g_beta;
+  // state checkpoints every ckpt_every tokens (0 = off)
+  float* ckpt;
+  const long long* ckpt_starts;
+  long long ckpt_cap;
+  int ckpt_every;
 };
 
 template <typename CuT>
@@ -212,16 +221,27 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     tma_load_2d(smem + KQ + 24576, &tm_q, &bars[0], qh * 128 + 64, (int)t0);
   }
   if (warp == 1) {  // gates: cumulative log decay, beta, gamma
-    const float nexpA = -expf(__ldg(p.A_log + h));
-    const float dtb = __ldg(p.dt_bias + h);
     float lg[2], bb[2];
+    if (p.gates_pre) {
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int t = 2 * lane + e;
-      const bool valid = t < Lc;
-      const size_t ti = (size_t)(t0 + (valid ? t : 0)) * p.HV + h;
-      lg[e] = valid ? nexpA * softplus_f(bf2f(p.a[ti]) + dtb) : 0.f;
-      bb[e] = valid ? sigmoid_f(bf2f(p.b[ti])) : 0.f;
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * lane + e;
+        const bool valid = t < Lc;
+        const size_t ti = (size_t)(t0 + (valid ? t : 0)) * p.HV + h;
+        lg[e] = valid ? log_alpha(p.g_alpha ? __ldg(p.g_alpha + ti) : 1.f) : 0.f;
+        bb[e] = valid ? (p.g_beta ? __ldg(p.g_beta + ti) : 1.f) : 0.f;
+      }
+    } else {
+      const float nexpA = -expf(__ldg(p.A_log + h));
+      const float dtb = __ldg(p.dt_bias + h);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * lane + e;
+        const bool valid = t < Lc;
+        const size_t ti = (size_t)(t0 + (valid ? t : 0)) * p.HV + h;
+        lg[e] = valid ? nexpA * softplus_f(bf2f(p.a[ti]) + dtb) : 0.f;
+        bb[e] = valid ? sigmoid_f(bf2f(p.b[ti])) : 0.f;
+      }
     }
     float x = lg[0] + lg[1];
 #pragma unroll
@@ -798,6 +818,15 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i) sv[i] += s2[i];
+        if (p.ckpt != nullptr) {  // state checkpoint after this chunk, when one is due
+          const long long ci = checkpoint_slot(p.ckpt_starts, n, min((long long)kC * (c + 1), L),
+                                               p.ckpt_every, p.ckpt_cap);
+          if (ci >= 0) {
+            float* cp = p.ckpt + ((size_t)ci * HV + h) * kHeadDim * kHeadDim;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) cp[(size_t)(v_lo + i) * kHeadDim + row] = sv[i];
+          }
+        }
         if (c + 1 == nchunks) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = sv[i];
@@ -923,7 +952,8 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
                  static_cast<__nv_bfloat16*>(p.out), order,
                  reinterpret_cast<const int*>(ws + lay.base), ws + lay.rec,
                  rec_bytes(p.l2norm), rec_lo_bytes(p.l2norm), p.T, p.N, p.HV, p.HV / p.HQ,
-                 p.scale};
+                 p.scale, p.gates_pre, p.g_alpha, p.g_beta, p.ckpt, p.ckpt_starts,
+                 p.ckpt_capacity, p.ckpt_every};
   if (p.cu_int64)
     return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
   return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);

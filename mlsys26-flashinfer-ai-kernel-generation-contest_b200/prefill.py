@@ -168,3 +168,91 @@ def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_
     """flashinfer-bench DPS entry point (12 parameters, no normalisation)."""
     return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                        new_state)
+
+
+def chunk_gated_delta_rule(q, k, v, g=None, beta=None, scale=None, initial_state=None,
+                           output_final_state: bool = False, cu_seqlens=None,
+                           use_qk_l2norm_in_kernel: bool = False, output=None, output_state=None,
+                           state_checkpoints=None, checkpoint_cu_starts=None,
+                           checkpoint_every_n_tokens: int = 0, *, kernel: str = "auto"):
+    """Prefill with precomputed gates and optional state checkpoints, in the argument
+    order and meaning of FlashInfer's ``chunk_gated_delta_rule``
+    (flashinfer/gdn_prefill.py:99-185).
+
+    ``g`` is the decay itself (alpha in [0, 1]) and ``beta`` the update gate, both fp32
+    [T, num_v_heads]; None means all ones.  ``cu_seqlens`` (int32 or int64) None means one
+    sequence of all T tokens.  With ``checkpoint_every_n_tokens`` = N > 0 (a multiple of
+    64) the state after every N tokens of sequence i is written to
+    ``state_checkpoints[checkpoint_cu_starts[i] + j]`` (``checkpoint_cu_starts`` int64
+    [num_seqs + 1], the prefix sums of len_i // N).  Returns ``output`` or
+    ``(output, final_state)`` when ``output_final_state``.
+    """
+    if kernel not in KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(KERNELS)}, got {kernel!r}")
+    dev = C.cuda_device(q)
+    C.tensor("q", q, torch.bfloat16, 3, dev)
+    C.tensor("k", k, torch.bfloat16, 3, dev)
+    C.tensor("v", v, torch.bfloat16, 3, dev)
+    T, HQ, D = q.shape
+    HK, HV = k.shape[1], v.shape[1]
+    C.heads(HQ, HK, HV, D)
+    C.shape("k", k, (T, HK, D))
+    C.shape("v", v, (T, HV, D))
+    for name, x in (("g", g), ("beta", beta)):
+        if x is not None:
+            C.tensor(name, x, torch.float32, 2, dev)
+            C.shape(name, x, (T, HV))
+    if cu_seqlens is None:
+        cu_seqlens = torch.tensor([0, T], dtype=torch.int64, device=dev)
+    if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dtype not in (torch.int32,
+                                                                             torch.int64):
+        raise TypeError("cu_seqlens must be an int32 or int64 tensor")
+    if cu_seqlens.dim() != 1 or cu_seqlens.device != dev or not cu_seqlens.is_contiguous():
+        raise ValueError("cu_seqlens must be a contiguous 1-D tensor on the same device as q")
+    N = cu_seqlens.numel() - 1
+    if initial_state is not None:
+        C.tensor("initial_state", initial_state, torch.float32, 4, dev)
+        C.shape("initial_state", initial_state, (N, HV, D, D))
+    sc = C.scale_arg(scale)
+    if output is None:
+        output = torch.empty(T, HV, D, dtype=torch.bfloat16, device=dev)
+    else:
+        C.tensor("output", output, torch.bfloat16, 3, dev)
+        C.shape("output", output, (T, HV, D))
+    if output_state is None:
+        output_state = torch.empty(max(N, 0), HV, D, D, dtype=torch.float32, device=dev)
+    else:
+        C.tensor("output_state", output_state, torch.float32, 4, dev)
+        C.shape("output_state", output_state, (N, HV, D, D))
+    every = int(checkpoint_every_n_tokens)
+    cap = 0
+    if every < 0 or (every > 0 and every % 64 != 0):
+        raise ValueError("checkpoint_every_n_tokens must be 0 or a positive multiple of 64")
+    if every > 0:
+        if state_checkpoints is None or checkpoint_cu_starts is None:
+            raise ValueError("checkpoints need state_checkpoints and checkpoint_cu_starts")
+        C.tensor("state_checkpoints", state_checkpoints, torch.float32, 4, dev)
+        if tuple(state_checkpoints.shape[1:]) != (HV, D, D):
+            raise ValueError(f"state_checkpoints must be [n, {HV}, {D}, {D}]")
+        C.tensor("checkpoint_cu_starts", checkpoint_cu_starts, torch.int64, 1, dev)
+        C.shape("checkpoint_cu_starts", checkpoint_cu_starts, (N + 1,))
+        cap = state_checkpoints.shape[0]
+    if N > 0:
+        ws_n = int(LIB.gdn_prefill_workspace_size_ext(KERNELS[kernel], T, N, HQ, HV, D,
+                                                      int(bool(use_qk_l2norm_in_kernel)), 1,
+                                                      every))
+        ws = _workspace(dev, ws_n) if ws_n > 0 else None
+        status = LIB.gdn_prefill_launch_ext(
+            KERNELS[kernel], q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            initial_state.data_ptr() if initial_state is not None else None, 1,
+            None, None, None, None,
+            g.data_ptr() if g is not None else None, beta.data_ptr() if beta is not None else None,
+            cu_seqlens.data_ptr(), int(cu_seqlens.dtype == torch.int64), sc, output.data_ptr(),
+            output_state.data_ptr(),
+            state_checkpoints.data_ptr() if every > 0 else None,
+            checkpoint_cu_starts.data_ptr() if every > 0 else None, cap, every,
+            T, N, HQ, HK, HV, D, int(bool(use_qk_l2norm_in_kernel)),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            C.stream_handle(dev))
+        check(f"gdn_prefill_launch_ext({kernel})", status)
+    return (output, output_state) if output_final_state else output

@@ -185,13 +185,37 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
 
     Token loop per sequence, vectorised over heads (``gdn.py:228-271``).
     """
+    g, beta = gates(A_log, a, dt_bias, b)                      # [T,HV]
+    out, new_state, _ = _prefill_core(q, k, v, state, g, beta, cu_seqlens, scale, dtype, 0)
+    return out, new_state
+
+
+@torch.no_grad()
+def prefill_gated(q, k, v, state, alpha, beta, cu_seqlens, scale, *, checkpoint_every=0,
+                  dtype=torch.float32):
+    """Prefill with precomputed per-token gates and optional state checkpoints, the
+    contract of FlashInfer's ``chunk_gated_delta_rule`` (``flashinfer/gdn_prefill.py:99-185``):
+    alpha = the decay g itself and beta, fp32 [T, HV] (None = all ones); with
+    ``checkpoint_every`` = N > 0 the state after every N tokens of each sequence is
+    returned, ``len // N`` per sequence in sequence order.
+
+    Same recurrence as :func:`prefill` with g, beta given instead of computed.
+    Returns (output, new_state, checkpoints [sum(len // N), HV, D, D] fp32 or None).
+    """
+    T, HV = q.shape[0], v.shape[1]
+    g = alpha.float() if alpha is not None else torch.ones(T, HV)
+    bt = beta.float() if beta is not None else torch.ones(T, HV)
+    return _prefill_core(q, k, v, state, g, bt, cu_seqlens, scale, dtype, checkpoint_every)
+
+
+def _prefill_core(q, k, v, state, g, beta, cu_seqlens, scale, dtype, checkpoint_every):
+    """Token loop per sequence, vectorised over heads (``gdn.py:228-271``)."""
     T, HQ, D = q.shape
     HK = k.shape[1]
     HV = v.shape[1]
     H = max(HQ, HV)
     N = int(cu_seqlens.numel()) - 1
     sc = _default_scale(scale, D)
-    g, beta = gates(A_log, a, dt_bias, b)                      # [T,HV]
     g = g.to(dtype)
     beta = beta.to(dtype)
     qe = q.to(dtype).repeat_interleave(HV // HQ, dim=1)        # [T,HV,D]
@@ -199,6 +223,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
     ve = v.to(dtype)
     out = torch.zeros(T, H, D, dtype=torch.bfloat16)
     new_state = torch.zeros(N, H, D, D, dtype=torch.float32)
+    ckpts = []
     cu = [int(x) for x in cu_seqlens.tolist()]
     for n in range(N):
         s0, s1 = cu[n], cu[n + 1]
@@ -214,8 +239,13 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
             delta = beta[t][:, None] * (ve[t] - old)
             S.add_(delta[:, :, None] * ke[t][:, None, :])
             out[t, :HV] = (sc * torch.einsum("hvk,hk->hv", S, qe[t])).to(torch.bfloat16)
+            if checkpoint_every > 0 and (t - s0 + 1) % checkpoint_every == 0:
+                ckpts.append(S.float().clone())
         new_state[n, :HV] = S.float()
-    return out, new_state
+    ck = None
+    if checkpoint_every > 0:
+        ck = torch.stack(ckpts) if ckpts else torch.zeros(0, HV, D, D)
+    return out, new_state, ck
 
 
 def flashinfer_allclose(actual: torch.Tensor, expected: torch.Tensor,

@@ -81,6 +81,29 @@ def test_mtp_padding_rows_and_single_token_equals_decode():
     assert torch.equal(o[:1], od) and torch.equal(s[2:3], sd)
 
 
+def test_prefill_gated_and_checkpoints_restate_prefill():
+    """Precomputed gates (the definition's g, beta) reproduce prefill exactly, and each
+    checkpoint is the final state of the matching prefix."""
+    W = __import__("conftest").load_pkg().workloads
+    lens = [130, 0, 64, 70]
+    inp = W.prefill_inputs(lens, hq=1, hv=2, seed=22)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+    o, s = O.prefill(q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+                     inp["b"], inp["cu_seqlens"], inp["scale"])
+    g, beta = O.gates(inp["A_log"], inp["a"], inp["dt_bias"], inp["b"])
+    og, sg, ck = O.prefill_gated(q, k, inp["v"], inp["state"], g, beta, inp["cu_seqlens"],
+                                 inp["scale"], checkpoint_every=64)
+    assert torch.equal(o, og) and torch.equal(s, sg)
+    assert ck.shape[0] == sum(n // 64 for n in lens) == 4
+    # checkpoint 1 = state of sequence 0 after 128 tokens
+    cu = torch.tensor([0, 128], dtype=torch.int32)
+    _, s128 = O.prefill(q[:128], k[:128], inp["v"][:128], inp["state"][:1], inp["A_log"],
+                        inp["a"][:128], inp["dt_bias"], inp["b"][:128], cu, inp["scale"])
+    assert torch.equal(ck[1], s128[0])
+    _, _, none_ck = O.prefill_gated(q, k, inp["v"], None, None, None, inp["cu_seqlens"], 0.0)
+    assert none_ck is None
+
+
 def test_oracle_fp32_vs_fp64():
     """The fp32 oracle is itself accurate: compare with its float64 evaluation."""
     d, m = load_golden("prefill_varlen_l2")
