@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode_b128|decode_b4|decode_b1024|prefill_p1|prefill_p2|prefill_p3|
-                                mtp_b128_t4]
+                                mtp_b128_t4|decode_b128_bf16state]
 
 Prints ONE JSON line (rank 0).  Default workload: one GDN decode step over
 batch 128 (state 128 x 32 x 128 x 128 fp32 = 268 MB read + 268 MB written per
@@ -185,17 +185,21 @@ class Dist:
 
 # --------------------------------------------------------------------------- workloads
 class DecodeWork:
-    """One decode step over `batch` sequences; state ping-pongs between two buffers."""
+    """One decode step over `batch` sequences; state ping-pongs between two buffers
+    (fp32, or bf16 with `state_bf16`)."""
 
-    def __init__(self, pkg, batch, dev, seed):
+    def __init__(self, pkg, batch, dev, seed, state_bf16=False):
         W = pkg.workloads
         self.pkg, self.batch, self.dev = pkg, batch, dev
         inp = W.decode_inputs(batch, seed=seed, device=str(dev))
+        if state_bf16:
+            inp["state"] = inp["state"].to(torch.bfloat16)
         self.inp = inp
         self.s = [inp["state"], torch.empty_like(inp["state"])]
         self.out = torch.empty_like(inp["v"])
         self.i = 0
-        self.units = W.decode_state_bytes(batch)     # algorithmic bytes per step
+        # algorithmic bytes per step (state read + write)
+        self.units = W.decode_state_bytes(batch) // (2 if state_bf16 else 1)
         self.io_bytes = W.decode_io_bytes(batch)
         self.launches = 1
 
@@ -211,11 +215,11 @@ class DecodeWork:
         d = self.inp
         self.h = {k: d[k].cpu().pin_memory() for k in ("q", "k", "v", "state", "a", "b")}
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
-        self.h_ns = torch.empty(d["state"].shape, dtype=torch.float32).pin_memory()
+        self.h_ns = torch.empty(d["state"].shape, dtype=d["state"].dtype).pin_memory()
         self.d_in = {k: torch.empty_like(d[k]) for k in self.h}
         self.d_ns = torch.empty_like(d["state"])
         h2d = sum(t.numel() * t.element_size() for t in self.h.values())
-        d2h = self.h_out.numel() * 2 + self.h_ns.numel() * 4
+        d2h = self.h_out.numel() * 2 + self.h_ns.numel() * self.h_ns.element_size()
         return h2d, d2h
 
     def e2e_step(self):
@@ -390,13 +394,15 @@ def time_steps(fn, steps, warmup, dist, per_launch_events=True):
     return dist.max(total) / steps, per_kernel
 
 
-def cpu_baseline_decode(batch, budget_s=10.0):
+def cpu_baseline_decode(batch, budget_s=10.0, state_bf16=False):
     from oracle import gdn_oracle as O
     pkg = importlib.import_module(PKG_NAME)
     W = pkg.workloads
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     inp = W.decode_inputs(batch, seed=0)
+    if state_bf16:
+        inp["state"] = inp["state"].to(torch.bfloat16)
     q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
     O.decode(q[:1], k[:1], inp["v"][:1], inp["state"][:1], inp["A_log"], inp["a"][:1],
              inp["dt_bias"], inp["b"][:1], inp["scale"])  # warm
@@ -409,7 +415,7 @@ def cpu_baseline_decode(batch, budget_s=10.0):
         if el > budget_s or reps >= 5:
             break
     per = el / reps
-    gbs = W.decode_state_bytes(batch) / per / 1e9
+    gbs = W.decode_state_bytes(batch) // (2 if state_bf16 else 1) / per / 1e9
     return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{reps} full decode step(s) of batch {batch} (oracle, fp32 torch CPU)",
             "sec_per_step": per}
@@ -439,8 +445,8 @@ def cpu_baseline_prefill(cfg_name, budget_tokens=4096):
 
 
 # --------------------------------------------------------------------------- arms
-def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True):
-    w = DecodeWork(pkg, batch, dev, seed=dist.rank)
+def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf16=False):
+    w = DecodeWork(pkg, batch, dev, seed=dist.rank, state_bf16=state_bf16)
     with ClockSampler(dev.index) as clk:
         ms, kern_ms = time_steps(w.step, steps, warmup, dist)
     total_bytes = w.units * dist.world
@@ -538,6 +544,7 @@ WORKLOADS = {
     "prefill_p1": ("prefill", "P1"), "prefill_p2": ("prefill", "P2"),
     "prefill_p3": ("prefill", "P3"),
     "mtp_b128_t4": ("mtp", 128),
+    "decode_b128_bf16state": ("decode_bf16state", 128),
 }
 
 
@@ -548,18 +555,22 @@ def run_ours(args, dist):
     pk, src = peaks()
     kind, param = WORKLOADS[args.workload]
     line = {"impl": "ours"}
-    if kind == "decode":
-        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev)
+    if kind in ("decode", "decode_bf16state"):
+        bf = kind == "decode_bf16state"
+        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev, state_bf16=bf)
         line.update({
             "metric": "decode state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+            "vs_baseline": None, "dtype": "fp32" + (" compute, bf16 state" if bf else ""),
+            "data": "synthetic (seeded)",
             "config": {"workload": f"GDN decode, batch {param} per GPU, 16 q/k + 32 v heads, "
-                                   f"head_dim 128, fp32 k-last state, q/k L2-normalised in-kernel",
+                                   f"head_dim 128, {'bf16' if bf else 'fp32'} k-last state, "
+                                   f"q/k L2-normalised in-kernel",
                        "batch_per_gpu": param, "global_batch": param * dist.world,
                        "parallelism": f"batch-sharded x{dist.world}, no collective",
-                       "l2": "inputs > L2: 537 MB state traffic per step, state ping-pong"},
+                       "l2": f"inputs > L2: {r['units'] / 1e6:.0f} MB state traffic per step, "
+                             f"state ping-pong"},
             "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
             "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_ms": round(r["kern_ms"], 5),
@@ -614,7 +625,8 @@ def run_ours(args, dist):
                                               pk, src)}
         line["prefill"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = (cpu_baseline_decode(param) if kind == "decode"
+        line["cpu_baseline"] = (cpu_baseline_decode(param, state_bf16=kind == "decode_bf16state")
+                                if kind in ("decode", "decode_bf16state")
                                 else cpu_baseline_mtp(param) if kind == "mtp"
                                 else cpu_baseline_prefill(param))
     return line
@@ -626,9 +638,10 @@ def run_reference(args, dist):
         return None
     kind, param = WORKLOADS[args.workload]
     steps = []
-    if kind == "decode":
+    if kind in ("decode", "decode_bf16state"):
         for _ in range(max(1, min(args.steps, 3))):
-            steps.append(cpu_baseline_decode(param, budget_s=5.0))
+            steps.append(cpu_baseline_decode(param, budget_s=5.0,
+                                             state_bf16=kind == "decode_bf16state"))
         v = statistics.median(s["value"] for s in steps)
         metric, unit = "decode state-traffic GB/s", "GB/s"
         ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3

@@ -107,6 +107,27 @@ int gdn_mtp_launch(const void* q, const void* k, const void* v, const float* ini
                    int num_v_heads, int head_size, int use_qk_l2norm, void* stream);
 
 /*
+ * bf16 state storage (the bf16-state backend of FlashInfer's decode,
+ * flashinfer/gdn_decode.py:146-149): same contracts as gdn_decode_launch and
+ * gdn_mtp_launch with state, new_state, the pool and the rollback buffer as bf16
+ * (same shapes, 8-byte aligned).  The state is widened to fp32 on load, updated in
+ * fp32 (across all tokens of a multi-token call) and rounded to nearest bf16 on every
+ * store; the state traffic is half that of the fp32 entry points.
+ */
+int gdn_decode_launch_bf16state(const void* q, const void* k, const void* v, const void* state,
+                                const float* A_log, const void* a, const float* dt_bias,
+                                const void* b, float scale, void* output, void* new_state,
+                                int batch, int num_q_heads, int num_k_heads, int num_v_heads,
+                                int head_size, int use_qk_l2norm, void* stream);
+int gdn_mtp_launch_bf16state(const void* q, const void* k, const void* v,
+                             const void* initial_state, const void* state_indices,
+                             int state_indices_int64, const float* A_log, const void* a,
+                             const float* dt_bias, const void* b, float scale, void* output,
+                             void* final_state, void* intermediate_states, int batch,
+                             int seq_len, int pool_size, int num_q_heads, int num_k_heads,
+                             int num_v_heads, int head_size, int use_qk_l2norm, void* stream);
+
+/*
  * Bytes of device workspace gdn_prefill_launch needs for this problem (may be 0).
  */
 size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_heads,

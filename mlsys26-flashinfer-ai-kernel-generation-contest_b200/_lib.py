@@ -27,6 +27,10 @@ SIGNATURES = {
                                _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_mtp_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp,
                             _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_decode_launch_bf16state": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
+                                         _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_mtp_launch_bf16state": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f, _vp,
+                                      _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "gdn_prefill_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp,
                                 _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),

@@ -59,6 +59,24 @@ __device__ __forceinline__ void st_stream_f4(float* p, float4 v) {
                : "memory");
 }
 
+// Four consecutive state values as fp32 from an fp32 state (one float4) or a bf16
+// state (8 bytes, widened exactly); stores round to nearest bf16 for a bf16 state.
+__device__ __forceinline__ float4 ld_state4(const float* p) { return ld_stream_f4(p); }
+__device__ __forceinline__ float4 ld_state4(const __nv_bfloat16* p) {
+  uint32_t x, y;
+  asm volatile("ld.global.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(x), "=r"(y) : "l"(p));
+  const float2 lo = bf2x2_to_f2(x), hi = bf2x2_to_f2(y);
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ void st_state4(float* p, float4 v) { st_stream_f4(p, v); }
+__device__ __forceinline__ void st_state4(__nv_bfloat16* p, float4 v) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+  asm volatile("st.global.L1::no_allocate.v2.u32 [%0], {%1,%2};" ::"l"(p),
+               "r"(*reinterpret_cast<uint32_t*>(&lo)), "r"(*reinterpret_cast<uint32_t*>(&hi))
+               : "memory");
+}
+
 __device__ __forceinline__ float xor_sum8(float x) {
   // Sum over the 8 lanes of an aligned 8-lane group.
   x += __shfl_xor_sync(0xffffffffu, x, 1);

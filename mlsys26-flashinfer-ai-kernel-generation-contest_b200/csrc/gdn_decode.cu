@@ -10,6 +10,11 @@
 // so the output needs no second pass over the state (the reference's two-pass
 // K-tiled configurations re-read it, kernel.py:176-213).
 //
+// The state may also be stored as bf16 (gdn_decode_launch_bf16state, the bf16-state
+// backend of FlashInfer's decode, flashinfer/gdn_decode.py:146-149): it is widened to
+// fp32 on load, updated in fp32 and rounded to nearest bf16 on store, halving the
+// state traffic.
+//
 // Thread mapping: 8 lanes own one 512-byte state row, each lane 4 float4 at
 // columns 4j + 32m (j = lane % 8, m = 0..3), so every 128-bit load instruction of
 // a warp covers four fully used 128-byte segments.  A warp owns RPW rows, a CTA
@@ -20,13 +25,13 @@
 namespace gdn {
 namespace {
 
-template <int RPW, bool L2NORM, bool HAS_STATE>
+template <int RPW, bool L2NORM, bool HAS_STATE, typename ST>
 __global__ void __launch_bounds__(256)
     decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                  const __nv_bfloat16* __restrict__ v, const float* state,
+                  const __nv_bfloat16* __restrict__ v, const ST* state,
                   const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
                   const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ b,
-                  float scale, __nv_bfloat16* __restrict__ out, float* new_state, int HQ,
+                  float scale, __nv_bfloat16* __restrict__ out, ST* new_state, int HQ,
                   int HV, int ratio) {
   constexpr int ROWS = 8 * RPW;            // state rows per CTA
   constexpr int VSPLIT = kHeadDim / ROWS;  // CTAs per (b, h)
@@ -47,11 +52,11 @@ __global__ void __launch_bounds__(256)
   // ---- issue the state loads first ----
   float4 S[NG][4];
   if constexpr (HAS_STATE) {
-    const float* sp = state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+    const ST* sp = state + head_base + (size_t)row0 * kHeadDim + 4 * j;
 #pragma unroll
     for (int r = 0; r < NG; ++r)
 #pragma unroll
-      for (int m = 0; m < 4; ++m) S[r][m] = ld_stream_f4(sp + r * 4 * kHeadDim + m * 32);
+      for (int m = 0; m < 4; ++m) S[r][m] = ld_state4(sp + r * 4 * kHeadDim + m * 32);
   } else {
 #pragma unroll
     for (int r = 0; r < NG; ++r)
@@ -105,7 +110,7 @@ __global__ void __launch_bounds__(256)
   kq = xor_sum8(kq);
 
   scale = default_scale(scale);
-  float* nsp = new_state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+  ST* nsp = new_state + head_base + (size_t)row0 * kHeadDim + 4 * j;
   __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
 #pragma unroll
   for (int r = 0; r < NG; ++r) {
@@ -129,16 +134,16 @@ __global__ void __launch_bounds__(256)
       s.y = fmaf(g, s.y, delta * kf[4 * m + 1]);
       s.z = fmaf(g, s.z, delta * kf[4 * m + 2]);
       s.w = fmaf(g, s.w, delta * kf[4 * m + 3]);
-      st_stream_f4(nsp + r * 4 * kHeadDim + m * 32, s);
+      st_state4(nsp + r * 4 * kHeadDim + m * 32, s);
     }
     if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
   }
 }
 
-template <int RPW>
-cudaError_t launch_rpw(const void* q, const void* k, const void* v, const float* state,
+template <int RPW, typename ST>
+cudaError_t launch_rpw(const void* q, const void* k, const void* v, const ST* state,
                        const float* A_log, const void* a, const float* dt_bias, const void* b,
-                       float scale, void* out, float* new_state, int batch, int HQ, int HV,
+                       float scale, void* out, ST* new_state, int batch, int HQ, int HV,
                        bool l2norm, cudaStream_t stream) {
   constexpr int VSPLIT = kHeadDim / (8 * RPW);
   const long long ctas = (long long)batch * HV * VSPLIT;
@@ -152,14 +157,14 @@ cudaError_t launch_rpw(const void* q, const void* k, const void* v, const float*
   auto O = static_cast<__nv_bfloat16*>(out);
   if (state != nullptr) {
     if (l2norm)
-      decode_kernel<RPW, true, true><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, true, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
     else
-      decode_kernel<RPW, false, true><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, false, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
   } else {
     if (l2norm)
-      decode_kernel<RPW, true, false><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, true, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
     else
-      decode_kernel<RPW, false, false><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, false, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
   }
   return cudaGetLastError();
 }
@@ -169,12 +174,13 @@ inline bool misaligned(const void* p, uintptr_t n) { return (reinterpret_cast<ui
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_decode_launch(const void* q, const void* k, const void* v, const float* state,
-                                 const float* A_log, const void* a, const float* dt_bias,
-                                 const void* b, float scale, void* output, float* new_state,
-                                 int batch, int num_q_heads, int num_k_heads, int num_v_heads,
-                                 int head_size, int use_qk_l2norm, void* stream) {
-  using namespace gdn;
+namespace gdn {
+namespace {
+template <typename ST>
+int decode_entry(const void* q, const void* k, const void* v, const ST* state, const float* A_log,
+                 const void* a, const float* dt_bias, const void* b, float scale, void* output,
+                 ST* new_state, int batch, int num_q_heads, int num_k_heads, int num_v_heads,
+                 int head_size, int use_qk_l2norm, void* stream) {
   if (batch < 0 || num_q_heads <= 0 || num_k_heads <= 0 || num_v_heads <= 0)
     return GDN_ERR_INVALID_ARGUMENT;
   if (head_size != kHeadDim || num_k_heads != num_q_heads || num_v_heads % num_q_heads != 0)
@@ -183,7 +189,7 @@ extern "C" int gdn_decode_launch(const void* q, const void* k, const void* v, co
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
     return GDN_ERR_INVALID_ARGUMENT;
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
-      misaligned(new_state, 16) || (state && misaligned(state, 16)))
+      misaligned(new_state, 4 * sizeof(ST)) || (state && misaligned(state, 4 * sizeof(ST))))
     return GDN_ERR_INVALID_ARGUMENT;
   const long long heads = (long long)batch * num_v_heads;
   if (heads * 4 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
@@ -192,10 +198,34 @@ extern "C" int gdn_decode_launch(const void* q, const void* k, const void* v, co
   cudaError_t err;
   // Enough CTAs to fill 148 SMs several times over; bigger CTAs when there are.
   if (heads >= 4 * 148)
-    err = launch_rpw<16>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<16, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
   else if (heads >= 2 * 148)
-    err = launch_rpw<8>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<8, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
   else
-    err = launch_rpw<4>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<4, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_decode_launch(const void* q, const void* k, const void* v, const float* state,
+                                 const float* A_log, const void* a, const float* dt_bias,
+                                 const void* b, float scale, void* output, float* new_state,
+                                 int batch, int num_q_heads, int num_k_heads, int num_v_heads,
+                                 int head_size, int use_qk_l2norm, void* stream) {
+  return gdn::decode_entry<float>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,
+                                  batch, num_q_heads, num_k_heads, num_v_heads, head_size,
+                                  use_qk_l2norm, stream);
+}
+
+extern "C" int gdn_decode_launch_bf16state(const void* q, const void* k, const void* v,
+                                           const void* state, const float* A_log, const void* a,
+                                           const float* dt_bias, const void* b, float scale,
+                                           void* output, void* new_state, int batch,
+                                           int num_q_heads, int num_k_heads, int num_v_heads,
+                                           int head_size, int use_qk_l2norm, void* stream) {
+  return gdn::decode_entry<__nv_bfloat16>(
+      q, k, v, static_cast<const __nv_bfloat16*>(state), A_log, a, dt_bias, b, scale, output,
+      static_cast<__nv_bfloat16*>(new_state), batch, num_q_heads, num_k_heads, num_v_heads,
+      head_size, use_qk_l2norm, stream);
 }

@@ -13,7 +13,9 @@
 // the state stays in registers across the T tokens, so the pool slot is read once
 // and written once.  The next token's q/k/v/gates are loaded while the current
 // token is applied.  A batch row whose index lies outside [0, pool_size) is a
-// padding row: its outputs are zero and no state is read or written.
+// padding row: its outputs are zero and no state is read or written.  The pool and
+// the rollback buffer may be bf16 (gdn_mtp_launch_bf16state): widened on load,
+// carried in fp32 through the T tokens, rounded to nearest bf16 on every store.
 #include "gdn_common.cuh"
 
 namespace gdn {
@@ -53,14 +55,14 @@ __device__ __forceinline__ void mtp_load_token(const __nv_bfloat16* __restrict__
   tk.beta = sigmoid_f(bf2f(b[bt * HV + h]));
 }
 
-template <int RPW, bool L2NORM, bool INTER, typename IdxT>
+template <int RPW, bool L2NORM, bool INTER, typename IdxT, typename ST>
 __global__ void __launch_bounds__(256)
     mtp_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-               const __nv_bfloat16* __restrict__ v, const float* pool,
+               const __nv_bfloat16* __restrict__ v, const ST* pool,
                const IdxT* __restrict__ indices, const float* __restrict__ A_log,
                const __nv_bfloat16* __restrict__ a, const float* __restrict__ dt_bias,
                const __nv_bfloat16* __restrict__ b, float scale, __nv_bfloat16* __restrict__ out,
-               float* new_pool, float* __restrict__ inter, int T, long long pool_size, int HQ,
+               ST* new_pool, ST* __restrict__ inter, int T, long long pool_size, int HQ,
                int HV, int ratio) {
   constexpr int ROWS = 8 * RPW;            // state rows per CTA
   constexpr int VSPLIT = kHeadDim / ROWS;  // CTAs per (b, h)
@@ -89,11 +91,11 @@ __global__ void __launch_bounds__(256)
 
   float4 S[NG][4];
   {
-    const float* sp = pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
+    const ST* sp = pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
 #pragma unroll
     for (int r = 0; r < NG; ++r)
 #pragma unroll
-      for (int m = 0; m < 4; ++m) S[r][m] = ld_stream_f4(sp + r * 4 * kHeadDim + m * 32);
+      for (int m = 0; m < 4; ++m) S[r][m] = ld_state4(sp + r * 4 * kHeadDim + m * 32);
   }
   const float nexpA = -expf(__ldg(A_log + h));
   const float dtb = __ldg(dt_bias + h);
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(256)
     kq = xor_sum8(kq);
     const float g = cur.g, beta = cur.beta;
     __nv_bfloat16* op = op0 + (size_t)t * HV * kHeadDim;
-    float* ip = nullptr;
+    ST* ip = nullptr;
     if constexpr (INTER)
       ip = inter + (((size_t)slot * T + t) * HV + h) * kHeadDim * kHeadDim +
            (size_t)row0 * kHeadDim + 4 * j;
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(256)
         s.z = fmaf(g, s.z, delta * cur.kf[4 * m + 2]);
         s.w = fmaf(g, s.w, delta * cur.kf[4 * m + 3]);
         S[r][m] = s;
-        if constexpr (INTER) st_stream_f4(ip + r * 4 * kHeadDim + m * 32, s);
+        if constexpr (INTER) st_state4(ip + r * 4 * kHeadDim + m * 32, s);
       }
       if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
     }
@@ -168,18 +170,18 @@ __global__ void __launch_bounds__(256)
       for (int r = 0; r < NG; ++r) vv[r] = vn[r];
     }
   }
-  float* nsp = new_pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
+  ST* nsp = new_pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
 #pragma unroll
   for (int r = 0; r < NG; ++r)
 #pragma unroll
-    for (int m = 0; m < 4; ++m) st_stream_f4(nsp + r * 4 * kHeadDim + m * 32, S[r][m]);
+    for (int m = 0; m < 4; ++m) st_state4(nsp + r * 4 * kHeadDim + m * 32, S[r][m]);
 }
 
-template <int RPW, typename IdxT>
-cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const float* pool,
+template <int RPW, typename IdxT, typename ST>
+cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const ST* pool,
                            const void* indices, const float* A_log, const void* a,
                            const float* dt_bias, const void* b, float scale, void* out,
-                           float* new_pool, float* inter, int batch, int T, long long pool_size,
+                           ST* new_pool, ST* inter, int batch, int T, long long pool_size,
                            int HQ, int HV, bool l2norm, cudaStream_t st) {
   constexpr int VSPLIT = kHeadDim / (8 * RPW);
   const dim3 grid((unsigned)((long long)batch * HV * VSPLIT)), block(256);
@@ -192,7 +194,7 @@ cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const fl
   auto I = static_cast<const IdxT*>(indices);
   const int ratio = HV / HQ;
 #define GDN_MTP_LAUNCH(L2, IN)                                                                \
-  mtp_kernel<RPW, L2, IN, IdxT><<<grid, block, 0, st>>>(Q, K, V, pool, I, A_log, A, dt_bias, \
+  mtp_kernel<RPW, L2, IN, IdxT, ST><<<grid, block, 0, st>>>(Q, K, V, pool, I, A_log, A, dt_bias, \
                                                         Bt, scale, O, new_pool, inter, T,    \
                                                         pool_size, HQ, HV, ratio)
   if (inter != nullptr) {
@@ -204,21 +206,21 @@ cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const fl
   return cudaGetLastError();
 }
 
-template <typename IdxT>
-cudaError_t launch_mtp(const void* q, const void* k, const void* v, const float* pool,
+template <typename IdxT, typename ST>
+cudaError_t launch_mtp(const void* q, const void* k, const void* v, const ST* pool,
                        const void* indices, const float* A_log, const void* a,
                        const float* dt_bias, const void* b, float scale, void* out,
-                       float* new_pool, float* inter, int batch, int T, long long pool_size,
+                       ST* new_pool, ST* inter, int batch, int T, long long pool_size,
                        int HQ, int HV, bool l2norm, cudaStream_t st) {
   // same CTA sizing as the decode kernel: enough CTAs to fill 148 SMs several times
   const long long heads = (long long)batch * HV;
   if (heads >= 4 * 148)
-    return launch_mtp_rpw<16, IdxT>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+    return launch_mtp_rpw<16, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
                                     new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
   if (heads >= 2 * 148)
-    return launch_mtp_rpw<8, IdxT>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+    return launch_mtp_rpw<8, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
                                    new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
-  return launch_mtp_rpw<4, IdxT>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+  return launch_mtp_rpw<4, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
                                  new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
 }
 
@@ -229,14 +231,15 @@ inline bool misaligned(const void* p, uintptr_t n) {
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_mtp_launch(const void* q, const void* k, const void* v,
-                              const float* initial_state, const void* state_indices,
-                              int state_indices_int64, const float* A_log, const void* a,
-                              const float* dt_bias, const void* b, float scale, void* output,
-                              float* final_state, float* intermediate_states, int batch,
-                              int seq_len, int pool_size, int num_q_heads, int num_k_heads,
-                              int num_v_heads, int head_size, int use_qk_l2norm, void* stream) {
-  using namespace gdn;
+namespace gdn {
+namespace {
+template <typename ST>
+int mtp_entry(const void* q, const void* k, const void* v, const ST* initial_state,
+              const void* state_indices, int state_indices_int64, const float* A_log,
+              const void* a, const float* dt_bias, const void* b, float scale, void* output,
+              ST* final_state, ST* intermediate_states, int batch, int seq_len, int pool_size,
+              int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+              int use_qk_l2norm, void* stream) {
   if (batch < 0 || seq_len < 0 || pool_size < 0 || num_q_heads <= 0 || num_k_heads <= 0 ||
       num_v_heads <= 0)
     return GDN_ERR_INVALID_ARGUMENT;
@@ -246,9 +249,10 @@ extern "C" int gdn_mtp_launch(const void* q, const void* k, const void* v,
   if (!q || !k || !v || !initial_state || !state_indices || !A_log || !a || !dt_bias || !b ||
       !output || !final_state)
     return GDN_ERR_INVALID_ARGUMENT;
+  constexpr uintptr_t sa = 4 * sizeof(ST);
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
-      misaligned(initial_state, 16) || misaligned(final_state, 16) ||
-      (intermediate_states && misaligned(intermediate_states, 16)) ||
+      misaligned(initial_state, sa) || misaligned(final_state, sa) ||
+      (intermediate_states && misaligned(intermediate_states, sa)) ||
       misaligned(state_indices, state_indices_int64 ? 8 : 4))
     return GDN_ERR_INVALID_ARGUMENT;
   if ((long long)batch * num_v_heads * 4 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
@@ -256,11 +260,43 @@ extern "C" int gdn_mtp_launch(const void* q, const void* k, const void* v,
   const bool l2 = use_qk_l2norm != 0;
   const cudaError_t err =
       state_indices_int64
-          ? launch_mtp<long long>(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b,
-                                  scale, output, final_state, intermediate_states, batch, seq_len,
-                                  pool_size, num_q_heads, num_v_heads, l2, st)
-          : launch_mtp<int>(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b, scale,
-                            output, final_state, intermediate_states, batch, seq_len, pool_size,
-                            num_q_heads, num_v_heads, l2, st);
+          ? launch_mtp<long long, ST>(q, k, v, initial_state, state_indices, A_log, a, dt_bias,
+                                      b, scale, output, final_state, intermediate_states, batch,
+                                      seq_len, pool_size, num_q_heads, num_v_heads, l2, st)
+          : launch_mtp<int, ST>(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b,
+                                scale, output, final_state, intermediate_states, batch, seq_len,
+                                pool_size, num_q_heads, num_v_heads, l2, st);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_mtp_launch(const void* q, const void* k, const void* v,
+                              const float* initial_state, const void* state_indices,
+                              int state_indices_int64, const float* A_log, const void* a,
+                              const float* dt_bias, const void* b, float scale, void* output,
+                              float* final_state, float* intermediate_states, int batch,
+                              int seq_len, int pool_size, int num_q_heads, int num_k_heads,
+                              int num_v_heads, int head_size, int use_qk_l2norm, void* stream) {
+  return gdn::mtp_entry<float>(q, k, v, initial_state, state_indices, state_indices_int64, A_log,
+                               a, dt_bias, b, scale, output, final_state, intermediate_states,
+                               batch, seq_len, pool_size, num_q_heads, num_k_heads, num_v_heads,
+                               head_size, use_qk_l2norm, stream);
+}
+
+extern "C" int gdn_mtp_launch_bf16state(const void* q, const void* k, const void* v,
+                                        const void* initial_state, const void* state_indices,
+                                        int state_indices_int64, const float* A_log,
+                                        const void* a, const float* dt_bias, const void* b,
+                                        float scale, void* output, void* final_state,
+                                        void* intermediate_states, int batch, int seq_len,
+                                        int pool_size, int num_q_heads, int num_k_heads,
+                                        int num_v_heads, int head_size, int use_qk_l2norm,
+                                        void* stream) {
+  using B16 = __nv_bfloat16;
+  return gdn::mtp_entry<B16>(q, k, v, static_cast<const B16*>(initial_state), state_indices,
+                             state_indices_int64, A_log, a, dt_bias, b, scale, output,
+                             static_cast<B16*>(final_state), static_cast<B16*>(intermediate_states),
+                             batch, seq_len, pool_size, num_q_heads, num_k_heads, num_v_heads,
+                             head_size, use_qk_l2norm, stream);
 }

@@ -18,7 +18,12 @@ from ._lib import LIB, check
 
 def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_state=None,
                *, use_qk_l2norm: bool = False):
-    """One decode step; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32)."""
+    """One decode step; ``use_qk_l2norm`` L2-normalises q and k in-kernel (fp32).
+
+    ``state`` / ``new_state`` may be fp32 (``gdn_decode_launch``) or bf16
+    (``gdn_decode_launch_bf16state``: widened on load, updated in fp32, rounded on
+    store; half the state traffic); both must then have the same dtype, which is taken
+    from ``state``, else from ``new_state``, else fp32."""
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 4, dev)
     C.tensor("k", k, torch.bfloat16, 4, dev)
@@ -31,8 +36,12 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
     C.heads(HQ, HK, HV, D)
     C.shape("k", k, (B, 1, HK, D))
     C.shape("v", v, (B, 1, HV, D))
+    sdt = state.dtype if isinstance(state, torch.Tensor) else (
+        new_state.dtype if isinstance(new_state, torch.Tensor) else torch.float32)
+    if sdt not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"state must be float32 or bfloat16, got {sdt}")
     if state is not None:
-        C.tensor("state", state, torch.float32, 4, dev)
+        C.tensor("state", state, sdt, 4, dev)
         C.shape("state", state, (B, HV, D, D))
     C.tensor("A_log", A_log, torch.float32, 1, dev)
     C.shape("A_log", A_log, (HV,))
@@ -49,17 +58,18 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
         C.tensor("output", output, torch.bfloat16, 4, dev)
         C.shape("output", output, (B, 1, HV, D))
     if new_state is None:
-        new_state = torch.empty(B, HV, D, D, dtype=torch.float32, device=dev)
+        new_state = torch.empty(B, HV, D, D, dtype=sdt, device=dev)
     else:
-        C.tensor("new_state", new_state, torch.float32, 4, dev)
+        C.tensor("new_state", new_state, sdt, 4, dev)
         C.shape("new_state", new_state, (B, HV, D, D))
-    status = LIB.gdn_decode_launch(
+    launch = LIB.gdn_decode_launch if sdt == torch.float32 else LIB.gdn_decode_launch_bf16state
+    status = launch(
         q.data_ptr(), k.data_ptr(), v.data_ptr(),
         state.data_ptr() if state is not None else None,
         A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), sc,
         output.data_ptr(), new_state.data_ptr(), B, HQ, HK, HV, D, int(bool(use_qk_l2norm)),
         C.stream_handle(dev))
-    check("gdn_decode_launch", status)
+    check("gdn_decode_launch" + ("" if sdt == torch.float32 else "_bf16state"), status)
     return output, new_state
 
 

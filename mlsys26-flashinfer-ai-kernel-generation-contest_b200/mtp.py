@@ -25,7 +25,10 @@ from ._lib import LIB, check
 def gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
             output=None, final_state=None, intermediate_states_buffer=None, *,
             use_qk_l2norm: bool = False):
-    """Returns ``(output, final_state)``; ``use_qk_l2norm`` L2-normalises q and k in-kernel."""
+    """Returns ``(output, final_state)``; ``use_qk_l2norm`` L2-normalises q and k in-kernel.
+
+    The pool (and the rollback buffer, which must match it) may be fp32 or bf16
+    (``gdn_mtp_launch_bf16state``: carried in fp32 through the tokens, rounded on store)."""
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 4, dev)
     C.tensor("k", k, torch.bfloat16, 4, dev)
@@ -36,7 +39,12 @@ def gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b,
     C.heads(HQ, HK, HV, D)
     C.shape("k", k, (B, T, HK, D))
     C.shape("v", v, (B, T, HV, D))
-    C.tensor("initial_state", initial_state, torch.float32, 4, dev)
+    if not isinstance(initial_state, torch.Tensor):
+        raise TypeError("initial_state must be a torch.Tensor")
+    sdt = initial_state.dtype
+    if sdt not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"initial_state must be float32 or bfloat16, got {sdt}")
+    C.tensor("initial_state", initial_state, sdt, 4, dev)
     P = initial_state.shape[0]
     C.shape("initial_state", initial_state, (P, HV, D, D))
     idx = initial_state_indices
@@ -61,21 +69,22 @@ def gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b,
     if final_state is None:
         final_state = initial_state
     else:
-        C.tensor("final_state", final_state, torch.float32, 4, dev)
+        C.tensor("final_state", final_state, sdt, 4, dev)
         C.shape("final_state", final_state, (P, HV, D, D))
         if final_state.data_ptr() != initial_state.data_ptr():
             final_state.copy_(initial_state)  # slots no row references keep their value
     inter = intermediate_states_buffer
     if inter is not None:
-        C.tensor("intermediate_states_buffer", inter, torch.float32, 5, dev)
+        C.tensor("intermediate_states_buffer", inter, sdt, 5, dev)
         C.shape("intermediate_states_buffer", inter, (P, T, HV, D, D))
-    status = LIB.gdn_mtp_launch(
+    launch = LIB.gdn_mtp_launch if sdt == torch.float32 else LIB.gdn_mtp_launch_bf16state
+    status = launch(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), final_state.data_ptr(), idx.data_ptr(),
         int(idx.dtype == torch.int64), A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(),
         b.data_ptr(), sc, output.data_ptr(), final_state.data_ptr(),
         inter.data_ptr() if inter is not None else None, B, T, P, HQ, HK, HV, D,
         int(bool(use_qk_l2norm)), C.stream_handle(dev))
-    check("gdn_mtp_launch", status)
+    check("gdn_mtp_launch" + ("" if sdt == torch.float32 else "_bf16state"), status)
     return output, final_state
 
 

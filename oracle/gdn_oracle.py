@@ -130,7 +130,10 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, *, dtype=torch.float32):
     delta = beta[..., None] * (ve - old)                       # beta (v - old)
     S_new = Sg + delta[..., :, None] * ke[..., None, :]        # + delta k^T  (k-last)
     out = sc * torch.einsum("bhvk,bhk->bhv", S_new, qe)
-    return out[:, None].to(torch.bfloat16), S_new.float()
+    # a bf16 state (the bf16-state storage format) is widened above and the new state
+    # rounded to nearest bf16 for storage; the output uses the unrounded state
+    sdt = torch.bfloat16 if (state is not None and state.dtype == torch.bfloat16) else torch.float32
+    return out[:, None].to(torch.bfloat16), S_new.to(sdt)
 
 
 @torch.no_grad()
@@ -149,12 +152,15 @@ def mtp(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b, scale, *,
     Every row starts from the initial pool, as in the definition.  A row whose index
     lies outside [0, P) is padding: zero output and no state change (the definition
     would index the pool with Python's negative-index wrap; the kernels skip such rows).
+    A bf16 pool (the bf16-state storage format) is widened on load, carried in fp32
+    through the T tokens and rounded to nearest bf16 in final_state and intermediate.
     """
     B, T = q.shape[:2]
     HV, D = v.shape[2], v.shape[3]
     P = initial_state.shape[0]
-    final = initial_state.clone().float()
-    inter = torch.zeros((P, T) + tuple(initial_state.shape[1:]), dtype=torch.float32) \
+    sdt = initial_state.dtype if initial_state.dtype == torch.bfloat16 else torch.float32
+    final = initial_state.clone().to(sdt)
+    inter = torch.zeros((P, T) + tuple(initial_state.shape[1:]), dtype=sdt) \
         if intermediate else None
     out = torch.zeros(B, T, HV, D, dtype=torch.bfloat16)
     idx = [int(i) for i in state_indices.tolist()]
@@ -169,8 +175,8 @@ def mtp(q, k, v, initial_state, state_indices, A_log, a, dt_bias, b, scale, *,
                       a[sel, t:t + 1], dt_bias, b[sel, t:t + 1], scale, dtype=dtype)
         out[sel, t] = o[:, 0]
         if inter is not None:
-            inter[slots, t] = S
-    final[slots] = S
+            inter[slots, t] = S.to(sdt)
+    final[slots] = S.to(sdt)
     return out, final, inter
 
 
