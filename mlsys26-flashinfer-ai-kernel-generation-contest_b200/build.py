@@ -20,8 +20,10 @@ import sys
 PKG = pathlib.Path(__file__).resolve().parent
 REPO = PKG.parent
 CSRC = PKG / "csrc"
-INCLUDE = REPO / "include"
-BUILD = REPO / "_build"
+# the repository keeps the C ABI header in include/; a packaged copy of the library
+# (submission.py) carries it inside the package
+INCLUDE = REPO / "include" if (REPO / "include" / "gdn_b200.h").exists() else PKG / "include"
+BUILD = pathlib.Path(os.environ.get("GDN_B200_BUILD_DIR", str(REPO / "_build")))
 LIB = PKG / "libgdn_b200.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -53,7 +55,7 @@ def _stale(obj: pathlib.Path, src: pathlib.Path) -> bool:
 
 def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = False) -> pathlib.Path:
     nvcc = nvcc_path()
-    BUILD.mkdir(exist_ok=True)
+    BUILD.mkdir(parents=True, exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     objs = []
     jobs = []
@@ -86,7 +88,7 @@ def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = False)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}{r.stderr}")
     if not quiet:
-        print(f"[build] {LIB.relative_to(REPO)} up to date")
+        print(f"[build] {LIB} up to date")
     return LIB
 
 
