@@ -42,6 +42,7 @@ The CUDA sources in gdn_b200/csrc are compiled for sm_100a by nvcc the first tim
 module is imported (into gdn_b200/libgdn_b200.so); `kernel` is the destination-passing
 entry point with the definition's exact parameter list.
 """
+import importlib.util
 import pathlib
 import sys
 
@@ -49,8 +50,10 @@ _HERE = pathlib.Path(__file__).resolve().parent
 if str(_HERE) not in sys.path:
     sys.path.insert(0, str(_HERE))
 
-from gdn_b200 import build as _build  # noqa: E402
-
+# build first, from the script itself (importing the package loads the library)
+_spec = importlib.util.spec_from_file_location("_gdn_b200_build", _HERE / "gdn_b200" / "build.py")
+_build = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(_build)
 _build.build(quiet=True)
 
 import gdn_b200 as _gdn  # noqa: E402
