@@ -606,7 +606,8 @@ def run_ours(args, dist):
                        "parallelism": plan_text(shard, dist.world),
                        "l2": "inputs > L2"},
             "tflops": round(r["tflops"], 2),
-            "roofline": roofline("tensor", r["achieved"], args.workload, pk, src),
+            "roofline": roofline("tensor", r["achieved"], args.workload if shard is None else "",
+                                 pk, src),
             "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_ms": round(r["kern_ms"], 5),
         })
@@ -621,7 +622,9 @@ def run_ours(args, dist):
             extra[nm] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
                          "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
                          "parallelism": plan_text(shard, dist.world),
-                         "roofline": roofline("tensor", r["achieved"], "prefill_" + nm.lower(),
+                         # the committed traffic capture is of the unsharded call
+                         "roofline": roofline("tensor", r["achieved"],
+                                              "prefill_" + nm.lower() if shard is None else "",
                                               pk, src)}
         line["prefill"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
