@@ -110,7 +110,7 @@ int gdn_mtp_launch(const void* q, const void* k, const void* v, const float* ini
  * bf16 state storage (the bf16-state backend of FlashInfer's decode,
  * flashinfer/gdn_decode.py:146-149): same contracts as gdn_decode_launch and
  * gdn_mtp_launch with state, new_state, the pool and the rollback buffer as bf16
- * (same shapes, 8-byte aligned).  The state is widened to fp32 on load, updated in
+ * (same shapes, 16-byte aligned).  The state is widened to fp32 on load, updated in
  * fp32 (across all tokens of a multi-token call) and rounded to nearest bf16 on every
  * store; the state traffic is half that of the fp32 entry points.
  */

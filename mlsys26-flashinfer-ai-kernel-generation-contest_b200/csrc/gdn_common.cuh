@@ -59,22 +59,86 @@ __device__ __forceinline__ void st_stream_f4(float* p, float4 v) {
                : "memory");
 }
 
-// Four consecutive state values as fp32 from an fp32 state (one float4) or a bf16
-// state (8 bytes, widened exactly); stores round to nearest bf16 for a bf16 state.
-__device__ __forceinline__ float4 ld_state4(const float* p) { return ld_stream_f4(p); }
-__device__ __forceinline__ float4 ld_state4(const __nv_bfloat16* p) {
-  uint32_t x, y;
-  asm volatile("ld.global.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(x), "=r"(y) : "l"(p));
-  const float2 lo = bf2x2_to_f2(x), hi = bf2x2_to_f2(y);
-  return make_float4(lo.x, lo.y, hi.x, hi.y);
+// The 16 columns one of the 8 lanes of a state row owns, accessed 16 bytes at a time
+// so that every warp-wide access covers whole 128-byte segments: kVec = 4 fp32 or 8 bf16
+// columns per access at col(m) = kVec*j + 8*kVec*m (m < kChunks), element e of access m
+// held in x[kVec*m + e].  q and k are read with the same column set.
+template <typename ST>
+struct RowSlice {
+  static constexpr int kVec = 16 / (int)sizeof(ST);
+  static constexpr int kChunks = 16 / kVec;
+  __device__ static __forceinline__ int col(int j, int m) { return kVec * j + 8 * kVec * m; }
+  __device__ static __forceinline__ void load(const ST* row, int j, float (&x)[16]);
+  __device__ static __forceinline__ void store(ST* row, int j, const float (&x)[16]);
+  // columns of a bf16 vector (q or k), widened
+  __device__ static __forceinline__ void load_bf16(const __nv_bfloat16* vec, int j,
+                                                   float (&x)[16]) {
+#pragma unroll
+    for (int m = 0; m < kChunks; ++m) {
+      const __nv_bfloat16* p = vec + col(j, m);
+      if constexpr (kVec == 4) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+        const float2 a = bf2x2_to_f2(u.x), b = bf2x2_to_f2(u.y);
+        x[4 * m] = a.x; x[4 * m + 1] = a.y; x[4 * m + 2] = b.x; x[4 * m + 3] = b.y;
+      } else {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = bf2x2_to_f2(w[e]);
+          x[8 * m + 2 * e] = f.x;
+          x[8 * m + 2 * e + 1] = f.y;
+        }
+      }
+    }
+  }
+};
+template <>
+__device__ __forceinline__ void RowSlice<float>::load(const float* row, int j, float (&x)[16]) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const float4 v = ld_stream_f4(row + col(j, m));
+    x[4 * m] = v.x; x[4 * m + 1] = v.y; x[4 * m + 2] = v.z; x[4 * m + 3] = v.w;
+  }
 }
-__device__ __forceinline__ void st_state4(float* p, float4 v) { st_stream_f4(p, v); }
-__device__ __forceinline__ void st_state4(__nv_bfloat16* p, float4 v) {
-  __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
-  __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
-  asm volatile("st.global.L1::no_allocate.v2.u32 [%0], {%1,%2};" ::"l"(p),
-               "r"(*reinterpret_cast<uint32_t*>(&lo)), "r"(*reinterpret_cast<uint32_t*>(&hi))
-               : "memory");
+template <>
+__device__ __forceinline__ void RowSlice<float>::store(float* row, int j, const float (&x)[16]) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+    st_stream_f4(row + col(j, m), make_float4(x[4 * m], x[4 * m + 1], x[4 * m + 2], x[4 * m + 3]));
+}
+template <>
+__device__ __forceinline__ void RowSlice<__nv_bfloat16>::load(const __nv_bfloat16* row, int j,
+                                                              float (&x)[16]) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    uint32_t w[4];
+    asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "l"(row + col(j, m)));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = bf2x2_to_f2(w[e]);
+      x[8 * m + 2 * e] = f.x;
+      x[8 * m + 2 * e + 1] = f.y;
+    }
+  }
+}
+template <>
+__device__ __forceinline__ void RowSlice<__nv_bfloat16>::store(__nv_bfloat16* row, int j,
+                                                               const float (&x)[16]) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(x[8 * m + 2 * e], x[8 * m + 2 * e + 1]);
+      w[e] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(row + col(j, m)),
+                 "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
 }
 
 __device__ __forceinline__ float xor_sum8(float x) {

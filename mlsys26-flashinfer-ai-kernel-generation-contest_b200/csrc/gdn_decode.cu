@@ -15,9 +15,10 @@
 // fp32 on load, updated in fp32 and rounded to nearest bf16 on store, halving the
 // state traffic.
 //
-// Thread mapping: 8 lanes own one 512-byte state row, each lane 4 float4 at
-// columns 4j + 32m (j = lane % 8, m = 0..3), so every 128-bit load instruction of
-// a warp covers four fully used 128-byte segments.  A warp owns RPW rows, a CTA
+// Thread mapping: 8 lanes own one state row, each lane 16 columns accessed 16 bytes
+// at a time (fp32: 4 float4 at columns 4j + 32m; bf16: 2 x 8 values at 8j + 64m;
+// j = lane % 8), so every 128-bit load instruction of a warp covers four fully used
+// 128-byte segments.  A warp owns RPW rows, a CTA
 // of 8 warps owns 8*RPW rows of one head; all of a thread's state loads are
 // issued before any arithmetic so each SM keeps ~64-128 KiB in flight.
 #include "gdn_common.cuh"
@@ -50,36 +51,23 @@ __global__ void __launch_bounds__(256)
   const size_t head_base = (size_t)bh * kHeadDim * kHeadDim;
 
   // ---- issue the state loads first ----
-  float4 S[NG][4];
+  using RS = RowSlice<ST>;
+  float S[NG][16];
   if constexpr (HAS_STATE) {
-    const ST* sp = state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+    const ST* sp = state + head_base + (size_t)row0 * kHeadDim;
 #pragma unroll
-    for (int r = 0; r < NG; ++r)
-#pragma unroll
-      for (int m = 0; m < 4; ++m) S[r][m] = ld_state4(sp + r * 4 * kHeadDim + m * 32);
+    for (int r = 0; r < NG; ++r) RS::load(sp + r * 4 * kHeadDim, j, S[r]);
   } else {
 #pragma unroll
     for (int r = 0; r < NG; ++r)
 #pragma unroll
-      for (int m = 0; m < 4; ++m) S[r][m] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int e = 0; e < 16; ++e) S[r][e] = 0.f;
   }
 
-  // ---- q, k slices (16 elements per lane), v values, gates ----
+  // ---- q, k slices (the lane's 16 columns), v values, gates ----
   float kf[16], qf[16];
-  {
-    const __nv_bfloat16* qp = q + ((size_t)bidx * HQ + qh) * kHeadDim + 4 * j;
-    const __nv_bfloat16* kp = k + ((size_t)bidx * HQ + qh) * kHeadDim + 4 * j;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const uint2 uq = __ldg(reinterpret_cast<const uint2*>(qp + 32 * m));
-      const uint2 uk = __ldg(reinterpret_cast<const uint2*>(kp + 32 * m));
-      float2 t;
-      t = bf2x2_to_f2(uq.x); qf[4 * m + 0] = t.x; qf[4 * m + 1] = t.y;
-      t = bf2x2_to_f2(uq.y); qf[4 * m + 2] = t.x; qf[4 * m + 3] = t.y;
-      t = bf2x2_to_f2(uk.x); kf[4 * m + 0] = t.x; kf[4 * m + 1] = t.y;
-      t = bf2x2_to_f2(uk.y); kf[4 * m + 2] = t.x; kf[4 * m + 3] = t.y;
-    }
-  }
+  RS::load_bf16(q + ((size_t)bidx * HQ + qh) * kHeadDim, j, qf);
+  RS::load_bf16(k + ((size_t)bidx * HQ + qh) * kHeadDim, j, kf);
   float vv[NG];
   const __nv_bfloat16* vp = v + (size_t)bh * kHeadDim + row0;
 #pragma unroll
@@ -110,32 +98,23 @@ __global__ void __launch_bounds__(256)
   kq = xor_sum8(kq);
 
   scale = default_scale(scale);
-  ST* nsp = new_state + head_base + (size_t)row0 * kHeadDim + 4 * j;
+  ST* nsp = new_state + head_base + (size_t)row0 * kHeadDim;
   __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
 #pragma unroll
   for (int r = 0; r < NG; ++r) {
     float sk = 0.f, sq = 0.f;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const float4 s = S[r][m];
-      sk = fmaf(s.x, kf[4 * m + 0], sk); sq = fmaf(s.x, qf[4 * m + 0], sq);
-      sk = fmaf(s.y, kf[4 * m + 1], sk); sq = fmaf(s.y, qf[4 * m + 1], sq);
-      sk = fmaf(s.z, kf[4 * m + 2], sk); sq = fmaf(s.z, qf[4 * m + 2], sq);
-      sk = fmaf(s.w, kf[4 * m + 3], sk); sq = fmaf(s.w, qf[4 * m + 3], sq);
+    for (int e = 0; e < 16; ++e) {
+      sk = fmaf(S[r][e], kf[e], sk);
+      sq = fmaf(S[r][e], qf[e], sq);
     }
     sk = xor_sum8(sk);
     sq = xor_sum8(sq);
     const float old = g * sk;
     const float delta = beta * (vv[r] - old);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      float4 s = S[r][m];
-      s.x = fmaf(g, s.x, delta * kf[4 * m + 0]);
-      s.y = fmaf(g, s.y, delta * kf[4 * m + 1]);
-      s.z = fmaf(g, s.z, delta * kf[4 * m + 2]);
-      s.w = fmaf(g, s.w, delta * kf[4 * m + 3]);
-      st_state4(nsp + r * 4 * kHeadDim + m * 32, s);
-    }
+    for (int e = 0; e < 16; ++e) S[r][e] = fmaf(g, S[r][e], delta * kf[e]);
+    RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
     if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
   }
 }
@@ -189,7 +168,7 @@ int decode_entry(const void* q, const void* k, const void* v, const ST* state, c
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
     return GDN_ERR_INVALID_ARGUMENT;
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
-      misaligned(new_state, 4 * sizeof(ST)) || (state && misaligned(state, 4 * sizeof(ST))))
+      misaligned(new_state, 16) || (state && misaligned(state, 16)))
     return GDN_ERR_INVALID_ARGUMENT;
   const long long heads = (long long)batch * num_v_heads;
   if (heads * 4 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;

@@ -26,7 +26,7 @@ struct MtpToken {
   float g, beta;
 };
 
-template <int NG>
+template <int NG, typename ST>
 __device__ __forceinline__ void mtp_load_token(const __nv_bfloat16* __restrict__ q,
                                                const __nv_bfloat16* __restrict__ k,
                                                const __nv_bfloat16* __restrict__ v,
@@ -35,18 +35,8 @@ __device__ __forceinline__ void mtp_load_token(const __nv_bfloat16* __restrict__
                                                size_t bt, int HQ, int HV, int qh, int h, int j,
                                                int row0, float nexpA, float dtb, MtpToken& tk,
                                                float (&vv)[NG]) {
-  const __nv_bfloat16* qp = q + (bt * HQ + qh) * kHeadDim + 4 * j;
-  const __nv_bfloat16* kp = k + (bt * HQ + qh) * kHeadDim + 4 * j;
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const uint2 uq = __ldg(reinterpret_cast<const uint2*>(qp + 32 * m));
-    const uint2 uk = __ldg(reinterpret_cast<const uint2*>(kp + 32 * m));
-    float2 t;
-    t = bf2x2_to_f2(uq.x); tk.qf[4 * m + 0] = t.x; tk.qf[4 * m + 1] = t.y;
-    t = bf2x2_to_f2(uq.y); tk.qf[4 * m + 2] = t.x; tk.qf[4 * m + 3] = t.y;
-    t = bf2x2_to_f2(uk.x); tk.kf[4 * m + 0] = t.x; tk.kf[4 * m + 1] = t.y;
-    t = bf2x2_to_f2(uk.y); tk.kf[4 * m + 2] = t.x; tk.kf[4 * m + 3] = t.y;
-  }
+  RowSlice<ST>::load_bf16(q + (bt * HQ + qh) * kHeadDim, j, tk.qf);
+  RowSlice<ST>::load_bf16(k + (bt * HQ + qh) * kHeadDim, j, tk.kf);
   const __nv_bfloat16* vp = v + (bt * HV + h) * kHeadDim + row0;
 #pragma unroll
   for (int r = 0; r < NG; ++r) vv[r] = bf2f(vp[4 * r]);
@@ -89,13 +79,12 @@ __global__ void __launch_bounds__(256)
   }
   const size_t head_base = ((size_t)slot * HV + h) * kHeadDim * kHeadDim;
 
-  float4 S[NG][4];
+  using RS = RowSlice<ST>;
+  float S[NG][16];
   {
-    const ST* sp = pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
+    const ST* sp = pool + head_base + (size_t)row0 * kHeadDim;
 #pragma unroll
-    for (int r = 0; r < NG; ++r)
-#pragma unroll
-      for (int m = 0; m < 4; ++m) S[r][m] = ld_state4(sp + r * 4 * kHeadDim + m * 32);
+    for (int r = 0; r < NG; ++r) RS::load(sp + r * 4 * kHeadDim, j, S[r]);
   }
   const float nexpA = -expf(__ldg(A_log + h));
   const float dtb = __ldg(dt_bias + h);
@@ -103,12 +92,12 @@ __global__ void __launch_bounds__(256)
 
   MtpToken cur;
   float vv[NG];
-  mtp_load_token<NG>(q, k, v, a, b, (size_t)bidx * T, HQ, HV, qh, h, j, row0, nexpA, dtb, cur, vv);
+  mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T, HQ, HV, qh, h, j, row0, nexpA, dtb, cur, vv);
   for (int t = 0; t < T; ++t) {
     MtpToken nxt;
     float vn[NG];
     if (t + 1 < T)
-      mtp_load_token<NG>(q, k, v, a, b, (size_t)bidx * T + t + 1, HQ, HV, qh, h, j, row0, nexpA,
+      mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T + t + 1, HQ, HV, qh, h, j, row0, nexpA,
                          dtb, nxt, vn);
     if constexpr (L2NORM) {
       float ssk = 0.f, ssq = 0.f;
@@ -136,32 +125,22 @@ __global__ void __launch_bounds__(256)
     ST* ip = nullptr;
     if constexpr (INTER)
       ip = inter + (((size_t)slot * T + t) * HV + h) * kHeadDim * kHeadDim +
-           (size_t)row0 * kHeadDim + 4 * j;
+           (size_t)row0 * kHeadDim;
 #pragma unroll
     for (int r = 0; r < NG; ++r) {
       float sk = 0.f, sq = 0.f;
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float4 s = S[r][m];
-        sk = fmaf(s.x, cur.kf[4 * m + 0], sk); sq = fmaf(s.x, cur.qf[4 * m + 0], sq);
-        sk = fmaf(s.y, cur.kf[4 * m + 1], sk); sq = fmaf(s.y, cur.qf[4 * m + 1], sq);
-        sk = fmaf(s.z, cur.kf[4 * m + 2], sk); sq = fmaf(s.z, cur.qf[4 * m + 2], sq);
-        sk = fmaf(s.w, cur.kf[4 * m + 3], sk); sq = fmaf(s.w, cur.qf[4 * m + 3], sq);
+      for (int e = 0; e < 16; ++e) {
+        sk = fmaf(S[r][e], cur.kf[e], sk);
+        sq = fmaf(S[r][e], cur.qf[e], sq);
       }
       sk = xor_sum8(sk);
       sq = xor_sum8(sq);
       const float old = g * sk;
       const float delta = beta * (vv[r] - old);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        float4 s = S[r][m];
-        s.x = fmaf(g, s.x, delta * cur.kf[4 * m + 0]);
-        s.y = fmaf(g, s.y, delta * cur.kf[4 * m + 1]);
-        s.z = fmaf(g, s.z, delta * cur.kf[4 * m + 2]);
-        s.w = fmaf(g, s.w, delta * cur.kf[4 * m + 3]);
-        S[r][m] = s;
-        if constexpr (INTER) st_state4(ip + r * 4 * kHeadDim + m * 32, s);
-      }
+      for (int e = 0; e < 16; ++e) S[r][e] = fmaf(g, S[r][e], delta * cur.kf[e]);
+      if constexpr (INTER) RS::store(ip + r * 4 * kHeadDim, j, S[r]);
       if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
     }
     if (t + 1 < T) {
@@ -170,11 +149,9 @@ __global__ void __launch_bounds__(256)
       for (int r = 0; r < NG; ++r) vv[r] = vn[r];
     }
   }
-  ST* nsp = new_pool + head_base + (size_t)row0 * kHeadDim + 4 * j;
+  ST* nsp = new_pool + head_base + (size_t)row0 * kHeadDim;
 #pragma unroll
-  for (int r = 0; r < NG; ++r)
-#pragma unroll
-    for (int m = 0; m < 4; ++m) st_state4(nsp + r * 4 * kHeadDim + m * 32, S[r][m]);
+  for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
 }
 
 template <int RPW, typename IdxT, typename ST>
@@ -249,7 +226,7 @@ int mtp_entry(const void* q, const void* k, const void* v, const ST* initial_sta
   if (!q || !k || !v || !initial_state || !state_indices || !A_log || !a || !dt_bias || !b ||
       !output || !final_state)
     return GDN_ERR_INVALID_ARGUMENT;
-  constexpr uintptr_t sa = 4 * sizeof(ST);
+  constexpr uintptr_t sa = 16;  // 16-byte state accesses
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
       misaligned(initial_state, sa) || misaligned(final_state, sa) ||
       (intermediate_states && misaligned(intermediate_states, sa)) ||
