@@ -154,8 +154,8 @@ constexpr uint32_t AT = 49152;    // fp32 [64][kLd]: A, T in place, then (P lo T
 constexpr uint32_t E = AT + 64 * kLd * 4;  // merge scratch; before it the diagonal decay blocks
 constexpr uint32_t ROWF = E + 64 * 20 * 4;  // fp32 [3][64]: exp(Lam_t - Lam_{16b+15}), b < t/16
 constexpr uint32_t COLF = ROWF + 1024;      // fp32 [64]:    exp(Lam_{j|15} - Lam_j)
-constexpr uint32_t VEC = COLF + 256;        // Lam beta gam rk rq (5 x 64 f32)
-constexpr uint32_t BARS = VEC + 5 * 256;
+constexpr uint32_t VEC = COLF + 256;        // rk rq, then per v-head: Lam beta gam (64 f32 each)
+constexpr uint32_t BARS = VEC + 8 * 256;
 constexpr uint32_t SMEM = BARS + 64;
 constexpr int kLdDE = 20;
 constexpr uint32_t TKQ = 0, TPT = 64;  // TMEM columns (128 allocated)
@@ -173,8 +173,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int row = sp * 32 + lane;  // TMEM lane of this thread
-  // v-head fastest: the two v-heads of a q/k head fetch the same K/Q tiles back to back
-  const int g = blockIdx.x / p.HV, h = blockIdx.x - g * p.HV;
+  // One CTA per (chunk, pair of v-heads sharing a q/k head) when the GVA ratio is even
+  // (one v-head otherwise): K/Q tiles, [K; Q] K^T and the norms serve both.
+  const int hpc = (p.ratio % 2 == 0) ? 2 : 1;
+  const int hgroups = p.HV / hpc;
+  const int g = blockIdx.x / hgroups, h0 = (blockIdx.x - g * hgroups) * hpc;
   const int total = p.chunk_base[p.N];
   if (g >= total) return;
   int lo = 0, hi = p.N - 1;  // the sequence of chunk g: largest n with base[n] <= g
@@ -187,17 +190,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   seq_range(static_cast<const CuT*>(p.cu), n, p.T, s0, s1);
   const long long t0 = s0 + (long long)kC * c;
   const int Lc = (int)min((long long)kC, s1 - t0);
-  const int qh = h / p.ratio;
-  uint8_t* rec = p.rec + ((size_t)g * p.HV + h) * rec_bytes(L2NORM);
+  const int qh = h0 / p.ratio;
   if ((sb & 1023u) != 0) {
     if (tid == 0) atomicOr(&g_split_device_error, ERR_SMEM_ALIGN);
     return;
   }
-  float* Lam = reinterpret_cast<float*>(smem + VEC);
-  float* beta = Lam + 64;
-  float* gam = Lam + 128;
-  float* rk = Lam + 192;
-  float* rq = Lam + 256;
+  float* rk = reinterpret_cast<float*>(smem + VEC);
+  float* rq = rk + 64;
+  auto head_vec = [&](int i) { return rk + 128 + 192 * i; };  // Lam | beta | gam of head i
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BARS);  // kqtma, kq, pt
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + 32);
   if (warp == 0) {
@@ -220,7 +220,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     tma_load_2d(smem + KQ + 8192, &tm_q, &bars[0], qh * 128, (int)t0);
     tma_load_2d(smem + KQ + 24576, &tm_q, &bars[0], qh * 128 + 64, (int)t0);
   }
-  if (warp == 1) {  // gates: cumulative log decay, beta, gamma
+  if (warp >= 1 && warp <= hpc) {  // gates of head warp - 1: cumulative log decay, beta, gamma
+    const int h = h0 + warp - 1;
+    float* Lam = head_vec(warp - 1);
+    float* beta = Lam + 64;
+    float* gam = Lam + 128;
     float lg[2], bb[2];
     if (p.gates_pre) {
 #pragma unroll
@@ -259,6 +263,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   }
   bool ok = true;
   uint64_t* pend = nullptr;  // copy or MMA group in flight
+  uint32_t pend_par = 0;
   do {
     pend = &bars[0];
     if (!(ok = cta_wait(&bars[0], 0, ERR_TMA_TIMEOUT))) break;
@@ -304,7 +309,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         rq[tid] = 1.f;
       }
     }
-    __syncthreads();
+    if (!(ok = cta_wait(&bars[1], 0, ERR_MMA_TIMEOUT))) break;  // also orders the norms
+    pend = nullptr;
+    for (int hi = 0; hi < hpc && ok; ++hi) {
+    const int h = h0 + hi;
+    uint8_t* rec = p.rec + ((size_t)g * p.HV + h) * rec_bytes(L2NORM);
+    const float* Lam = head_vec(hi);
+    const float* beta = Lam + 64;
+    const float* gam = Lam + 128;
     // decay factors exp(Lam_t - Lam_j), j <= t, with no positive exponent: directly
     // inside the diagonal 16x16 blocks; across blocks through the last token e of j's
     // block, exp(Lam_t - Lam_e) exp(Lam_e - Lam_j)
@@ -325,8 +337,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
           RF[64 * blk + tid] = (16 * blk + 15 < tid) ? __expf(Lam[tid] - Lam[16 * blk + 15]) : 0.f;
       }
     }
-    if (!(ok = cta_wait(&bars[1], 0, ERR_MMA_TIMEOUT))) break;
-    pend = nullptr;
+    __syncthreads();
     tc_fence_after();
     // A (from Skk) -> AT; P (from Sqk) -> [P hi; P lo] image over the consumed K/Q tiles
     {
@@ -424,7 +435,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
       umma_commit(&bars[2]);
     }
     pend = &bars[2];
-    if (!(ok = cta_wait(&bars[2], 0, ERR_MMA_TIMEOUT))) break;
+    pend_par = hi & 1;
+    if (!(ok = cta_wait(&bars[2], hi & 1, ERR_MMA_TIMEOUT))) break;
     pend = nullptr;
     tc_fence_after();
     // P T = (P hi T) + (P lo T): lanes 64..127 hand their part over through AT
@@ -464,9 +476,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         }
       }
     }
+    // the next head reuses AT, the P image and the P T columns
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    }  // per v-head
   } while (0);
   if (!ok && tid == 0 && pend != nullptr) {  // let the copy / MMA in flight land
-    mbar_wait(pend, 0, 1u << 20);
+    mbar_wait(pend, pend_par, 1u << 20);
   }
   tc_fence_before();
   __syncthreads();
@@ -895,7 +912,9 @@ cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const C
                                             const_cast<int*>(sp.chunk_base));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  ka<<<dim3((unsigned)(slots * sp.HV)), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk, sp);
+  const int hpc = (sp.ratio % 2 == 0) ? 2 : 1;  // v-heads per preparation CTA
+  ka<<<dim3((unsigned)(slots * (sp.HV / hpc))), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk,
+                                                                                      sp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   kb<<<dim3((unsigned)((long long)sp.N * sp.HV * st::kSplitV)), dim3(st::kThreads), st::SMEM,

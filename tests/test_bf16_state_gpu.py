@@ -35,6 +35,20 @@ def test_decode_bf16_state_vs_oracle(cuda, l2):
     assert (s.cpu() == rs).float().mean().item() > 0.999
 
 
+def test_decode_bf16_state_many_heads_vs_oracle(cuda):
+    """B=32 x 32 v-heads (1024 heads: the largest-CTA configuration of the kernel)."""
+    pkg = load_pkg()
+    inp = bf16_state(pkg.workloads.decode_inputs(32, seed=65))
+    ro, rs = O.decode(O.l2norm(inp["q"]), O.l2norm(inp["k"]), inp["v"], inp["state"],
+                      inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+    d = to(inp, cuda)
+    o, s = pkg.gdn_decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
+                          d["b"], d["scale"], use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert_parity(o, s.float(), ro, rs.float(), what="bf16 B=32")
+    assert (s.cpu() == rs).float().mean().item() > 0.999
+
+
 def test_decode_bf16_state_b1024_equals_shards_bitwise(cuda):
     pkg = load_pkg()
     inp = to(bf16_state(pkg.workloads.decode_inputs(1024, seed=62)), cuda)
