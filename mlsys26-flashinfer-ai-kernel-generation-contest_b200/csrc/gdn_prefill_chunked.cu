@@ -737,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace pl {
 constexpr int kThreads = 512;
 constexpr uint32_t kGroup = 256;        // threads per warp group
-constexpr uint32_t kBarState = 1, kBarPrep = 2;
+constexpr uint32_t kBarState = 1, kBarPrep = 2, kBarGates = 3;
 // shared memory
 constexpr uint32_t KQ0 = 0, KQ1 = 32768;  // per buffer: K0 | Q0 | K1 | Q1 (8 KB each)
 constexpr uint32_t V = 65536;             // V0 | V1
@@ -873,25 +873,24 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
     // =========================== prep group: chunk c one ahead of the state group
     // raw bf16 bits, converted where they are used one chunk later (so that nothing
     // waits for these loads while the current chunk is processed)
-    uint32_t ga[2] = {0u, 0u}, gb[2] = {0u, 0u};
+    // Gates: warps 14 and 15, one token per lane (gt = token; -1.. for the other warps).
+    // Raw bits are loaded one chunk ahead and converted where they are used.
+    const int gt = u - 192;
+    uint32_t ga = 0u, gb = 0u;
     auto load_gates = [&](int cc) {
       const long long tc0 = s0 + (long long)kC * cc;
       const int Lcc = (int)min((long long)kC, s1 - tc0);
       const unsigned short* ra = reinterpret_cast<const unsigned short*>(p.a);
       const unsigned short* rb = reinterpret_cast<const unsigned short*>(p.b);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = 2 * lane + e;
-        if (t < Lcc) {
-          const size_t ti = (size_t)(tc0 + t) * HV + h;
-          if (p.gates_pre) {  // fp32 bits of the precomputed decay and beta
-            ga[e] = p.g_alpha ? __float_as_uint(p.g_alpha[ti]) : 0x3F800000u;
-            gb[e] = p.g_beta ? __float_as_uint(p.g_beta[ti]) : 0x3F800000u;
-          } else {            // bf16 bits of a and b
-            ga[e] = ra[ti];
-            gb[e] = rb[ti];
-          }
-        }
+      // unconditional loads (tokens past the end re-read the last one; compute_gates
+      // masks them), so that nothing waits for the values before they are used
+      const size_t ti = (size_t)(tc0 + min(gt, Lcc - 1)) * HV + h;
+      if (p.gates_pre) {  // fp32 bits of the precomputed decay and beta
+        ga = p.g_alpha ? __float_as_uint(p.g_alpha[ti]) : 0x3F800000u;
+        gb = p.g_beta ? __float_as_uint(p.g_beta[ti]) : 0x3F800000u;
+      } else {            // bf16 bits of a and b
+        ga = ra[ti];
+        gb = rb[ti];
       }
     };
     // log decays (inclusive cumsum), beta and gamma of chunk cc into its vector set
@@ -901,33 +900,31 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       float* Lam = vecp(cc % 3, 0);
       float* beta = vecp(cc % 3, 1);
       float* gam = vecp(cc % 3, 2);
-      float lg[2], bb[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const bool valid = 2 * lane + e < Lcc;
-        if (p.gates_pre) {
-          lg[e] = valid ? log_alpha(__uint_as_float(ga[e])) : 0.f;
-          bb[e] = valid ? __uint_as_float(gb[e]) : 0.f;
-        } else {
-          lg[e] = valid ? nexpA * softplus_f(__uint_as_float(ga[e] << 16) + dtb) : 0.f;
-          bb[e] = valid ? sigmoid_f(__uint_as_float(gb[e] << 16)) : 0.f;
-        }
+      const bool valid = gt < Lcc;
+      float lg, bb;
+      if (p.gates_pre) {
+        lg = valid ? log_alpha(__uint_as_float(ga)) : 0.f;
+        bb = valid ? __uint_as_float(gb) : 0.f;
+      } else {
+        lg = valid ? nexpA * softplus_f(__uint_as_float(ga << 16) + dtb) : 0.f;
+        bb = valid ? sigmoid_f(__uint_as_float(gb << 16)) : 0.f;
       }
-      float x = lg[0] + lg[1];
+      float x = lg;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const float y = __shfl_up_sync(0xffffffffu, x, off);
         if (lane >= off) x += y;
       }
-      const float x0 = x - lg[1];
-      Lam[2 * lane] = x0;
-      Lam[2 * lane + 1] = x;
-      beta[2 * lane] = bb[0];
-      beta[2 * lane + 1] = bb[1];
-      gam[2 * lane] = expf(x0);
-      gam[2 * lane + 1] = expf(x);
+      if (gt < 32) Lam[gt] = x;
+      group_sync(kBarGates, 64);  // warp 15 continues from warp 14's last sum
+      if (gt >= 32) {
+        x += Lam[31];
+        Lam[gt] = x;
+      }
+      beta[gt] = bb;
+      gam[gt] = expf(x);
     };
-    if (warp == 9) {
+    if (gt >= 0) {
       load_gates(0);
       compute_gates(0);
       if (nchunks > 1) load_gates(1);
@@ -988,8 +985,8 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         }
         umma_commit(&bars->kq);
       }
-      // while the MMA runs: gates (warp 9) and q/k row norms (warps 10-13)
-      if (warp == 9 && c + 1 < nchunks) {  // gates of chunk c + 1, then prefetch c + 2
+      // while the MMA runs: gates (warps 14-15) and q/k row norms (warps 10-13)
+      if (gt >= 0 && c + 1 < nchunks) {  // gates of chunk c + 1, then prefetch c + 2
         compute_gates(c + 1);
         if (c + 2 < nchunks) load_gates(c + 2);
       }
@@ -1342,6 +1339,9 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       }
       pend_bar[0] = nullptr;
       tc_fence_after();
+      // K/Q buffer `par`, the P buffer of this parity and this chunk's vector set are
+      // consumed: fetch chunk c + 2 now, so that its copy overlaps this epilogue
+      if (tid == 0 && c + 2 < nchunks) issue_kq(c + 2);
       // epilogue: S(c+1) -> bf16 hi/lo in TMEM (or the final state to global); O -> staging
       const bool last = c + 1 == nchunks;
       // state checkpoint after this chunk, when one is due
@@ -1409,7 +1409,6 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         }
       }
       group_sync(kBarState, kGroup);
-      if (tid == 0 && c + 2 < nchunks) issue_kq(c + 2);  // buffer `par` is free again
     }
   }
   // a wait ran out: tell the other group, give our in-flight copies / MMAs one more
