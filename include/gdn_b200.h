@@ -270,8 +270,9 @@ int gdn_prefill_launch_noalloc(const void* q, const void* k, const void* v, cons
 /*
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
- * wait ran out, 2 = a tensor-core wait ran out; -1 = the device reported an
- * error).  Every wait inside the kernels is bounded; a wait that runs out sets
+ * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory
+ * stage of the streaming decode kernel was never released; -1 = the device
+ * reported an error).  Every wait inside the kernels is bounded; a wait that runs out sets
  * a bit, the kernel releases its resources and returns instead of hanging.
  * The bits are cleared when `clear` != 0.  No counterpart in the reference.
  */

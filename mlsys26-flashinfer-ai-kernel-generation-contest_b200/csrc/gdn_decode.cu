@@ -22,6 +22,7 @@
 // of 8 warps owns 8*RPW rows of one head; all of a thread's state loads are
 // issued before any arithmetic so each SM keeps ~64-128 KiB in flight.
 #include "gdn_common.cuh"
+#include "sm100.cuh"
 
 namespace gdn {
 namespace {
@@ -155,6 +156,286 @@ inline bool misaligned(const void* p, uintptr_t n) { return (reinterpret_cast<ui
 
 namespace gdn {
 namespace {
+// ------------------------------------------------------------ streaming variant
+// For batches that fill the GPU: a persistent kernel (one or two CTAs per SM) whose
+// copy warp streams each head's state, q, k and v rows into a ring of shared-memory
+// stages with plain bulk copies (cp.async.bulk, mbarrier completion), while 8 compute
+// warps work on the stage before it.  Up to (stages - 1) heads of state are in flight
+// per CTA at any time, independent of how long the compute warps take, so HBM sees a
+// steady stream instead of the load-all / compute / store waves of decode_kernel.
+// Rows are read from the stage one at a time (few registers per thread).  Per row the
+// arithmetic is decode_kernel's, in the same order (identical results).
+__device__ unsigned int g_decode_device_error = 0;
+constexpr unsigned kDecodeErrCopyTimeout = 1u;  // a stage's copies never landed
+constexpr unsigned kDecodeErrFreeTimeout = 8u;  // a stage was never released
+
+template <typename ST>
+struct StreamCfg {
+  static constexpr uint32_t kStateBytes = kHeadDim * kHeadDim * sizeof(ST);
+  static constexpr uint32_t kStage = kStateBytes + 1024;  // state | q | k | v (256 B each)
+  static constexpr int kStages = 3;
+  static constexpr int kCtasPerSm = sizeof(ST) == 2 ? 2 : 1;
+  static constexpr uint32_t kBars = kStages * kStage;
+  static constexpr uint32_t kSmem = kBars + 64;
+  static constexpr int kThreads = 288;  // 8 compute warps + the copy warp
+};
+
+// 16 columns of a state row held in shared memory (same column set as RowSlice)
+template <typename ST>
+__device__ __forceinline__ void load_row_smem(uint32_t row_addr, int j, float (&x)[16]) {
+  using RS = RowSlice<ST>;
+#pragma unroll
+  for (int m = 0; m < RS::kChunks; ++m) {
+    const uint4 u = sm100::ld_shared_v4(row_addr + (uint32_t)(RS::col(j, m) * sizeof(ST)));
+    if constexpr (sizeof(ST) == 4) {
+      x[4 * m] = __uint_as_float(u.x);
+      x[4 * m + 1] = __uint_as_float(u.y);
+      x[4 * m + 2] = __uint_as_float(u.z);
+      x[4 * m + 3] = __uint_as_float(u.w);
+    } else {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = bf2x2_to_f2(w[e]);
+        x[8 * m + 2 * e] = f.x;
+        x[8 * m + 2 * e + 1] = f.y;
+      }
+    }
+  }
+}
+// the lane's 16 columns of a bf16 vector in shared memory
+template <typename ST>
+__device__ __forceinline__ void load_vec_smem(uint32_t vec_addr, int j, float (&x)[16]) {
+  using RS = RowSlice<ST>;
+#pragma unroll
+  for (int m = 0; m < RS::kChunks; ++m) {
+    const uint32_t a = vec_addr + 2u * (uint32_t)RS::col(j, m);
+    if constexpr (RS::kVec == 4) {
+      uint32_t w0, w1;
+      asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(a));
+      const float2 f0 = bf2x2_to_f2(w0), f1 = bf2x2_to_f2(w1);
+      x[4 * m] = f0.x; x[4 * m + 1] = f0.y; x[4 * m + 2] = f1.x; x[4 * m + 3] = f1.y;
+    } else {
+      const uint4 u = sm100::ld_shared_v4(a);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = bf2x2_to_f2(w[e]);
+        x[8 * m + 2 * e] = f.x;
+        x[8 * m + 2 * e + 1] = f.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool stream_wait(uint64_t* bar, uint32_t parity,
+                                            volatile int* abort_flag, unsigned code) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (sm100::mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  atomicOr(&g_decode_device_error, code);
+  *abort_flag = 1;
+  return false;
+}
+
+template <bool L2NORM, typename ST>
+__global__ void __launch_bounds__(StreamCfg<ST>::kThreads, StreamCfg<ST>::kCtasPerSm)
+    decode_stream_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                         const __nv_bfloat16* __restrict__ v, const ST* state,
+                         const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
+                         const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ b,
+                         float scale, __nv_bfloat16* __restrict__ out, ST* new_state, int HQ,
+                         int HV, int ratio, int heads) {
+  using C = StreamCfg<ST>;
+  using RS = RowSlice<ST>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sb = sm100::smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBars);
+  uint64_t* empty = full + C::kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int nmine = heads > (int)blockIdx.x ? (heads - 1 - (int)blockIdx.x) / G + 1 : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 8);
+    }
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ============================== copy warp
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nmine; ++i) {
+        const int slot = i % C::kStages;
+        if (i >= C::kStages &&
+            !stream_wait(&empty[slot], ((i / C::kStages) - 1) & 1, abort_flag, kDecodeErrFreeTimeout))
+          break;
+        const int bh = (int)blockIdx.x + i * G;
+        const int bidx = bh / HV, h = bh - bidx * HV, qh = h / ratio;
+        uint8_t* st = smem + (size_t)slot * C::kStage;
+        sm100::mbar_arrive_expect_tx(&full[slot], C::kStateBytes + 768u);
+        sm100::bulk_load(st, state + (size_t)bh * kHeadDim * kHeadDim, C::kStateBytes, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes, q + ((size_t)bidx * HQ + qh) * kHeadDim, 256u, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes + 256, k + ((size_t)bidx * HQ + qh) * kHeadDim, 256u, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes + 512, v + (size_t)bh * kHeadDim, 256u, &full[slot]);
+        issued = i + 1;
+      }
+      if (*abort_flag) {  // let copies still in flight land before the CTA exits (bounded)
+        for (int i = issued - C::kStages > 0 ? issued - C::kStages : 0; i < issued; ++i)
+          sm100::mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, 1u << 20);
+      }
+    }
+    return;
+  }
+  // ============================== compute warps: 16 rows each (rows row0 + 4r)
+  const int sub = lane >> 3, j = lane & 7;
+  const int row0 = warp * 16 + sub;
+  scale = default_scale(scale);
+  // gate inputs of the next head, loaded one head ahead
+  auto load_gate_inputs = [&](int i, float& al, float& av, float& db, float& bv) {
+    const int bh = (int)blockIdx.x + i * G;
+    const int h = bh % HV;
+    al = __ldg(A_log + h);
+    db = __ldg(dt_bias + h);
+    av = bf2f(a[bh]);
+    bv = bf2f(b[bh]);
+  };
+  float nal = 0.f, nav = 0.f, ndb = 0.f, nbv = 0.f;
+  if (nmine > 0) load_gate_inputs(0, nal, nav, ndb, nbv);
+  for (int i = 0; i < nmine; ++i) {
+    const float al = nal, av = nav, db = ndb, bv = nbv;
+    if (i + 1 < nmine) load_gate_inputs(i + 1, nal, nav, ndb, nbv);
+    const int slot = i % C::kStages;
+    if (!stream_wait(&full[slot], (i / C::kStages) & 1, abort_flag, kDecodeErrCopyTimeout)) break;
+    const int bh = (int)blockIdx.x + i * G;
+    const uint32_t st = sb + (uint32_t)slot * C::kStage;
+    float kf[16], qf[16], vv[4];
+    load_vec_smem<ST>(st + C::kStateBytes, j, qf);
+    load_vec_smem<ST>(st + C::kStateBytes + 256u, j, kf);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      uint16_t bits;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits)
+                   : "r"(st + C::kStateBytes + 512u + 2u * (uint32_t)(row0 + 4 * r)));
+      vv[r] = __uint_as_float((uint32_t)bits << 16);
+    }
+    const float g = expf(gate_log_g(al, av, db));
+    const float beta = sigmoid_f(bv);
+    if constexpr (L2NORM) {
+      float ssk = 0.f, ssq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        ssk = fmaf(kf[e], kf[e], ssk);
+        ssq = fmaf(qf[e], qf[e], ssq);
+      }
+      ssk = xor_sum8(ssk);
+      ssq = xor_sum8(ssq);
+      const float rk = rsqrtf(ssk + kL2NormEps);
+      const float rq = rsqrtf(ssq + kL2NormEps);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        kf[e] *= rk;
+        qf[e] *= rq;
+      }
+    }
+    float kq = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) kq = fmaf(kf[e], qf[e], kq);
+    kq = xor_sum8(kq);
+    ST* nsp = new_state + (size_t)bh * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
+    __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float Sr[16];
+      load_row_smem<ST>(st + (uint32_t)((row0 + 4 * r) * kHeadDim * sizeof(ST)), j, Sr);
+      if (r == 3) {  // this warp's last read of the stage: release it
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&empty[slot]);
+      }
+      float sk = 0.f, sq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        sk = fmaf(Sr[e], kf[e], sk);
+        sq = fmaf(Sr[e], qf[e], sq);
+      }
+      sk = xor_sum8(sk);
+      sq = xor_sum8(sq);
+      const float old = g * sk;
+      const float delta = beta * (vv[r] - old);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) Sr[e] = fmaf(g, Sr[e], delta * kf[e]);
+      RS::store(nsp + r * 4 * kHeadDim, j, Sr);
+      if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
+    }
+  }
+}
+
+template <typename ST>
+cudaError_t launch_stream(const void* q, const void* k, const void* v, const ST* state,
+                          const float* A_log, const void* a, const float* dt_bias, const void* b,
+                          float scale, void* out, ST* new_state, int batch, int HQ, int HV,
+                          bool l2norm, cudaStream_t stream) {
+  using C = StreamCfg<ST>;
+  static int sms[64] = {};
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return cudaErrorInvalidValue;
+    cudaError_t e1 = cudaFuncSetAttribute(decode_stream_kernel<true, ST>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaError_t e2 = cudaFuncSetAttribute(decode_stream_kernel<false, ST>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) return cudaErrorInvalidValue;
+    configured[dev] = true;
+  }
+  const int heads = batch * HV;
+  const int grid = heads < sms[dev] * C::kCtasPerSm ? heads : sms[dev] * C::kCtasPerSm;
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  auto A = static_cast<const __nv_bfloat16*>(a);
+  auto Bt = static_cast<const __nv_bfloat16*>(b);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  if (l2norm)
+    decode_stream_kernel<true, ST><<<grid, C::kThreads, C::kSmem, stream>>>(
+        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, HV / HQ, heads);
+  else
+    decode_stream_kernel<false, ST><<<grid, C::kThreads, C::kSmem, stream>>>(
+        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, HV / HQ, heads);
+  return cudaGetLastError();
+}
+}  // namespace
+
+// Device error bits of the streaming decode kernel (bounded waits that ran out).
+unsigned read_decode_device_error(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+  if (clear && v != 0) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_decode_device_error, &zero, sizeof(zero)) != cudaSuccess) return ~0u;
+  }
+  return v;
+}
+}  // namespace gdn
+
+namespace gdn {
+namespace {
+// Where the streaming kernel is the faster one (measured on B200): bf16 state from a
+// few waves of heads on.
+template <typename ST>
+bool stream_pays(long long heads) {
+  return sizeof(ST) == 2 && heads >= 4 * 148;
+}
+
 template <typename ST>
 int decode_entry(const void* q, const void* k, const void* v, const ST* state, const float* A_log,
                  const void* a, const float* dt_bias, const void* b, float scale, void* output,
@@ -175,8 +456,14 @@ int decode_entry(const void* q, const void* k, const void* v, const ST* state, c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool l2 = use_qk_l2norm != 0;
   cudaError_t err;
-  // Enough CTAs to fill 148 SMs several times over; bigger CTAs when there are.
-  if (heads >= 4 * 148)
+  // Batches that fill the GPU several times over: the streaming kernel (bulk copies
+  // need 16-byte aligned q, k, v rows); otherwise one-shot CTAs, bigger when there are
+  // enough heads to fill 148 SMs several times over.
+  if (state != nullptr && stream_pays<ST>(heads) && !misaligned(q, 16) && !misaligned(k, 16) &&
+      !misaligned(v, 16))
+    err = launch_stream<ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch,
+                            num_q_heads, num_v_heads, l2, st);
+  else if (heads >= 4 * 148)
     err = launch_rpw<16, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
   else if (heads >= 2 * 148)
     err = launch_rpw<8, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);

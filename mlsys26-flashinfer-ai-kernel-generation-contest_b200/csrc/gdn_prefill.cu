@@ -212,6 +212,7 @@ extern "C" int gdn_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
   const unsigned a = gdn::read_device_error(clear != 0);
   const unsigned b = gdn::read_split_device_error(clear != 0);
-  if (a == ~0u || b == ~0u) return -1;
-  return (int)(a | b);
+  const unsigned d = gdn::read_decode_device_error(clear != 0);
+  if (a == ~0u || b == ~0u || d == ~0u) return -1;
+  return (int)(a | b | d);
 }

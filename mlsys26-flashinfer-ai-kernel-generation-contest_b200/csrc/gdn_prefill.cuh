@@ -69,5 +69,7 @@ unsigned read_split_device_error(bool clear);
 
 // Device-side error flag set by a bounded wait that ran out (0 = none).
 unsigned read_device_error(bool clear);
+// Same for the streaming decode kernel.
+unsigned read_decode_device_error(bool clear);
 
 }  // namespace gdn

@@ -62,6 +62,28 @@ def test_decode_bf16_state_b1024_equals_shards_bitwise(cuda):
         assert torch.equal(po, o[sl]) and torch.equal(ps, s[sl])
 
 
+def test_decode_bf16_streaming_equals_one_shot_bitwise(cuda):
+    """B=32 (1024 heads) takes the streaming kernel, B=4 slices the one-shot kernel: the
+    per-row arithmetic is the same, so the results are bitwise equal; also in place."""
+    pkg = load_pkg()
+    inp = to(bf16_state(pkg.workloads.decode_inputs(32, seed=66)), cuda)
+    args = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")
+    o, s = pkg.gdn_decode(*[inp[x] for x in args], inp["scale"], use_qk_l2norm=True)
+    for r in range(8):
+        sl = slice(4 * r, 4 * (r + 1))
+        part = {x: (inp[x][sl].contiguous() if x not in ("A_log", "dt_bias") else inp[x])
+                for x in args}
+        po, ps = pkg.gdn_decode(*[part[x] for x in args], inp["scale"], use_qk_l2norm=True)
+        assert torch.equal(po, o[sl]) and torch.equal(ps, s[sl])
+    st = inp["state"].clone()
+    o2, s2 = pkg.gdn_decode(*[inp[x] if x != "state" else st for x in args], inp["scale"], None, st,
+                            use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert s2.data_ptr() == st.data_ptr()
+    assert torch.equal(o2, o) and torch.equal(st, s)
+    assert pkg.device_error() == 0
+
+
 def test_decode_bf16_zero_state(cuda):
     pkg = load_pkg()
     inp = pkg.workloads.decode_inputs(3, hq=1, hv=2, seed=63, with_state=False)
