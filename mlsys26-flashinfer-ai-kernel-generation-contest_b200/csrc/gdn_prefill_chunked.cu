@@ -757,7 +757,7 @@ constexpr uint32_t SMEM = COLF + 64 * 4;
 constexpr int kLdDE = 20;  // row stride of DEF (floats): conflict-free float4 rows
 static_assert(SMEM <= 232448, "shared memory budget");
 // TMEM columns
-constexpr uint32_t TS = 0, TSH = 128, TSL = 192, TUT = 256, TO = 320, TSK = 384, TKQ = 448;
+constexpr uint32_t TS = 0, TSH = 128, TSL = 192, TUT = 256, TSK = 320, TO = 384, TKQ = 448;
 
 struct Bars {
   uint64_t kqtma[2], vtma, kq, g1, g2, g3, t_ready, t_free;
@@ -1177,15 +1177,16 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       // G1: S K^T (S hi + S lo) and O = S_hi Q~^T, A operands from TMEM
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+        // S_hi [K; Q~]^T as one N = 128 MMA per k-step (K rows then Q~ rows are one
+        // 128-row tile; D columns TSK.. then TO = TSK + 64), then S_lo K^T (N = 64)
+        const uint32_t id128 = umma_idesc_bf16(128, 128, false, false);
+        const uint32_t id64 = umma_idesc_bf16(128, 64, false, false);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
           const uint64_t kd = umma_desc_k(sb + kqb + off);
-          umma_bf16_tmem_a(tmem + TSK, tmem + TSH + 8u * ks, kd, idesc, ks > 0);
-          umma_bf16_tmem_a(tmem + TSK, tmem + TSL + 8u * ks, kd, idesc, 1);
-          umma_bf16_tmem_a(tmem + TO, tmem + TSH + 8u * ks, umma_desc_k(sb + kqb + 8192u + off),
-                           idesc, ks > 0);
+          umma_bf16_tmem_a(tmem + TSK, tmem + TSH + 8u * ks, kd, id128, ks > 0);
+          umma_bf16_tmem_a(tmem + TSK, tmem + TSL + 8u * ks, kd, id64, 1);
         }
         umma_commit(&bars->g1);
       }
