@@ -87,7 +87,9 @@ __device__ __forceinline__ void st_v4(uint32_t addr, uint4 v) {
 // ---- warp-level tensor-core products for the inverse's block merges ----
 // D(16x8) = X(16xK) * Y(Kx8), fp32 operands as 3xTF32 (hi.hi + hi.lo + lo.hi;
 // hi = the top 10 mantissa bits, lo = the exact residual), so the result carries
-// ~21 significant bits.  Fragment layout of mma.m16n8k8 (tf32): g = lane/4,
+// ~21 significant bits.  The three terms accumulate separately (three independent
+// mma.sync chains instead of one, which matters where tcgen05 MMAs of the same CTA
+// keep the tensor pipe busy) and are summed at the end.  Fragment layout of mma.m16n8k8 (tf32): g = lane/4,
 // t = lane%4; A: (g, t) (g+8, t) (g, t+4) (g+8, t+4); B: (t, g) (t+4, g);
 // C: (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1).
 
@@ -102,6 +104,7 @@ __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
 __device__ __forceinline__ void mma_tile_tf32x3(const float* X, int ldx, const float* Y, int ldy,
                                                 int K, float (&c)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
   c[0] = c[1] = c[2] = c[3] = 0.f;
   for (int k0 = 0; k0 < K; k0 += 8) {
     const float af[4] = {X[g * ldx + k0 + t], X[(g + 8) * ldx + k0 + t],
@@ -118,10 +121,12 @@ __device__ __forceinline__ void mma_tile_tf32x3(const float* X, int ldx, const f
       bh[i] = __float_as_uint(bf[i]) & 0xFFFFE000u;
       bl[i] = __float_as_uint(bf[i] - __uint_as_float(bh[i]));
     }
-    mma_tf32(c, al, bh);
-    mma_tf32(c, ah, bl);
+    mma_tf32(c1, al, bh);
+    mma_tf32(c2, ah, bl);
     mma_tf32(c, ah, bh);
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] += c1[i] + c2[i];
 }
 __device__ __forceinline__ void store_tile(float* D, int ldd, const float (&c)[4], float sgn) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
