@@ -366,20 +366,25 @@ class PrefillWork:
 
 
 # --------------------------------------------------------------------------- timing
-def time_steps(fn, steps, warmup, dist, per_launch_events=True):
-    """Returns (max-over-ranks ms per step, mean kernel ms per step on this rank)."""
+def time_steps(fn, steps, warmup, dist, per_launch_events=True, flush=None):
+    """Returns (max-over-ranks ms per step, mean kernel ms per step on this rank).
+    With `flush` (workloads smaller than L2), L2 is flushed before every step outside the
+    per-step events, and the step time is the mean of those events (max over ranks)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
+    per_launch_events = per_launch_events or flush is not None
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(steps)] if per_launch_events else []
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for i in range(steps):
+        if flush is not None:
+            flush()
         if per_launch_events:
             ev[i][0].record(stream)
         fn()
@@ -391,7 +396,35 @@ def time_steps(fn, steps, warmup, dist, per_launch_events=True):
     torch.cuda.synchronize()
     total = t0.elapsed_time(t1)
     per_kernel = (sum(a.elapsed_time(b) for a, b in ev) / steps) if ev else total / steps
+    if flush is not None:
+        return dist.max(per_kernel * steps) / steps, per_kernel
     return dist.max(total) / steps, per_kernel
+
+
+def graph_steps(work, n_graphs):
+    """CUDA graphs of `n_graphs` consecutive steps of `work`, one step per graph (decode
+    ping-pongs its state between two buffers, so two graphs alternate), replayed in turn:
+    the way a serving loop launches decode, without the Python wrapper's host time between
+    kernels.  Returns the replay function and the graphs (kept alive by the caller)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # first calls (one-time kernel configuration) off capture
+        for _ in range(n_graphs):
+            work.step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = []
+    for _ in range(n_graphs):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            work.step()
+        graphs.append(g)
+    turn = [0]
+
+    def replay():
+        graphs[turn[0]].replay()
+        turn[0] = (turn[0] + 1) % n_graphs
+    return replay, graphs
 
 
 def cpu_baseline_decode(batch, budget_s=10.0, state_bf16=False):
@@ -445,10 +478,22 @@ def cpu_baseline_prefill(cfg_name, budget_tokens=4096):
 
 
 # --------------------------------------------------------------------------- arms
-def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf16=False):
+def l2_flusher(units, dev):
+    """None when a step moves more than L2 holds; else a function that overwrites L2."""
+    if units > L2_BYTES:
+        return None
+    buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    return lambda: buf.fill_(1.0)
+
+
+def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf16=False,
+                   graphs=True):
     w = DecodeWork(pkg, batch, dev, seed=dist.rank, state_bf16=state_bf16)
+    fn, keep = graph_steps(w, 2) if graphs else (w.step, None)
+    flush = l2_flusher(w.units, dev)
     with ClockSampler(dev.index) as clk:
-        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+        ms, kern_ms = time_steps(fn, steps, warmup, dist, flush=flush)
+    del keep
     total_bytes = w.units * dist.world
     res = {"ms": ms, "kern_ms": kern_ms, "value": total_bytes / (ms * 1e-3) / 1e9,
            "achieved": w.units / (kern_ms * 1e-3) / 1e9, "clocks": clk.summary(),
@@ -463,10 +508,13 @@ def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf
     return res
 
 
-def measure_mtp(pkg, dist, batch, steps, warmup, dev, with_e2e=True):
+def measure_mtp(pkg, dist, batch, steps, warmup, dev, with_e2e=True, graphs=True):
     w = MtpWork(pkg, batch, dev, seed=dist.rank)
+    fn, keep = graph_steps(w, 1) if graphs else (w.step, None)
+    flush = l2_flusher(w.units, dev)
     with ClockSampler(dev.index) as clk:
-        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+        ms, kern_ms = time_steps(fn, steps, warmup, dist, flush=flush)
+    del keep
     total_bytes = w.units * dist.world
     res = {"ms": ms, "kern_ms": kern_ms, "value": total_bytes / (ms * 1e-3) / 1e9,
            "achieved": w.units / (kern_ms * 1e-3) / 1e9, "clocks": clk.summary(),
@@ -557,7 +605,8 @@ def run_ours(args, dist):
     line = {"impl": "ours"}
     if kind in ("decode", "decode_bf16state"):
         bf = kind == "decode_bf16state"
-        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev, state_bf16=bf)
+        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev, state_bf16=bf,
+                           graphs=not args.no_graphs)
         line.update({
             "metric": "decode state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
@@ -569,14 +618,18 @@ def run_ours(args, dist):
                                    f"q/k L2-normalised in-kernel",
                        "batch_per_gpu": param, "global_batch": param * dist.world,
                        "parallelism": f"batch-sharded x{dist.world}, no collective",
-                       "l2": f"inputs > L2: {r['units'] / 1e6:.0f} MB state traffic per step, "
-                             f"state ping-pong"},
+                       "l2": (f"inputs > L2: {r['units'] / 1e6:.0f} MB state traffic per step, "
+                              f"state ping-pong" if r["units"] > L2_BYTES else
+                              f"L2 flushed before every step ({r['units'] / 1e6:.1f} MB state "
+                              f"traffic per step)"),
+                       "launch": "CUDA graph replay" if not args.no_graphs else "eager"},
             "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
             "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_ms": round(r["kern_ms"], 5),
         })
     elif kind == "mtp":
-        r = measure_mtp(pkg, dist, param, args.steps, args.warmup, dev)
+        r = measure_mtp(pkg, dist, param, args.steps, args.warmup, dev,
+                        graphs=not args.no_graphs)
         line.update({
             "metric": "mtp state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
@@ -588,7 +641,8 @@ def run_ours(args, dist):
                                    f"L2-normalised in-kernel",
                        "batch_per_gpu": param, "draft_tokens": MTP_T,
                        "parallelism": f"batch-sharded x{dist.world}, no collective",
-                       "l2": f"inputs > L2: {r['units'] / 1e9:.2f} GB state traffic per step"},
+                       "l2": f"inputs > L2: {r['units'] / 1e9:.2f} GB state traffic per step",
+                       "launch": "CUDA graph replay" if not args.no_graphs else "eager"},
             "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
             "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
             "kernel_ms": round(r["kern_ms"], 5),
@@ -683,6 +737,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_b128")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-extra", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
