@@ -767,6 +767,10 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         tmem_st8(tl + TST + 32u + vq, sc);
         tmem_wait_st();
       }
+      // this thread's V slice and vectors, read while G1 runs
+      const int rr = sp < 2 ? row : row - 64;
+      const float bj = vec[rr], cj = vec[64 + rr], ut = vec[128 + rr], ct = vec[192 + rr];
+      const uint4 va = ld_shared_v4(sb + (bf ? V1 : V0) + rr * (2 * kVB) + 16 * qc);
       if (!wait_or_abort(&bars->g1, par, abort_flag, ERR_MMA_TIMEOUT)) break;
       tc_fence_after();
       if (sp < 2) {
@@ -774,8 +778,6 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         float sk[8], sk2[8];
         tmem_ld8(tl + TG1 + vq, sk);
         tmem_ld8(tl + TG1 + 32u + vq, sk2);
-        const float bj = vec[row], cj = vec[64 + row];
-        const uint4 va = ld_shared_v4(sb + (bf ? V1 : V0) + row * (2 * kVB) + 16 * qc);
         tmem_wait_ld();
         const uint32_t vw[4] = {va.x, va.y, va.z, va.w};
         float x[8];
@@ -793,7 +795,6 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         float uv[8], uv2[8];
         tmem_ld8(tl + TG2 + vq, uv);
         tmem_ld8(tl + TG2 + 32u + vq, uv2);
-        const float ut = vec[128 + row];
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i) x[i] = ut * (uv[i] + uv2[i]);
@@ -809,7 +810,6 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         tmem_ld8(tl + TG1 + 32u + vq, q2);
         tmem_ld8(tl + TG2 + vq, pu);
         tmem_ld8(tl + TG2 + 32u + vq, p2);
-        const float ct = vec[192 + t];
         tmem_wait_ld();
         warp_arrive(&bars->o_done);  // TG1 / TG2 read out: the next G1 / G2 may overwrite
         if (t < Lc) {
