@@ -112,7 +112,11 @@ int gdn_mtp_launch(const void* q, const void* k, const void* v, const float* ini
  * gdn_mtp_launch with state, new_state, the pool and the rollback buffer as bf16
  * (same shapes, 16-byte aligned).  The state is widened to fp32 on load, updated in
  * fp32 (across all tokens of a multi-token call) and rounded to nearest bf16 on every
- * store; the state traffic is half that of the fp32 entry points.
+ * store; the state traffic is half that of the fp32 entry points.  Decode calls with
+ * at least 592 (batch x v-head) pairs, a non-NULL state and 16-byte aligned q, k, v
+ * run a persistent streaming kernel (bulk copies into shared memory); its results are
+ * bitwise those of the one-shot kernel used otherwise.  Its first call on a device sets
+ * the kernel's shared-memory attribute (make it before any stream capture).
  */
 int gdn_decode_launch_bf16state(const void* q, const void* k, const void* v, const void* state,
                                 const float* A_log, const void* a, const float* dt_bias,
