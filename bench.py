@@ -44,6 +44,7 @@ sys.path.insert(0, str(REPO))
 import torch  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
+E2E_SLICES = 8  # batch slices of the pipelined end-to-end decode step
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -224,16 +225,30 @@ class DecodeWork:
 
     def e2e_step(self):
         """Host inputs -> device -> the C-ABI entry point (gdn_decode_launch, same flags as
-        the device-timed step) -> host outputs."""
-        di = self.d_in
-        for k_, t in self.h.items():
-            di[k_].copy_(t, non_blocking=True)
-        d = self.inp
-        self.pkg.gdn_decode(di["q"], di["k"], di["v"], di["state"], d["A_log"], di["a"],
-                            d["dt_bias"], di["b"], d["scale"], self.out, self.d_ns,
-                            use_qk_l2norm=True)
-        self.h_out.copy_(self.out, non_blocking=True)
-        self.h_ns.copy_(self.d_ns, non_blocking=True)
+        the device-timed step) -> host outputs, pipelined over slices of the batch: slice
+        i + 1 goes up while slice i is computed and slice i - 1 comes back (PCIe is full
+        duplex), on two copy streams besides the compute stream."""
+        cur = torch.cuda.current_stream()
+        if not hasattr(self, "s_up"):
+            self.s_up, self.s_down = torch.cuda.Stream(), torch.cuda.Stream()
+        n = E2E_SLICES if self.batch % E2E_SLICES == 0 else 1
+        rows = self.batch // n
+        di, d = self.d_in, self.inp
+        self.s_up.wait_stream(cur)  # inputs of the previous step are consumed
+        for i in range(n):
+            sl = slice(i * rows, (i + 1) * rows)
+            with torch.cuda.stream(self.s_up):
+                for k_, t in self.h.items():
+                    di[k_][sl].copy_(t[sl], non_blocking=True)
+            cur.wait_stream(self.s_up)
+            self.pkg.gdn_decode(di["q"][sl], di["k"][sl], di["v"][sl], di["state"][sl],
+                                d["A_log"], di["a"][sl], d["dt_bias"], di["b"][sl], d["scale"],
+                                self.out[sl], self.d_ns[sl], use_qk_l2norm=True)
+            self.s_down.wait_stream(cur)
+            with torch.cuda.stream(self.s_down):
+                self.h_out[sl].copy_(self.out[sl], non_blocking=True)
+                self.h_ns[sl].copy_(self.d_ns[sl], non_blocking=True)
+        cur.wait_stream(self.s_down)  # the step ends when its results are on the host
 
 
 class MtpWork:
