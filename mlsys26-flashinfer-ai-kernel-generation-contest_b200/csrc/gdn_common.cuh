@@ -80,9 +80,10 @@ struct RowSlice {
         const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
         const float2 a = bf2x2_to_f2(u.x), b = bf2x2_to_f2(u.y);
         x[4 * m] = a.x; x[4 * m + 1] = a.y; x[4 * m + 2] = b.x; x[4 * m + 3] = b.y;
-      } else {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      } else {  // two 8-byte loads: q and k rows need only 8-byte alignment
+        const uint2 u0 = __ldg(reinterpret_cast<const uint2*>(p));
+        const uint2 u1 = __ldg(reinterpret_cast<const uint2*>(p + 4));
+        const uint32_t w[4] = {u0.x, u0.y, u1.x, u1.y};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = bf2x2_to_f2(w[e]);

@@ -84,6 +84,26 @@ def test_decode_bf16_streaming_equals_one_shot_bitwise(cuda):
     assert pkg.device_error() == 0
 
 
+def test_decode_bf16_unaligned_qkv_takes_one_shot_path(cuda):
+    """q/k/v only 8-byte aligned: the streaming kernel's bulk copies need 16 bytes, so the
+    call runs the one-shot kernel; the results are the same bits."""
+    pkg = load_pkg()
+    inp = to(bf16_state(pkg.workloads.decode_inputs(32, seed=67)), cuda)
+    args = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")
+    o, s = pkg.gdn_decode(*[inp[x] for x in args], inp["scale"], use_qk_l2norm=True)
+    shifted = dict(inp)
+    for x in ("q", "k", "v"):
+        t = inp[x]
+        buf = torch.empty(t.numel() + 4, dtype=t.dtype, device=cuda)
+        view = buf[4:].view(t.shape)  # 8 bytes past a 16-byte boundary
+        view.copy_(t)
+        assert view.data_ptr() % 16 == 8
+        shifted[x] = view
+    o2, s2 = pkg.gdn_decode(*[shifted[x] for x in args], inp["scale"], use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, o) and torch.equal(s2, s)
+
+
 def test_decode_bf16_zero_state(cuda):
     pkg = load_pkg()
     inp = pkg.workloads.decode_inputs(3, hq=1, hv=2, seed=63, with_state=False)
