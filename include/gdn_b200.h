@@ -149,7 +149,8 @@ size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_head
  *            non-decreasing, cu_seqlens[0] == 0, cu_seqlens[num_seqs] == total_tokens
  *   output   bf16 [total_tokens, max(num_q_heads, num_v_heads), 128]  (written)
  *   new_state fp32 [num_seqs, max(num_q_heads, num_v_heads), 128, 128] (written)
- *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes
+ *   workspace  device buffer of >= gdn_prefill_workspace_size(...) bytes, 16-byte
+ *              aligned (cudaMalloc's alignment is more than enough)
  *              (may be NULL when that size is 0).  Scratch only: it holds the
  *              longest-first order in which the sequences are scheduled and,
  *              for the split kernels, the per-chunk records (33,808 bytes per

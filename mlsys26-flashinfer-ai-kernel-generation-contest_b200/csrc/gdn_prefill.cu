@@ -111,6 +111,7 @@ int prefill_entry(int variant, const void* q, const void* k, const void* v, cons
   if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
   const size_t need = variant_workspace(variant, total_tokens, num_seqs, num_v_heads, need_split);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
+  if (need > 0 && misaligned(workspace, 16)) return GDN_ERR_INVALID_ARGUMENT;  // 16-byte records
 
   PrefillArgs p{q,        k,     v,      state,      A_log,        a,           dt_bias,
                 b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,

@@ -76,6 +76,18 @@ def test_prefill_argument_checks_return_before_launch():
     assert call(d=256) == -2
     assert call() == -1
     assert call(T=-1) == -1
+    fake = 0x1000
+    ptrs = dict(q=fake, k=fake, v=fake, A_log=fake, a=fake, dt_bias=fake, b=fake, cu=fake,
+                out=fake, ns=fake)
+    size = lib.gdn_prefill_workspace_size_variant(3, 4096, 1, 16, 32, 128)
+    assert size > 0
+    # a workspace that is not 16-byte aligned is refused before anything is launched
+    vcall = lambda **kw: lib.gdn_prefill_launch_variant(3, *{**dict(  # noqa: E731
+        q=None, k=None, v=None, state=None, A_log=None, a=None, dt_bias=None, b=None, cu=None,
+        cu64=0, scale=0.0, out=None, ns=None, T=4096, N=1, hq=16, hk=16, hv=32, d=128, l2=1,
+        ws=None, wsb=0, stream=None), **kw}.values())
+    assert vcall(**ptrs, ws=fake + 8, wsb=size) == -1
+    assert vcall(**ptrs, ws=fake, wsb=size - 1) == -4  # too small
 
 
 def test_host_rejects_cpu_tensors_and_bad_dtypes():
