@@ -305,8 +305,9 @@ MTP_T = 4  # draft tokens verified per row (speculative decoding)
 
 def prefill_plan(pkg, name, dist):
     """This rank's part of prefill config `name`: None at N=1; whole sequences
-    (longest-first packing) when there are at least as many sequences as ranks;
-    else a q/k-head group with its v-heads.  No collective either way."""
+    (longest-first packing) when there are at least as many sequences as ranks; one
+    sequence over 4 or more ranks: consecutive token segments chained through their state
+    maps (one all-gather per call); else a q/k-head group with its v-heads."""
     if dist.world == 1:
         return None
     W = pkg.workloads
@@ -314,6 +315,8 @@ def prefill_plan(pkg, name, dist):
     if cfg.n >= dist.world:
         lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
         return ("seqs", pkg.sharding.lpt_assign(lens, dist.world)[dist.rank])
+    if cfg.n == 1 and dist.world >= 4:
+        return ("segments", dist.world, dist.rank)
     return ("heads",) + tuple(pkg.sharding.head_range(W.HQ, dist.world, dist.rank))
 
 
@@ -322,14 +325,20 @@ def plan_text(plan, world):
         return "single GPU"
     if plan[0] == "seqs":
         return f"sequence-sharded x{world} (LPT), no collective"
+    if plan[0] == "segments":
+        return f"token-segment scan x{world} (one all-gather of the segments' state maps)"
     return f"q/k-head-group-sharded x{world}, no collective"
 
 
 class PrefillWork:
-    def __init__(self, pkg, cfg_name, dev, seed, shard=None):
+    def __init__(self, pkg, cfg_name, dev, seed, shard=None, dist=None):
         W = pkg.workloads
         self.pkg, self.dev = pkg, dev
         inp = W.prefill_config_inputs(cfg_name, seed=seed, device="cpu")
+        self.segments = shard is not None and shard[0] == "segments"
+        if self.segments:
+            self._init_segment(inp, shard[1], shard[2], dist)
+            return
         head_frac = 1.0
         if shard is not None and shard[0] == "seqs":  # this rank's sequences, re-packed
             inp = pkg.sharding.prefill_shard(inp, shard[1])
@@ -349,8 +358,74 @@ class PrefillWork:
         self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
         self.launches = pkg.prefill.launches_per_call(T, N, self.inp["q"].shape[1], self.inp["v"].shape[1])
 
+    def _init_segment(self, inp, world, rank, dist):
+        """Segment `rank` of the single sequence.  Rank 0 runs it from the initial state;
+        every other rank first runs, in one call of two sequences, the segment from the
+        identity with v = 0 and from a zero state (its state map A, B: the doubled input
+        is a layout prepared once), then, after the all-gather of every rank's (A, B), the
+        segment from its chained start state."""
+        S, W = self.pkg.sharding, self.pkg.workloads
+        self.world, self.rank, self.dist = world, rank, dist
+        lo, hi = S.segment_bounds(inp["q"].shape[0], world)[rank]
+        seg = S.segment_inputs(inp, lo, hi)
+        L, HQ, HV = hi - lo, inp["q"].shape[1], inp["v"].shape[1]
+        dev = self.dev
+        self.inp = {k_: (v_.to(dev) if isinstance(v_, torch.Tensor) else v_)
+                    for k_, v_ in seg.items()}
+        if rank == 0:
+            if self.inp.get("state") is None:
+                self.inp["state"] = torch.zeros(1, HV, 128, 128, device=dev)
+        else:
+            eye = torch.eye(128).expand(1, HV, 128, 128)
+            dbl = dict(seg)
+            for key in ("q", "k", "a", "b"):
+                dbl[key] = torch.cat([seg[key], seg[key]], dim=0)
+            dbl["v"] = torch.cat([torch.zeros_like(seg["v"]), seg["v"]], dim=0)
+            dbl["state"] = torch.cat([eye, torch.zeros(1, HV, 128, 128)], dim=0).contiguous()
+            dbl["cu_seqlens"] = torch.tensor([0, L, 2 * L], dtype=seg["cu_seqlens"].dtype)
+            self.dbl = {k_: (v_.to(dev) if isinstance(v_, torch.Tensor) else v_)
+                        for k_, v_ in dbl.items()}
+            self.dbl_out = torch.empty(2 * L, HV, 128, dtype=torch.bfloat16, device=dev)
+            self.dbl_ns = torch.empty(2, HV, 128, 128, device=dev)
+            self.start = torch.empty(1, HV, 128, 128, device=dev)
+        self.out = torch.empty(L, HV, 128, dtype=torch.bfloat16, device=dev)
+        self.ns = torch.empty(1, HV, 128, 128, device=dev)
+        self.A = torch.zeros(1, HV, 128, 128, device=dev)
+        self.parts_A = [torch.empty_like(self.A) for _ in range(world)]
+        self.parts_B = [torch.empty_like(self.A) for _ in range(world)]
+        self.lens = [L]
+        self.cpu_inp = seg
+        self.tokens = L
+        self.flops = L * W.prefill_flops_per_token(HQ, HV)
+        per = self.pkg.prefill.launches_per_call
+        self.launches = per(L, 1, HQ, HV) + (0 if rank == 0 else per(2 * L, 2, HQ, HV))
+
+    def _segment_step(self, d):
+        P = self.pkg
+        if self.rank == 0:
+            P.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
+                          d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
+                          use_qk_l2norm=True)
+            A, B = self.A, self.ns
+        else:
+            e = self.dbl
+            P.gdn_prefill(e["q"], e["k"], e["v"], e["state"], e["A_log"], e["a"], e["dt_bias"],
+                          e["b"], e["cu_seqlens"], e["scale"], self.dbl_out, self.dbl_ns,
+                          use_qk_l2norm=True)
+            A, B = self.dbl_ns[0:1], self.dbl_ns[1:2]
+        self.dist.pg.all_gather(self.parts_A, A.contiguous())
+        self.dist.pg.all_gather(self.parts_B, B.contiguous())
+        if self.rank > 0:
+            self.start.copy_(self.pkg.sharding.chain_start(self.parts_A, self.parts_B, self.rank))
+            P.gdn_prefill(d["q"], d["k"], d["v"], self.start, d["A_log"], d["a"], d["dt_bias"],
+                          d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
+                          use_qk_l2norm=True)
+
     def step(self):
         d = self.inp
+        if self.segments:
+            self._segment_step(d)
+            return
         self.pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
                              d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
                              use_qk_l2norm=True)
@@ -373,6 +448,17 @@ class PrefillWork:
         for k_, t in self.h.items():
             di[k_].copy_(t, non_blocking=True)
         d = self.inp
+        if self.segments:  # the segment's inputs, duplicated on the device for the maps
+            if self.rank > 0:
+                L = di["q"].shape[0]
+                for key in ("q", "k", "a", "b"):
+                    self.dbl[key][:L].copy_(di[key])
+                    self.dbl[key][L:].copy_(di[key])
+                self.dbl["v"][L:].copy_(di["v"])
+            self._segment_step({**d, **di})
+            self.h_out.copy_(self.out, non_blocking=True)
+            self.h_ns.copy_(self.ns, non_blocking=True)
+            return
         self.pkg.gdn_prefill(di["q"], di["k"], di["v"], di.get("state"), d["A_log"], di["a"],
                              d["dt_bias"], di["b"], di["cu_seqlens"], d["scale"], self.out,
                              self.ns, use_qk_l2norm=True)
@@ -569,7 +655,7 @@ def cpu_baseline_mtp(batch, budget_s=10.0):
 
 
 def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True):
-    w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard)
+    w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard, dist=dist)
     with ClockSampler(dev.index) as clk:
         ms, kern_ms = time_steps(w.step, steps, warmup, dist)
     tokens_all = w.tokens

@@ -16,6 +16,10 @@ Load balance for prefill uses longest-processing-time bin packing on token
 counts.  There is no exchange step on the data path, so there is no NCCL
 call in the timed region; results are gathered (to the host, outside timing)
 only for verification.
+
+One long sequence can also be split into consecutive token segments, one per rank, with a
+segment-level scan of its affine state map (``segment_scan_rank``, end of this file): that
+has one real exchange step, an all-gather of each segment's (A, B) state map.
 """
 from __future__ import annotations
 
@@ -138,3 +142,130 @@ def prefill_head_unshard(outputs: Sequence[torch.Tensor], states: Sequence[torch
     out = torch.cat([o.cpu() for o in outputs], dim=1)
     st = torch.cat([s.cpu() for s in states], dim=1)
     return out, st
+
+
+# --------------------------------------------------------------------------------------
+# One long sequence over several ranks: a segment-level scan of the state map.
+#
+# Over a segment of tokens the recurrence is affine in the state: with the k-last state
+# S[v, k], every token applies S <- S g (I - beta k k^T) + beta v k^T, so a segment maps
+# S_in to S_out = S_in A + B, where A (k x k) is what the segment makes of the identity
+# when v = 0 (row v of the identity evolves like state row v) and B is the segment's final
+# state from a zero state.  Rank r takes segment r: rank 0 runs its segment from the
+# caller's initial state (its outputs and final state are final); every other rank
+# computes its (A, B) with two runs, the (A, B) of all ranks are exchanged (the one
+# collective), each rank chains S_start(r) = S_start(r-1) A_{r-1} + B_{r-1}, with
+# (A_0, B_0) = (0, rank 0's final state), and runs its segment from S_start(r).  The
+# serial chain shrinks from the whole sequence to two segments; the price is three runs
+# of each segment but the first, on ranks whose SMs would otherwise sit idle.
+# `run(segment_inputs, state, zero_v)` is the prefill call (it returns (output,
+# final_state)); states are [1, HV, 128, 128] fp32.
+
+
+def segment_bounds(total_tokens: int, world: int, align: int = 64) -> List[Tuple[int, int]]:
+    """[start, end) token ranges of `world` consecutive segments of one sequence, the
+    boundaries on multiples of `align` (the prefill chunk) and the last one taking the
+    remainder; a segment may be empty when the sequence is short."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    chunks = (total_tokens + align - 1) // align
+    bounds, start = [], 0
+    for r in range(world):
+        lo_c, hi_c = batch_range(chunks, world, r)
+        end = min(hi_c * align, total_tokens)
+        bounds.append((start, end))
+        start = end
+    return bounds
+
+
+def segment_inputs(inp: Dict[str, torch.Tensor], lo: int, hi: int) -> Dict[str, torch.Tensor]:
+    """Tokens [lo, hi) of a single-sequence prefill problem as a one-sequence problem."""
+    out = dict(inp)
+    for key in ("q", "k", "v", "a", "b"):
+        out[key] = inp[key][lo:hi].contiguous()
+    out["cu_seqlens"] = torch.tensor([0, hi - lo], dtype=inp["cu_seqlens"].dtype,
+                                     device=inp["cu_seqlens"].device)
+    return out
+
+
+def segment_map(run, seg: Dict[str, torch.Tensor]) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(A, B) of one segment: A from the identity with v = 0, B from a zero state (an
+    empty segment is the identity map: the prefill call would return a zero state)."""
+    HV = seg["v"].shape[1]
+    dev = seg["v"].device
+    eye = torch.eye(128, dtype=torch.float32, device=dev).expand(1, HV, 128, 128).contiguous()
+    zero = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
+    if seg["q"].shape[0] == 0:
+        return eye, zero
+    _, A = run(seg, eye, True)
+    _, B = run(seg, zero, False)
+    return A, B
+
+
+def _run_from(run, seg: Dict[str, torch.Tensor], state: torch.Tensor
+              ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """A segment's run from `state`; an empty segment leaves the state as it is."""
+    if seg["q"].shape[0] == 0:
+        out = torch.empty((0,) + tuple(seg["v"].shape[1:]), dtype=torch.bfloat16,
+                          device=seg["v"].device)
+        return out, state
+    return run(seg, state, False)
+
+
+def chain_start(As: Sequence[torch.Tensor], Bs: Sequence[torch.Tensor], r: int) -> torch.Tensor:
+    """S_start(r) = S_start(r-1) A_{r-1} + B_{r-1} from S_start(1) = B_0 (r >= 1), in fp32."""
+    S = Bs[0]
+    for m in range(1, r):
+        S = torch.matmul(S, As[m]) + Bs[m]
+    return S
+
+
+def segment_scan_rank(run, inp: Dict[str, torch.Tensor], world: int, rank: int, all_gather
+                      ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """This rank's part of the segment scan.  `all_gather(t)` returns the list of every
+    rank's `t` (rank order).  Returns (output of this rank's tokens, final state after
+    them); the last rank's final state is the sequence's."""
+    T = inp["q"].shape[0]
+    lo, hi = segment_bounds(T, world)[rank]
+    seg = segment_inputs(inp, lo, hi)
+    HV = inp["v"].shape[1]
+    if rank == 0:
+        state = inp.get("state")
+        if state is None:
+            state = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=inp["v"].device)
+        out, fin = _run_from(run, seg, state)
+        A, B = torch.zeros_like(fin), fin
+    else:
+        A, B = segment_map(run, seg)
+    As, Bs = all_gather(A.contiguous()), all_gather(B.contiguous())
+    if rank == 0:
+        return out, fin
+    return _run_from(run, seg, chain_start(As, Bs, rank).contiguous())
+
+
+def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
+                       ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The whole segment scan in one process (every rank's work in turn): the
+    sequence's output and final state."""
+    T = inp["q"].shape[0]
+    parts = []
+    maps = []
+    for r, (lo, hi) in enumerate(segment_bounds(T, world)):
+        seg = segment_inputs(inp, lo, hi)
+        if r == 0:
+            HV = inp["v"].shape[1]
+            state = inp.get("state")
+            if state is None:
+                state = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=inp["v"].device)
+            out, fin = _run_from(run, seg, state)
+            maps.append((torch.zeros_like(fin), fin))
+            parts.append(out)
+        else:
+            maps.append(segment_map(run, seg))
+    As, Bs = [m[0] for m in maps], [m[1] for m in maps]
+    for r, (lo, hi) in enumerate(segment_bounds(T, world)):
+        if r == 0:
+            continue
+        out, fin = _run_from(run, segment_inputs(inp, lo, hi), chain_start(As, Bs, r).contiguous())
+        parts.append(out)
+    return torch.cat(parts, dim=0), fin

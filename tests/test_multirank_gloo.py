@@ -3,6 +3,8 @@
 * sharded decode and prefill (by sequence and by q/k-head group; oracle as the
   per-rank compute) reassemble into
   the unsharded result, and the max-over-ranks timing reduction works;
+* one sequence split into segments over 2 and 3 ranks (segment-level scan, the segments'
+  state maps exchanged with all_gather) gives the unsplit result;
 * failure detection on the host: a rank that dies before the barrier makes
   the surviving rank's next collective end with an error within the process
   group's short timeout instead of hanging.
@@ -93,6 +95,42 @@ def _worker_sharded(rank, world, port, q):
         q.put(("error", traceback.format_exc()))
 
 
+def _worker_segments(rank, world, port, q):
+    """One sequence split into `world` segments: the (A, B) state maps are exchanged with
+    all_gather and the last rank's final state is the unsplit sequence's."""
+    try:
+        sys.path.insert(0, str(REPO))
+        import importlib
+        pkg = importlib.import_module(PKG_NAME)
+        from oracle import gdn_oracle as O
+        _init(rank, world, port, 60)
+        inp = pkg.workloads.prefill_inputs([200], hq=2, hv=4, seed=83)
+
+        def run(seg, state, zero_v):
+            v = torch.zeros_like(seg["v"]) if zero_v else seg["v"]
+            return O.prefill(O.l2norm(seg["q"]), O.l2norm(seg["k"]), v, state, seg["A_log"],
+                             seg["a"], seg["dt_bias"], seg["b"], seg["cu_seqlens"],
+                             seg["scale"])
+
+        def all_gather(t):
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            return parts
+
+        out, fin = pkg.sharding.segment_scan_rank(run, inp, world, rank, all_gather)
+        outs = [None] * world
+        dist.all_gather_object(outs, (out, fin))
+        if rank == 0:
+            ro, rs = run(inp, inp["state"], False)
+            full = torch.cat([o for o, _ in outs], dim=0)
+            ok_o, _, _, _ = O.flashinfer_allclose(full, ro, 2e-2, 2e-2)
+            q.put(("ok", bool(ok_o), float(O.state_rel_err(outs[-1][1], rs))))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
 def _worker_failing(rank, world, port, q):
     try:
         _init(rank, world, port, 3)
@@ -137,3 +175,11 @@ def test_two_rank_sharded_results_match_unsharded():
 def test_dead_rank_is_detected_not_hung():
     items = _run(_worker_failing)
     assert ("detected",) == items[0][:1], items
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_segment_scan_over_ranks_matches_unsplit(world):
+    items = _run(_worker_segments, world)
+    assert items and all(i[0] == "ok" for i in items), items
+    _, ok_out, err = items[0]
+    assert ok_out and err < 1e-5

@@ -87,3 +87,40 @@ def test_head_ranges_and_shard_roundtrip_matches_unsharded_oracle():
         S.prefill_head_shard(inp, 2, 2)
     with pytest.raises(ValueError):
         S.prefill_head_shard(W.prefill_inputs([3], hq=2, hv=3, seed=1), 0, 1)
+
+
+def _oracle_run(seg, state, zero_v):
+    """The prefill call of one segment, on the CPU oracle (normalised q/k)."""
+    v = torch.zeros_like(seg["v"]) if zero_v else seg["v"]
+    return O.prefill(O.l2norm(seg["q"]), O.l2norm(seg["k"]), v, state, seg["A_log"], seg["a"],
+                     seg["dt_bias"], seg["b"], seg["cu_seqlens"], seg["scale"])
+
+
+def test_segment_bounds():
+    S = load_pkg().sharding
+    assert S.segment_bounds(32768, 8)[1] == (4096, 8192)
+    assert S.segment_bounds(130, 4) == [(0, 64), (64, 128), (128, 130), (130, 130)]
+    for T, w in [(1, 3), (640, 4), (1000, 7)]:
+        b = S.segment_bounds(T, w)
+        assert b[0][0] == 0 and b[-1][1] == T
+        assert all(b[i][1] == b[i + 1][0] for i in range(w - 1))
+        assert all(lo % 64 == 0 or lo == T for lo, _ in b)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4])
+def test_segment_scan_matches_unsegmented_oracle(world):
+    """One sequence split into segments, each segment's (A, B) state map chained: the
+    output and final state of the unsplit sequence (also with an empty last segment)."""
+    pkg = load_pkg()
+    inp = pkg.workloads.prefill_inputs([300], hq=2, hv=4, seed=81)
+    ro, rs = _oracle_run(inp, inp["state"], False)
+    out, fin = pkg.sharding.segment_scan_local(_oracle_run, inp, world)
+    ok, frac, _, _ = O.flashinfer_allclose(out, ro, 2e-2, 2e-2)
+    assert ok, frac
+    assert O.state_rel_err(fin, rs) < 1e-5
+    # a short sequence leaves the last segment empty
+    short = pkg.workloads.prefill_inputs([70], hq=1, hv=2, seed=82)
+    ro, rs = _oracle_run(short, short["state"], False)
+    out, fin = pkg.sharding.segment_scan_local(_oracle_run, short, 3)
+    assert out.shape == ro.shape
+    assert O.state_rel_err(fin, rs) < 1e-5
