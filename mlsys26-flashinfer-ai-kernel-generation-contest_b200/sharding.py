@@ -1,4 +1,4 @@
-"""Multi-GPU partitioning of the GDN workloads (one process per GPU, no collective).
+"""Multi-GPU partitioning of the GDN workloads (one process per GPU).
 
 Every unit of GDN work is independent of every other one:
 
