@@ -162,17 +162,25 @@ def prefill_head_unshard(outputs: Sequence[torch.Tensor], states: Sequence[torch
 # final_state)); states are [1, HV, 128, 128] fp32.
 
 
-def segment_bounds(total_tokens: int, world: int, align: int = 64) -> List[Tuple[int, int]]:
+def segment_bounds(total_tokens: int, world: int, align: int = 64,
+                   first_weight: int = 2) -> List[Tuple[int, int]]:
     """[start, end) token ranges of `world` consecutive segments of one sequence, the
-    boundaries on multiples of `align` (the prefill chunk) and the last one taking the
-    remainder; a segment may be empty when the sequence is short."""
+    boundaries on multiples of `align` (the prefill chunk) and the last one ending at the
+    sequence's end; a segment may be empty when the sequence is short.  The first segment
+    gets `first_weight` shares and every other one share: its rank runs it once, while the
+    others run their segment three times (the two runs of its state map, then the final
+    one), two of them before the exchange."""
     if world <= 0:
         raise ValueError("world must be positive")
     chunks = (total_tokens + align - 1) // align
+    shares = [first_weight] + [1] * (world - 1)
+    total_share, cum = sum(shares), 0
     bounds, start = [], 0
     for r in range(world):
-        lo_c, hi_c = batch_range(chunks, world, r)
-        end = min(hi_c * align, total_tokens)
+        cum += shares[r]
+        end = min((chunks * cum // total_share) * align, total_tokens)
+        if r == world - 1:
+            end = total_tokens
         bounds.append((start, end))
         start = end
     return bounds

@@ -37,6 +37,6 @@ def test_segment_scan_short_sequence_with_empty_segment(cuda):
     d = to(pkg.workloads.prefill_inputs([130], hq=2, hv=4, seed=84), cuda)
     run = _kernel_run(pkg)
     ro, rs = run(d, d["state"], False)
-    out, fin = pkg.sharding.segment_scan_local(run, d, 4)  # the last segment is empty
+    out, fin = pkg.sharding.segment_scan_local(run, d, 4)  # the second segment is empty
     torch.cuda.synchronize()
     assert_parity(out, fin, ro.cpu(), rs.cpu(), what="130 tokens in 4 segments")

@@ -98,8 +98,12 @@ def _oracle_run(seg, state, zero_v):
 
 def test_segment_bounds():
     S = load_pkg().sharding
-    assert S.segment_bounds(32768, 8)[1] == (4096, 8192)
-    assert S.segment_bounds(130, 4) == [(0, 64), (64, 128), (128, 130), (130, 130)]
+    # 512 chunks, the first segment two shares of nine
+    assert S.segment_bounds(32768, 8) == [(0, 7232), (7232, 10880), (10880, 14528),
+                                          (14528, 18176), (18176, 21824), (21824, 25472),
+                                          (25472, 29120), (29120, 32768)]
+    assert S.segment_bounds(32768, 8, first_weight=1)[1] == (4096, 8192)
+    assert S.segment_bounds(130, 4) == [(0, 64), (64, 64), (64, 128), (128, 130)]
     for T, w in [(1, 3), (640, 4), (1000, 7)]:
         b = S.segment_bounds(T, w)
         assert b[0][0] == 0 and b[-1][1] == T
@@ -110,7 +114,7 @@ def test_segment_bounds():
 @pytest.mark.parametrize("world", [1, 2, 3, 4])
 def test_segment_scan_matches_unsegmented_oracle(world):
     """One sequence split into segments, each segment's (A, B) state map chained: the
-    output and final state of the unsplit sequence (also with an empty last segment)."""
+    output and final state of the unsplit sequence (also with an empty segment)."""
     pkg = load_pkg()
     inp = pkg.workloads.prefill_inputs([300], hq=2, hv=4, seed=81)
     ro, rs = _oracle_run(inp, inp["state"], False)
@@ -118,7 +122,7 @@ def test_segment_scan_matches_unsegmented_oracle(world):
     ok, frac, _, _ = O.flashinfer_allclose(out, ro, 2e-2, 2e-2)
     assert ok, frac
     assert O.state_rel_err(fin, rs) < 1e-5
-    # a short sequence leaves the last segment empty
+    # a short sequence leaves a segment empty
     short = pkg.workloads.prefill_inputs([70], hq=1, hv=2, seed=82)
     ro, rs = _oracle_run(short, short["state"], False)
     out, fin = pkg.sharding.segment_scan_local(_oracle_run, short, 3)
