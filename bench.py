@@ -303,11 +303,13 @@ class MtpWork:
 MTP_T = 4  # draft tokens verified per row (speculative decoding)
 
 
-def prefill_plan(pkg, name, dist):
+def prefill_plan(pkg, name, dist, force="auto"):
     """This rank's part of prefill config `name`: None at N=1; whole sequences
     (longest-first packing) when there are at least as many sequences as ranks; one
     sequence over 4 or more ranks: consecutive token segments chained through their state
-    maps (one all-gather per call); else a q/k-head group with its v-heads."""
+    maps (one all-gather per call); else a q/k-head group with its v-heads.  `force`
+    ("heads" or "segments") overrides the choice for a config with fewer sequences than
+    ranks."""
     if dist.world == 1:
         return None
     W = pkg.workloads
@@ -315,7 +317,8 @@ def prefill_plan(pkg, name, dist):
     if cfg.n >= dist.world:
         lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
         return ("seqs", pkg.sharding.lpt_assign(lens, dist.world)[dist.rank])
-    if cfg.n == 1 and dist.world >= 4:
+    segments = cfg.n == 1 and dist.world >= 4 if force == "auto" else force == "segments"
+    if segments and cfg.n == 1:
         return ("segments", dist.world, dist.rank)
     return ("heads",) + tuple(pkg.sharding.head_range(W.HQ, dist.world, dist.rank))
 
@@ -749,7 +752,7 @@ def run_ours(args, dist):
             "kernel_ms": round(r["kern_ms"], 5),
         })
     else:
-        shard = prefill_plan(pkg, param, dist)
+        shard = prefill_plan(pkg, param, dist, args.prefill_plan)
         r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
         line.update({
             "metric": "prefill tokens/s", "value": round(r["value"], 1), "unit": "tokens/s",
@@ -838,6 +841,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_b128")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-extra", action="store_true")
+    ap.add_argument("--prefill-plan", choices=["auto", "heads", "segments"], default="auto",
+                    help="multi-GPU split of a single prefill sequence (default: segments "
+                         "from 4 GPUs, head groups below)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()
