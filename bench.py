@@ -363,10 +363,11 @@ class PrefillWork:
 
     def _init_segment(self, inp, world, rank, dist):
         """Segment `rank` of the single sequence.  Rank 0 runs it from the initial state;
-        every other rank first runs, in one call of two sequences, the segment from the
-        identity with v = 0 and from a zero state (its state map A, B: the doubled input
-        is a layout prepared once), then, after the all-gather of every rank's (A, B), the
-        segment from its chained start state."""
+        every other rank runs, in one call of two sequences, the segment from the identity
+        with v = 0 and from a zero state (its state map A, B and the two runs' outputs: the
+        doubled input is a layout prepared once), then, after the all-gather of every
+        rank's (A, B), assembles its outputs and final state from its chained start state
+        with fp32 matrix products."""
         S, W = self.pkg.sharding, self.pkg.workloads
         self.world, self.rank, self.dist = world, rank, dist
         lo, hi = S.segment_bounds(inp["q"].shape[0], world)[rank]
@@ -390,18 +391,16 @@ class PrefillWork:
                         for k_, v_ in dbl.items()}
             self.dbl_out = torch.empty(2 * L, HV, 128, dtype=torch.bfloat16, device=dev)
             self.dbl_ns = torch.empty(2, HV, 128, 128, device=dev)
-            self.start = torch.empty(1, HV, 128, 128, device=dev)
         self.out = torch.empty(L, HV, 128, dtype=torch.bfloat16, device=dev)
         self.ns = torch.empty(1, HV, 128, 128, device=dev)
         self.A = torch.zeros(1, HV, 128, 128, device=dev)
-        self.parts_A = [torch.empty_like(self.A) for _ in range(world)]
-        self.parts_B = [torch.empty_like(self.A) for _ in range(world)]
+        self.parts = [torch.empty(2, HV, 128, 128, device=dev) for _ in range(world)]
         self.lens = [L]
         self.cpu_inp = seg
         self.tokens = L
         self.flops = L * W.prefill_flops_per_token(HQ, HV)
         per = self.pkg.prefill.launches_per_call
-        self.launches = per(L, 1, HQ, HV) + (0 if rank == 0 else per(2 * L, 2, HQ, HV))
+        self.launches = per(L, 1, HQ, HV) if rank == 0 else per(2 * L, 2, HQ, HV)
 
     def _segment_step(self, d):
         P = self.pkg
@@ -409,20 +408,23 @@ class PrefillWork:
             P.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
                           d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
                           use_qk_l2norm=True)
-            A, B = self.A, self.ns
+            mine = torch.cat([self.A, self.ns], dim=0)
         else:
             e = self.dbl
             P.gdn_prefill(e["q"], e["k"], e["v"], e["state"], e["A_log"], e["a"], e["dt_bias"],
                           e["b"], e["cu_seqlens"], e["scale"], self.dbl_out, self.dbl_ns,
                           use_qk_l2norm=True)
-            A, B = self.dbl_ns[0:1], self.dbl_ns[1:2]
-        self.dist.pg.all_gather(self.parts_A, A.contiguous())
-        self.dist.pg.all_gather(self.parts_B, B.contiguous())
+            mine = self.dbl_ns
+        self.dist.pg.all_gather(self.parts, mine)
         if self.rank > 0:
-            self.start.copy_(self.pkg.sharding.chain_start(self.parts_A, self.parts_B, self.rank))
-            P.gdn_prefill(d["q"], d["k"], d["v"], self.start, d["A_log"], d["a"], d["dt_bias"],
-                          d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
-                          use_qk_l2norm=True)
+            S = self.pkg.sharding
+            start = S.chain_start([p_[0:1] for p_ in self.parts],
+                                  [p_[1:2] for p_ in self.parts], self.rank)
+            L = self.out.shape[0]
+            out, fin = S.segment_finish(start, self.dbl_ns[0:1], self.dbl_ns[1:2],
+                                        self.dbl_out[:L], self.dbl_out[L:])
+            self.out.copy_(out)
+            self.ns.copy_(fin)
 
     def step(self):
         d = self.inp

@@ -151,13 +151,17 @@ def prefill_head_unshard(outputs: Sequence[torch.Tensor], states: Sequence[torch
 # S[v, k], every token applies S <- S g (I - beta k k^T) + beta v k^T, so a segment maps
 # S_in to S_out = S_in A + B, where A (k x k) is what the segment makes of the identity
 # when v = 0 (row v of the identity evolves like state row v) and B is the segment's final
-# state from a zero state.  Rank r takes segment r: rank 0 runs its segment from the
-# caller's initial state (its outputs and final state are final); every other rank
-# computes its (A, B) with two runs, the (A, B) of all ranks are exchanged (the one
-# collective), each rank chains S_start(r) = S_start(r-1) A_{r-1} + B_{r-1}, with
-# (A_0, B_0) = (0, rank 0's final state), and runs its segment from S_start(r).  The
-# serial chain shrinks from the whole sequence to two segments; the price is three runs
-# of each segment but the first, on ranks whose SMs would otherwise sit idle.
+# state from a zero state.  The outputs are affine in S_in too: o_t = scale S_t q_t =
+# S_in o^I_t + o^0_t, with o^I_t the output of the identity run (v = 0) and o^0_t that of
+# the run from zero.  Rank r takes segment r: rank 0 runs its segment from the caller's
+# initial state (its outputs and final state are final); every other rank runs its
+# segment from the identity with v = 0 and from a zero state (one call of two sequences),
+# the (A, B) of all ranks are exchanged (the one collective), each rank chains
+# S_start(r) = S_start(r-1) A_{r-1} + B_{r-1}, with (A_0, B_0) = (0, rank 0's final state),
+# and assembles its outputs S_start(r) o^I_t + o^0_t and final state S_start(r) A_r + B_r
+# with fp32 matrix products.  The serial chain shrinks from the whole sequence to the
+# first segment; the price is two runs of each other segment, on ranks whose SMs would
+# otherwise sit idle.
 # `run(segment_inputs, state, zero_v)` is the prefill call (it returns (output,
 # final_state)); states are [1, HV, 128, 128] fp32.
 
@@ -168,8 +172,8 @@ def segment_bounds(total_tokens: int, world: int, align: int = 64,
     boundaries on multiples of `align` (the prefill chunk) and the last one ending at the
     sequence's end; a segment may be empty when the sequence is short.  The first segment
     gets `first_weight` shares and every other one share: its rank runs it once, while the
-    others run their segment three times (the two runs of its state map, then the final
-    one), two of them before the exchange."""
+    others run their segment twice (from the identity with v = 0 and from zero; as one call
+    of two sequences that is two waves of the state kernel), all before the exchange."""
     if world <= 0:
         raise ValueError("world must be positive")
     chunks = (total_tokens + align - 1) // align
@@ -196,18 +200,30 @@ def segment_inputs(inp: Dict[str, torch.Tensor], lo: int, hi: int) -> Dict[str, 
     return out
 
 
-def segment_map(run, seg: Dict[str, torch.Tensor]) -> Tuple[torch.Tensor, torch.Tensor]:
-    """(A, B) of one segment: A from the identity with v = 0, B from a zero state (an
-    empty segment is the identity map: the prefill call would return a zero state)."""
+def segment_map(run, seg: Dict[str, torch.Tensor]
+                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(A, B, o^I, o^0) of one segment: A and o^I from the identity with v = 0, B and o^0
+    from a zero state (an empty segment is the identity map with no outputs: the prefill
+    call would return a zero state)."""
     HV = seg["v"].shape[1]
     dev = seg["v"].device
     eye = torch.eye(128, dtype=torch.float32, device=dev).expand(1, HV, 128, 128).contiguous()
     zero = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
     if seg["q"].shape[0] == 0:
-        return eye, zero
-    _, A = run(seg, eye, True)
-    _, B = run(seg, zero, False)
-    return A, B
+        none = torch.empty((0, HV, 128), dtype=torch.bfloat16, device=dev)
+        return eye, zero, none, none
+    o_id, A = run(seg, eye, True)
+    o_zero, B = run(seg, zero, False)
+    return A, B, o_id, o_zero
+
+
+def segment_finish(start: torch.Tensor, A: torch.Tensor, B: torch.Tensor, o_id: torch.Tensor,
+                   o_zero: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """A segment's outputs and final state from its start state [1, HV, 128, 128] and its
+    map: o_t[h, v] = sum_j start[h, v, j] o^I_t[h, j] + o^0_t[h, v] (bf16, summed in fp32)
+    and start A + B (fp32)."""
+    out = torch.einsum("thj,hvj->thv", o_id.float(), start[0]) + o_zero.float()
+    return out.to(torch.bfloat16), torch.matmul(start, A) + B
 
 
 def _run_from(run, seg: Dict[str, torch.Tensor], state: torch.Tensor
@@ -244,11 +260,12 @@ def segment_scan_rank(run, inp: Dict[str, torch.Tensor], world: int, rank: int, 
         out, fin = _run_from(run, seg, state)
         A, B = torch.zeros_like(fin), fin
     else:
-        A, B = segment_map(run, seg)
-    As, Bs = all_gather(A.contiguous()), all_gather(B.contiguous())
+        A, B, o_id, o_zero = segment_map(run, seg)
+    parts = all_gather(torch.cat([A, B], dim=0).contiguous())
     if rank == 0:
         return out, fin
-    return _run_from(run, seg, chain_start(As, Bs, rank).contiguous())
+    As, Bs = [p_[0:1] for p_ in parts], [p_[1:2] for p_ in parts]
+    return segment_finish(chain_start(As, Bs, rank), A, B, o_id, o_zero)
 
 
 def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
@@ -266,14 +283,12 @@ def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
             if state is None:
                 state = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=inp["v"].device)
             out, fin = _run_from(run, seg, state)
-            maps.append((torch.zeros_like(fin), fin))
+            maps.append((torch.zeros_like(fin), fin, None, None))
             parts.append(out)
         else:
             maps.append(segment_map(run, seg))
     As, Bs = [m[0] for m in maps], [m[1] for m in maps]
-    for r, (lo, hi) in enumerate(segment_bounds(T, world)):
-        if r == 0:
-            continue
-        out, fin = _run_from(run, segment_inputs(inp, lo, hi), chain_start(As, Bs, r).contiguous())
+    for r in range(1, world):
+        out, fin = segment_finish(chain_start(As, Bs, r), *maps[r])
         parts.append(out)
     return torch.cat(parts, dim=0), fin
