@@ -273,6 +273,25 @@ int gdn_prefill_launch_noalloc(const void* q, const void* k, const void* v, cons
                                int head_size, int use_qk_l2norm, void* stream);
 
 /*
+ * Segment-scan output assembly (multi-GPU prefill of one long sequence split
+ * into token segments; no counterpart in the reference, whose prefill walks a
+ * sequence on one device).  Over a segment the outputs are affine in the
+ * segment's start state S: o_t = S o^I_t + o^0_t, with o^I the segment's
+ * output from the identity state with v = 0 and o^0 its output from a zero
+ * state (both from ordinary prefill calls).  This forms, on `stream`,
+ *   output[t][h][v] = bf16( sum_j start_state[h][v][j] o_identity[t][h][j]
+ *                           + o_zero[t][h][v] )
+ * for t < num_tokens, h < num_v_heads.  Layouts: o_identity, o_zero, output
+ * [num_tokens, num_v_heads, head_size] bf16 (o_identity 16-byte aligned);
+ * start_state [num_v_heads, head_size, head_size] fp32 (k-last), 16-byte
+ * aligned.  start_state is split into bf16 hi + lo in the kernel, so the sum
+ * carries fp32-level precision in S.  head_size must be 128.
+ */
+int gdn_segment_outputs_launch(const void* o_identity, const void* o_zero,
+                               const float* start_state, void* output, int num_tokens,
+                               int num_v_heads, int head_size, void* stream);
+
+/*
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
  * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory

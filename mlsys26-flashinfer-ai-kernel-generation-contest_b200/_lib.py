@@ -45,6 +45,7 @@ SIGNATURES = {
     "gdn_prefill_launch_ext": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _i, _f, _vp, _vp, _vp, _vp, ctypes.c_longlong, _i, _i,
                                     _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_segment_outputs_launch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gdn_device_error": (_i, [_i]),
 }
 

@@ -221,9 +221,22 @@ def segment_finish(start: torch.Tensor, A: torch.Tensor, B: torch.Tensor, o_id: 
                    o_zero: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """A segment's outputs and final state from its start state [1, HV, 128, 128] and its
     map: o_t[h, v] = sum_j start[h, v, j] o^I_t[h, j] + o^0_t[h, v] (bf16, summed in fp32)
-    and start A + B (fp32)."""
+    and start A + B (fp32).  On the GPU the outputs come from one kernel of the library
+    (gdn_segment_outputs_launch: start split into bf16 hi + lo, bf16 tensor-core products
+    with fp32 sums, o^0 added before the bf16 rounding)."""
+    fin = torch.baddbmm(B[0], start[0], A[0]).unsqueeze(0)
+    if o_id.is_cuda:
+        from ._checks import stream_handle
+        from ._lib import LIB, check
+        out = torch.empty_like(o_zero)
+        st = start[0].contiguous()
+        o_id, o_zero = o_id.contiguous(), o_zero.contiguous()
+        check("gdn_segment_outputs_launch", LIB.gdn_segment_outputs_launch(
+            o_id.data_ptr(), o_zero.data_ptr(), st.data_ptr(), out.data_ptr(),
+            o_id.shape[0], o_id.shape[1], o_id.shape[2], stream_handle(o_id.device)))
+        return out, fin
     out = torch.einsum("thj,hvj->thv", o_id.float(), start[0]) + o_zero.float()
-    return out.to(torch.bfloat16), torch.matmul(start, A) + B
+    return out.to(torch.bfloat16), fin
 
 
 def _run_from(run, seg: Dict[str, torch.Tensor], state: torch.Tensor
@@ -238,10 +251,10 @@ def _run_from(run, seg: Dict[str, torch.Tensor], state: torch.Tensor
 
 def chain_start(As: Sequence[torch.Tensor], Bs: Sequence[torch.Tensor], r: int) -> torch.Tensor:
     """S_start(r) = S_start(r-1) A_{r-1} + B_{r-1} from S_start(1) = B_0 (r >= 1), in fp32."""
-    S = Bs[0]
+    S = Bs[0][0]
     for m in range(1, r):
-        S = torch.matmul(S, As[m]) + Bs[m]
-    return S
+        S = torch.baddbmm(Bs[m][0], S, As[m][0])
+    return S.unsqueeze(0)
 
 
 def segment_scan_rank(run, inp: Dict[str, torch.Tensor], world: int, rank: int, all_gather

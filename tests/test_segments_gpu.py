@@ -40,3 +40,40 @@ def test_segment_scan_short_sequence_with_empty_segment(cuda):
     out, fin = pkg.sharding.segment_scan_local(run, d, 4)  # the second segment is empty
     torch.cuda.synchronize()
     assert_parity(out, fin, ro.cpu(), rs.cpu(), what="130 tokens in 4 segments")
+
+
+@pytest.mark.parametrize("L,hv", [(1, 1), (130, 4), (3648, 32)])
+def test_segment_outputs_kernel_vs_fp64(cuda, L, hv):
+    """gdn_segment_outputs_launch: out = S o^I + o^0 per v-head against an fp64 product of
+    the same bf16 inputs (ragged last tile, one token, P2's eight-way segment length)."""
+    pkg = load_pkg()
+    g = torch.Generator().manual_seed(L + hv)
+    o_id = (torch.randn(L, hv, 128, generator=g) * 0.1).bfloat16()
+    o_zero = (torch.randn(L, hv, 128, generator=g) * 0.1).bfloat16()
+    start = torch.randn(1, hv, 128, 128, generator=g) * 0.05
+    A = torch.randn(1, hv, 128, 128, generator=g) * 0.05
+    B = torch.randn(1, hv, 128, 128, generator=g) * 0.05
+    out, fin = pkg.sharding.segment_finish(start.to(cuda), A.to(cuda), B.to(cuda),
+                                           o_id.to(cuda), o_zero.to(cuda))
+    torch.cuda.synchronize()
+    ref = torch.einsum("thj,hvj->thv", o_id.double(), start[0].double()) + o_zero.double()
+    err = (out.cpu().double() - ref).abs()
+    # bf16 rounding of the result is the only visible error (S is carried as hi + lo)
+    assert (err <= 2.0 ** -8 * ref.abs() + 1e-6).all(), err.max().item()
+    ref_fin = torch.matmul(start.double(), A.double()) + B.double()
+    assert torch.allclose(fin.cpu().double(), ref_fin, rtol=1e-5, atol=1e-6)
+
+
+def test_segment_outputs_kernel_rejects_bad_arguments(cuda):
+    pkg = load_pkg()
+    from importlib import import_module
+    lib = import_module(pkg.__name__ + "._lib").LIB
+    t = torch.zeros(4, 2, 128, dtype=torch.bfloat16, device=cuda)
+    s = torch.zeros(2, 128, 128, device=cuda)
+    assert lib.gdn_segment_outputs_launch(t.data_ptr(), t.data_ptr(), s.data_ptr(), t.data_ptr(),
+                                          4, 2, 64, None) == -2          # head_size
+    assert lib.gdn_segment_outputs_launch(None, t.data_ptr(), s.data_ptr(), t.data_ptr(),
+                                          4, 2, 128, None) == -1         # null input
+    assert lib.gdn_segment_outputs_launch(t.data_ptr() + 8, t.data_ptr(), s.data_ptr(),
+                                          t.data_ptr(), 3, 2, 128, None) == -1  # unaligned
+    assert lib.gdn_segment_outputs_launch(None, None, None, None, 0, 2, 128, None) == 0
