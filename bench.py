@@ -394,13 +394,14 @@ class PrefillWork:
         self.out = torch.empty(L, HV, 128, dtype=torch.bfloat16, device=dev)
         self.ns = torch.empty(1, HV, 128, 128, device=dev)
         self.A = torch.zeros(1, HV, 128, 128, device=dev)
-        self.parts = [torch.empty(2, HV, 128, 128, device=dev) for _ in range(world)]
+        self.maps = torch.empty(world, 2, HV, 128, 128, device=dev)
         self.lens = [L]
         self.cpu_inp = seg
         self.tokens = L
         self.flops = L * W.prefill_flops_per_token(HQ, HV)
         per = self.pkg.prefill.launches_per_call
-        self.launches = per(L, 1, HQ, HV) if rank == 0 else per(2 * L, 2, HQ, HV)
+        # rank > 0: the two-sequence call, then the chain and output kernels
+        self.launches = per(L, 1, HQ, HV) if rank == 0 else per(2 * L, 2, HQ, HV) + 2
 
     def _segment_step(self, d):
         P = self.pkg
@@ -415,16 +416,11 @@ class PrefillWork:
                           e["b"], e["cu_seqlens"], e["scale"], self.dbl_out, self.dbl_ns,
                           use_qk_l2norm=True)
             mine = self.dbl_ns
-        self.dist.pg.all_gather(self.parts, mine)
+        self.dist.pg.all_gather_into_tensor(self.maps, mine)
         if self.rank > 0:
-            S = self.pkg.sharding
-            start = S.chain_start([p_[0:1] for p_ in self.parts],
-                                  [p_[1:2] for p_ in self.parts], self.rank)
             L = self.out.shape[0]
-            out, fin = S.segment_finish(start, self.dbl_ns[0:1], self.dbl_ns[1:2],
-                                        self.dbl_out[:L], self.dbl_out[L:])
-            self.out.copy_(out)
-            self.ns.copy_(fin)
+            self.pkg.sharding.segment_assemble(self.maps, self.rank, self.dbl_out[:L],
+                                               self.dbl_out[L:], out=self.out, final=self.ns)
 
     def step(self):
         d = self.inp

@@ -292,6 +292,21 @@ int gdn_segment_outputs_launch(const void* o_identity, const void* o_zero,
                                int num_v_heads, int head_size, void* stream);
 
 /*
+ * Segment-scan state chain (same multi-GPU scan; no counterpart in the
+ * reference).  maps holds every segment's state map as all-gathered,
+ * [num_maps][2][num_v_heads][head_size][head_size] fp32 (A_m then B_m; a
+ * segment maps S to S A_m + B_m, and segment 0's entry is (unused, its final
+ * state)).  For segment `rank` (1 <= rank < num_maps) this writes, on
+ * `stream`, its start state S = (..(B_0 A_1 + B_1) A_2 + ..) A_{rank-1} +
+ * B_{rank-1} and its final state S A_rank + B_rank, both
+ * [num_v_heads][head_size][head_size] fp32, in fp32 arithmetic.  All pointers
+ * 16-byte aligned; head_size must be 128.
+ */
+int gdn_segment_chain_launch(const float* maps, int num_maps, int rank, float* start_state,
+                             float* final_state, int num_v_heads, int head_size,
+                             void* stream);
+
+/*
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
  * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory

@@ -46,6 +46,7 @@ SIGNATURES = {
                                     _vp, _i, _f, _vp, _vp, _vp, _vp, ctypes.c_longlong, _i, _i,
                                     _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_segment_outputs_launch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "gdn_segment_chain_launch": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_device_error": (_i, [_i]),
 }
 

@@ -257,6 +257,41 @@ def chain_start(As: Sequence[torch.Tensor], Bs: Sequence[torch.Tensor], r: int) 
     return S.unsqueeze(0)
 
 
+def segment_assemble(maps: torch.Tensor, rank: int, o_id: torch.Tensor, o_zero: torch.Tensor,
+                     out: torch.Tensor = None, final: torch.Tensor = None
+                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Segment `rank`'s (>= 1) outputs and final state from every segment's map, `maps`
+    [world, 2, HV, 128, 128] (A then B; the first segment's entry is (unused, its final
+    state)), and its two runs' outputs o^I, o^0.  On the GPU: two kernels of the library
+    (gdn_segment_chain_launch: the chained start state and the final state in fp32;
+    gdn_segment_outputs_launch: the outputs); on the CPU the same algebra in torch.
+    `out` / `final` (contiguous, of the result's shape) receive the results when given."""
+    if not maps.is_cuda:
+        As, Bs = [m[0:1] for m in maps], [m[1:2] for m in maps]
+        o, f = segment_finish(chain_start(As, Bs, rank), maps[rank, 0:1], maps[rank, 1:2],
+                              o_id, o_zero)
+        if out is not None:
+            o = out.copy_(o)
+        if final is not None:
+            f = final.copy_(f)
+        return o, f
+    from ._checks import stream_handle
+    from ._lib import LIB, check
+    maps = maps.contiguous()
+    W, _, HV, D, _ = maps.shape
+    start = torch.empty(1, HV, D, D, dtype=torch.float32, device=maps.device)
+    fin = final if final is not None else torch.empty_like(start)
+    stream = stream_handle(maps.device)
+    check("gdn_segment_chain_launch", LIB.gdn_segment_chain_launch(
+        maps.data_ptr(), W, rank, start.data_ptr(), fin.data_ptr(), HV, D, stream))
+    out = out if out is not None else torch.empty_like(o_zero)
+    o_id, o_zero = o_id.contiguous(), o_zero.contiguous()
+    check("gdn_segment_outputs_launch", LIB.gdn_segment_outputs_launch(
+        o_id.data_ptr(), o_zero.data_ptr(), start.data_ptr(), out.data_ptr(),
+        o_id.shape[0], HV, D, stream))
+    return out, fin
+
+
 def segment_scan_rank(run, inp: Dict[str, torch.Tensor], world: int, rank: int, all_gather
                       ) -> Tuple[torch.Tensor, torch.Tensor]:
     """This rank's part of the segment scan.  `all_gather(t)` returns the list of every
@@ -277,8 +312,7 @@ def segment_scan_rank(run, inp: Dict[str, torch.Tensor], world: int, rank: int, 
     parts = all_gather(torch.cat([A, B], dim=0).contiguous())
     if rank == 0:
         return out, fin
-    As, Bs = [p_[0:1] for p_ in parts], [p_[1:2] for p_ in parts]
-    return segment_finish(chain_start(As, Bs, rank), A, B, o_id, o_zero)
+    return segment_assemble(torch.stack(list(parts)), rank, o_id, o_zero)
 
 
 def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
@@ -300,8 +334,8 @@ def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
             parts.append(out)
         else:
             maps.append(segment_map(run, seg))
-    As, Bs = [m[0] for m in maps], [m[1] for m in maps]
+    stacked = torch.stack([torch.cat([m[0], m[1]], dim=0) for m in maps])
     for r in range(1, world):
-        out, fin = segment_finish(chain_start(As, Bs, r), *maps[r])
+        out, fin = segment_assemble(stacked, r, maps[r][2], maps[r][3])
         parts.append(out)
     return torch.cat(parts, dim=0), fin

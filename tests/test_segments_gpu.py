@@ -77,3 +77,41 @@ def test_segment_outputs_kernel_rejects_bad_arguments(cuda):
     assert lib.gdn_segment_outputs_launch(t.data_ptr() + 8, t.data_ptr(), s.data_ptr(),
                                           t.data_ptr(), 3, 2, 128, None) == -1  # unaligned
     assert lib.gdn_segment_outputs_launch(None, None, None, None, 0, 2, 128, None) == 0
+
+
+@pytest.mark.parametrize("world,hv", [(2, 1), (4, 3), (8, 32)])
+def test_segment_chain_kernel_vs_fp64(cuda, world, hv):
+    """gdn_segment_chain_launch: every rank's chained start state and final state against
+    an fp64 chain of the same maps (maps scaled like contracting state maps)."""
+    pkg = load_pkg()
+    g = torch.Generator().manual_seed(world * 100 + hv)
+    maps = torch.randn(world, 2, hv, 128, 128, generator=g) * 0.05
+    maps[:, 0] += torch.eye(128) * 0.5  # A_m near a scaled identity, as decaying segments give
+    # o^I[t][h][j] = (t == j): the outputs then read back the start state, out[t][h][v] =
+    # bf16(start[h][v][t])
+    eye = torch.eye(128).unsqueeze(1).expand(128, hv, 128).bfloat16().contiguous()
+    zero = torch.zeros(128, hv, 128, dtype=torch.bfloat16)
+    md = maps.double()
+    for r in range(1, world):
+        S = md[0, 1]
+        for m in range(1, r):
+            S = torch.matmul(S, md[m, 0]) + md[m, 1]
+        ref_fin = torch.matmul(S, md[r, 0]) + md[r, 1]
+        out, fin = pkg.sharding.segment_assemble(maps.to(cuda), r, eye.to(cuda), zero.to(cuda))
+        torch.cuda.synchronize()
+        assert torch.allclose(fin.cpu()[0].double(), ref_fin, rtol=1e-5, atol=1e-6), r
+        start_read = out.cpu().double().permute(1, 2, 0)  # [h][v][t]
+        assert ((start_read - S).abs() <= 2.0 ** -8 * S.abs() + 1e-7).all(), r
+
+
+def test_segment_chain_kernel_rejects_bad_arguments(cuda):
+    pkg = load_pkg()
+    from importlib import import_module
+    lib = import_module(pkg.__name__ + "._lib").LIB
+    m = torch.zeros(2, 2, 1, 128, 128, device=cuda)
+    s = torch.zeros(1, 128, 128, device=cuda)
+    p = (m.data_ptr(), s.data_ptr(), s.data_ptr())
+    assert lib.gdn_segment_chain_launch(p[0], 2, 0, p[1], p[2], 1, 128, None) == -1  # rank 0
+    assert lib.gdn_segment_chain_launch(p[0], 2, 2, p[1], p[2], 1, 128, None) == -1  # rank >= maps
+    assert lib.gdn_segment_chain_launch(p[0], 2, 1, p[1], p[2], 1, 64, None) == -2   # head_size
+    assert lib.gdn_segment_chain_launch(p[0] + 4, 2, 1, p[1], p[2], 1, 128, None) == -1
