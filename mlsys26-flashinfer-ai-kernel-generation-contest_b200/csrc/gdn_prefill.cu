@@ -214,6 +214,7 @@ extern "C" int gdn_device_error(int clear) {
   const unsigned a = gdn::read_device_error(clear != 0);
   const unsigned b = gdn::read_split_device_error(clear != 0);
   const unsigned d = gdn::read_decode_device_error(clear != 0);
-  if (a == ~0u || b == ~0u || d == ~0u) return -1;
-  return (int)(a | b | d);
+  const unsigned e = gdn::read_segment_device_error(clear != 0);
+  if (a == ~0u || b == ~0u || d == ~0u || e == ~0u) return -1;
+  return (int)(a | b | d | e);
 }

@@ -71,5 +71,6 @@ unsigned read_split_device_error(bool clear);
 unsigned read_device_error(bool clear);
 // Same for the streaming decode kernel.
 unsigned read_decode_device_error(bool clear);
+unsigned read_segment_device_error(bool clear);
 
 }  // namespace gdn

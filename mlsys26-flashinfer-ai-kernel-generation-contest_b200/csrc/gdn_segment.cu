@@ -1,47 +1,44 @@
-// Output assembly of the segment-level scan (one long sequence split into token segments,
-// one per GPU).  Over a segment the outputs are affine in the segment's start state S
-// (k-last [v][j] per v-head): o_t = S o^I_t + o^0_t, where o^I is the output of the segment
-// run from the identity state with v = 0 and o^0 its output from a zero state.  Once the
-// start state is known (after the exchange of the segments' state maps), this kernel forms
+// Segment-level scan of one long sequence split into token segments, one per GPU: the
+// state-map chain and the output assembly.  Over a segment the outputs are affine in the
+// segment's start state S (k-last [v][j] per v-head): o_t = S o^I_t + o^0_t, where o^I is
+// the output of the segment run from the identity state with v = 0 and o^0 its output
+// from a zero state.  Once the start state is known (after the exchange of the segments'
+// state maps, chained below), the output kernel forms
 //     out[t][h][v] = bf16( sum_j S[h][v][j] o^I[t][h][j] + o^0[t][h][v] )
 // in one pass over o^I and o^0.
 //
-// One CTA per (128-token tile, v-head), 8 warps of 16 tokens each.  S[h] is split once per
-// CTA into bf16 hi + lo (S = hi + lo to ~2^-17 relative) in shared memory; o^I is bf16
-// already, so the products run as bf16 tensor-core fragments (m16n8k16, fp32 accumulate),
-// two per output tile (hi and lo).  Rows are padded to 136 elements so that the fragment
-// reads of the 32 lanes fall into 32 distinct banks.  The kernel moves
-// 3 x T x HV x 128 x 2 bytes (o^I and o^0 in, out) and is HBM-bound.
+// Output kernel: one CTA of 4 warps per (128-token tile, v-head).  The o^I tile and S[h],
+// split into bf16 hi + lo (S = hi + lo to 2^-15 relative), are written to shared memory
+// in the 128-byte-swizzled K-major layout; one thread issues the 16 tcgen05 MMAs
+// (M = 128 tokens, N = 128 v, K = 128 j; hi then lo) into an fp32 TMEM accumulator while
+// every thread loads its token's o^0 row; the epilogue reads its TMEM lane, adds o^0 and
+// rounds once to bf16.  It moves 3 x T x HV x 128 x 2 bytes (o^I and o^0 in, out) plus
+// S from L2, and is HBM-bound.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "gdn_b200.h"
+#include "gdn_chunk_math.cuh"
+#include "sm100.cuh"
 
 namespace {
 
+using namespace gdn::sm100;
+
 constexpr int kD = 128;
-constexpr int kTile = 128;               // tokens per CTA
-constexpr int kWarps = kTile / 16;
-constexpr int kThreads = 32 * kWarps;
-constexpr int kLd = kD + 8;              // padded row (bf16 elements)
-constexpr size_t kSmem = (size_t)(2 * kD + kTile) * kLd * sizeof(__nv_bfloat16);
+constexpr int kTile = 128;    // tokens per CTA (the MMA's M)
+constexpr int kThreads = 128;
+constexpr uint32_t kOI = 0, kSH = 32768, kSL = 65536, kBarOff = 98304;  // SW128 images
+constexpr size_t kSmem = kBarOff + 64 + 1024;  // + slack to align the base to 1024 bytes
+constexpr unsigned kErrMmaTimeout = 2u;
 
-// Four 8 x 8 bf16 matrices from shared memory; lane l gives the row address of matrix l / 8.
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const __nv_bfloat16* row) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(row));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
+__device__ unsigned g_segment_device_error;
 
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// Row r (128 bf16 = two 64-element halves) of a K-major SW128 image at `base`: the 16-byte
+// piece `ch` (8 elements) goes to half ch / 8, swizzled chunk ch % 8.
+__device__ __forceinline__ uint32_t img_off(uint32_t r, uint32_t ch) {
+  return (ch >> 3) * 16384u + sw128(r, ch & 7u);
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -49,99 +46,107 @@ __global__ void __launch_bounds__(kThreads, 2)
                            const __nv_bfloat16* __restrict__ o_zero,
                            const float* __restrict__ start, __nv_bfloat16* __restrict__ out,
                            int L, int HV) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* shi = reinterpret_cast<__nv_bfloat16*>(smem);  // [v][j]
-  __nv_bfloat16* slo = shi + kD * kLd;
-  __nv_bfloat16* oit = slo + kD * kLd;                           // [t][j]
-  const int h = blockIdx.y;
-  const int t0 = blockIdx.x * kTile;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  const uint32_t sb = smem_u32(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 8);
+  const int h = blockIdx.y, t0 = blockIdx.x * kTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  // o^I tile: 128 rows of 256 bytes (16 x 16-byte pieces); rows past L are zero.  All of a
-  // thread's loads are issued before the first store (the loads are independent).
+  if (warp == 0) {
+    tmem_alloc(slot, 128);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  // o^I tile: 128 token rows x 16 pieces; rows past L are zero
   {
-    constexpr int kPer = kTile * 16 / kThreads;
-    uint4 w[kPer];
+    uint4 w[16];
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
+    for (int k = 0; k < 16; ++k) {
       const int i = tid + k * kThreads, r = i >> 4, p = i & 15, t = t0 + r;
       w[k] = t < L ? __ldg(reinterpret_cast<const uint4*>(o_id + ((size_t)t * HV + h) * kD) + p)
                    : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
+    for (int k = 0; k < 16; ++k) {
       const int i = tid + k * kThreads;
-      *reinterpret_cast<uint4*>(oit + (i >> 4) * kLd + 8 * (i & 15)) = w[k];
+      st_shared_v4(sb + kOI + img_off(i >> 4, i & 15), w[k].x, w[k].y, w[k].z, w[k].w);
     }
   }
-  // S[h] -> hi | lo (fp32 rows of 128, four elements per load), in two batches of loads
-  const float4* s4 = reinterpret_cast<const float4*>(start + (size_t)h * kD * kD);
-#pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    constexpr int kPer = kD * kD / 4 / kThreads / 2;
-    float4 x[kPer];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) x[k] = __ldg(s4 + tid + (b * kPer + k) * kThreads);
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = tid + (b * kPer + k) * kThreads;
-      const int v = i >> 5, j = (i & 31) * 4;
-      const __nv_bfloat162 h01 = __floats2bfloat162_rn(x[k].x, x[k].y);
-      const __nv_bfloat162 h23 = __floats2bfloat162_rn(x[k].z, x[k].w);
-      const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
-      const __nv_bfloat162 l01 = __floats2bfloat162_rn(x[k].x - f01.x, x[k].y - f01.y);
-      const __nv_bfloat162 l23 = __floats2bfloat162_rn(x[k].z - f23.x, x[k].w - f23.y);
-      uint2 hv, lv;
-      hv.x = *reinterpret_cast<const uint32_t*>(&h01);
-      hv.y = *reinterpret_cast<const uint32_t*>(&h23);
-      lv.x = *reinterpret_cast<const uint32_t*>(&l01);
-      lv.y = *reinterpret_cast<const uint32_t*>(&l23);
-      *reinterpret_cast<uint2*>(shi + v * kLd + j) = hv;
-      *reinterpret_cast<uint2*>(slo + v * kLd + j) = lv;
-    }
+  // S[h] rows v -> hi | lo images (8 fp32 per piece)
+  const float* sh = start + (size_t)h * kD * kD;
+#pragma unroll 4
+  for (int k = 0; k < 16; ++k) {
+    const int i = tid + k * kThreads, v = i >> 4, p = i & 15;
+    const float4 x = __ldg(reinterpret_cast<const float4*>(sh + v * kD + 8 * p));
+    const float4 y = __ldg(reinterpret_cast<const float4*>(sh + v * kD + 8 * p + 4));
+    const float f[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+    uint4 hi, lo;
+    gdn::cm::split8(f, hi, lo);
+    st_shared_v4(sb + kSH + img_off(v, p), hi.x, hi.y, hi.z, hi.w);
+    st_shared_v4(sb + kSL + img_off(v, p), lo.x, lo.y, lo.z, lo.w);
   }
+  fence_proxy_async();
+  tc_fence_before();
   __syncthreads();
-
-  const int g = lane >> 2, c = lane & 3;
-  const int r0 = 16 * warp;  // this warp's rows in the tile
-  float acc[16][4];
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (tid == 0) {  // D[t][v] = sum_j oI[t][j] (S_hi[v][j] + S_lo[v][j])
+    const uint32_t idesc = umma_idesc_bf16(128, 128, false, false);
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  // ldmatrix row addresses: A matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15) of the warp's
-  // 16 rows; B matrices (n-tile nt: v 0-7, nt + 1: v 8-15) x (k 0-7 | 8-15), B[k][n] = S[v][j]
-  const int lr = lane & 7, lm = lane >> 3;
-  const __nv_bfloat16* a_row = oit + (r0 + lr + 8 * (lm & 1)) * kLd + 8 * (lm >> 1);
-  const int b_off = (lr + 8 * (lm >> 1)) * kLd + 8 * (lm & 1);
+    for (int term = 0; term < 2; ++term)
 #pragma unroll
-  for (int ks = 0; ks < kD / 16; ++ks) {
-    uint32_t a[4];
-    ldmatrix_x4(a, a_row + 16 * ks);
-#pragma unroll
-    for (int np = 0; np < 8; ++np) {  // pairs of n-tiles
-      uint32_t bh[4], bl[4];
-      ldmatrix_x4(bh, shi + (16 * np) * kLd + b_off + 16 * ks);
-      ldmatrix_x4(bl, slo + (16 * np) * kLd + b_off + 16 * ks);
-      mma_bf16_16816(acc[2 * np], a, bh[0], bh[1]);
-      mma_bf16_16816(acc[2 * np], a, bl[0], bl[1]);
-      mma_bf16_16816(acc[2 * np + 1], a, bh[2], bh[3]);
-      mma_bf16_16816(acc[2 * np + 1], a, bl[2], bl[3]);
-    }
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
+        umma_bf16(tmem, umma_desc_k(sb + kOI + off), umma_desc_k(sb + (term ? kSL : kSH) + off),
+                  idesc, (term | ks) != 0);
+      }
+    umma_commit(bar);
   }
-  // + o^0, bf16 out (two adjacent v per store)
+  // this thread's token (TMEM lane 32 warp + lane): its o^0 row, loaded while the MMAs run
+  const int t = t0 + 32 * warp + lane;
+  uint4 z[16];
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int t = t0 + r0 + g + 8 * half;
-    if (t >= L) continue;
-    const size_t row = ((size_t)t * HV + h) * kD;
+  for (int p = 0; p < 16; ++p)
+    z[p] = t < L ? __ldg(reinterpret_cast<const uint4*>(o_zero + ((size_t)t * HV + h) * kD) + p)
+                 : make_uint4(0u, 0u, 0u, 0u);
+  const bool done = mbar_wait(bar, 0, 1u << 22);
+  if (!done && lane == 0) atomicOr(&g_segment_device_error, kErrMmaTimeout);
+  tc_fence_after();
+  if (done) {
+    const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int v = 8 * nt + 2 * c;
-      const __nv_bfloat162 z = *reinterpret_cast<const __nv_bfloat162*>(o_zero + row + v);
-      const float2 zf = __bfloat1622float2(z);
-      *reinterpret_cast<__nv_bfloat162*>(out + row + v) =
-          __floats2bfloat162_rn(acc[nt][2 * half] + zf.x, acc[nt][2 * half + 1] + zf.y);
+    for (int q = 0; q < 4; ++q) {
+      float d[32];
+      tmem_ld32(tl + 32u * q, d);
+      tmem_wait_ld();
+      if (t < L) {
+        uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)t * HV + h) * kD + 32 * q);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t zw[4] = {z[4 * q + p].x, z[4 * q + p].y, z[4 * q + p].z, z[4 * q + p].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 zf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zw[e]));
+            const __nv_bfloat162 r =
+                __floats2bfloat162_rn(d[8 * p + 2 * e] + zf.x, d[8 * p + 2 * e + 1] + zf.y);
+            o[e] = *reinterpret_cast<const uint32_t*>(&r);
+          }
+          dst[p] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
     }
+  } else if (tid == 0) {
+    mbar_wait(bar, 0, 1u << 22);  // the MMAs still in flight land before TMEM is freed
   }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
 // Start state and final state of segment `rank` from every segment's state map
@@ -195,15 +200,20 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     cp_async_wait_all();
     __syncthreads();  // A_m and S in place; the other A buffer is no longer read
     if (m < rank) prefetch(m + 1, csm + (m & 1) * kD * kD);
-    float acc[4][8];
+    // B_m rows: loaded now, added after the product (their latency hides behind it)
+    float4 bq[4][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float4* b4 =
           reinterpret_cast<const float4*>(B(m) + (size_t)(r0 + 4 * rq + i) * kD + 8 * cb);
-      const float4 x = __ldg(b4), y = __ldg(b4 + 1);
-      acc[i][0] = x.x; acc[i][1] = x.y; acc[i][2] = x.z; acc[i][3] = x.w;
-      acc[i][4] = y.x; acc[i][5] = y.y; acc[i][6] = y.z; acc[i][7] = y.w;
+      bq[i][0] = __ldg(b4);
+      bq[i][1] = __ldg(b4 + 1);
     }
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
     const float* srow = S + (4 * rq) * kSLd;
 #pragma unroll 4
     for (int j = 0; j < kD; ++j) {
@@ -216,6 +226,12 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(si, av[e], acc[i][e]);
       }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[i][0] += bq[i][0].x; acc[i][1] += bq[i][0].y; acc[i][2] += bq[i][0].z;
+      acc[i][3] += bq[i][0].w; acc[i][4] += bq[i][1].x; acc[i][5] += bq[i][1].y;
+      acc[i][6] += bq[i][1].z; acc[i][7] += bq[i][1].w;
     }
     if (m == rank) {  // the segment's own map: its final state; S holds its start state
 #pragma unroll
@@ -245,6 +261,18 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
 
 }  // namespace
+
+namespace gdn {
+unsigned read_segment_device_error(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_segment_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+  if (clear) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(g_segment_device_error, &zero, sizeof(zero));
+  }
+  return v;
+}
+}  // namespace gdn
 
 extern "C" int gdn_segment_outputs_launch(const void* o_identity, const void* o_zero,
                                           const float* start_state, void* output,

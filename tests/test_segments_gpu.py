@@ -58,8 +58,10 @@ def test_segment_outputs_kernel_vs_fp64(cuda, L, hv):
     torch.cuda.synchronize()
     ref = torch.einsum("thj,hvj->thv", o_id.double(), start[0].double()) + o_zero.double()
     err = (out.cpu().double() - ref).abs()
-    # bf16 rounding of the result is the only visible error (S is carried as hi + lo)
-    assert (err <= 2.0 ** -8 * ref.abs() + 1e-6).all(), err.max().item()
+    # the bf16 rounding of the result, plus the residual of S = hi + lo (below 2^-15 of |S|)
+    # over the summed terms: bounded by the magnitude of the terms, not of their sum
+    mag = torch.einsum("thj,hvj->thv", o_id.double().abs(), start[0].double().abs())
+    assert (err <= 2.0 ** -8 * ref.abs() + 2.0 ** -14 * mag + 1e-7).all(), err.max().item()
     ref_fin = torch.matmul(start.double(), A.double()) + B.double()
     assert torch.allclose(fin.cpu().double(), ref_fin, rtol=1e-5, atol=1e-6)
 
@@ -101,7 +103,8 @@ def test_segment_chain_kernel_vs_fp64(cuda, world, hv):
         torch.cuda.synchronize()
         assert torch.allclose(fin.cpu()[0].double(), ref_fin, rtol=1e-5, atol=1e-6), r
         start_read = out.cpu().double().permute(1, 2, 0)  # [h][v][t]
-        assert ((start_read - S).abs() <= 2.0 ** -8 * S.abs() + 1e-7).all(), r
+        # one bf16 rounding of S carried as hi + lo (2^-15): at most half an ulp plus that
+        assert ((start_read - S).abs() <= (2.0 ** -8 + 2.0 ** -13) * S.abs() + 1e-7).all(), r
 
 
 def test_segment_chain_kernel_rejects_bad_arguments(cuda):
