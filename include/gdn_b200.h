@@ -282,7 +282,7 @@ int gdn_prefill_launch_noalloc(const void* q, const void* k, const void* v, cons
  *   output[t][h][v] = bf16( sum_j start_state[h][v][j] o_identity[t][h][j]
  *                           + o_zero[t][h][v] )
  * for t < num_tokens, h < num_v_heads.  Layouts: o_identity, o_zero, output
- * [num_tokens, num_v_heads, head_size] bf16 (o_identity 16-byte aligned);
+ * [num_tokens, num_v_heads, head_size] bf16, 16-byte aligned;
  * start_state [num_v_heads, head_size, head_size] fp32 (k-last), 16-byte
  * aligned.  start_state is split into bf16 hi + lo in the kernel, so the sum
  * carries fp32-level precision in S.  head_size must be 128.

@@ -7,19 +7,22 @@
 //     out[t][h][v] = bf16( sum_j S[h][v][j] o^I[t][h][j] + o^0[t][h][v] )
 // in one pass over o^I and o^0.
 //
-// Output kernel: one CTA of 4 warps per (128-token tile, v-head).  The o^I tile and S[h],
-// split into bf16 hi + lo (S = hi + lo to 2^-15 relative), are written to shared memory
-// in the 128-byte-swizzled K-major layout; one thread issues the 16 tcgen05 MMAs
-// (M = 128 tokens, N = 128 v, K = 128 j; hi then lo) into an fp32 TMEM accumulator while
-// every thread loads its token's o^0 row; the epilogue reads its TMEM lane, adds o^0 and
-// rounds once to bf16.  It moves 3 x T x HV x 128 x 2 bytes (o^I and o^0 in, out) plus
-// S from L2, and is HBM-bound.
+// Output kernel: one CTA of 4 warps per (v-head, group of 128-token tiles), one CTA per SM.
+// S[h], split into bf16 hi + lo (S = hi + lo to 2^-15 relative), is written once to shared
+// memory in the 128-byte-swizzled K-major layout; the o^I and o^0 tiles arrive by TMA in
+// the same layout, two tiles in flight; per tile one thread issues the 16 tcgen05 MMAs
+// (M = 128 tokens, N = 128 v, K = 128 j; hi then lo) into an fp32 TMEM accumulator, and the
+// epilogue reads its TMEM lane, adds o^0 and rounds once to bf16.  It moves
+// 3 x T x HV x 128 x 2 bytes (o^I and o^0 in, out) and is HBM-bound.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "gdn_b200.h"
 #include "gdn_chunk_math.cuh"
+#include "gdn_prefill.cuh"
 #include "sm100.cuh"
 
 namespace {
@@ -27,55 +30,81 @@ namespace {
 using namespace gdn::sm100;
 
 constexpr int kD = 128;
-constexpr int kTile = 128;    // tokens per CTA (the MMA's M)
+constexpr int kTile = 128;    // tokens per tile (the MMA's M)
 constexpr int kThreads = 128;
-constexpr uint32_t kOI = 0, kSH = 32768, kSL = 65536, kBarOff = 98304;  // SW128 images
+// shared memory (1024-aligned): S hi | S lo images, then two buffers of [o^I | o^0] tile
+// images (each 32 KB: two 64-column halves of 128 rows, 128-byte swizzle), then barriers
+constexpr uint32_t kSH = 0, kSL = 32768, kBuf0 = 65536, kBufBytes = 65536, kOZ = 32768;
+constexpr uint32_t kBarOff = kBuf0 + 2 * kBufBytes;
 constexpr size_t kSmem = kBarOff + 64 + 1024;  // + slack to align the base to 1024 bytes
-constexpr unsigned kErrMmaTimeout = 2u;
+constexpr unsigned kErrTmaTimeout = 1u, kErrMmaTimeout = 2u;
+constexpr uint32_t kWaitLimit = 1u << 22;
 
 __device__ unsigned g_segment_device_error;
 
-// Row r (128 bf16 = two 64-element halves) of a K-major SW128 image at `base`: the 16-byte
-// piece `ch` (8 elements) goes to half ch / 8, swizzled chunk ch % 8.
+// Row r (128 bf16 = two 64-element halves) of a K-major SW128 image: the 16-byte piece `ch`
+// (8 elements) sits in half ch / 8, swizzled chunk ch % 8.
 __device__ __forceinline__ uint32_t img_off(uint32_t r, uint32_t ch) {
   return (ch >> 3) * 16384u + sw128(r, ch & 7u);
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-    segment_outputs_kernel(const __nv_bfloat16* __restrict__ o_id,
-                           const __nv_bfloat16* __restrict__ o_zero,
+// o^I and o^0 of tile `tile` -> buffer at `buf` (four 64 x 64 boxes each; rows past the end
+// of the segment arrive as zeros), completion counted on `bar`.
+__device__ __forceinline__ void load_tile(uint8_t* buf, const CUtensorMap* m_id,
+                                          const CUtensorMap* m_zero, uint64_t* bar, int h,
+                                          int tile) {
+  mbar_arrive_expect_tx(bar, kBufBytes);
+#pragma unroll
+  for (int half = 0; half < 2; ++half)
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const int x = h * kD + 64 * half, y = tile * kTile + 64 * rb;
+      const uint32_t off = 16384u * half + 8192u * rb;
+      tma_load_2d(buf + off, m_id, bar, x, y);
+      tma_load_2d(buf + kOZ + off, m_zero, bar, x, y);
+    }
+}
+
+// One CTA per (v-head, group of token tiles): S[h] is split once and stays in shared
+// memory; the tiles of the group stream through two buffers (the next tile's TMA loads run
+// while the current tile's MMAs and epilogue do).
+__global__ void __launch_bounds__(kThreads, 1)
+    segment_outputs_kernel(const __grid_constant__ CUtensorMap m_id,
+                           const __grid_constant__ CUtensorMap m_zero,
                            const float* __restrict__ start, __nv_bfloat16* __restrict__ out,
                            int L, int HV) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 8);
-  const int h = blockIdx.y, t0 = blockIdx.x * kTile;
+  uint64_t* bar_in = reinterpret_cast<uint64_t*>(smem + kBarOff);  // [2]
+  uint64_t* bar_mma = bar_in + 2;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + 28);
+  const int h = blockIdx.y, group = blockIdx.x, groups = gridDim.x;
+  const int ntiles = (L + kTile - 1) / kTile;
+  const int mine = ntiles > group ? (ntiles - group + groups - 1) / groups : 0;  // tiles g, g+G, ..
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (mine == 0) return;
   if (warp == 0) {
     tmem_alloc(slot, 128);
     tmem_relinquish();
   }
   if (tid == 32) {
-    mbar_init(bar, 1);
+    mbar_init(&bar_in[0], 1);
+    mbar_init(&bar_in[1], 1);
+    mbar_init(bar_mma, 1);
+    *abort_flag = 0;
     fence_mbar_init();
   }
-  // o^I tile: 128 token rows x 16 pieces; rows past L are zero
-  {
-    uint4 w[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int i = tid + k * kThreads, r = i >> 4, p = i & 15, t = t0 + r;
-      w[k] = t < L ? __ldg(reinterpret_cast<const uint4*>(o_id + ((size_t)t * HV + h) * kD) + p)
-                   : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int i = tid + k * kThreads;
-      st_shared_v4(sb + kOI + img_off(i >> 4, i & 15), w[k].x, w[k].y, w[k].z, w[k].w);
-    }
+  __syncthreads();
+  int issued = 0;  // tiles whose loads were issued (thread 0)
+  if (tid == 0) {
+    tma_prefetch_desc(&m_id);
+    tma_prefetch_desc(&m_zero);
+    for (; issued < 2 && issued < mine; ++issued)
+      load_tile(smem + kBuf0 + issued * kBufBytes, &m_id, &m_zero, &bar_in[issued], h,
+                group + issued * groups);
   }
   // S[h] rows v -> hi | lo images (8 fp32 per piece)
   const float* sh = start + (size_t)h * kD * kD;
@@ -95,29 +124,45 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *slot;
-  if (tid == 0) {  // D[t][v] = sum_j oI[t][j] (S_hi[v][j] + S_lo[v][j])
-    const uint32_t idesc = umma_idesc_bf16(128, 128, false, false);
+  const uint32_t idesc = umma_idesc_bf16(128, 128, false, false);
+  const int r = 32 * warp + lane;  // this thread's token row in a tile (its TMEM lane)
+  bool ok = true, mma_pending = false;
+  for (int i = 0; i < mine && ok; ++i) {
+    const int b = i & 1;
+    const uint32_t par = (i >> 1) & 1;
+    const uint32_t buf = sb + kBuf0 + b * kBufBytes;
+    if (!mbar_wait(&bar_in[b], par, kWaitLimit)) {
+      atomicOr(&g_segment_device_error, kErrTmaTimeout);
+      ok = false;
+    }
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 0) {  // D[t][v] = sum_j oI[t][j] (S_hi[v][j] + S_lo[v][j])
 #pragma unroll
-    for (int term = 0; term < 2; ++term)
+      for (int term = 0; term < 2; ++term)
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
-        umma_bf16(tmem, umma_desc_k(sb + kOI + off), umma_desc_k(sb + (term ? kSL : kSH) + off),
-                  idesc, (term | ks) != 0);
-      }
-    umma_commit(bar);
-  }
-  // this thread's token (TMEM lane 32 warp + lane): its o^0 row, loaded while the MMAs run
-  const int t = t0 + 32 * warp + lane;
-  uint4 z[16];
-#pragma unroll
-  for (int p = 0; p < 16; ++p)
-    z[p] = t < L ? __ldg(reinterpret_cast<const uint4*>(o_zero + ((size_t)t * HV + h) * kD) + p)
-                 : make_uint4(0u, 0u, 0u, 0u);
-  const bool done = mbar_wait(bar, 0, 1u << 22);
-  if (!done && lane == 0) atomicOr(&g_segment_device_error, kErrMmaTimeout);
-  tc_fence_after();
-  if (done) {
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = 16384u * (ks >> 2) + 32u * (ks & 3);
+          umma_bf16(tmem, umma_desc_k(buf + off), umma_desc_k(sb + (term ? kSL : kSH) + off),
+                    idesc, (term | ks) != 0);
+        }
+      umma_commit(bar_mma);
+    }
+    mma_pending = true;
+    if (!mbar_wait(bar_mma, i & 1, kWaitLimit)) {
+      if (lane == 0) atomicOr(&g_segment_device_error, kErrMmaTimeout);
+      ok = false;
+    }
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    mma_pending = false;
+    tc_fence_after();
+    const int t = (group + i * groups) * kTile + r;
     const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -128,21 +173,31 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)t * HV + h) * kD + 32 * q);
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const uint32_t zw[4] = {z[4 * q + p].x, z[4 * q + p].y, z[4 * q + p].z, z[4 * q + p].w};
+          const uint4 zv = ld_shared_v4(buf + kOZ + img_off(r, 4 * q + p));
+          const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 zf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zw[e]));
-            const __nv_bfloat162 r =
+            const __nv_bfloat162 rr =
                 __floats2bfloat162_rn(d[8 * p + 2 * e] + zf.x, d[8 * p + 2 * e + 1] + zf.y);
-            o[e] = *reinterpret_cast<const uint32_t*>(&r);
+            o[e] = *reinterpret_cast<const uint32_t*>(&rr);
           }
           dst[p] = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }
-  } else if (tid == 0) {
-    mbar_wait(bar, 0, 1u << 22);  // the MMAs still in flight land before TMEM is freed
+    tc_fence_before();
+    __syncthreads();  // buffer b and the accumulator are free
+    if (tid == 0 && issued < mine) {
+      load_tile(smem + kBuf0 + b * kBufBytes, &m_id, &m_zero, &bar_in[b], h,
+                group + issued * groups);
+      ++issued;
+    }
+  }
+  if (!ok && tid == 0) {  // copies and MMAs still in flight land before the CTA exits
+    if (mma_pending) mbar_wait(bar_mma, 0, kWaitLimit);
+    for (int j = max(issued - 2, 0); j < issued; ++j) mbar_wait(&bar_in[j & 1], (j >> 1) & 1, kWaitLimit);
   }
   tc_fence_before();
   __syncthreads();
@@ -283,22 +338,30 @@ extern "C" int gdn_segment_outputs_launch(const void* o_identity, const void* o_
   if (num_tokens == 0) return GDN_OK;
   if (o_identity == nullptr || o_zero == nullptr || start_state == nullptr || output == nullptr)
     return GDN_ERR_INVALID_ARGUMENT;
-  if (misaligned(o_identity, 16) || misaligned(start_state, 16) || misaligned(o_zero, 4) ||
-      misaligned(output, 4))
+  if (misaligned(o_identity, 16) || misaligned(start_state, 16) || misaligned(o_zero, 16) ||
+      misaligned(output, 16))
     return GDN_ERR_INVALID_ARGUMENT;
   static bool configured[64] = {};
+  static int sms[64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
+  if (!configured[dev]) {
     if (cudaFuncSetAttribute(segment_outputs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmem) != cudaSuccess)
+                             (int)kSmem) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return GDN_ERR_LAUNCH;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    configured[dev] = true;
   }
-  const dim3 grid((unsigned)((num_tokens + kTile - 1) / kTile), (unsigned)num_v_heads);
+  CUtensorMap m_id, m_zero;
+  if (!gdn::make_tile_map(&m_id, o_identity, num_v_heads, num_tokens) ||
+      !gdn::make_tile_map(&m_zero, o_zero, num_v_heads, num_tokens))
+    return GDN_ERR_UNSUPPORTED;
+  // one CTA per SM: the SMs split over the v-heads, each CTA a group of token tiles
+  const int ntiles = (num_tokens + kTile - 1) / kTile;
+  const int groups = std::max(1, std::min(ntiles, sms[dev] / num_v_heads));
+  const dim3 grid((unsigned)groups, (unsigned)num_v_heads);
   segment_outputs_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(o_identity), static_cast<const __nv_bfloat16*>(o_zero),
-      start_state, static_cast<__nv_bfloat16*>(output), num_tokens, num_v_heads);
+      m_id, m_zero, start_state, static_cast<__nv_bfloat16*>(output), num_tokens, num_v_heads);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
