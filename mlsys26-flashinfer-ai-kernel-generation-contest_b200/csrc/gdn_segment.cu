@@ -231,6 +231,9 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   float* S = csm + 2 * kD * kD;  // [row][kSLd]
   const int h = blockIdx.y, r0 = kChainRows * blockIdx.x;
   const int tid = threadIdx.x, rq = tid >> 4, cb = tid & 15;
+  // this thread's 8 columns: two groups of 4, 64 apart, so that the 16 column blocks of a
+  // half-warp read 256 contiguous bytes of an A row (no bank conflicts)
+  const int c0 = 4 * cb, c1 = 64 + 4 * cb;
   const size_t mat = (size_t)kD * kD;
   auto A = [&](int m) { return maps + ((size_t)(2 * m) * HV + h) * mat; };
   auto B = [&](int m) { return maps + ((size_t)(2 * m + 1) * HV + h) * mat; };
@@ -259,10 +262,9 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     float4 bq[4][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float4* b4 =
-          reinterpret_cast<const float4*>(B(m) + (size_t)(r0 + 4 * rq + i) * kD + 8 * cb);
-      bq[i][0] = __ldg(b4);
-      bq[i][1] = __ldg(b4 + 1);
+      const float* brow = B(m) + (size_t)(r0 + 4 * rq + i) * kD;
+      bq[i][0] = __ldg(reinterpret_cast<const float4*>(brow + c0));
+      bq[i][1] = __ldg(reinterpret_cast<const float4*>(brow + c1));
     }
     float acc[4][8];
 #pragma unroll
@@ -272,8 +274,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     const float* srow = S + (4 * rq) * kSLd;
 #pragma unroll 4
     for (int j = 0; j < kD; ++j) {
-      const float4 x = *reinterpret_cast<const float4*>(As + j * kD + 8 * cb);
-      const float4 y = *reinterpret_cast<const float4*>(As + j * kD + 8 * cb + 4);
+      const float4 x = *reinterpret_cast<const float4*>(As + j * kD + c0);
+      const float4 y = *reinterpret_cast<const float4*>(As + j * kD + c1);
       const float av[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -291,18 +293,18 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     if (m == rank) {  // the segment's own map: its final state; S holds its start state
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float* dst = final_out + ((size_t)h * kD + r0 + 4 * rq + i) * kD + 8 * cb;
-        reinterpret_cast<float4*>(dst)[0] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        reinterpret_cast<float4*>(dst)[1] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        float* dst = final_out + ((size_t)h * kD + r0 + 4 * rq + i) * kD;
+        *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
       break;
     }
     __syncthreads();  // every read of S done
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float* d = S + (4 * rq + i) * kSLd + 8 * cb;
-      reinterpret_cast<float4*>(d)[0] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-      reinterpret_cast<float4*>(d)[1] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      float* d = S + (4 * rq + i) * kSLd;
+      *reinterpret_cast<float4*>(d + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      *reinterpret_cast<float4*>(d + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
     }
   }
   // start state = S (rows of this CTA)
