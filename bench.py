@@ -306,8 +306,8 @@ MTP_T = 4  # draft tokens verified per row (speculative decoding)
 def prefill_plan(pkg, name, dist, force="auto"):
     """This rank's part of prefill config `name`: None at N=1; whole sequences
     (longest-first packing) when there are at least as many sequences as ranks; one
-    sequence over 4 or more ranks: consecutive token segments chained through their state
-    maps (one all-gather per call); else a q/k-head group with its v-heads.  `force`
+    sequence: consecutive token segments chained through their state maps (one all-gather
+    per call); else a q/k-head group with its v-heads.  `force`
     ("heads" or "segments") overrides the choice for a config with fewer sequences than
     ranks."""
     if dist.world == 1:
@@ -317,7 +317,7 @@ def prefill_plan(pkg, name, dist, force="auto"):
     if cfg.n >= dist.world:
         lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
         return ("seqs", pkg.sharding.lpt_assign(lens, dist.world)[dist.rank])
-    segments = cfg.n == 1 and dist.world >= 4 if force == "auto" else force == "segments"
+    segments = cfg.n == 1 if force == "auto" else force == "segments"
     if segments and cfg.n == 1:
         return ("segments", dist.world, dist.rank)
     return ("heads",) + tuple(pkg.sharding.head_range(W.HQ, dist.world, dist.rank))
@@ -840,8 +840,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-extra", action="store_true")
     ap.add_argument("--prefill-plan", choices=["auto", "heads", "segments"], default="auto",
-                    help="multi-GPU split of a single prefill sequence (default: segments "
-                         "from 4 GPUs, head groups below)")
+                    help="multi-GPU split of a single prefill sequence (default: token "
+                         "segments)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()
