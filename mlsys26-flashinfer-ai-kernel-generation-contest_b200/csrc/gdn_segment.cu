@@ -272,17 +272,30 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
     const float* srow = S + (4 * rq) * kSLd;
-#pragma unroll 4
+    // software-pipelined: the shared-memory operands of step j + 1 are loaded while the
+    // FMAs of step j issue (one warp per scheduler cannot hide the load latency otherwise)
+    float4 x = *reinterpret_cast<const float4*>(As + c0);
+    float4 y = *reinterpret_cast<const float4*>(As + c1);
+    float sv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sv[i] = srow[i * kSLd];
+#pragma unroll 2
     for (int j = 0; j < kD; ++j) {
-      const float4 x = *reinterpret_cast<const float4*>(As + j * kD + c0);
-      const float4 y = *reinterpret_cast<const float4*>(As + j * kD + c1);
+      const int jn = (j + 1) & (kD - 1);  // the last prefetch wraps to row 0 and is unused
+      const float4 xn = *reinterpret_cast<const float4*>(As + jn * kD + c0);
+      const float4 yn = *reinterpret_cast<const float4*>(As + jn * kD + c1);
+      float svn[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) svn[i] = srow[i * kSLd + jn];
       const float av[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float si = srow[i * kSLd + j];
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(si, av[e], acc[i][e]);
-      }
+        for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(sv[i], av[e], acc[i][e]);
+      x = xn;
+      y = yn;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sv[i] = svn[i];
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
