@@ -12,17 +12,20 @@ line also carries a ``prefill`` object with the P1 (8 varlen sequences) and P2
 
 N > 1 (torchrun, one process per GPU): weak scaling -- every rank runs the
 same per-GPU workload on its own data (decode: 128 sequences per GPU, so N=8
-is the 1024-sequence configuration sharded by batch; prefill: the 64-sequence
-P3 set sharded by sequence with longest-first bin packing, and the single
-sequence of P2 sharded by q/k-head group); there is no collective on the data
-path.  Time is the max over ranks of the device time.
+is the 1024-sequence configuration sharded by batch); the prefill extras are
+strong scaling (the 64-sequence P3 set sharded by sequence with longest-first
+bin packing; the single sequence of P2 sharded by q/k-head group, and, as a
+separate line, by the token-segment scan with its one all-gather).  Decode has
+no collective on the data path.  Time is the max over ranks of the device time.
 
 Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
 the launching stream, barrier + synchronize on both sides.  Inputs are larger
 than L2 (126 MB) and decode ping-pongs its state between two buffers.
 ``--impl reference`` times the CPU restatement of the reference's algorithm
 (the oracle port; the reference itself is Triton-only and has no CPU path) on
-the host's cores, on the same workload and metric.
+the host's cores, on the same workload, metric, config and step count, with
+the flashinfer-bench definition reference timed beside it on a small sample;
+it never imports the package or loads its CUDA library.
 """
 from __future__ import annotations
 
@@ -303,33 +306,44 @@ class MtpWork:
 MTP_T = 4  # draft tokens verified per row (speculative decoding)
 
 
-def prefill_plan(pkg, name, dist, force="auto"):
-    """This rank's part of prefill config `name`: None at N=1; whole sequences
-    (longest-first packing) when there are at least as many sequences as ranks; one
-    sequence: consecutive token segments chained through their state maps (one all-gather
-    per call); else a q/k-head group with its v-heads.  `force`
-    ("heads" or "segments") overrides the choice for a config with fewer sequences than
-    ranks."""
-    if dist.world == 1:
+def plan_kind(W, name, world, force="auto"):
+    """How prefill config `name` is split over `world` GPUs: None (one GPU), "seqs" (whole
+    sequences, longest-first packing; at least as many sequences as ranks), "heads" (q/k-head
+    groups with their v-heads; the default when there are fewer sequences than ranks, no
+    collective) or "segments" (one sequence as consecutive token segments chained through
+    their state maps, one all-gather per call; opt-in with force="segments")."""
+    if world == 1:
         return None
-    W = pkg.workloads
     cfg = W.PREFILL_CONFIGS[name]
-    if cfg.n >= dist.world:
+    if cfg.n >= world:
+        return "seqs"
+    return "segments" if (force == "segments" and cfg.n == 1) else "heads"
+
+
+def prefill_plan(pkg, name, dist, force="auto"):
+    """This rank's part of prefill config `name` (see plan_kind)."""
+    W = pkg.workloads
+    kind = plan_kind(W, name, dist.world, force)
+    if kind is None:
+        return None
+    if kind == "seqs":
+        cfg = W.PREFILL_CONFIGS[name]
         lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
         return ("seqs", pkg.sharding.lpt_assign(lens, dist.world)[dist.rank])
-    segments = cfg.n == 1 if force == "auto" else force == "segments"
-    if segments and cfg.n == 1:
+    if kind == "segments":
         return ("segments", dist.world, dist.rank)
     return ("heads",) + tuple(pkg.sharding.head_range(W.HQ, dist.world, dist.rank))
 
 
 def plan_text(plan, world):
-    if plan is None:
+    kind = plan if (plan is None or isinstance(plan, str)) else plan[0]
+    if kind is None:
         return "single GPU"
-    if plan[0] == "seqs":
+    if kind == "seqs":
         return f"sequence-sharded x{world} (LPT), no collective"
-    if plan[0] == "segments":
-        return f"token-segment scan x{world} (one all-gather of the segments' state maps)"
+    if kind == "segments":
+        return (f"token-segment scan x{world} (one all-gather of the segments' state maps per "
+                f"call: departs from the no-collective v-head plan)")
     return f"q/k-head-group-sharded x{world}, no collective"
 
 
@@ -529,39 +543,62 @@ def graph_steps(work, n_graphs):
     return replay, graphs
 
 
-def cpu_baseline_decode(batch, budget_s=10.0, state_bf16=False):
-    from oracle import gdn_oracle as O
-    pkg = importlib.import_module(PKG_NAME)
-    W = pkg.workloads
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    inp = W.decode_inputs(batch, seed=0)
+_CPU_MODS = None
+
+
+def cpu_modules():
+    """(workloads, oracle) for the CPU legs, loaded from their files without importing the
+    package: the package's import maps the CUDA library, which a CPU arm must not load."""
+    global _CPU_MODS
+    if _CPU_MODS is None:
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_gdn_bench_workloads",
+                                                      REPO / PKG_NAME / "workloads.py")
+        W = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = W
+        spec.loader.exec_module(W)
+        from oracle import gdn_oracle as O
+        _CPU_MODS = (W, O)
+    return _CPU_MODS
+
+
+def host_threads():
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_decode_step(batch, seed=0, state_bf16=False):
+    """One full decode step of the oracle port on the host, as a callable (inputs built
+    once); returns (step, state bytes per step)."""
+    W, O = cpu_modules()
+    inp = W.decode_inputs(batch, seed=seed)
     if state_bf16:
         inp["state"] = inp["state"].to(torch.bfloat16)
     q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
-    O.decode(q[:1], k[:1], inp["v"][:1], inp["state"][:1], inp["A_log"], inp["a"][:1],
-             inp["dt_bias"], inp["b"][:1], inp["scale"])  # warm
-    reps, t_start = 0, time.perf_counter()
-    while True:
+
+    def step():
         O.decode(q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
                  inp["scale"])
-        reps += 1
-        el = time.perf_counter() - t_start
-        if el > budget_s or reps >= 5:
-            break
-    per = el / reps
-    gbs = W.decode_state_bytes(batch) // (2 if state_bf16 else 1) / per / 1e9
-    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} full decode step(s) of batch {batch} (oracle, fp32 torch CPU)",
-            "sec_per_step": per}
+    return step, W.decode_state_bytes(batch) // (2 if state_bf16 else 1)
 
 
-def cpu_baseline_prefill(cfg_name, budget_tokens=4096):
-    from oracle import gdn_oracle as O
-    pkg = importlib.import_module(PKG_NAME)
-    W = pkg.workloads
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+def cpu_mtp_step(rows, seed=0):
+    W, O = cpu_modules()
+    inp = W.mtp_inputs(rows, MTP_T, rows, seed=seed)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+
+    def step():
+        O.mtp(q, k, inp["v"], inp["state"], inp["state_indices"], inp["A_log"], inp["a"],
+              inp["dt_bias"], inp["b"], inp["scale"], intermediate=True)
+    return step, W.mtp_state_bytes(rows, MTP_T, intermediate=True)
+
+
+def cpu_prefill_step(cfg_name, budget_tokens):
+    """The oracle port's prefill over the first `budget_tokens` tokens of config
+    `cfg_name` (its first sequences, the last one cut), as a callable; returns (step,
+    tokens per step, sample text)."""
+    W, O = cpu_modules()
     inp = W.prefill_config_inputs(cfg_name, seed=0)
     cu = inp["cu_seqlens"].tolist()
     n = 1
@@ -571,12 +608,79 @@ def cpu_baseline_prefill(cfg_name, budget_tokens=4096):
     sub_cu = torch.tensor([min(c, T) for c in cu[:n + 1]], dtype=torch.int32)
     st = inp["state"][:n] if inp["state"] is not None else None
     q, k = O.l2norm(inp["q"][:T]), O.l2norm(inp["k"][:T])
+
+    def step():
+        O.prefill(q, k, inp["v"][:T], st, inp["A_log"], inp["a"][:T], inp["dt_bias"],
+                  inp["b"][:T], sub_cu, inp["scale"])
+    return step, T, f"first {T} tokens of {cfg_name} ({n} sequence(s))"
+
+
+def timed_cpu(step, steps, warmup):
+    for _ in range(warmup):
+        step()
     t0 = time.perf_counter()
-    O.prefill(q, k, inp["v"][:T], st, inp["A_log"], inp["a"][:T], inp["dt_bias"], inp["b"][:T],
-              sub_cu, inp["scale"])
-    el = time.perf_counter() - t0
-    return {"value": T / el, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"first {T} tokens of {cfg_name} ({n} sequence(s); oracle, fp32 torch CPU)"}
+    for _ in range(steps):
+        step()
+    return (time.perf_counter() - t0) / steps
+
+
+def definition_baseline(kind, param):
+    """The flashinfer-bench definition reference itself (`_gdn_decode_reference` /
+    `_gdn_prefill_reference`, the Python loops the contest's speedups divide by) on a
+    bounded sample, fed host-normalised q/k like the oracle.  None when it cannot be
+    imported."""
+    try:
+        from flashinfer.trace.templates.gdn import (_gdn_decode_reference,
+                                                    _gdn_prefill_reference)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    W, O = cpu_modules()
+    threads = host_threads()
+    if kind in ("decode", "decode_bf16state", "mtp"):
+        rows = 8
+        inp = W.decode_inputs(rows, seed=0)
+        q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+        args = (q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                inp["scale"])
+        per = timed_cpu(lambda: _gdn_decode_reference(*args), 2, 1)
+        return {"value": W.decode_state_bytes(rows) / per / 1e9, "unit": "GB/s",
+                "cores": threads, "kind": "definition",
+                "sample": f"one fp32 decode step of {rows} rows (flashinfer-bench definition "
+                          f"_gdn_decode_reference)"}
+    tokens = 128
+    inp = W.prefill_inputs([tokens], seed=0)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+    args = (q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+            inp["cu_seqlens"], inp["scale"])
+    per = timed_cpu(lambda: _gdn_prefill_reference(*args), 1, 1)
+    return {"value": tokens / per, "unit": "tokens/s", "cores": threads, "kind": "definition",
+            "sample": f"{tokens} tokens of one sequence (flashinfer-bench definition "
+                      f"_gdn_prefill_reference)"}
+
+
+def cpu_baseline(kind, param, budget_s=10.0):
+    """The oracle port on the host cores, bounded sample (rank 0, N = 1 only)."""
+    threads = host_threads()
+    if kind in ("decode", "decode_bf16state"):
+        step, units = cpu_decode_step(param, state_bf16=kind == "decode_bf16state")
+        reps = max(1, min(5, int(budget_s / max(timed_cpu(step, 1, 0), 1e-3))))
+        per = timed_cpu(step, reps, 0)
+        res = {"value": units / per / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{reps} full decode step(s) of batch {param} (oracle, fp32 torch CPU)"}
+    elif kind == "mtp":
+        rows = min(param, 16)
+        step, units = cpu_mtp_step(rows)
+        per = timed_cpu(step, 2, 1)
+        res = {"value": units / per / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} rows x {MTP_T} tokens of the same workload (oracle, fp32 "
+                         f"torch CPU)"}
+    else:
+        step, T, sample = cpu_prefill_step(param, 4096)
+        per = timed_cpu(step, 1, 0)
+        res = {"value": T / per, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": sample + " (oracle, fp32 torch CPU)"}
+    res["definition"] = definition_baseline(kind, param)
+    return res
 
 
 # --------------------------------------------------------------------------- arms
@@ -631,30 +735,6 @@ def measure_mtp(pkg, dist, batch, steps, warmup, dev, with_e2e=True, graphs=True
     return res
 
 
-def cpu_baseline_mtp(batch, budget_s=10.0):
-    from oracle import gdn_oracle as O
-    pkg = importlib.import_module(PKG_NAME)
-    W = pkg.workloads
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    rows = min(batch, 16)  # bounded sample: `rows` rows of the same workload
-    inp = W.mtp_inputs(rows, MTP_T, rows, seed=0)
-    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
-    reps, t_start = 0, time.perf_counter()
-    while True:
-        O.mtp(q, k, inp["v"], inp["state"], inp["state_indices"], inp["A_log"], inp["a"],
-              inp["dt_bias"], inp["b"], inp["scale"], intermediate=True)
-        reps += 1
-        el = time.perf_counter() - t_start
-        if el > budget_s or reps >= 5:
-            break
-    per = el / reps
-    gbs = W.mtp_state_bytes(rows, MTP_T, intermediate=True) / per / 1e9
-    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} call(s) of {rows} rows x {MTP_T} tokens (oracle, fp32 torch CPU)",
-            "sec_per_step": per * batch / rows}
-
-
 def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True):
     w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard, dist=dist)
     with ClockSampler(dev.index) as clk:
@@ -698,135 +778,156 @@ WORKLOADS = {
 }
 
 
+def workload_config(W, kind, param, world, args):
+    """`config` of the JSON line (the same dict for both arms): what one step is."""
+    launch = "CUDA graph replay" if not args.no_graphs else "eager"
+    if kind in ("decode", "decode_bf16state"):
+        bf = kind == "decode_bf16state"
+        units = W.decode_state_bytes(param) // (2 if bf else 1)
+        return {"workload": f"GDN decode, batch {param} per GPU, 16 q/k + 32 v heads, "
+                            f"head_dim 128, {'bf16' if bf else 'fp32'} k-last state, "
+                            f"q/k L2-normalised in-kernel",
+                "batch_per_gpu": param, "global_batch": param * world,
+                "parallelism": f"batch-sharded x{world}, no collective",
+                "l2": (f"inputs > L2: {units / 1e6:.0f} MB state traffic per step, state "
+                       f"ping-pong" if units > L2_BYTES else
+                       f"L2 flushed before every step ({units / 1e6:.1f} MB state traffic "
+                       f"per step)"),
+                "launch": launch}
+    if kind == "mtp":
+        units = W.mtp_state_bytes(param, MTP_T, intermediate=True)
+        return {"workload": f"GDN multi-token decode, {param} rows x {MTP_T} tokens per GPU, "
+                            f"16 q/k + 32 v heads, fp32 k-last state pool updated in place, "
+                            f"rollback buffer written per token, q/k L2-normalised in-kernel",
+                "batch_per_gpu": param, "draft_tokens": MTP_T,
+                "parallelism": f"batch-sharded x{world}, no collective",
+                "l2": f"inputs > L2: {units / 1e9:.2f} GB state traffic per step",
+                "launch": launch}
+    cfg = W.PREFILL_CONFIGS[param]
+    lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
+    return {"workload": f"GDN prefill {param}", "tokens": int(sum(lens)),
+            "parallelism": plan_text(plan_kind(W, param, world, args.prefill_plan), world),
+            "l2": "inputs > L2"}
+
+
+def metric_of(kind):
+    if kind in ("decode", "decode_bf16state"):
+        return "decode state-traffic GB/s", "GB/s"
+    if kind == "mtp":
+        return "mtp state-traffic GB/s", "GB/s"
+    return "prefill tokens/s", "tokens/s"
+
+
+def dtype_of(kind):
+    return {"decode": "fp32", "decode_bf16state": "fp32 compute, bf16 state",
+            "mtp": "fp32"}.get(kind, "bf16")
+
+
 def run_ours(args, dist):
     pkg = importlib.import_module(PKG_NAME)
     dev = torch.device("cuda", dist.local)
     torch.cuda.set_device(dev)
     pk, src = peaks()
     kind, param = WORKLOADS[args.workload]
-    line = {"impl": "ours"}
-    if kind in ("decode", "decode_bf16state"):
-        bf = kind == "decode_bf16state"
-        r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev, state_bf16=bf,
-                           graphs=not args.no_graphs)
-        line.update({
-            "metric": "decode state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
-            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp32" + (" compute, bf16 state" if bf else ""),
-            "data": "synthetic (seeded)",
-            "config": {"workload": f"GDN decode, batch {param} per GPU, 16 q/k + 32 v heads, "
-                                   f"head_dim 128, {'bf16' if bf else 'fp32'} k-last state, "
-                                   f"q/k L2-normalised in-kernel",
-                       "batch_per_gpu": param, "global_batch": param * dist.world,
-                       "parallelism": f"batch-sharded x{dist.world}, no collective",
-                       "l2": (f"inputs > L2: {r['units'] / 1e6:.0f} MB state traffic per step, "
-                              f"state ping-pong" if r["units"] > L2_BYTES else
-                              f"L2 flushed before every step ({r['units'] / 1e6:.1f} MB state "
-                              f"traffic per step)"),
-                       "launch": "CUDA graph replay" if not args.no_graphs else "eager"},
-            "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
-            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
-            "kernel_ms": round(r["kern_ms"], 5),
-        })
-    elif kind == "mtp":
-        r = measure_mtp(pkg, dist, param, args.steps, args.warmup, dev,
-                        graphs=not args.no_graphs)
-        line.update({
-            "metric": "mtp state-traffic GB/s", "value": round(r["value"], 2), "unit": "GB/s",
-            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-            "config": {"workload": f"GDN multi-token decode, {param} rows x {MTP_T} tokens per "
-                                   f"GPU, 16 q/k + 32 v heads, fp32 k-last state pool updated "
-                                   f"in place, rollback buffer written per token, q/k "
-                                   f"L2-normalised in-kernel",
-                       "batch_per_gpu": param, "draft_tokens": MTP_T,
-                       "parallelism": f"batch-sharded x{dist.world}, no collective",
-                       "l2": f"inputs > L2: {r['units'] / 1e9:.2f} GB state traffic per step",
-                       "launch": "CUDA graph replay" if not args.no_graphs else "eager"},
-            "roofline": roofline("hbm", r["achieved"], args.workload, pk, src),
-            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
-            "kernel_ms": round(r["kern_ms"], 5),
-        })
+    metric, unit = metric_of(kind)
+    line = {"impl": "ours", "metric": metric}
+    cfg = workload_config(pkg.workloads, kind, param, dist.world, args)
+    if kind in ("decode", "decode_bf16state", "mtp"):
+        if kind == "mtp":
+            r = measure_mtp(pkg, dist, param, args.steps, args.warmup, dev,
+                            graphs=not args.no_graphs)
+        else:
+            r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev,
+                               state_bf16=kind == "decode_bf16state", graphs=not args.no_graphs)
+        value, bound, scaling = round(r["value"], 2), "hbm", "weak"
     else:
         shard = prefill_plan(pkg, param, dist, args.prefill_plan)
         r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
-        line.update({
-            "metric": "prefill tokens/s", "value": round(r["value"], 1), "unit": "tokens/s",
-            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(r["ms"], 5), "higher_is_better": True,
-            "scaling": "strong" if dist.world > 1 else "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": {"workload": f"GDN prefill {param}", "tokens": r["tokens_all"],
-                       "parallelism": plan_text(shard, dist.world),
-                       "l2": "inputs > L2"},
-            "tflops": round(r["tflops"], 2),
-            "roofline": roofline("tensor", r["achieved"], args.workload if shard is None else "",
-                                 pk, src),
-            "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
-            "kernel_ms": round(r["kern_ms"], 5),
-        })
-    # secondary: the prefill configurations next to the decode headline
+        value, bound = round(r["value"], 1), "tensor"
+        scaling = "strong" if dist.world > 1 else "weak"
+    line.update({
+        "value": value, "unit": unit, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": dtype_of(kind),
+        "data": "synthetic (seeded)", "config": cfg,
+        "roofline": roofline(bound, r["achieved"],
+                             args.workload if (bound == "hbm" or dist.world == 1) else "",
+                             pk, src),
+        "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
+        "kernel_ms": round(r["kern_ms"], 5),
+    })
+    if bound == "tensor":
+        line["tflops"] = round(r["tflops"], 2)
+    # secondary: the latency-bound decode config and the prefill configurations
     if kind == "decode" and not args.no_prefill_extra:
+        d1 = measure_decode(pkg, dist, 4, max(20, min(args.steps, 100)), 5, dev, with_e2e=False)
+        line["decode_b4"] = {
+            "us_per_step": round(d1["ms"] * 1e3, 2), "kernel_us": round(d1["kern_ms"] * 1e3, 2),
+            "state_gb_per_s": round(d1["value"], 1), "launch": cfg["launch"],
+            "l2": "L2 overwritten before every step (16.8 MB state traffic per step per GPU)",
+            "global_batch": 4 * dist.world}
         extra = {}
-        names = ["P1", "P2"] if dist.world == 1 else ["P2", "P3"]
-        for nm in names:
-            shard = prefill_plan(pkg, nm, dist)
+        names = [("P1", "auto"), ("P2", "auto")] if dist.world == 1 else \
+            [("P2", "heads"), ("P2_segment_scan", "segments"), ("P3", "auto")]
+        for label, force in names:
+            nm = label.split("_")[0]
+            shard = prefill_plan(pkg, nm, dist, force)
             r = measure_prefill(pkg, dist, nm, max(3, min(args.steps, 10)), 3, dev, shard=shard,
                                 with_e2e=False)
-            extra[nm] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
-                         "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
-                         "parallelism": plan_text(shard, dist.world),
-                         # the committed traffic capture is of the unsharded call
-                         "roofline": roofline("tensor", r["achieved"],
-                                              "prefill_" + nm.lower() if shard is None else "",
-                                              pk, src)}
+            extra[label] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
+                            "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
+                            "parallelism": plan_text(shard, dist.world),
+                            # the committed traffic capture is of the unsharded call
+                            "roofline": roofline("tensor", r["achieved"],
+                                                 "prefill_" + nm.lower() if shard is None else "",
+                                                 pk, src)}
         line["prefill"] = extra
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = (cpu_baseline_decode(param, state_bf16=kind == "decode_bf16state")
-                                if kind in ("decode", "decode_bf16state")
-                                else cpu_baseline_mtp(param) if kind == "mtp"
-                                else cpu_baseline_prefill(param))
+        line["cpu_baseline"] = cpu_baseline(kind, param)
     return line
 
 
 def run_reference(args, dist):
-    """The reference's CPU path (oracle port) on the host cores, same workload/metric."""
+    """The reference's CPU path on the host cores: the reference itself is Triton-only, so
+    the CPU restatement of its algorithm (the oracle port) is timed, with every host thread,
+    on the same workload, metric and config as the GPU arm, for exactly `steps` steps after
+    `warmup` untimed ones (decode and multi-token decode: whole steps of the global batch
+    up to 256 rows, each further row costing the same; prefill: a bounded sample of 1024
+    tokens per step).  Only rank 0 runs; the package (and so the CUDA library) is never
+    imported."""
     if dist.rank != 0:
         return None
+    W, _ = cpu_modules()
+    threads = host_threads()
     kind, param = WORKLOADS[args.workload]
-    steps = []
+    metric, unit = metric_of(kind)
+    cfg = workload_config(W, kind, param, dist.world, args)
     if kind in ("decode", "decode_bf16state"):
-        for _ in range(max(1, min(args.steps, 3))):
-            steps.append(cpu_baseline_decode(param, budget_s=5.0,
-                                             state_bf16=kind == "decode_bf16state"))
-        v = statistics.median(s["value"] for s in steps)
-        metric, unit = "decode state-traffic GB/s", "GB/s"
-        ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3
+        rows = min(param * dist.world, 256)
+        step, units = cpu_decode_step(rows, state_bf16=kind == "decode_bf16state")
+        per = timed_cpu(step, args.steps, args.warmup)
+        value = units / per / 1e9
+        sample = f"full decode steps of {rows} rows (oracle, fp32 torch CPU)"
     elif kind == "mtp":
-        for _ in range(max(1, min(args.steps, 3))):
-            steps.append(cpu_baseline_mtp(param, budget_s=5.0))
-        v = statistics.median(s["value"] for s in steps)
-        metric, unit = "mtp state-traffic GB/s", "GB/s"
-        ms = statistics.median(s["sec_per_step"] for s in steps) * 1e3
+        rows = min(param * dist.world, 16)
+        step, units = cpu_mtp_step(rows)
+        per = timed_cpu(step, args.steps, args.warmup)
+        value = units / per / 1e9
+        sample = f"{rows} rows x {MTP_T} tokens per step (oracle, fp32 torch CPU)"
     else:
-        for _ in range(max(1, min(args.steps, 2))):
-            steps.append(cpu_baseline_prefill(param))
-        v = statistics.median(s["value"] for s in steps)
-        metric, unit = "prefill tokens/s", "tokens/s"
-        ms = None
-    cb = dict(steps[0])
-    cb["value"] = v
-    cb.pop("sec_per_step", None)
-    return {"impl": "reference", "metric": metric, "value": round(v, 4), "unit": unit,
-            "n_gpus": dist.world, "steps": len(steps), "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp32", "data": "synthetic (seeded)",
-            "config": {"workload": args.workload, "note": "reference has no CPU path; the CPU "
-                       "restatement of its algorithm (oracle port) is timed"},
-            "cpu_baseline": cb,
-            "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0,
+        step, T, sample = cpu_prefill_step(param, 1024)
+        per = timed_cpu(step, args.steps, args.warmup)
+        value = T / per
+        sample += " per step (oracle, fp32 torch CPU)"
+    cb = {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample,
+          "definition": definition_baseline(kind, param)}
+    return {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit,
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong" if (kind == "prefill" and dist.world > 1) else "weak",
+            "vs_baseline": None, "dtype": dtype_of(kind), "data": "synthetic (seeded)",
+            "config": cfg, "cpu_baseline": cb,
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 
@@ -840,8 +941,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-extra", action="store_true")
     ap.add_argument("--prefill-plan", choices=["auto", "heads", "segments"], default="auto",
-                    help="multi-GPU split of a single prefill sequence (default: token "
-                         "segments)")
+                    help="multi-GPU split of a config with fewer sequences than GPUs "
+                         "(default: q/k-head groups, no collective; 'segments': token-segment "
+                         "scan of one sequence, one all-gather per call)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()

@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t idesc = umma_idesc_bf16(128, 128, false, false);
   const int r = 32 * warp + lane;  // this thread's token row in a tile (its TMEM lane)
   bool ok = true, mma_pending = false;
+  uint32_t mma_par = 0;  // phase of bar_mma that the pending MMA group completes
   for (int i = 0; i < mine && ok; ++i) {
     const int b = i & 1;
     const uint32_t par = (i >> 1) & 1;
@@ -152,7 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(bar_mma);
     }
     mma_pending = true;
-    if (!mbar_wait(bar_mma, i & 1, kWaitLimit)) {
+    mma_par = i & 1;
+    if (!mbar_wait(bar_mma, mma_par, kWaitLimit)) {
       if (lane == 0) atomicOr(&g_segment_device_error, kErrMmaTimeout);
       ok = false;
     }
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (!ok && tid == 0) {  // copies and MMAs still in flight land before the CTA exits
-    if (mma_pending) mbar_wait(bar_mma, 0, kWaitLimit);
+    if (mma_pending) mbar_wait(bar_mma, mma_par, kWaitLimit);
     for (int j = max(issued - 2, 0); j < issued; ++j) mbar_wait(&bar_in[j & 1], (j >> 1) & 1, kWaitLimit);
   }
   tc_fence_before();

@@ -4,10 +4,13 @@ That entry point exists for callers that cannot allocate device memory where
 they launch (allocator or memory-pool callbacks, runtimes whose device memory
 is fully pre-reserved, plugin hosts that pass only inputs and outputs): it
 uses a fixed scratch array inside the library instead of a caller workspace.
-This test calls it through the C ABI twice in a row and checks both results
-against the regular entry point (gdn_prefill_launch with a workspace), with
-the same tolerances as the other prefill tests, and checks that a request
-beyond its fixed capacity is refused without launching anything.
+These tests call it through the C ABI twice in a row and check both results
+against the CPU oracle and against the regular entry point (gdn_prefill_launch
+with a workspace), with the same tolerances as the other prefill tests; run it
+on buffers only 8 bytes past a 16-byte boundary right after a tensor-core call
+has left its contents in the scratch array (that call takes the token-serial
+kernel); and check that a request beyond its fixed capacity is refused
+without launching anything.
 
 The file name sorts last so that a run stopping at the first failure has
 already run every other test.
@@ -16,10 +19,12 @@ import pytest
 import torch
 
 from conftest import load_pkg
-from gpu_util import OUT_ATOL, STATE_REL
+from gpu_util import OUT_ATOL, STATE_REL, assert_parity, oracle_prefill
 from oracle import gdn_oracle as O
 
 pytestmark = pytest.mark.gpu
+
+LENS = [70, 5, 129, 0, 64, 200, 1]  # several sequences: the scratch order is used
 
 
 def _noalloc(pkg, d, out, ns, l2):
@@ -33,10 +38,19 @@ def _noalloc(pkg, d, out, ns, l2):
         HV, D, int(l2), torch.cuda.current_stream().cuda_stream)
 
 
-def test_noalloc_matches_workspace_entry_point_twice(cuda):
+def _shifted(t, dev):
+    """A copy of `t` whose data starts 8 bytes past a 16-byte boundary."""
+    buf = torch.empty(t.numel() + 4, dtype=t.dtype, device=dev)
+    view = buf[4:].view(t.shape)
+    view.copy_(t)
+    assert view.data_ptr() % 16 == 8
+    return view
+
+
+def test_noalloc_matches_oracle_and_workspace_entry_point_twice(cuda):
     pkg = load_pkg()
-    lens = [70, 5, 129, 0, 64, 200, 1]  # several sequences: the scratch order is used
-    inp = pkg.workloads.prefill_inputs(lens, seed=41)
+    inp = pkg.workloads.prefill_inputs(LENS, seed=41)
+    ro, rs = oracle_prefill(inp, True)
     d = {k: (v.to(cuda) if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
     ref_o, ref_s = pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
                                    d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"],
@@ -47,9 +61,31 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
         status = _noalloc(pkg, d, out, ns, True)
         assert status == 0, pkg.LIB.gdn_status_string(status)
         torch.cuda.synchronize()
+        assert_parity(out, ns, ro, rs, what="no-alloc vs oracle")
         ok, frac, mabs, _ = O.flashinfer_allclose(out.cpu(), ref_o.cpu(), OUT_ATOL, OUT_ATOL)
         assert ok, (frac, mabs)
         assert O.state_rel_err(ns.cpu(), ref_s.cpu()) <= STATE_REL
+    assert pkg.device_error() == 0
+
+
+def test_noalloc_unaligned_buffers_after_a_tensor_core_call(cuda):
+    pkg = load_pkg()
+    inp = pkg.workloads.prefill_inputs(LENS, seed=43)
+    ro, rs = oracle_prefill(inp, True)
+    d = {k: (v.to(cuda) if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    out = torch.empty(d["v"].shape, dtype=torch.bfloat16, device=cuda)
+    ns = torch.empty_like(d["state"])
+    assert _noalloc(pkg, d, out, ns, True) == 0  # aligned: the tensor-core kernel
+    torch.cuda.synchronize()
+    assert_parity(out, ns, ro, rs, what="no-alloc aligned")
+    sh = dict(d)
+    for key in ("q", "k", "v"):
+        sh[key] = _shifted(d[key], cuda)
+    out2 = _shifted(torch.full_like(out, float("nan")), cuda)
+    ns2 = torch.full_like(ns, float("nan"))
+    assert _noalloc(pkg, sh, out2, ns2, True) == 0  # 8-byte aligned: token-serial kernel
+    torch.cuda.synchronize()
+    assert_parity(out2, ns2, ro, rs, what="no-alloc unaligned")
     assert pkg.device_error() == 0
 
 
