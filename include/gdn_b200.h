@@ -79,6 +79,26 @@ int gdn_decode_launch(const void* q, const void* k, const void* v, const float* 
                       int use_qk_l2norm, void* stream);
 
 /*
+ * gdn_decode_launch for q, k, v, a, b and output whose batch rows are strided, as the
+ * reference's wrapper allows by handing every stride to its kernel
+ * (gdn_decode/solution/triton/kernel.py:255-264): slices of a fused projection, say.
+ * Each *_stride is the number of elements between consecutive batch rows of that
+ * tensor; within a row the heads stay dense (head stride 128 for q, k, v and output,
+ * 1 for a and b).  Rows of one tensor must not overlap (q/k/v/output strides >= heads *
+ * 128, a/b strides >= num_v_heads) and q/k strides must be multiples of 4 (8-byte
+ * rows); else GDN_ERR_INVALID_ARGUMENT.  Strides that keep every row 16-byte aligned
+ * (multiples of 8) keep the fastest kernels available.  state and new_state stay dense.
+ * The dense strides reproduce gdn_decode_launch exactly.
+ */
+int gdn_decode_launch_strided(const void* q, const void* k, const void* v, const float* state,
+                              const float* A_log, const void* a, const float* dt_bias,
+                              const void* b, float scale, void* output, float* new_state,
+                              int batch, int num_q_heads, int num_k_heads, int num_v_heads,
+                              int head_size, int use_qk_l2norm, long long q_stride,
+                              long long k_stride, long long v_stride, long long a_stride,
+                              long long b_stride, long long output_stride, void* stream);
+
+/*
  * Multi-token decode (speculative-decoding verification): `seq_len` tokens per batch
  * row applied in order to the row's state in a pool, as the flashinfer-bench
  * definition `_gdn_mtp_reference` does (flashinfer/trace/templates/gdn.py:379-466;
@@ -248,6 +268,30 @@ int gdn_prefill_launch_ext(int variant, const void* q, const void* k, const void
                            int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
                            int use_qk_l2norm, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/*
+ * gdn_prefill_launch_variant for q, k, v, a, b and output whose token rows are
+ * strided, as the reference's wrapper allows by handing every stride to its kernel
+ * (gdn_prefill/solution/triton/kernel.py:318-325): slices of a fused QKV projection,
+ * say.  Each *_stride is the number of elements between consecutive tokens of that
+ * tensor; within a token the heads stay dense (head stride 128 for q, k, v and output,
+ * 1 for a and b).  Rows of one tensor must not overlap (q/k/v/output strides >= heads *
+ * 128, a/b strides >= num_v_heads) and q/k strides must be multiples of 4; else
+ * GDN_ERR_INVALID_ARGUMENT.  The tensor-core kernels (GDN_PREFILL_FUSED / _SPLIT) also
+ * need q/k/v/output strides that are multiples of 8 (16-byte rows): otherwise they
+ * return GDN_ERR_UNSUPPORTED and GDN_PREFILL_AUTO runs the token-serial kernel.  The
+ * dense strides reproduce gdn_prefill_launch_variant exactly.
+ */
+int gdn_prefill_launch_strided(int variant, const void* q, const void* k, const void* v,
+                               const float* state, const float* A_log, const void* a,
+                               const float* dt_bias, const void* b, const void* cu_seqlens,
+                               int cu_seqlens_int64, float scale, void* output,
+                               float* new_state, int total_tokens, int num_seqs,
+                               int num_q_heads, int num_k_heads, int num_v_heads, int head_size,
+                               int use_qk_l2norm, long long q_stride, long long k_stride,
+                               long long v_stride, long long a_stride, long long b_stride,
+                               long long output_stride, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /*
  * Allocation-free variant of gdn_prefill_launch (no counterpart in the

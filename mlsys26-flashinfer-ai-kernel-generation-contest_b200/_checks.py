@@ -11,7 +11,10 @@ import torch
 HEAD_SIZE = 128
 
 
-def tensor(name: str, x, dtype: torch.dtype, ndim: int, device: torch.device):
+def tensor(name: str, x, dtype: torch.dtype, ndim: int, device: torch.device,
+           strided: bool = False):
+    """Type, rank and device checks.  Without `strided` the tensor must be contiguous;
+    with it any layout is accepted here (see `row_stride` / `rows_in` / `rows_out`)."""
     if not isinstance(x, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor, got {type(x).__name__}")
     if x.dtype != dtype:
@@ -20,9 +23,51 @@ def tensor(name: str, x, dtype: torch.dtype, ndim: int, device: torch.device):
         raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(x.shape)}")
     if x.device != device:
         raise ValueError(f"{name} is on {x.device}, expected {device}")
-    if not x.is_contiguous():
+    if not strided and not x.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
     return x
+
+
+def row_stride(x: torch.Tensor, align: int = 1):
+    """Elements between consecutive rows (dim 0) of `x` when the dims after the first are
+    dense (a token row of a fused projection, say), the rows do not overlap and the stride
+    is a multiple of `align`; None otherwise."""
+    inner = 1
+    for d in range(x.dim() - 1, 0, -1):
+        if x.shape[d] != 1 and x.stride(d) != inner:
+            return None
+        inner *= x.shape[d]
+    if x.shape[0] <= 1:
+        return inner
+    rs = x.stride(0)
+    return rs if (rs >= inner and rs % align == 0) else None
+
+
+def rows_in(x: torch.Tensor, align: int = 1):
+    """(tensor, row stride) for a token-indexed input: strided rows are passed to the
+    kernels as they are; any other layout is first copied into a dense tensor on the
+    device."""
+    rs = row_stride(x, align)
+    if rs is None:
+        x = x.contiguous()
+        rs = row_stride(x, align)
+    return x, rs
+
+
+def rows_out(x: torch.Tensor, align: int = 1):
+    """(target, row stride, copy_back) for a token-indexed output: strided rows are
+    written in place; for any other layout the kernels write a dense temporary that the
+    caller copies into `x` afterwards (copy_back is True)."""
+    rs = row_stride(x, align)
+    if rs is not None:
+        return x, rs, False
+    t = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    return t, row_stride(t, align), True
+
+
+def dense_or_copy(x):
+    """A contiguous tensor with x's values (x itself when it already is one)."""
+    return x if (x is None or x.is_contiguous()) else x.contiguous()
 
 
 def shape(name: str, x: torch.Tensor, expected) -> None:

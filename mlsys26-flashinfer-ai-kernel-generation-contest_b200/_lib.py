@@ -20,6 +20,7 @@ GDN_ERR_TOO_LARGE = -5
 
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
 _vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+_ll = ctypes.c_longlong
 SIGNATURES = {
     "gdn_b200_version": (_i, []),
     "gdn_status_string": (ctypes.c_char_p, [_i]),
@@ -27,6 +28,9 @@ SIGNATURES = {
                                _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_mtp_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp,
                             _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "gdn_decode_launch_strided": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
+                                       _i, _i, _i, _i, _i, _i, _ll, _ll, _ll, _ll, _ll, _ll,
+                                       _vp]),
     "gdn_decode_launch_bf16state": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
                                          _i, _i, _i, _i, _i, _i, _vp]),
     "gdn_mtp_launch_bf16state": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f, _vp,
@@ -41,6 +45,9 @@ SIGNATURES = {
     "gdn_prefill_workspace_size_variant": (_sz, [_i, _i, _i, _i, _i, _i]),
     "gdn_prefill_launch_variant": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
                                         _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "gdn_prefill_launch_strided": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f,
+                                        _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _ll, _ll, _ll, _ll,
+                                        _ll, _ll, _vp, _sz, _vp]),
     "gdn_prefill_workspace_size_ext": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i, _i]),
     "gdn_prefill_launch_ext": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _i, _f, _vp, _vp, _vp, _vp, ctypes.c_longlong, _i, _i,

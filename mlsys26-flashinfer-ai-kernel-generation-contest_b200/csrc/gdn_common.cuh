@@ -12,6 +12,17 @@ namespace gdn {
 constexpr int kHeadDim = 128;
 constexpr float kL2NormEps = 1e-6f;
 
+// Elements between consecutive rows (tokens in prefill, batch rows in decode) of the
+// token-indexed tensors; within a row the heads are dense (head stride 128 for q, k, v
+// and the output, 1 for a and b).  Dense tensors have q = HQ * 128, a = HV, ...
+struct RowStrides {
+  long long q, k, v, a, b, o;
+};
+inline RowStrides dense_rows(int HQ, int HV) {
+  return RowStrides{(long long)HQ * kHeadDim, (long long)HQ * kHeadDim, (long long)HV * kHeadDim,
+                    (long long)HV,            (long long)HV,            (long long)HV * kHeadDim};
+}
+
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 // Two packed bf16 (low half first in memory) -> two floats.

@@ -33,8 +33,8 @@ __global__ void __launch_bounds__(256)
                   const __nv_bfloat16* __restrict__ v, const ST* state,
                   const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
                   const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ b,
-                  float scale, __nv_bfloat16* __restrict__ out, ST* new_state, int HQ,
-                  int HV, int ratio) {
+                  float scale, __nv_bfloat16* __restrict__ out, ST* new_state,
+                  const RowStrides rs, int HV, int ratio) {
   constexpr int ROWS = 8 * RPW;            // state rows per CTA
   constexpr int VSPLIT = kHeadDim / ROWS;  // CTAs per (b, h)
   constexpr int NG = RPW / 4;              // 4-row groups per warp
@@ -67,14 +67,15 @@ __global__ void __launch_bounds__(256)
 
   // ---- q, k slices (the lane's 16 columns), v values, gates ----
   float kf[16], qf[16];
-  RS::load_bf16(q + ((size_t)bidx * HQ + qh) * kHeadDim, j, qf);
-  RS::load_bf16(k + ((size_t)bidx * HQ + qh) * kHeadDim, j, kf);
+  RS::load_bf16(q + (size_t)bidx * rs.q + qh * kHeadDim, j, qf);
+  RS::load_bf16(k + (size_t)bidx * rs.k + qh * kHeadDim, j, kf);
   float vv[NG];
-  const __nv_bfloat16* vp = v + (size_t)bh * kHeadDim + row0;
+  const __nv_bfloat16* vp = v + (size_t)bidx * rs.v + h * kHeadDim + row0;
 #pragma unroll
   for (int r = 0; r < NG; ++r) vv[r] = bf2f(vp[4 * r]);
-  const float g = expf(gate_log_g(__ldg(A_log + h), bf2f(a[bh]), __ldg(dt_bias + h)));
-  const float beta = sigmoid_f(bf2f(b[bh]));
+  const float g =
+      expf(gate_log_g(__ldg(A_log + h), bf2f(a[(size_t)bidx * rs.a + h]), __ldg(dt_bias + h)));
+  const float beta = sigmoid_f(bf2f(b[(size_t)bidx * rs.b + h]));
 
   if constexpr (L2NORM) {
     float ssk = 0.f, ssq = 0.f;
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(256)
 
   scale = default_scale(scale);
   ST* nsp = new_state + head_base + (size_t)row0 * kHeadDim;
-  __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
+  __nv_bfloat16* op = out + (size_t)bidx * rs.o + h * kHeadDim + row0;
 #pragma unroll
   for (int r = 0; r < NG; ++r) {
     float sk = 0.f, sq = 0.f;
@@ -124,7 +125,7 @@ template <int RPW, typename ST>
 cudaError_t launch_rpw(const void* q, const void* k, const void* v, const ST* state,
                        const float* A_log, const void* a, const float* dt_bias, const void* b,
                        float scale, void* out, ST* new_state, int batch, int HQ, int HV,
-                       bool l2norm, cudaStream_t stream) {
+                       const RowStrides& rs, bool l2norm, cudaStream_t stream) {
   constexpr int VSPLIT = kHeadDim / (8 * RPW);
   const long long ctas = (long long)batch * HV * VSPLIT;
   const dim3 grid((unsigned)ctas), block(256);
@@ -137,14 +138,14 @@ cudaError_t launch_rpw(const void* q, const void* k, const void* v, const ST* st
   auto O = static_cast<__nv_bfloat16*>(out);
   if (state != nullptr) {
     if (l2norm)
-      decode_kernel<RPW, true, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, true, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
     else
-      decode_kernel<RPW, false, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, false, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
   } else {
     if (l2norm)
-      decode_kernel<RPW, true, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, true, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
     else
-      decode_kernel<RPW, false, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, ratio);
+      decode_kernel<RPW, false, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
   }
   return cudaGetLastError();
 }
@@ -245,8 +246,8 @@ __global__ void __launch_bounds__(StreamCfg<ST>::kThreads, StreamCfg<ST>::kCtasP
                          const __nv_bfloat16* __restrict__ v, const ST* state,
                          const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
                          const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ b,
-                         float scale, __nv_bfloat16* __restrict__ out, ST* new_state, int HQ,
-                         int HV, int ratio, int heads) {
+                         float scale, __nv_bfloat16* __restrict__ out, ST* new_state,
+                         const RowStrides rs, int HV, int ratio, int heads) {
   using C = StreamCfg<ST>;
   using RS = RowSlice<ST>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -281,9 +282,9 @@ __global__ void __launch_bounds__(StreamCfg<ST>::kThreads, StreamCfg<ST>::kCtasP
         uint8_t* st = smem + (size_t)slot * C::kStage;
         sm100::mbar_arrive_expect_tx(&full[slot], C::kStateBytes + 768u);
         sm100::bulk_load(st, state + (size_t)bh * kHeadDim * kHeadDim, C::kStateBytes, &full[slot]);
-        sm100::bulk_load(st + C::kStateBytes, q + ((size_t)bidx * HQ + qh) * kHeadDim, 256u, &full[slot]);
-        sm100::bulk_load(st + C::kStateBytes + 256, k + ((size_t)bidx * HQ + qh) * kHeadDim, 256u, &full[slot]);
-        sm100::bulk_load(st + C::kStateBytes + 512, v + (size_t)bh * kHeadDim, 256u, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes, q + (size_t)bidx * rs.q + qh * kHeadDim, 256u, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes + 256, k + (size_t)bidx * rs.k + qh * kHeadDim, 256u, &full[slot]);
+        sm100::bulk_load(st + C::kStateBytes + 512, v + (size_t)bidx * rs.v + h * kHeadDim, 256u, &full[slot]);
         issued = i + 1;
       }
       if (*abort_flag) {  // let copies still in flight land before the CTA exits (bounded)
@@ -300,11 +301,11 @@ __global__ void __launch_bounds__(StreamCfg<ST>::kThreads, StreamCfg<ST>::kCtasP
   // gate inputs of the next head, loaded one head ahead
   auto load_gate_inputs = [&](int i, float& al, float& av, float& db, float& bv) {
     const int bh = (int)blockIdx.x + i * G;
-    const int h = bh % HV;
+    const int bidx = bh / HV, h = bh - bidx * HV;
     al = __ldg(A_log + h);
     db = __ldg(dt_bias + h);
-    av = bf2f(a[bh]);
-    bv = bf2f(b[bh]);
+    av = bf2f(a[(size_t)bidx * rs.a + h]);
+    bv = bf2f(b[(size_t)bidx * rs.b + h]);
   };
   float nal = 0.f, nav = 0.f, ndb = 0.f, nbv = 0.f;
   if (nmine > 0) load_gate_inputs(0, nal, nav, ndb, nbv);
@@ -349,7 +350,7 @@ __global__ void __launch_bounds__(StreamCfg<ST>::kThreads, StreamCfg<ST>::kCtasP
     for (int e = 0; e < 16; ++e) kq = fmaf(kf[e], qf[e], kq);
     kq = xor_sum8(kq);
     ST* nsp = new_state + (size_t)bh * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
-    __nv_bfloat16* op = out + (size_t)bh * kHeadDim + row0;
+    __nv_bfloat16* op = out + (size_t)(bh / HV) * rs.o + (bh % HV) * kHeadDim + row0;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       float Sr[16];
@@ -380,7 +381,7 @@ template <typename ST>
 cudaError_t launch_stream(const void* q, const void* k, const void* v, const ST* state,
                           const float* A_log, const void* a, const float* dt_bias, const void* b,
                           float scale, void* out, ST* new_state, int batch, int HQ, int HV,
-                          bool l2norm, cudaStream_t stream) {
+                          const RowStrides& rs, bool l2norm, cudaStream_t stream) {
   using C = StreamCfg<ST>;
   static int sms[64] = {};
   static bool configured[64] = {};
@@ -407,10 +408,10 @@ cudaError_t launch_stream(const void* q, const void* k, const void* v, const ST*
   auto O = static_cast<__nv_bfloat16*>(out);
   if (l2norm)
     decode_stream_kernel<true, ST><<<grid, C::kThreads, C::kSmem, stream>>>(
-        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, HV / HQ, heads);
+        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, HV / HQ, heads);
   else
     decode_stream_kernel<false, ST><<<grid, C::kThreads, C::kSmem, stream>>>(
-        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, HQ, HV, HV / HQ, heads);
+        Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, HV / HQ, heads);
   return cudaGetLastError();
 }
 }  // namespace
@@ -440,7 +441,8 @@ template <typename ST>
 int decode_entry(const void* q, const void* k, const void* v, const ST* state, const float* A_log,
                  const void* a, const float* dt_bias, const void* b, float scale, void* output,
                  ST* new_state, int batch, int num_q_heads, int num_k_heads, int num_v_heads,
-                 int head_size, int use_qk_l2norm, void* stream) {
+                 int head_size, int use_qk_l2norm, void* stream,
+                 const RowStrides* strides = nullptr) {
   if (batch < 0 || num_q_heads <= 0 || num_k_heads <= 0 || num_v_heads <= 0)
     return GDN_ERR_INVALID_ARGUMENT;
   if (head_size != kHeadDim || num_k_heads != num_q_heads || num_v_heads % num_q_heads != 0)
@@ -451,6 +453,12 @@ int decode_entry(const void* q, const void* k, const void* v, const ST* state, c
   if (misaligned(q, 8) || misaligned(k, 8) || misaligned(v, 2) || misaligned(output, 2) ||
       misaligned(new_state, 16) || (state && misaligned(state, 16)))
     return GDN_ERR_INVALID_ARGUMENT;
+  const RowStrides rs = strides ? *strides : dense_rows(num_q_heads, num_v_heads);
+  const long long qk_row = (long long)num_q_heads * kHeadDim, v_row = (long long)num_v_heads * kHeadDim;
+  // rows of one tensor never overlap; q/k rows keep their 8-byte alignment
+  if (rs.q < qk_row || rs.k < qk_row || rs.v < v_row || rs.o < v_row || rs.a < num_v_heads ||
+      rs.b < num_v_heads || rs.q % 4 != 0 || rs.k % 4 != 0)
+    return GDN_ERR_INVALID_ARGUMENT;
   const long long heads = (long long)batch * num_v_heads;
   if (heads * 4 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -459,16 +467,17 @@ int decode_entry(const void* q, const void* k, const void* v, const ST* state, c
   // Batches that fill the GPU several times over: the streaming kernel (bulk copies
   // need 16-byte aligned q, k, v rows); otherwise one-shot CTAs, bigger when there are
   // enough heads to fill 148 SMs several times over.
-  if (state != nullptr && stream_pays<ST>(heads) && !misaligned(q, 16) && !misaligned(k, 16) &&
-      !misaligned(v, 16))
+  const bool rows16 = !misaligned(q, 16) && !misaligned(k, 16) && !misaligned(v, 16) &&
+                      rs.q % 8 == 0 && rs.k % 8 == 0 && rs.v % 8 == 0;
+  if (state != nullptr && stream_pays<ST>(heads) && rows16)
     err = launch_stream<ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch,
-                            num_q_heads, num_v_heads, l2, st);
+                            num_q_heads, num_v_heads, rs, l2, st);
   else if (heads >= 4 * 148)
-    err = launch_rpw<16, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<16, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
   else if (heads >= 2 * 148)
-    err = launch_rpw<8, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<8, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
   else
-    err = launch_rpw<4, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, l2, st);
+    err = launch_rpw<4, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 }  // namespace
@@ -494,4 +503,19 @@ extern "C" int gdn_decode_launch_bf16state(const void* q, const void* k, const v
       q, k, v, static_cast<const __nv_bfloat16*>(state), A_log, a, dt_bias, b, scale, output,
       static_cast<__nv_bfloat16*>(new_state), batch, num_q_heads, num_k_heads, num_v_heads,
       head_size, use_qk_l2norm, stream);
+}
+
+extern "C" int gdn_decode_launch_strided(const void* q, const void* k, const void* v,
+                                         const float* state, const float* A_log, const void* a,
+                                         const float* dt_bias, const void* b, float scale,
+                                         void* output, float* new_state, int batch,
+                                         int num_q_heads, int num_k_heads, int num_v_heads,
+                                         int head_size, int use_qk_l2norm, long long q_stride,
+                                         long long k_stride, long long v_stride,
+                                         long long a_stride, long long b_stride,
+                                         long long output_stride, void* stream) {
+  const gdn::RowStrides rs{q_stride, k_stride, v_stride, a_stride, b_stride, output_stride};
+  return gdn::decode_entry<float>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state,
+                                  batch, num_q_heads, num_k_heads, num_v_heads, head_size,
+                                  use_qk_l2norm, stream, &rs);
 }

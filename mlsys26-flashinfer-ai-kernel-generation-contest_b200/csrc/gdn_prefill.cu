@@ -83,7 +83,7 @@ int prefill_entry(int variant, const void* q, const void* k, const void* v, cons
                   float* new_state, int total_tokens, int num_seqs, int num_q_heads,
                   int num_k_heads, int num_v_heads, int head_size, int use_qk_l2norm,
                   void* workspace, size_t workspace_bytes, void* stream,
-                  const PrefillExt& ext = PrefillExt{}) {
+                  const PrefillExt& ext = PrefillExt{}, const gdn::RowStrides* strides = nullptr) {
   using namespace gdn;
   if (variant < GDN_PREFILL_AUTO || variant > GDN_PREFILL_SPLIT) return GDN_ERR_INVALID_ARGUMENT;
   if (total_tokens < 0 || num_seqs < 0 || num_q_heads <= 0 || num_k_heads <= 0 ||
@@ -109,6 +109,14 @@ int prefill_entry(int variant, const void* q, const void* k, const void* v, cons
       (state && misaligned(state, 16)) || misaligned(cu_seqlens, cu_seqlens_int64 ? 8 : 4))
     return GDN_ERR_INVALID_ARGUMENT;
   if ((long long)num_seqs * num_v_heads * 8 > 0x7fffffffLL) return GDN_ERR_INVALID_ARGUMENT;
+  const RowStrides rs = strides ? *strides : dense_rows(num_q_heads, num_v_heads);
+  {  // token rows of one tensor never overlap; q/k rows keep their 8-byte alignment
+    const long long qk_row = (long long)num_q_heads * kHeadDim;
+    const long long v_row = (long long)num_v_heads * kHeadDim;
+    if (rs.q < qk_row || rs.k < qk_row || rs.v < v_row || rs.o < v_row ||
+        rs.a < num_v_heads || rs.b < num_v_heads || rs.q % 4 != 0 || rs.k % 4 != 0)
+      return GDN_ERR_INVALID_ARGUMENT;
+  }
   const size_t need = variant_workspace(variant, total_tokens, num_seqs, num_v_heads, need_split);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return GDN_ERR_WORKSPACE;
   if (need > 0 && misaligned(workspace, 16)) return GDN_ERR_INVALID_ARGUMENT;  // 16-byte records
@@ -117,6 +125,7 @@ int prefill_entry(int variant, const void* q, const void* k, const void* v, cons
                 b,        cu_seqlens, cu_seqlens_int64 != 0, scale, output, new_state,
                 (long long)total_tokens, num_seqs, num_q_heads, num_v_heads,
                 use_qk_l2norm != 0, workspace, workspace_bytes};
+  p.rs = rs;
   p.gates_pre = ext.gates_pre;
   p.g_alpha = ext.g_alpha;
   p.g_beta = ext.g_beta;
@@ -217,4 +226,19 @@ extern "C" int gdn_device_error(int clear) {
   const unsigned e = gdn::read_segment_device_error(clear != 0);
   if (a == ~0u || b == ~0u || d == ~0u || e == ~0u) return -1;
   return (int)(a | b | d | e);
+}
+
+extern "C" int gdn_prefill_launch_strided(
+    int variant, const void* q, const void* k, const void* v, const float* state,
+    const float* A_log, const void* a, const float* dt_bias, const void* b,
+    const void* cu_seqlens, int cu_seqlens_int64, float scale, void* output, float* new_state,
+    int total_tokens, int num_seqs, int num_q_heads, int num_k_heads, int num_v_heads,
+    int head_size, int use_qk_l2norm, long long q_stride, long long k_stride,
+    long long v_stride, long long a_stride, long long b_stride, long long output_stride,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const gdn::RowStrides rs{q_stride, k_stride, v_stride, a_stride, b_stride, output_stride};
+  return prefill_entry(variant, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                       cu_seqlens_int64, scale, output, new_state, total_tokens, num_seqs,
+                       num_q_heads, num_k_heads, num_v_heads, head_size, use_qk_l2norm, workspace,
+                       workspace_bytes, stream, PrefillExt{}, &rs);
 }

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include "gdn_common.cuh"
+
 namespace gdn {
 
 struct PrefillArgs {
@@ -40,6 +42,9 @@ struct PrefillArgs {
   const long long* ckpt_starts = nullptr;
   long long ckpt_capacity = 0;
   int ckpt_every = 0;
+  // token strides of q, k, v, a, b and the output (elements); dense when not set by the
+  // caller (the entry point fills them in)
+  RowStrides rs{};
 };
 
 // Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).
@@ -53,12 +58,14 @@ bool prefill_chunked_supported(const PrefillArgs& p);
 size_t prefill_chunked_workspace(int num_seqs);
 cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st);
 
-// TMA descriptor of a [rows][heads * 128] bf16 matrix with 64 x 64 boxes and the
-// 128-byte swizzle (false if the driver's encoder is unavailable or refuses it).
-bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows);
+// TMA descriptor of a [rows][heads * 128] bf16 matrix whose rows are `row_stride`
+// elements apart (a multiple of 8), with 64 x 64 boxes and the 128-byte swizzle (false if
+// the driver's encoder is unavailable or refuses it).
+bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows,
+                   long long row_stride);
 // Same with `box_x` (<= 64) columns per box, 128-byte swizzle or none.
-bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows, int box_x,
-                       bool swizzle128);
+bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows,
+                       long long row_stride, int box_x, bool swizzle128);
 
 // Split path: a chunk-parallel preparation kernel and a sequential state kernel
 // split over v-blocks.  Same requirements as the chunked kernel; the workspace

@@ -119,6 +119,7 @@ struct ChunkedParams {
   float* new_state;
   __nv_bfloat16* out;
   const int* order;  // longest-first sequence order (may be null: natural order)
+  long long a_rs, b_rs, o_rs;  // token strides of a, b and the output (elements)
   long long T;
   int cu64;
   int HV;
@@ -360,9 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = 0; e < 2; ++e) {
       const int t = 2 * lane + e;
       if (t < Lcc) {
-        const size_t ti = (size_t)(tc0 + t) * HV + h;
-        ga[e] = bf2f(p.a[ti]);
-        gb[e] = bf2f(p.b[ti]);
+        ga[e] = bf2f(p.a[(size_t)(tc0 + t) * p.a_rs + h]);
+        gb[e] = bf2f(p.b[(size_t)(tc0 + t) * p.b_rs + h]);
       }
     }
   };
@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     // coalesced output rows (t < Lc): 16 x 16-byte pieces per 256-byte row
     {
-      __nv_bfloat16* obase = p.out + ((size_t)t0 * HV + h) * kHeadDim;
+      __nv_bfloat16* obase = p.out + (size_t)t0 * p.o_rs + (size_t)h * kHeadDim;
       constexpr int kUnits = 64 * 16 / kThreads;  // 16-byte pieces per thread
       uint4 v4[kUnits];
 #pragma unroll
@@ -701,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k4 = 0; k4 < kUnits; ++k4) {
         const int u = tid + kThreads * k4, t = u >> 4;
         if (t < Lc)
-          *reinterpret_cast<uint4*>(obase + (size_t)t * HV * kHeadDim + 8 * (u & 15)) = v4[k4];
+          *reinterpret_cast<uint4*>(obase + (size_t)t * p.o_rs + 8 * (u & 15)) = v4[k4];
       }
     }
   }
@@ -884,13 +884,14 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       const unsigned short* rb = reinterpret_cast<const unsigned short*>(p.b);
       // unconditional loads (tokens past the end re-read the last one; compute_gates
       // masks them), so that nothing waits for the values before they are used
-      const size_t ti = (size_t)(tc0 + min(gt, Lcc - 1)) * HV + h;
-      if (p.gates_pre) {  // fp32 bits of the precomputed decay and beta
+      const size_t tok = (size_t)(tc0 + min(gt, Lcc - 1));
+      if (p.gates_pre) {  // fp32 bits of the precomputed decay and beta (dense [T, HV])
+        const size_t ti = tok * HV + h;
         ga = p.g_alpha ? __float_as_uint(p.g_alpha[ti]) : 0x3F800000u;
         gb = p.g_beta ? __float_as_uint(p.g_beta[ti]) : 0x3F800000u;
       } else {            // bf16 bits of a and b
-        ga = ra[ti];
-        gb = rb[ti];
+        ga = ra[tok * p.a_rs + h];
+        gb = rb[tok * p.b_rs + h];
       }
     };
     // log decays (inclusive cumsum), beta and gamma of chunk cc into its vector set
@@ -1395,7 +1396,7 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
       tc_fence_before();
       group_sync(kBarState, kGroup);
       {
-        __nv_bfloat16* obase = p.out + ((size_t)t0 * HV + h) * kHeadDim;
+        __nv_bfloat16* obase = p.out + (size_t)t0 * p.o_rs + (size_t)h * kHeadDim;
         uint4 v4[4];
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
@@ -1406,7 +1407,7 @@ __global__ void __launch_bounds__(pl::kThreads, 1)
         for (int k4 = 0; k4 < 4; ++k4) {
           const int unit = u + 256 * k4, t = unit >> 4;
           if (t < Lc)
-            *reinterpret_cast<uint4*>(obase + (size_t)t * HV * kHeadDim + 8 * (unit & 15)) = v4[k4];
+            *reinterpret_cast<uint4*>(obase + (size_t)t * p.o_rs + 8 * (unit & 15)) = v4[k4];
         }
       }
       group_sync(kBarState, kGroup);
@@ -1490,13 +1491,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// [rows][heads * 128] bf16 matrix, 64 x 64 boxes, 128-byte swizzle.
-bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows, int box_x,
-                       bool swizzle128) {
+// [rows][heads * 128] bf16 matrix with rows `row_stride` elements apart, 64 x 64 boxes,
+// 128-byte swizzle.
+bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long rows,
+                       long long row_stride, int box_x, bool swizzle128) {
   auto enc = tensor_map_encoder();
-  if (enc == nullptr) return false;
+  if (enc == nullptr || row_stride < (long long)heads * kHeadDim || row_stride % 8 != 0)
+    return false;
   cuuint64_t dims[2] = {(cuuint64_t)heads * kHeadDim, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)heads * kHeadDim * 2};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
   cuuint32_t box[2] = {(cuuint32_t)box_x, 64};
   cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
@@ -1506,8 +1509,9 @@ bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long ro
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows) {
-  return make_tile_map_box(m, base, heads, rows, 64, true);
+bool make_tile_map(CUtensorMap* m, const void* base, int heads, long long rows,
+                   long long row_stride) {
+  return make_tile_map_box(m, base, heads, rows, row_stride, 64, true);
 }
 
 size_t prefill_chunked_workspace(int num_seqs) {
@@ -1517,14 +1521,16 @@ size_t prefill_chunked_workspace(int num_seqs) {
 
 bool prefill_chunked_supported(const PrefillArgs& p) {
   const auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  // TMA rows and 16-byte output stores: every token row starts on a 16-byte boundary
+  const bool rows16 = p.rs.q % 8 == 0 && p.rs.k % 8 == 0 && p.rs.v % 8 == 0 && p.rs.o % 8 == 0;
   return p.T > 0 && p.T < (1LL << 31) && a16(p.q) && a16(p.k) && a16(p.v) && a16(p.out) &&
-         tensor_map_encoder() != nullptr;
+         rows16 && tensor_map_encoder() != nullptr;
 }
 
 cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
-  if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
-      !make_tile_map(&mv, p.v, p.HV, p.T))
+  if (!make_tile_map(&mq, p.q, p.HQ, p.T, p.rs.q) || !make_tile_map(&mk, p.k, p.HQ, p.T, p.rs.k) ||
+      !make_tile_map(&mv, p.v, p.HV, p.T, p.rs.v))
     return cudaErrorInvalidValue;
   int* order = nullptr;
   if (p.N > 1 && p.N <= kLptMaxSeqs && p.workspace != nullptr &&
@@ -1553,7 +1559,8 @@ cudaError_t launch_prefill_chunked(const PrefillArgs& p, cudaStream_t st) {
   }
   ChunkedParams cp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
                    p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
-                   static_cast<__nv_bfloat16*>(p.out), order, p.T, p.cu_int64 ? 1 : 0, p.HV,
+                   static_cast<__nv_bfloat16*>(p.out), order, p.rs.a, p.rs.b, p.rs.o, p.T,
+                   p.cu_int64 ? 1 : 0, p.HV,
                    p.HV / p.HQ, p.scale, p.gates_pre, p.g_alpha, p.g_beta, p.ckpt,
                    p.ckpt_starts, p.ckpt_capacity, p.ckpt_every};
   if (!p.l2norm && (p.gates_pre || p.ckpt != nullptr))

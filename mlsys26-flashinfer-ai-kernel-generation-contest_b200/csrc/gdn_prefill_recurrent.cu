@@ -35,23 +35,23 @@ struct GateSrc {
 
 __device__ __forceinline__ void load_tok(TokIn& t, const __nv_bfloat16* q, const __nv_bfloat16* k,
                                          const __nv_bfloat16* v, const GateSrc& gs,
-                                         long long tok, int HQ, int HV,
+                                         long long tok, const RowStrides& rs, int HV,
                                          int qh, int h, int row, int j) {
-  const __nv_bfloat16* qp = q + ((size_t)tok * HQ + qh) * kHeadDim + 4 * j;
-  const __nv_bfloat16* kp = k + ((size_t)tok * HQ + qh) * kHeadDim + 4 * j;
+  const __nv_bfloat16* qp = q + (size_t)tok * rs.q + qh * kHeadDim + 4 * j;
+  const __nv_bfloat16* kp = k + (size_t)tok * rs.k + qh * kHeadDim + 4 * j;
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     t.q[m] = __ldg(reinterpret_cast<const uint2*>(qp + 32 * m));
     t.k[m] = __ldg(reinterpret_cast<const uint2*>(kp + 32 * m));
   }
-  t.v = bf2f(v[((size_t)tok * HV + h) * kHeadDim + row]);
-  const size_t ti = (size_t)tok * HV + h;
-  if (gs.pre) {
+  t.v = bf2f(v[(size_t)tok * rs.v + h * kHeadDim + row]);
+  if (gs.pre) {  // precomputed gates: dense fp32 [T, HV]
+    const size_t ti = (size_t)tok * HV + h;
     t.a = gs.alpha ? __ldg(gs.alpha + ti) : 1.f;
     t.b = gs.beta ? __ldg(gs.beta + ti) : 1.f;
   } else {
-    t.a = bf2f(gs.a[ti]);
-    t.b = bf2f(gs.b[ti]);
+    t.a = bf2f(gs.a[(size_t)tok * rs.a + h]);
+    t.b = bf2f(gs.b[(size_t)tok * rs.b + h]);
   }
 }
 
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(128)
                              const float* __restrict__ dt_bias,
                              const __nv_bfloat16* __restrict__ b, const CuT* __restrict__ cu,
                              float scale, __nv_bfloat16* __restrict__ out, float* new_state,
-                             long long T, int HQ, int HV, int ratio, int seq_offset,
+                             long long T, const RowStrides rs, int HV, int ratio, int seq_offset,
                              const float* __restrict__ g_alpha, const float* __restrict__ g_beta,
                              bool gates_pre, float* __restrict__ ckpt,
                              const long long* __restrict__ ckpt_starts, long long ckpt_cap,
@@ -99,9 +99,9 @@ __global__ void __launch_bounds__(128)
   const GateSrc gs{a, b, g_alpha, g_beta, gates_pre};
 
   TokIn cur, nxt;
-  if (s1 > s0) load_tok(cur, q, k, v, gs, s0, HQ, HV, qh, h, row, j);
+  if (s1 > s0) load_tok(cur, q, k, v, gs, s0, rs, HV, qh, h, row, j);
   for (long long t = s0; t < s1; ++t) {
-    if (t + 1 < s1) load_tok(nxt, q, k, v, gs, t + 1, HQ, HV, qh, h, row, j);
+    if (t + 1 < s1) load_tok(nxt, q, k, v, gs, t + 1, rs, HV, qh, h, row, j);
     float kf[16], qf[16];
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(128)
       S[m].w = fmaf(g, S[m].w, dk * kf[4 * m + 3]);
     }
     if (j == 0)
-      out[((size_t)t * HV + h) * kHeadDim + row] =
+      out[(size_t)t * rs.o + h * kHeadDim + row] =
           __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
     if (ckpt != nullptr) {
       const long long ci = checkpoint_slot(ckpt_starts, n, t - s0 + 1, ckpt_every, ckpt_cap);
@@ -181,7 +181,7 @@ cudaError_t launch_rec_t(const PrefillArgs& p, const CuT* cu, int seq_offset, in
   auto O = static_cast<__nv_bfloat16*>(p.out);
 #define GDN_REC_LAUNCH(L2, HS)                                                              \
   prefill_recurrent_kernel<L2, HS, CuT><<<grid, block, 0, st>>>(                            \
-      Q, K, V, p.state, p.A_log, A, p.dt_bias, Bt, cu, p.scale, O, p.new_state, p.T, p.HQ,    \
+      Q, K, V, p.state, p.A_log, A, p.dt_bias, Bt, cu, p.scale, O, p.new_state, p.T, p.rs,    \
       p.HV, ratio, seq_offset, p.g_alpha, p.g_beta, p.gates_pre, p.ckpt, p.ckpt_starts,        \
       p.ckpt_capacity, p.ckpt_every)
   if (p.state) {

@@ -96,6 +96,7 @@ struct SplitParams {
   const long long* ckpt_starts;
   long long ckpt_cap;
   int ckpt_every;
+  long long a_rs = 0, b_rs = 0, o_rs = 0;  // token strides of a, b and the output (elements)
 };
 
 template <typename CuT>
@@ -242,9 +243,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
       for (int e = 0; e < 2; ++e) {
         const int t = 2 * lane + e;
         const bool valid = t < Lc;
-        const size_t ti = (size_t)(t0 + (valid ? t : 0)) * p.HV + h;
-        lg[e] = valid ? nexpA * softplus_f(bf2f(p.a[ti]) + dtb) : 0.f;
-        bb[e] = valid ? sigmoid_f(bf2f(p.b[ti])) : 0.f;
+        const size_t tok = (size_t)(t0 + (valid ? t : 0));
+        lg[e] = valid ? nexpA * softplus_f(bf2f(p.a[tok * p.a_rs + h]) + dtb) : 0.f;
+        bb[e] = valid ? sigmoid_f(bf2f(p.b[tok * p.b_rs + h])) : 0.f;
       }
     }
     float x = lg[0] + lg[1];
@@ -820,7 +821,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             w[e] = cvt_bf16x2(ct * (qs[i] + q2[i]) + scale * (pu[i] + p2[i]),
                               ct * (qs[i + 1] + q2[i + 1]) + scale * (pu[i + 1] + p2[i + 1]));
           }
-          *reinterpret_cast<uint4*>(p.out + ((size_t)(t0 + t) * HV + h) * kHeadDim + v_lo) =
+          *reinterpret_cast<uint4*>(p.out + (size_t)(t0 + t) * p.o_rs + (size_t)h * kHeadDim + v_lo) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
@@ -945,8 +946,8 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   if (lay.slots * p.HV > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
     return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv;  // V in [64 tokens][32 v] boxes, unswizzled (read by the CUDA cores)
-  if (!make_tile_map(&mq, p.q, p.HQ, p.T) || !make_tile_map(&mk, p.k, p.HQ, p.T) ||
-      !make_tile_map_box(&mv, p.v, p.HV, p.T, st::kVB, false))
+  if (!make_tile_map(&mq, p.q, p.HQ, p.T, p.rs.q) || !make_tile_map(&mk, p.k, p.HQ, p.T, p.rs.k) ||
+      !make_tile_map_box(&mv, p.v, p.HV, p.T, p.rs.v, st::kVB, false))
     return cudaErrorInvalidValue;
   uint8_t* ws = static_cast<uint8_t*>(p.workspace);
   int* order = nullptr;
@@ -973,6 +974,9 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
                  rec_bytes(p.l2norm), rec_lo_bytes(p.l2norm), p.T, p.N, p.HV, p.HV / p.HQ,
                  p.scale, p.gates_pre, p.g_alpha, p.g_beta, p.ckpt, p.ckpt_starts,
                  p.ckpt_capacity, p.ckpt_every};
+  sp.a_rs = p.rs.a;
+  sp.b_rs = p.rs.b;
+  sp.o_rs = p.rs.o;
   if (p.cu_int64)
     return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
   return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);

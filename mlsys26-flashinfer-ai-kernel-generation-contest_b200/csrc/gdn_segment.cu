@@ -370,8 +370,9 @@ extern "C" int gdn_segment_outputs_launch(const void* o_identity, const void* o_
     configured[dev] = true;
   }
   CUtensorMap m_id, m_zero;
-  if (!gdn::make_tile_map(&m_id, o_identity, num_v_heads, num_tokens) ||
-      !gdn::make_tile_map(&m_zero, o_zero, num_v_heads, num_tokens))
+  const long long row = (long long)num_v_heads * 128;
+  if (!gdn::make_tile_map(&m_id, o_identity, num_v_heads, num_tokens, row) ||
+      !gdn::make_tile_map(&m_zero, o_zero, num_v_heads, num_tokens, row))
     return GDN_ERR_UNSUPPORTED;
   // one CTA per SM: the SMs split over the v-heads, each CTA a group of token tiles
   const int ntiles = (num_tokens + kTile - 1) / kTile;

@@ -23,11 +23,18 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
     ``state`` / ``new_state`` may be fp32 (``gdn_decode_launch``) or bf16
     (``gdn_decode_launch_bf16state``: widened on load, updated in fp32, rounded on
     store; half the state traffic); both must then have the same dtype, which is taken
-    from ``state``, else from ``new_state``, else fp32."""
+    from ``state``, else from ``new_state``, else fp32.
+
+    Like the reference, which hands every stride to its kernel, q, k, v, a, b and
+    ``output`` may be views whose batch rows are strided (slices of a fused projection,
+    say): with fp32 state they go to ``gdn_decode_launch_strided`` as they are.  Other
+    layouts (and strided rows with bf16 state) are copied into dense tensors on the
+    device first, and a non-dense ``output`` / ``new_state`` is written through a dense
+    temporary."""
     dev = C.cuda_device(q)
-    C.tensor("q", q, torch.bfloat16, 4, dev)
-    C.tensor("k", k, torch.bfloat16, 4, dev)
-    C.tensor("v", v, torch.bfloat16, 4, dev)
+    C.tensor("q", q, torch.bfloat16, 4, dev, strided=True)
+    C.tensor("k", k, torch.bfloat16, 4, dev, strided=True)
+    C.tensor("v", v, torch.bfloat16, 4, dev, strided=True)
     B, T, HQ, D = q.shape
     HK = k.shape[2]
     HV = v.shape[2]
@@ -41,35 +48,62 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
     if sdt not in (torch.float32, torch.bfloat16):
         raise TypeError(f"state must be float32 or bfloat16, got {sdt}")
     if state is not None:
-        C.tensor("state", state, sdt, 4, dev)
+        C.tensor("state", state, sdt, 4, dev, strided=True)
         C.shape("state", state, (B, HV, D, D))
-    C.tensor("A_log", A_log, torch.float32, 1, dev)
+    C.tensor("A_log", A_log, torch.float32, 1, dev, strided=True)
     C.shape("A_log", A_log, (HV,))
-    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev)
+    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev, strided=True)
     C.shape("dt_bias", dt_bias, (HV,))
-    C.tensor("a", a, torch.bfloat16, 3, dev)
+    C.tensor("a", a, torch.bfloat16, 3, dev, strided=True)
     C.shape("a", a, (B, 1, HV))
-    C.tensor("b", b, torch.bfloat16, 3, dev)
+    C.tensor("b", b, torch.bfloat16, 3, dev, strided=True)
     C.shape("b", b, (B, 1, HV))
     sc = C.scale_arg(scale)
     if output is None:
         output = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev)
     else:
-        C.tensor("output", output, torch.bfloat16, 4, dev)
+        C.tensor("output", output, torch.bfloat16, 4, dev, strided=True)
         C.shape("output", output, (B, 1, HV, D))
     if new_state is None:
         new_state = torch.empty(B, HV, D, D, dtype=sdt, device=dev)
     else:
-        C.tensor("new_state", new_state, sdt, 4, dev)
+        C.tensor("new_state", new_state, sdt, 4, dev, strided=True)
         C.shape("new_state", new_state, (B, HV, D, D))
-    launch = LIB.gdn_decode_launch if sdt == torch.float32 else LIB.gdn_decode_launch_bf16state
-    status = launch(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(),
-        state.data_ptr() if state is not None else None,
-        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), sc,
-        output.data_ptr(), new_state.data_ptr(), B, HQ, HK, HV, D, int(bool(use_qk_l2norm)),
-        C.stream_handle(dev))
-    check("gdn_decode_launch" + ("" if sdt == torch.float32 else "_bf16state"), status)
+    if B == 0:
+        return output, new_state
+    state_in, A_log, dt_bias = C.dense_or_copy(state), C.dense_or_copy(A_log), \
+        C.dense_or_copy(dt_bias)
+    ns = new_state if new_state.is_contiguous() else torch.empty(
+        new_state.shape, dtype=sdt, device=dev)
+    if ns is not new_state and state is not None and state_in.data_ptr() == new_state.data_ptr():
+        state_in = state_in.clone()  # keep the in-place contract through the temporary
+    if sdt == torch.bfloat16:  # dense rows only
+        q, k, v, a, b = (C.dense_or_copy(x) for x in (q, k, v, a, b))
+    (q, qs), (k, ks) = C.rows_in(q, 4), C.rows_in(k, 4)
+    (v, vs), (a, as_), (b, bs) = C.rows_in(v), C.rows_in(a), C.rows_in(b)
+    out, os_, out_back = C.rows_out(output) if sdt == torch.float32 else (
+        (output, None, False) if output.is_contiguous() else
+        (torch.empty(output.shape, dtype=output.dtype, device=dev), None, True))
+    common = (q.data_ptr(), k.data_ptr(), v.data_ptr(),
+              state_in.data_ptr() if state_in is not None else None,
+              A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), sc,
+              out.data_ptr(), ns.data_ptr(), B, HQ, HK, HV, D, int(bool(use_qk_l2norm)))
+    dense = (HQ * D, HQ * D, HV * D, HV, HV, HV * D)
+    if sdt == torch.bfloat16:
+        name = "gdn_decode_launch_bf16state"
+        status = LIB.gdn_decode_launch_bf16state(*common, C.stream_handle(dev))
+    elif (qs, ks, vs, as_, bs, os_) == dense:
+        name = "gdn_decode_launch"
+        status = LIB.gdn_decode_launch(*common, C.stream_handle(dev))
+    else:
+        name = "gdn_decode_launch_strided"
+        status = LIB.gdn_decode_launch_strided(*common, qs, ks, vs, as_, bs, os_,
+                                               C.stream_handle(dev))
+    check(name, status)
+    if out_back:
+        output.copy_(out)
+    if ns is not new_state:
+        new_state.copy_(ns)
     return output, new_state
 
 

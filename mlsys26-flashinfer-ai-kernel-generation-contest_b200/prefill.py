@@ -91,7 +91,7 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=
         def launch(*args):
             return LIB.gdn_prefill_launch_variant(variant, *args)
     return _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
-                    output, new_state, use_qk_l2norm, kernel)
+                    output, new_state, use_qk_l2norm, kernel, KERNELS[kernel])
 
 
 def gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output=None,
@@ -100,15 +100,20 @@ def gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scal
     (``gdn_prefill_launch_recurrent``): the definition's recurrence step by step."""
     return _prefill(LIB.gdn_prefill_launch_recurrent, "gdn_prefill_launch_recurrent", q, k, v,
                     state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                    use_qk_l2norm, "recurrent")
+                    use_qk_l2norm, "recurrent", GDN_PREFILL_RECURRENT)
 
 
 def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-             new_state, use_qk_l2norm, kernel):
+             new_state, use_qk_l2norm, kernel, variant):
+    """Checks, then one launch.  Like the reference, which hands every stride to its
+    kernel, q, k, v, a, b and ``output`` may be views whose token rows are strided (slices
+    of a fused projection, say): those go to ``gdn_prefill_launch_strided`` as they are.
+    Other layouts are copied into dense tensors on the device first, and a non-dense
+    ``output`` / ``new_state`` is written through a dense temporary."""
     dev = C.cuda_device(q)
-    C.tensor("q", q, torch.bfloat16, 3, dev)
-    C.tensor("k", k, torch.bfloat16, 3, dev)
-    C.tensor("v", v, torch.bfloat16, 3, dev)
+    C.tensor("q", q, torch.bfloat16, 3, dev, strided=True)
+    C.tensor("k", k, torch.bfloat16, 3, dev, strided=True)
+    C.tensor("v", v, torch.bfloat16, 3, dev, strided=True)
     T, HQ, D = q.shape
     HK = k.shape[1]
     HV = v.shape[1]
@@ -121,46 +126,63 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
         raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
     if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
         raise ValueError("cu_seqlens must be 1-D with num_seqs + 1 entries")
-    if cu_seqlens.device != dev or not cu_seqlens.is_contiguous():
-        raise ValueError("cu_seqlens must be a contiguous tensor on the same device as q")
+    if cu_seqlens.device != dev:
+        raise ValueError("cu_seqlens must be on the same device as q")
     N = cu_seqlens.numel() - 1
     H = max(HQ, HV)
     if state is not None:
-        C.tensor("state", state, torch.float32, 4, dev)
+        C.tensor("state", state, torch.float32, 4, dev, strided=True)
         C.shape("state", state, (N, HV, D, D))
-    C.tensor("A_log", A_log, torch.float32, 1, dev)
+    C.tensor("A_log", A_log, torch.float32, 1, dev, strided=True)
     C.shape("A_log", A_log, (HV,))
-    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev)
+    C.tensor("dt_bias", dt_bias, torch.float32, 1, dev, strided=True)
     C.shape("dt_bias", dt_bias, (HV,))
-    C.tensor("a", a, torch.bfloat16, 2, dev)
+    C.tensor("a", a, torch.bfloat16, 2, dev, strided=True)
     C.shape("a", a, (T, HV))
-    C.tensor("b", b, torch.bfloat16, 2, dev)
+    C.tensor("b", b, torch.bfloat16, 2, dev, strided=True)
     C.shape("b", b, (T, HV))
     sc = C.scale_arg(scale)
     if output is None:
         output = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
     else:
-        C.tensor("output", output, torch.bfloat16, 3, dev)
+        C.tensor("output", output, torch.bfloat16, 3, dev, strided=True)
         C.shape("output", output, (T, H, D))
     if new_state is None:
         new_state = torch.empty(N, H, D, D, dtype=torch.float32, device=dev)
     else:
-        C.tensor("new_state", new_state, torch.float32, 4, dev)
+        C.tensor("new_state", new_state, torch.float32, 4, dev, strided=True)
         C.shape("new_state", new_state, (N, H, D, D))
     if N == 0:
         return output, new_state
+    cu_seqlens = C.dense_or_copy(cu_seqlens)
+    state_in, A_log, dt_bias = C.dense_or_copy(state), C.dense_or_copy(A_log), \
+        C.dense_or_copy(dt_bias)
+    ns = new_state if new_state.is_contiguous() else torch.empty(
+        new_state.shape, dtype=torch.float32, device=dev)
+    if ns is not new_state and state is not None and state_in.data_ptr() == new_state.data_ptr():
+        state_in = state_in.clone()  # keep the in-place contract through the temporary
+    (q, qs), (k, ks) = C.rows_in(q, 4), C.rows_in(k, 4)
+    (v, vs), (a, as_), (b, bs) = C.rows_in(v), C.rows_in(a), C.rows_in(b)
+    out, os_, out_back = C.rows_out(output)
     ws_n = workspace_bytes(T, N, HQ, HV, D, kernel)
     ws = _workspace(dev, ws_n) if ws_n > 0 else None
-    status = launch(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(),
-        state.data_ptr() if state is not None else None,
-        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
-        cu_seqlens.data_ptr(), int(cu_seqlens.dtype == torch.int64), sc,
-        output.data_ptr(), new_state.data_ptr(), T, N, HQ, HK, HV, D,
-        int(bool(use_qk_l2norm)),
-        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-        C.stream_handle(dev))
+    head = (q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            state_in.data_ptr() if state_in is not None else None,
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+            cu_seqlens.data_ptr(), int(cu_seqlens.dtype == torch.int64), sc,
+            out.data_ptr(), ns.data_ptr(), T, N, HQ, HK, HV, D, int(bool(use_qk_l2norm)))
+    tail = (ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            C.stream_handle(dev))
+    if (qs, ks, vs, as_, bs, os_) == (HQ * D, HQ * D, HV * D, HV, HV, H * D):
+        status = launch(*head, *tail)
+    else:
+        name = f"gdn_prefill_launch_strided({kernel})"
+        status = LIB.gdn_prefill_launch_strided(variant, *head, qs, ks, vs, as_, bs, os_, *tail)
     check(name, status)
+    if out_back:
+        output.copy_(out)
+    if ns is not new_state:
+        new_state.copy_(ns)
     return output, new_state
 
 

@@ -4,19 +4,23 @@
 
 The contest harness (reference README.md:60-110, FAQ.md:46-62, 144-168) packs a solution
 from ``config.toml`` plus the source files under ``solution/<language>/`` (or takes a
-``packed_solution.json``), builds it from source on an sm_100a machine without network,
+``solution.json``), builds it from source on an sm_100a machine without network,
 and calls the entry point named in ``config.toml`` in destination-passing style.  This
 writes, for one operator:
 
 * ``config.toml`` — ``[solution]`` name / definition / author, ``[build]`` language
-  "python" and entry point ``kernel.py::kernel``;
+  "python", entry point ``kernel.py::kernel`` and ``destination_passing_style = true``
+  (the reference's build section, gdn_prefill/config.toml:6-8, and the flag its packer
+  forwards, gdn_prefill/scripts/pack_solution.py:56-62);
 * ``solution/python/kernel.py`` — compiles the bundled CUDA sources for sm_100a with nvcc
   on first import (no prebuilt binary is shipped) and binds ``kernel`` to the
-  exact-arity DPS function (11 parameters for decode, 12 for prefill);
+  exact-arity DPS function (11 parameters for decode, 12 for prefill, 13 for multi-token
+  decode);
 * ``solution/python/gdn_b200/`` — this package's host code, CUDA sources and C ABI header;
-* ``packed_solution.json`` — the same files as a Solution document (name, definition,
-  author, description, spec {language, target_hardware, entry_point, dependencies},
-  sources [{path, content}]), following flashinfer-bench's Solution fields.
+* ``solution.json`` (the name the reference's packer writes by default) — the same files
+  as a Solution document (name, definition, author, description, spec {language,
+  target_hardware, entry_point, destination_passing_style, dependencies}, sources [{path,
+  content}]), following flashinfer-bench's Solution and BuildSpec fields.
 """
 from __future__ import annotations
 
@@ -94,7 +98,8 @@ def write(out: pathlib.Path, op: str, name: str, author: str, definition: str = 
         f'author = "{author}"\n\n'
         "[build]\n"
         'language = "python"\n'
-        'entry_point = "kernel.py::kernel"\n')
+        'entry_point = "kernel.py::kernel"\n'
+        "destination_passing_style = true\n")
     doc = {
         "name": name,
         "definition": definition,
@@ -102,10 +107,11 @@ def write(out: pathlib.Path, op: str, name: str, author: str, definition: str = 
         "description": f"{op}: hand-written sm_100a CUDA (tcgen05 / TMEM / TMA) built from "
                        "source at load time; destination-passing entry point.",
         "spec": {"language": "python", "target_hardware": ["cuda"],
-                 "entry_point": "kernel.py::kernel", "dependencies": []},
+                 "entry_point": "kernel.py::kernel", "destination_passing_style": True,
+                 "dependencies": []},
         "sources": [{"path": rel, "content": text} for rel, text in sorted(files.items())],
     }
-    (out / "packed_solution.json").write_text(json.dumps(doc, indent=2))
+    (out / "solution.json").write_text(json.dumps(doc, indent=2))
     return doc
 
 

@@ -109,3 +109,47 @@ def test_dps_entry_point_arity_matches_reference():
     assert len(inspect.signature(pkg.decode_kernel).parameters) == 11
     assert len(inspect.signature(pkg.prefill_kernel).parameters) == 12
     assert list(inspect.signature(pkg.prefill_kernel).parameters)[8] == "cu_seqlens"
+
+
+def test_strided_entry_points_refuse_overlapping_or_unaligned_rows():
+    """The strided entry points check the row strides before anything is launched: rows
+    of one tensor must not overlap and q/k rows must stay 8-byte aligned."""
+    lib = load_pkg().LIB
+    fake = 0x1000
+    dense = dict(qs=16 * 128, ks=16 * 128, vs=32 * 128, as_=32, bs=32, os=32 * 128)
+
+    def dcall(**kw):
+        s = {**dense, **kw}
+        return lib.gdn_decode_launch_strided(fake, fake, fake, None, fake, fake, fake, fake, 0.0,
+                                             fake, fake, 4, 16, 16, 32, 128, 0, s["qs"], s["ks"],
+                                             s["vs"], s["as_"], s["bs"], s["os"], None)
+
+    def pcall(**kw):
+        s = {**dense, **kw}
+        return lib.gdn_prefill_launch_strided(0, fake, fake, fake, None, fake, fake, fake, fake,
+                                              fake, 0, 0.0, fake, fake, 100, 1, 16, 16, 32, 128,
+                                              1, s["qs"], s["ks"], s["vs"], s["as_"], s["bs"],
+                                              s["os"], None, 0, None)
+
+    for call in (dcall, pcall):
+        assert call(qs=16 * 128 - 8) == -1   # q rows overlap
+        assert call(vs=31 * 128) == -1       # v rows overlap
+        assert call(os=32 * 128 - 1) == -1  # output rows overlap
+        assert call(as_=31) == -1            # a rows overlap
+        assert call(ks=16 * 128 + 2) == -1   # k rows lose their 8-byte alignment
+
+
+def test_row_stride_of_views():
+    pkg = load_pkg()
+    from importlib import import_module
+    C = import_module(pkg.__name__ + "._checks")
+    fused = torch.zeros(10, 2 * 16 * 128 + 32 * 128, dtype=torch.bfloat16)
+    q = fused[:, :16 * 128].view(10, 16, 128)
+    v = fused[:, 2 * 16 * 128:].view(10, 32, 128)
+    assert C.row_stride(q) == fused.stride(0) and C.row_stride(v) == fused.stride(0)
+    assert C.row_stride(torch.zeros(10, 16, 128)) == 16 * 128
+    assert C.row_stride(q.transpose(1, 2)) is None          # heads not dense: copied
+    x, rs = C.rows_in(q.transpose(1, 2))
+    assert x.is_contiguous() and rs == 16 * 128
+    odd = torch.zeros(10, 16 * 128 + 2, dtype=torch.bfloat16)[:, :16 * 128].view(10, 16, 128)
+    assert C.row_stride(odd, 4) is None and C.row_stride(odd) == 16 * 128 + 2

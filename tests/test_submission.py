@@ -1,4 +1,4 @@
-"""CPU: the flashinfer-bench submission writer (config.toml, solution/python, packed JSON)."""
+"""CPU: the flashinfer-bench submission writer (config.toml, solution/python, solution.json)."""
 import ast
 import importlib.util
 import json
@@ -17,6 +17,7 @@ def test_submission_tree(tmp_path, op, fn):
     doc = mod.write(tmp_path, op, "team-x", "me")
     cfg = (tmp_path / "config.toml").read_text()
     assert 'language = "python"' in cfg and 'entry_point = "kernel.py::kernel"' in cfg
+    assert "destination_passing_style = true" in cfg
     assert f'definition = "{doc["definition"]}"' in cfg
     src = tmp_path / "solution" / "python"
     tree = ast.parse((src / "kernel.py").read_text())
@@ -29,8 +30,9 @@ def test_submission_tree(tmp_path, op, fn):
         assert f"gdn_b200/csrc/{cu.name}" in paths
     assert "gdn_b200/include/gdn_b200.h" in paths and "kernel.py" in paths
     assert not any(p.endswith((".so", ".o", ".cubin", ".fatbin")) for p in paths)
-    packed = json.loads((tmp_path / "packed_solution.json").read_text())
+    packed = json.loads((tmp_path / "solution.json").read_text())
     assert packed["spec"]["entry_point"] == "kernel.py::kernel"
+    assert packed["spec"]["destination_passing_style"] is True
     assert packed["spec"]["language"] == "python" and len(packed["sources"]) == len(paths)
     # the bundled build script finds the bundled header (no repository around it)
     spec = importlib.util.spec_from_file_location("_bundled_build", src / "gdn_b200" / "build.py")

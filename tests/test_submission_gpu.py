@@ -1,38 +1,92 @@
 """GPU: a written flashinfer-bench submission builds from its bundled sources and its
-`kernel` entry point matches the oracle (decode, 11-parameter DPS form)."""
+`kernel` entry point, called with the definition's exact parameter list in
+destination-passing style, matches the oracle (decode: 11 parameters, prefill: 12,
+multi-token decode: 13)."""
 import importlib.util
 import inspect
-import os
 import sys
 
 import pytest
 import torch
 
 from conftest import load_pkg
-from gpu_util import assert_parity, oracle_decode, to
+from gpu_util import assert_parity, oracle_decode, oracle_prefill, to
+from oracle import gdn_oracle as O
 
 pytestmark = pytest.mark.gpu
 
 
-def test_decode_submission_builds_and_runs(cuda, tmp_path, monkeypatch):
+def submitted_kernel(tmp_path, monkeypatch, op):
+    """Write the submission of `op`, build it from its own sources (first import of its
+    kernel.py) and return its `kernel`."""
     pkg = load_pkg()
     mod = __import__("importlib").import_module(pkg.__name__ + ".submission")
-    mod.write(tmp_path, "gdn_decode", "t", "a")
+    mod.write(tmp_path, op, "t", "a")
     monkeypatch.setenv("GDN_B200_BUILD_DIR", str(tmp_path / "_obj"))
     src = tmp_path / "solution" / "python"
     monkeypatch.syspath_prepend(str(src))
-    spec = importlib.util.spec_from_file_location("_submitted_kernel", src / "kernel.py")
+    sys.modules.pop("gdn_b200", None)  # another op's submission may have been imported
+    spec = importlib.util.spec_from_file_location(f"_submitted_{op}", src / "kernel.py")
     km = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(km)
     assert (src / "gdn_b200" / "libgdn_b200.so").exists()
-    assert len(inspect.signature(km.kernel).parameters) == 11
+    return km.kernel
+
+
+def test_decode_submission_builds_and_runs(cuda, tmp_path, monkeypatch):
+    pkg = load_pkg()
+    kern = submitted_kernel(tmp_path, monkeypatch, "gdn_decode")
+    assert len(inspect.signature(kern).parameters) == 11
     inp = pkg.workloads.decode_inputs(3, hq=2, hv=4, seed=71)
     d = to(inp, cuda)
     out = torch.empty_like(d["v"])
     ns = torch.empty_like(d["state"])
-    o, s = km.kernel(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
-                     d["b"], d["scale"], out, ns)
+    o, s = kern(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+                d["scale"], out, ns)
     torch.cuda.synchronize()
+    assert o.data_ptr() == out.data_ptr() and s.data_ptr() == ns.data_ptr()
     ro, rs = oracle_decode(inp, False)
-    assert_parity(o, s, ro, rs, what="submission")
+    assert_parity(o, s, ro, rs, what="decode submission")
+    sys.modules.pop("gdn_b200", None)
+
+
+def test_prefill_submission_builds_and_runs(cuda, tmp_path, monkeypatch):
+    pkg = load_pkg()
+    kern = submitted_kernel(tmp_path, monkeypatch, "gdn_prefill")
+    params = list(inspect.signature(kern).parameters)
+    assert len(params) == 12 and params[8] == "cu_seqlens"
+    # raw q/k as the contest calls it; short sequences keep the state finite
+    inp = pkg.workloads.prefill_inputs([3, 40, 0, 65], seed=72)
+    d = to(inp, cuda)
+    out = torch.empty_like(d["v"])
+    ns = torch.empty_like(d["state"])
+    o, s = kern(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+                d["cu_seqlens"], d["scale"], out, ns)
+    torch.cuda.synchronize()
+    assert o.data_ptr() == out.data_ptr() and s.data_ptr() == ns.data_ptr()
+    ro, rs = oracle_prefill(inp, False)
+    assert_parity(o, s, ro, rs, what="prefill submission")
+    sys.modules.pop("gdn_b200", None)
+
+
+def test_mtp_submission_builds_and_runs(cuda, tmp_path, monkeypatch):
+    pkg = load_pkg()
+    kern = submitted_kernel(tmp_path, monkeypatch, "gdn_mtp")
+    assert len(inspect.signature(kern).parameters) == 13
+    inp = pkg.workloads.mtp_inputs(4, 3, 6, seed=73)
+    d = to(inp, cuda)
+    P, HV = d["state"].shape[:2]
+    inter = torch.zeros(P, 3, HV, 128, 128, device=cuda)
+    out = torch.empty_like(d["v"])
+    fin = d["state"].clone()
+    o, s = kern(d["q"], d["k"], d["v"], d["state"], d["state_indices"], d["A_log"], d["a"],
+                d["dt_bias"], d["b"], d["scale"], inter, out, fin)
+    torch.cuda.synchronize()
+    assert o.data_ptr() == out.data_ptr() and s.data_ptr() == fin.data_ptr()
+    ro, rs, ri = O.mtp(inp["q"], inp["k"], inp["v"], inp["state"], inp["state_indices"],
+                       inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"],
+                       intermediate=True)
+    assert_parity(o, s, ro, rs, what="mtp submission")
+    rows = inp["state_indices"].long()
+    assert O.state_rel_err(inter.cpu()[rows], ri[rows]) <= 1e-3
     sys.modules.pop("gdn_b200", None)
