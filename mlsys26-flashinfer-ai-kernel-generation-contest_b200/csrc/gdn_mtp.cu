@@ -17,6 +17,8 @@
 // the rollback buffer may be bf16 (gdn_mtp_launch_bf16state): widened on load,
 // carried in fp32 through the T tokens, rounded to nearest bf16 on every store.
 #include "gdn_common.cuh"
+#include "gdn_stream.cuh"
+#include "sm100.cuh"
 
 namespace gdn {
 namespace {
@@ -154,6 +156,255 @@ __global__ void __launch_bounds__(256)
   for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
 }
 
+// ------------------------------------------------------------ streaming variant
+// With the rollback buffer a call writes T + 1 states per slot for every one it reads, so
+// mtp_kernel (one CTA per (row, v-head), one CTA per SM at its register count) spends
+// most of each CTA's life writing and only reads the next slot once the CTA is done.
+// This persistent variant keeps one CTA per SM writing while its copy warp streams the
+// next slots' states into a ring of shared-memory stages (plain bulk copies, mbarrier
+// transaction counts), so reads run under the writes.  Each of the 8 compute warps takes
+// 16 rows of a (row, v-head) exactly as mtp_kernel<16> does (rows warp * 16 + sub + 4 r,
+// the same columns per lane), moves them from the stage into registers, releases the stage
+// at once and runs the T tokens with mtp_kernel's arithmetic in the same order (identical
+// results).  Every wait is bounded: one that runs out sets a bit of g_mtp_device_error
+// and the CTA gives up (after letting its copies in flight land).
+__device__ unsigned int g_mtp_device_error = 0;
+constexpr unsigned kMtpErrCopyTimeout = 1u;  // a stage's copy never landed
+constexpr unsigned kMtpErrFreeTimeout = 8u;  // a stage was never released
+
+template <typename ST>
+struct MtpStreamCfg {
+  static constexpr uint32_t kStateBytes = kHeadDim * kHeadDim * sizeof(ST);
+  static constexpr int kStages = sizeof(ST) == 4 ? 3 : 6;  // 192 KB of stages either way
+  static constexpr uint32_t kBars = kStages * kStateBytes;
+  static constexpr uint32_t kSmem = kBars + 128;
+  static constexpr int kThreads = 288;  // 8 compute warps + the copy warp
+};
+
+__device__ __forceinline__ bool mtp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                         unsigned code) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (sm100::mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  atomicOr(&g_mtp_device_error, code);
+  *abort_flag = 1;
+  return false;
+}
+
+// 288 threads x 224 registers fill the register file of one SM (the compute warps hold
+// 64 state values, two tokens' q/k slices and the row pointers without spilling; the
+// launch-bounds heuristic settles on 168 registers and spills)
+template <bool L2NORM, bool INTER, typename IdxT, typename ST>
+__global__ void __maxnreg__(224)
+    mtp_stream_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                      const __nv_bfloat16* __restrict__ v, const ST* pool,
+                      const IdxT* __restrict__ indices, const float* __restrict__ A_log,
+                      const __nv_bfloat16* __restrict__ a, const float* __restrict__ dt_bias,
+                      const __nv_bfloat16* __restrict__ b, float scale,
+                      __nv_bfloat16* __restrict__ out, ST* new_pool, ST* __restrict__ inter,
+                      int T, long long pool_size, int HQ, int HV, int ratio, int items) {
+  using C = MtpStreamCfg<ST>;
+  using RS = RowSlice<ST>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sb = sm100::smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBars);
+  uint64_t* empty = full + C::kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::kStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int nmine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / G + 1 : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 8);
+    }
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ============================== copy warp: the slot states, in item order
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nmine; ++i) {
+        const int stage = i % C::kStages;
+        if (i >= C::kStages && !mtp_wait(&empty[stage], ((i / C::kStages) - 1) & 1, abort_flag,
+                                         kMtpErrFreeTimeout))
+          break;
+        const int bh = (int)blockIdx.x + i * G;
+        const int bidx = bh / HV, h = bh - bidx * HV;
+        const long long slot = (long long)indices[bidx];
+        if (slot < 0 || slot >= pool_size) {  // padding row: nothing to read
+          sm100::mbar_arrive(&full[stage]);
+        } else {
+          sm100::mbar_arrive_expect_tx(&full[stage], C::kStateBytes);
+          sm100::bulk_load(smem + (size_t)stage * C::kStateBytes,
+                           pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim, C::kStateBytes,
+                           &full[stage]);
+        }
+        issued = i + 1;
+      }
+      if (*abort_flag) {  // let copies still in flight land before the CTA exits (bounded)
+        for (int i = issued - C::kStages > 0 ? issued - C::kStages : 0; i < issued; ++i)
+          sm100::mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, 1u << 20);
+      }
+    }
+    return;
+  }
+  // ============================== compute warps: 16 rows each (rows row0 + 4 r)
+  constexpr int NG = 4;
+  const int sub = lane >> 3, j = lane & 7;
+  const int row0 = warp * 16 + sub;
+  scale = default_scale(scale);
+  for (int i = 0; i < nmine; ++i) {
+    const int stage = i % C::kStages;
+    const int bh = (int)blockIdx.x + i * G;
+    const int bidx = bh / HV, h = bh - bidx * HV, qh = h / ratio;
+    const float nexpA = -expf(__ldg(A_log + h));
+    const float dtb = __ldg(dt_bias + h);
+    MtpToken cur;
+    float vv[NG];
+    mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T, HQ, HV, qh, h, j, row0, nexpA, dtb,
+                           cur, vv);
+    if (!mtp_wait(&full[stage], (i / C::kStages) & 1, abort_flag, kMtpErrCopyTimeout)) break;
+    const long long slot = (long long)indices[bidx];
+    __nv_bfloat16* op0 = out + ((size_t)bidx * T * HV + h) * kHeadDim + row0;
+    if (slot < 0 || slot >= pool_size) {  // padding row
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[stage]);
+      if (j == 0)
+        for (int t = 0; t < T; ++t)
+#pragma unroll
+          for (int r = 0; r < NG; ++r)
+            op0[(size_t)t * HV * kHeadDim + 4 * r] = __float2bfloat16_rn(0.f);
+      continue;
+    }
+    float S[NG][16];
+    const uint32_t st = sb + (uint32_t)stage * C::kStateBytes;
+#pragma unroll
+    for (int r = 0; r < NG; ++r)
+      load_row_smem<ST>(st + (uint32_t)((row0 + 4 * r) * kHeadDim * sizeof(ST)), j, S[r]);
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(&empty[stage]);  // the rows are in registers
+    for (int t = 0; t < T; ++t) {
+      MtpToken nxt;
+      float vn[NG];
+      if (t + 1 < T)
+        mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T + t + 1, HQ, HV, qh, h, j, row0,
+                               nexpA, dtb, nxt, vn);
+      if constexpr (L2NORM) {
+        float ssk = 0.f, ssq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          ssk = fmaf(cur.kf[e], cur.kf[e], ssk);
+          ssq = fmaf(cur.qf[e], cur.qf[e], ssq);
+        }
+        ssk = xor_sum8(ssk);
+        ssq = xor_sum8(ssq);
+        const float rk = rsqrtf(ssk + kL2NormEps);
+        const float rq = rsqrtf(ssq + kL2NormEps);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          cur.kf[e] *= rk;
+          cur.qf[e] *= rq;
+        }
+      }
+      float kq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) kq = fmaf(cur.kf[e], cur.qf[e], kq);
+      kq = xor_sum8(kq);
+      const float g = cur.g, beta = cur.beta;
+      __nv_bfloat16* op = op0 + (size_t)t * HV * kHeadDim;
+      ST* ip = nullptr;
+      if constexpr (INTER)
+        ip = inter + (((size_t)slot * T + t) * HV + h) * kHeadDim * kHeadDim +
+             (size_t)row0 * kHeadDim;
+#pragma unroll
+      for (int r = 0; r < NG; ++r) {
+        float sk = 0.f, sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          sk = fmaf(S[r][e], cur.kf[e], sk);
+          sq = fmaf(S[r][e], cur.qf[e], sq);
+        }
+        sk = xor_sum8(sk);
+        sq = xor_sum8(sq);
+        const float old = g * sk;
+        const float delta = beta * (vv[r] - old);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) S[r][e] = fmaf(g, S[r][e], delta * cur.kf[e]);
+        if constexpr (INTER) RS::store(ip + r * 4 * kHeadDim, j, S[r]);
+        if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
+      }
+      if (t + 1 < T) {
+        cur = nxt;
+#pragma unroll
+        for (int r = 0; r < NG; ++r) vv[r] = vn[r];
+      }
+    }
+    ST* nsp = new_pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
+#pragma unroll
+    for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
+  }
+}
+
+template <bool L2, typename IdxT, typename ST>
+cudaError_t launch_mtp_stream_t(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                const __nv_bfloat16* V, const ST* pool, const IdxT* I,
+                                const float* A_log, const __nv_bfloat16* A,
+                                const float* dt_bias, const __nv_bfloat16* Bt, float scale,
+                                __nv_bfloat16* O, ST* new_pool, ST* inter, int T,
+                                long long pool_size, int HQ, int HV, int items, int grid,
+                                cudaStream_t st) {
+  using C = MtpStreamCfg<ST>;
+  auto kern = mtp_stream_kernel<L2, true, IdxT, ST>;
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  kern<<<grid, C::kThreads, C::kSmem, st>>>(Q, K, V, pool, I, A_log, A, dt_bias, Bt, scale, O,
+                                             new_pool, inter, T, pool_size, HQ, HV, HV / HQ,
+                                             items);
+  return cudaGetLastError();
+}
+
+// Streaming variant for calls with the rollback buffer (see mtp_stream_kernel).
+template <typename IdxT, typename ST>
+cudaError_t launch_mtp_stream(const void* q, const void* k, const void* v, const ST* pool,
+                              const void* indices, const float* A_log, const void* a,
+                              const float* dt_bias, const void* b, float scale, void* out,
+                              ST* new_pool, ST* inter, int batch, int T, long long pool_size,
+                              int HQ, int HV, bool l2norm, cudaStream_t st) {
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (sms[dev] == 0 &&
+      cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cudaErrorInvalidValue;
+  const int items = batch * HV;
+  const int grid = items < sms[dev] ? items : sms[dev];
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  auto A = static_cast<const __nv_bfloat16*>(a);
+  auto Bt = static_cast<const __nv_bfloat16*>(b);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  auto I = static_cast<const IdxT*>(indices);
+  return l2norm ? launch_mtp_stream_t<true, IdxT, ST>(Q, K, V, pool, I, A_log, A, dt_bias, Bt,
+                                                     scale, O, new_pool, inter, T, pool_size,
+                                                     HQ, HV, items, grid, st)
+                : launch_mtp_stream_t<false, IdxT, ST>(Q, K, V, pool, I, A_log, A, dt_bias, Bt,
+                                                      scale, O, new_pool, inter, T, pool_size,
+                                                      HQ, HV, items, grid, st);
+}
+
 template <int RPW, typename IdxT, typename ST>
 cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const ST* pool,
                            const void* indices, const float* A_log, const void* a,
@@ -189,8 +440,13 @@ cudaError_t launch_mtp(const void* q, const void* k, const void* v, const ST* po
                        const float* dt_bias, const void* b, float scale, void* out,
                        ST* new_pool, ST* inter, int batch, int T, long long pool_size,
                        int HQ, int HV, bool l2norm, cudaStream_t st) {
-  // same CTA sizing as the decode kernel: enough CTAs to fill 148 SMs several times
+  // same CTA sizing as the decode kernel: enough CTAs to fill 148 SMs several times;
+  // with the rollback buffer (T + 1 state writes per read) and that many heads, the
+  // streaming variant, whose reads run under the writes
   const long long heads = (long long)batch * HV;
+  if (inter != nullptr && T >= 2 && heads >= 4 * 148)
+    return launch_mtp_stream<IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+                                       new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
   if (heads >= 4 * 148)
     return launch_mtp_rpw<16, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
                                     new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
@@ -277,3 +533,16 @@ extern "C" int gdn_mtp_launch_bf16state(const void* q, const void* k, const void
                              batch, seq_len, pool_size, num_q_heads, num_k_heads, num_v_heads,
                              head_size, use_qk_l2norm, stream);
 }
+
+namespace gdn {
+// Device error bits of the streaming multi-token decode kernel (bounded waits that ran out).
+unsigned read_mtp_device_error(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_mtp_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+  if (clear && v != 0) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_mtp_device_error, &zero, sizeof(zero)) != cudaSuccess) return ~0u;
+  }
+  return v;
+}
+}  // namespace gdn

@@ -114,3 +114,36 @@ def test_dps_kernel_arity_and_errors(cuda):
     ro, rs, _ = oracle_mtp({k_: (v_.cpu() if isinstance(v_, torch.Tensor) else v_)
                             for k_, v_ in inp.items()}, False)
     assert_parity(o, s, ro, rs, what="dps")
+
+
+@pytest.mark.parametrize("state_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("inplace", [True, False])
+def test_streaming_rollback_path_matches_one_shot_path_bitwise(cuda, state_dtype, inplace):
+    """With the rollback buffer and enough (row, v-head) pairs the call runs the streaming
+    kernel (states read into shared memory while the previous ones are written); without
+    the buffer it runs the one-CTA-per-pair kernel.  Both apply the same arithmetic: the
+    outputs and final pools agree bit for bit, padding rows included, and the buffer's
+    last token holds the final state."""
+    pkg = load_pkg()
+    B, T, P = 40, 3, 48
+    idx = list(range(3, 43))
+    idx[5], idx[17] = -1, P + 2  # padding rows
+    inp = to(pkg.workloads.mtp_inputs(B, T, P, seed=35, indices=idx), cuda)
+    inp["state"] = inp["state"].to(state_dtype)
+    args = lambda pool: (inp["q"], inp["k"], inp["v"], pool, inp["state_indices"],  # noqa: E731
+                         inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
+    pool_a = inp["state"].clone()
+    o_a, s_a = pkg.gdn_mtp(*args(pool_a), use_qk_l2norm=True)            # one-shot kernel
+    pool_b = inp["state"].clone()
+    buf = torch.zeros((P, T) + tuple(pool_b.shape[1:]), dtype=state_dtype, device=cuda)
+    fin = None if inplace else torch.full_like(pool_b, float("nan"))
+    o_b, s_b = pkg.gdn_mtp(*args(pool_b), None, fin, buf, use_qk_l2norm=True)  # streaming
+    torch.cuda.synchronize()
+    assert pkg.device_error() == 0
+    assert torch.equal(o_a, o_b) and torch.equal(s_a, s_b)
+    rows = torch.tensor([i for i in idx if 0 <= i < P], device=cuda)
+    assert torch.equal(buf[rows, T - 1], s_b[rows])
+    assert o_b[5].abs().max().item() == 0.0 and o_b[17].abs().max().item() == 0.0
+    ro, rs, _ = oracle_mtp({k_: (v_.cpu() if isinstance(v_, torch.Tensor) else v_)
+                            for k_, v_ in inp.items()}, True)
+    assert_parity(o_b, s_b.float(), ro, rs.float(), what=f"streaming {state_dtype}")
