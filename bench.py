@@ -692,6 +692,24 @@ def l2_flusher(units, dev):
     return lambda: buf.fill_(1.0)
 
 
+def copy_reference(units, dev, reps=20):
+    """GB/s of a device-to-device copy that moves the same bytes as one step (units / 2
+    read, units / 2 written; two buffer pairs alternate so the source is not in L2): the
+    HBM rate a plain copy reaches at this size, beside the roofline's fixed denominator."""
+    n = max(1, units // 2 // 4)
+    bufs = [(torch.ones(n, device=dev), torch.empty(n, device=dev)) for _ in range(2)]
+    for i in range(4):
+        bufs[i & 1][1].copy_(bufs[i & 1][0])
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(reps):
+        bufs[i & 1][1].copy_(bufs[i & 1][0])
+    t1.record()
+    torch.cuda.synchronize()
+    return 2 * n * 4 * reps / (t0.elapsed_time(t1) * 1e-3) / 1e9
+
+
 def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf16=False,
                    graphs=True):
     w = DecodeWork(pkg, batch, dev, seed=dist.rank, state_bf16=state_bf16)
@@ -856,6 +874,10 @@ def run_ours(args, dist):
         "e2e": r["e2e"], "gpu_launches": r["launches"], "clocks": r["clocks"],
         "kernel_ms": round(r["kern_ms"], 5),
     })
+    if bound == "hbm":  # context: what a plain copy of the step's bytes reaches at this size
+        cr = copy_reference(r["units"], dev)
+        line["roofline"]["copy_same_bytes_gbs"] = round(cr, 1)
+        line["roofline"]["frac_of_copy_same_bytes"] = round(r["achieved"] / cr, 4)
     if bound == "tensor":
         line["tflops"] = round(r["tflops"], 2)
     # secondary: the latency-bound decode config and the prefill configurations
