@@ -160,14 +160,16 @@ __global__ void __launch_bounds__(256)
 // With the rollback buffer a call writes T + 1 states per slot for every one it reads, so
 // mtp_kernel (one CTA per (row, v-head), one CTA per SM at its register count) spends
 // most of each CTA's life writing and only reads the next slot once the CTA is done.
-// This persistent variant keeps one CTA per SM writing while its copy warp streams the
-// next slots' states into a ring of shared-memory stages (plain bulk copies, mbarrier
-// transaction counts), so reads run under the writes.  Each of the 8 compute warps takes
-// 16 rows of a (row, v-head) exactly as mtp_kernel<16> does (rows warp * 16 + sub + 4 r,
-// the same columns per lane), moves them from the stage into registers, releases the stage
-// at once and runs the T tokens with mtp_kernel's arithmetic in the same order (identical
-// results).  Every wait is bounded: one that runs out sets a bit of g_mtp_device_error
-// and the CTA gives up (after letting its copies in flight land).
+// This persistent variant keeps one CTA per SM writing while the states of its next
+// (row, v-head) items stream into a ring of shared-memory stages (plain bulk copies,
+// mbarrier transaction counts), so reads run under the writes.  Each of the 8 warps takes
+// 16 rows of an item exactly as mtp_kernel<16> does (rows warp * 16 + sub + 4 r, the same
+// columns per lane), moves them from the stage into registers, releases the stage at once
+// and runs the T tokens with mtp_kernel's arithmetic in the same order (identical
+// results).  Lane 0 of warp 0 refills a stage once all warps have released it (no
+// separate copy warp: a ninth warp would cap the registers at 168 and make the compute
+// warps spill).  Every wait is bounded: one that runs out sets a bit of
+// g_mtp_device_error and the CTA gives up (after letting its copies in flight land).
 __device__ unsigned int g_mtp_device_error = 0;
 constexpr unsigned kMtpErrCopyTimeout = 1u;  // a stage's copy never landed
 constexpr unsigned kMtpErrFreeTimeout = 8u;  // a stage was never released
@@ -178,7 +180,7 @@ struct MtpStreamCfg {
   static constexpr int kStages = sizeof(ST) == 4 ? 3 : 6;  // 192 KB of stages either way
   static constexpr uint32_t kBars = kStages * kStateBytes;
   static constexpr uint32_t kSmem = kBars + 128;
-  static constexpr int kThreads = 288;  // 8 compute warps + the copy warp
+  static constexpr int kThreads = 256;
 };
 
 __device__ __forceinline__ bool mtp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -192,11 +194,8 @@ __device__ __forceinline__ bool mtp_wait(uint64_t* bar, uint32_t parity, volatil
   return false;
 }
 
-// 288 threads x 224 registers fill the register file of one SM (the compute warps hold
-// 64 state values, two tokens' q/k slices and the row pointers without spilling; the
-// launch-bounds heuristic settles on 168 registers and spills)
 template <bool L2NORM, bool INTER, typename IdxT, typename ST>
-__global__ void __maxnreg__(224)
+__global__ void __launch_bounds__(MtpStreamCfg<ST>::kThreads, 1)
     mtp_stream_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                       const __nv_bfloat16* __restrict__ v, const ST* pool,
                       const IdxT* __restrict__ indices, const float* __restrict__ A_log,
@@ -214,46 +213,34 @@ __global__ void __maxnreg__(224)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
   const int nmine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / G + 1 : 0;
-  if (threadIdx.x == 0) {
+  const bool issuer = threadIdx.x == 0;
+  // the state of item i into stage i % kStages (a padding row has nothing to read)
+  auto issue = [&](int i) {
+    const int stage = i % C::kStages;
+    const int bh = (int)blockIdx.x + i * G;
+    const int bidx = bh / HV, h = bh - bidx * HV;
+    const long long slot = (long long)indices[bidx];
+    if (slot < 0 || slot >= pool_size) {
+      sm100::mbar_arrive(&full[stage]);
+    } else {
+      sm100::mbar_arrive_expect_tx(&full[stage], C::kStateBytes);
+      sm100::bulk_load(smem + (size_t)stage * C::kStateBytes,
+                       pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim, C::kStateBytes,
+                       &full[stage]);
+    }
+  };
+  int issued = 0;  // items whose copies were issued (thread 0)
+  if (issuer) {
     for (int s = 0; s < C::kStages; ++s) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 8);
     }
     *abort_flag = 0;
     sm100::fence_mbar_init();
+    for (; issued < C::kStages && issued < nmine; ++issued) issue(issued);
   }
   __syncthreads();
 
-  if (warp == 8) {
-    // ============================== copy warp: the slot states, in item order
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nmine; ++i) {
-        const int stage = i % C::kStages;
-        if (i >= C::kStages && !mtp_wait(&empty[stage], ((i / C::kStages) - 1) & 1, abort_flag,
-                                         kMtpErrFreeTimeout))
-          break;
-        const int bh = (int)blockIdx.x + i * G;
-        const int bidx = bh / HV, h = bh - bidx * HV;
-        const long long slot = (long long)indices[bidx];
-        if (slot < 0 || slot >= pool_size) {  // padding row: nothing to read
-          sm100::mbar_arrive(&full[stage]);
-        } else {
-          sm100::mbar_arrive_expect_tx(&full[stage], C::kStateBytes);
-          sm100::bulk_load(smem + (size_t)stage * C::kStateBytes,
-                           pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim, C::kStateBytes,
-                           &full[stage]);
-        }
-        issued = i + 1;
-      }
-      if (*abort_flag) {  // let copies still in flight land before the CTA exits (bounded)
-        for (int i = issued - C::kStages > 0 ? issued - C::kStages : 0; i < issued; ++i)
-          sm100::mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, 1u << 20);
-      }
-    }
-    return;
-  }
-  // ============================== compute warps: 16 rows each (rows row0 + 4 r)
   constexpr int NG = 4;
   const int sub = lane >> 3, j = lane & 7;
   const int row0 = warp * 16 + sub;
@@ -270,10 +257,22 @@ __global__ void __maxnreg__(224)
                            cur, vv);
     if (!mtp_wait(&full[stage], (i / C::kStages) & 1, abort_flag, kMtpErrCopyTimeout)) break;
     const long long slot = (long long)indices[bidx];
+    const bool pad = slot < 0 || slot >= pool_size;
+    float S[NG][16];
+    if (!pad) {
+      const uint32_t st = sb + (uint32_t)stage * C::kStateBytes;
+#pragma unroll
+      for (int r = 0; r < NG; ++r)
+        load_row_smem<ST>(st + (uint32_t)((row0 + 4 * r) * kHeadDim * sizeof(ST)), j, S[r]);
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(&empty[stage]);  // this warp is done with the stage
+    if (issuer && issued < nmine) {  // refill it with item i + kStages once every warp is
+      if (!mtp_wait(&empty[stage], (i / C::kStages) & 1, abort_flag, kMtpErrFreeTimeout)) break;
+      issue(issued++);
+    }
     __nv_bfloat16* op0 = out + ((size_t)bidx * T * HV + h) * kHeadDim + row0;
-    if (slot < 0 || slot >= pool_size) {  // padding row
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&empty[stage]);
+    if (pad) {
       if (j == 0)
         for (int t = 0; t < T; ++t)
 #pragma unroll
@@ -281,13 +280,6 @@ __global__ void __maxnreg__(224)
             op0[(size_t)t * HV * kHeadDim + 4 * r] = __float2bfloat16_rn(0.f);
       continue;
     }
-    float S[NG][16];
-    const uint32_t st = sb + (uint32_t)stage * C::kStateBytes;
-#pragma unroll
-    for (int r = 0; r < NG; ++r)
-      load_row_smem<ST>(st + (uint32_t)((row0 + 4 * r) * kHeadDim * sizeof(ST)), j, S[r]);
-    __syncwarp();
-    if (lane == 0) sm100::mbar_arrive(&empty[stage]);  // the rows are in registers
     for (int t = 0; t < T; ++t) {
       MtpToken nxt;
       float vn[NG];
@@ -347,6 +339,10 @@ __global__ void __maxnreg__(224)
     ST* nsp = new_pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
 #pragma unroll
     for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
+  }
+  if (issuer && *abort_flag) {  // let copies still in flight land before the CTA exits
+    for (int i = issued - C::kStages > 0 ? issued - C::kStages : 0; i < issued; ++i)
+      sm100::mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, 1u << 20);
   }
 }
 
