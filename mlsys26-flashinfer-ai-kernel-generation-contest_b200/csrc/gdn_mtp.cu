@@ -157,30 +157,36 @@ __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------ streaming variant
-// With the rollback buffer a call writes T + 1 states per slot for every one it reads, so
-// mtp_kernel (one CTA per (row, v-head), one CTA per SM at its register count) spends
-// most of each CTA's life writing and only reads the next slot once the CTA is done.
-// This persistent variant keeps one CTA per SM writing while the states of its next
-// (row, v-head) items stream into a ring of shared-memory stages (plain bulk copies,
-// mbarrier transaction counts), so reads run under the writes.  Each of the 8 warps takes
-// 16 rows of an item exactly as mtp_kernel<16> does (rows warp * 16 + sub + 4 r, the same
-// columns per lane), moves them from the stage into registers, releases the stage at once
-// and runs the T tokens with mtp_kernel's arithmetic in the same order (identical
-// results).  Lane 0 of warp 0 refills a stage once all warps have released it (no
-// separate copy warp: a ninth warp would cap the registers at 168 and make the compute
-// warps spill).  Every wait is bounded: one that runs out sets a bit of
-// g_mtp_device_error and the CTA gives up (after letting its copies in flight land).
+// With the rollback buffer a call writes T + 1 states per slot for every one it reads.
+// mtp_kernel (one CTA per (row, v-head)) then stalls on every token: the next token's q,
+// k, v and gates come from global memory while the token's own work is only a few hundred
+// cycles, so each SM issues its stores in bursts and HBM idles between them.  This
+// persistent variant (one CTA per SM) streams, a few items ahead, each item's slot state
+// and the q, k, v rows of all its T tokens into a ring of shared-memory stages (plain bulk
+// copies, mbarrier transaction counts); the gates of all T tokens are computed once per
+// item, one token per lane.  The token loop then touches global memory only to store.
+// Each of the 8 warps takes 16 rows of an item exactly as mtp_kernel<16> does (rows
+// warp * 16 + sub + 4 r, the same columns per lane) and runs the T tokens with
+// mtp_kernel's arithmetic in the same order (identical results).  Lane 0 of warp 0
+// refills a stage once every warp has finished with it (a ninth copy warp would cap the
+// registers at 168 and make the compute warps spill).  Every wait is bounded: one that
+// runs out sets a bit of g_mtp_device_error and the CTA gives up (after letting its
+// copies in flight land).
 __device__ unsigned int g_mtp_device_error = 0;
 constexpr unsigned kMtpErrCopyTimeout = 1u;  // a stage's copy never landed
 constexpr unsigned kMtpErrFreeTimeout = 8u;  // a stage was never released
+constexpr int kMtpStreamMaxT = 8;           // tokens whose q, k, v rows fit a stage
 
 template <typename ST>
 struct MtpStreamCfg {
   static constexpr uint32_t kStateBytes = kHeadDim * kHeadDim * sizeof(ST);
-  static constexpr int kStages = sizeof(ST) == 4 ? 3 : 6;  // 192 KB of stages either way
-  static constexpr uint32_t kBars = kStages * kStateBytes;
+  static constexpr uint32_t kTokBytes = 3 * kHeadDim * 2;  // q | k | v rows, bf16
+  static constexpr uint32_t kStage = kStateBytes + kMtpStreamMaxT * kTokBytes;
+  static constexpr int kStages = sizeof(ST) == 4 ? 3 : 5;  // 210 / 190 KB
+  static constexpr uint32_t kBars = kStages * kStage;
   static constexpr uint32_t kSmem = kBars + 128;
   static constexpr int kThreads = 256;
+  static_assert(kSmem <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ bool mtp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -214,19 +220,27 @@ __global__ void __launch_bounds__(MtpStreamCfg<ST>::kThreads, 1)
   const int G = gridDim.x;
   const int nmine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / G + 1 : 0;
   const bool issuer = threadIdx.x == 0;
-  // the state of item i into stage i % kStages (a padding row has nothing to read)
+  // item i -> stage i % kStages: its slot state (state | q_0 k_0 v_0 | q_1 k_1 v_1 | ..);
+  // a padding row has nothing to read
   auto issue = [&](int i) {
     const int stage = i % C::kStages;
     const int bh = (int)blockIdx.x + i * G;
-    const int bidx = bh / HV, h = bh - bidx * HV;
+    const int bidx = bh / HV, h = bh - bidx * HV, qh = h / ratio;
     const long long slot = (long long)indices[bidx];
     if (slot < 0 || slot >= pool_size) {
       sm100::mbar_arrive(&full[stage]);
-    } else {
-      sm100::mbar_arrive_expect_tx(&full[stage], C::kStateBytes);
-      sm100::bulk_load(smem + (size_t)stage * C::kStateBytes,
-                       pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim, C::kStateBytes,
-                       &full[stage]);
+      return;
+    }
+    uint8_t* dst = smem + (size_t)stage * C::kStage;
+    sm100::mbar_arrive_expect_tx(&full[stage], C::kStateBytes + (uint32_t)T * C::kTokBytes);
+    sm100::bulk_load(dst, pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim, C::kStateBytes,
+                     &full[stage]);
+    for (int t = 0; t < T; ++t) {
+      const size_t bt = (size_t)bidx * T + t;
+      uint8_t* tok = dst + C::kStateBytes + (size_t)t * C::kTokBytes;
+      sm100::bulk_load(tok, q + (bt * HQ + qh) * kHeadDim, 256u, &full[stage]);
+      sm100::bulk_load(tok + 256, k + (bt * HQ + qh) * kHeadDim, 256u, &full[stage]);
+      sm100::bulk_load(tok + 512, v + (bt * HV + h) * kHeadDim, 256u, &full[stage]);
     }
   };
   int issued = 0;  // items whose copies were issued (thread 0)
@@ -248,22 +262,90 @@ __global__ void __launch_bounds__(MtpStreamCfg<ST>::kThreads, 1)
   for (int i = 0; i < nmine; ++i) {
     const int stage = i % C::kStages;
     const int bh = (int)blockIdx.x + i * G;
-    const int bidx = bh / HV, h = bh - bidx * HV, qh = h / ratio;
-    const float nexpA = -expf(__ldg(A_log + h));
-    const float dtb = __ldg(dt_bias + h);
-    MtpToken cur;
-    float vv[NG];
-    mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T, HQ, HV, qh, h, j, row0, nexpA, dtb,
-                           cur, vv);
+    const int bidx = bh / HV, h = bh - bidx * HV;
+    // gates of token `lane` (lanes < T), the same expression as mtp_load_token
+    float gl = 0.f, bl = 0.f;
+    if (lane < T) {
+      const size_t ti = ((size_t)bidx * T + lane) * HV + h;
+      gl = expf(-expf(__ldg(A_log + h)) * softplus_f(bf2f(a[ti]) + __ldg(dt_bias + h)));
+      bl = sigmoid_f(bf2f(b[ti]));
+    }
     if (!mtp_wait(&full[stage], (i / C::kStages) & 1, abort_flag, kMtpErrCopyTimeout)) break;
     const long long slot = (long long)indices[bidx];
-    const bool pad = slot < 0 || slot >= pool_size;
-    float S[NG][16];
-    if (!pad) {
-      const uint32_t st = sb + (uint32_t)stage * C::kStateBytes;
+    __nv_bfloat16* op0 = out + ((size_t)bidx * T * HV + h) * kHeadDim + row0;
+    if (slot >= 0 && slot < pool_size) {
+      const uint32_t st = sb + (uint32_t)stage * C::kStage;
+      float S[NG][16];
 #pragma unroll
       for (int r = 0; r < NG; ++r)
         load_row_smem<ST>(st + (uint32_t)((row0 + 4 * r) * kHeadDim * sizeof(ST)), j, S[r]);
+      for (int t = 0; t < T; ++t) {
+        const uint32_t tok = st + C::kStateBytes + (uint32_t)t * C::kTokBytes;
+        float kf[16], qf[16], vv[NG];
+        load_vec_smem<ST>(tok, j, qf);
+        load_vec_smem<ST>(tok + 256u, j, kf);
+#pragma unroll
+        for (int r = 0; r < NG; ++r) {
+          uint16_t bits;
+          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits)
+                       : "r"(tok + 512u + 2u * (uint32_t)(row0 + 4 * r)));
+          vv[r] = __uint_as_float((uint32_t)bits << 16);
+        }
+        const float g = __shfl_sync(0xffffffffu, gl, t);
+        const float beta = __shfl_sync(0xffffffffu, bl, t);
+        if constexpr (L2NORM) {
+          float ssk = 0.f, ssq = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            ssk = fmaf(kf[e], kf[e], ssk);
+            ssq = fmaf(qf[e], qf[e], ssq);
+          }
+          ssk = xor_sum8(ssk);
+          ssq = xor_sum8(ssq);
+          const float rk = rsqrtf(ssk + kL2NormEps);
+          const float rq = rsqrtf(ssq + kL2NormEps);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            kf[e] *= rk;
+            qf[e] *= rq;
+          }
+        }
+        float kq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) kq = fmaf(kf[e], qf[e], kq);
+        kq = xor_sum8(kq);
+        __nv_bfloat16* op = op0 + (size_t)t * HV * kHeadDim;
+        ST* ip = nullptr;
+        if constexpr (INTER)
+          ip = inter + (((size_t)slot * T + t) * HV + h) * kHeadDim * kHeadDim +
+               (size_t)row0 * kHeadDim;
+#pragma unroll
+        for (int r = 0; r < NG; ++r) {
+          float sk = 0.f, sq = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            sk = fmaf(S[r][e], kf[e], sk);
+            sq = fmaf(S[r][e], qf[e], sq);
+          }
+          sk = xor_sum8(sk);
+          sq = xor_sum8(sq);
+          const float old = g * sk;
+          const float delta = beta * (vv[r] - old);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) S[r][e] = fmaf(g, S[r][e], delta * kf[e]);
+          if constexpr (INTER) RS::store(ip + r * 4 * kHeadDim, j, S[r]);
+          if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
+        }
+      }
+      ST* nsp =
+          new_pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
+#pragma unroll
+      for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
+    } else if (j == 0) {  // padding row: zero outputs, no state
+      for (int t = 0; t < T; ++t)
+#pragma unroll
+        for (int r = 0; r < NG; ++r)
+          op0[(size_t)t * HV * kHeadDim + 4 * r] = __float2bfloat16_rn(0.f);
     }
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(&empty[stage]);  // this warp is done with the stage
@@ -271,74 +353,6 @@ __global__ void __launch_bounds__(MtpStreamCfg<ST>::kThreads, 1)
       if (!mtp_wait(&empty[stage], (i / C::kStages) & 1, abort_flag, kMtpErrFreeTimeout)) break;
       issue(issued++);
     }
-    __nv_bfloat16* op0 = out + ((size_t)bidx * T * HV + h) * kHeadDim + row0;
-    if (pad) {
-      if (j == 0)
-        for (int t = 0; t < T; ++t)
-#pragma unroll
-          for (int r = 0; r < NG; ++r)
-            op0[(size_t)t * HV * kHeadDim + 4 * r] = __float2bfloat16_rn(0.f);
-      continue;
-    }
-    for (int t = 0; t < T; ++t) {
-      MtpToken nxt;
-      float vn[NG];
-      if (t + 1 < T)
-        mtp_load_token<NG, ST>(q, k, v, a, b, (size_t)bidx * T + t + 1, HQ, HV, qh, h, j, row0,
-                               nexpA, dtb, nxt, vn);
-      if constexpr (L2NORM) {
-        float ssk = 0.f, ssq = 0.f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          ssk = fmaf(cur.kf[e], cur.kf[e], ssk);
-          ssq = fmaf(cur.qf[e], cur.qf[e], ssq);
-        }
-        ssk = xor_sum8(ssk);
-        ssq = xor_sum8(ssq);
-        const float rk = rsqrtf(ssk + kL2NormEps);
-        const float rq = rsqrtf(ssq + kL2NormEps);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          cur.kf[e] *= rk;
-          cur.qf[e] *= rq;
-        }
-      }
-      float kq = 0.f;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) kq = fmaf(cur.kf[e], cur.qf[e], kq);
-      kq = xor_sum8(kq);
-      const float g = cur.g, beta = cur.beta;
-      __nv_bfloat16* op = op0 + (size_t)t * HV * kHeadDim;
-      ST* ip = nullptr;
-      if constexpr (INTER)
-        ip = inter + (((size_t)slot * T + t) * HV + h) * kHeadDim * kHeadDim +
-             (size_t)row0 * kHeadDim;
-#pragma unroll
-      for (int r = 0; r < NG; ++r) {
-        float sk = 0.f, sq = 0.f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          sk = fmaf(S[r][e], cur.kf[e], sk);
-          sq = fmaf(S[r][e], cur.qf[e], sq);
-        }
-        sk = xor_sum8(sk);
-        sq = xor_sum8(sq);
-        const float old = g * sk;
-        const float delta = beta * (vv[r] - old);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) S[r][e] = fmaf(g, S[r][e], delta * cur.kf[e]);
-        if constexpr (INTER) RS::store(ip + r * 4 * kHeadDim, j, S[r]);
-        if (j == 0) op[4 * r] = __float2bfloat16_rn(scale * fmaf(g, sq, delta * kq));
-      }
-      if (t + 1 < T) {
-        cur = nxt;
-#pragma unroll
-        for (int r = 0; r < NG; ++r) vv[r] = vn[r];
-      }
-    }
-    ST* nsp = new_pool + ((size_t)slot * HV + h) * kHeadDim * kHeadDim + (size_t)row0 * kHeadDim;
-#pragma unroll
-    for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
   }
   if (issuer && *abort_flag) {  // let copies still in flight land before the CTA exits
     for (int i = issued - C::kStages > 0 ? issued - C::kStages : 0; i < issued; ++i)
@@ -436,11 +450,14 @@ cudaError_t launch_mtp(const void* q, const void* k, const void* v, const ST* po
                        const float* dt_bias, const void* b, float scale, void* out,
                        ST* new_pool, ST* inter, int batch, int T, long long pool_size,
                        int HQ, int HV, bool l2norm, cudaStream_t st) {
+  // the streaming variant bulk-copies q, k and v rows: 16-byte aligned bases
+  const bool rows16 = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
   // same CTA sizing as the decode kernel: enough CTAs to fill 148 SMs several times;
   // with the rollback buffer (T + 1 state writes per read) and that many heads, the
   // streaming variant, whose reads run under the writes
   const long long heads = (long long)batch * HV;
-  if (inter != nullptr && T >= 2 && heads >= 4 * 148)
+  if (inter != nullptr && T >= 2 && T <= kMtpStreamMaxT && heads >= 4 * 148 && rows16)
     return launch_mtp_stream<IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
                                        new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
   if (heads >= 4 * 148)
