@@ -79,6 +79,5 @@ unsigned read_device_error(bool clear);
 // Same for the streaming decode kernel.
 unsigned read_decode_device_error(bool clear);
 unsigned read_segment_device_error(bool clear);
-unsigned read_mtp_device_error(bool clear);
 
 }  // namespace gdn

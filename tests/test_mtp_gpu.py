@@ -118,12 +118,11 @@ def test_dps_kernel_arity_and_errors(cuda):
 
 @pytest.mark.parametrize("state_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("inplace", [True, False])
-def test_streaming_rollback_path_matches_one_shot_path_bitwise(cuda, state_dtype, inplace):
-    """With the rollback buffer and enough (row, v-head) pairs the call runs the streaming
-    kernel (states read into shared memory while the previous ones are written); without
-    the buffer it runs the one-CTA-per-pair kernel.  Both apply the same arithmetic: the
-    outputs and final pools agree bit for bit, padding rows included, and the buffer's
-    last token holds the final state."""
+def test_rollback_buffer_leaves_results_unchanged_bitwise(cuda, state_dtype, inplace):
+    """With enough (row, v-head) pairs for the largest CTAs, a call with the rollback
+    buffer and one without agree bit for bit (outputs and final pools, padding rows
+    included), in place and out of place, for fp32 and bf16 pools; the buffer's last
+    token holds the final state."""
     pkg = load_pkg()
     B, T, P = 40, 3, 48
     idx = list(range(3, 43))
@@ -133,11 +132,11 @@ def test_streaming_rollback_path_matches_one_shot_path_bitwise(cuda, state_dtype
     args = lambda pool: (inp["q"], inp["k"], inp["v"], pool, inp["state_indices"],  # noqa: E731
                          inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["scale"])
     pool_a = inp["state"].clone()
-    o_a, s_a = pkg.gdn_mtp(*args(pool_a), use_qk_l2norm=True)            # one-shot kernel
+    o_a, s_a = pkg.gdn_mtp(*args(pool_a), use_qk_l2norm=True)
     pool_b = inp["state"].clone()
     buf = torch.zeros((P, T) + tuple(pool_b.shape[1:]), dtype=state_dtype, device=cuda)
     fin = None if inplace else torch.full_like(pool_b, float("nan"))
-    o_b, s_b = pkg.gdn_mtp(*args(pool_b), None, fin, buf, use_qk_l2norm=True)  # streaming
+    o_b, s_b = pkg.gdn_mtp(*args(pool_b), None, fin, buf, use_qk_l2norm=True)
     torch.cuda.synchronize()
     assert pkg.device_error() == 0
     assert torch.equal(o_a, o_b) and torch.equal(s_a, s_b)
@@ -146,4 +145,4 @@ def test_streaming_rollback_path_matches_one_shot_path_bitwise(cuda, state_dtype
     assert o_b[5].abs().max().item() == 0.0 and o_b[17].abs().max().item() == 0.0
     ro, rs, _ = oracle_mtp({k_: (v_.cpu() if isinstance(v_, torch.Tensor) else v_)
                             for k_, v_ in inp.items()}, True)
-    assert_parity(o_b, s_b.float(), ro, rs.float(), what=f"streaming {state_dtype}")
+    assert_parity(o_b, s_b.float(), ro, rs.float(), what=f"rollback {state_dtype}")
