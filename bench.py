@@ -13,9 +13,9 @@ line also carries a ``prefill`` object with the P1 (8 varlen sequences) and P2
 N > 1 (torchrun, one process per GPU): weak scaling -- every rank runs the
 same per-GPU workload on its own data (decode: 128 sequences per GPU, so N=8
 is the 1024-sequence configuration sharded by batch); the prefill extras are
-strong scaling (the 64-sequence P3 set sharded by sequence with longest-first
-bin packing; the single sequence of P2 sharded by q/k-head group, and, as a
-separate line, by the token-segment scan with its one all-gather).  Decode has
+strong scaling: P2 (one sequence) and P3 (64 sequences) sharded by q/k-head
+group, with P3 by sequence (longest-first packing) and P2 by the token-segment
+scan (its one all-gather) as separate lines.  Decode has
 no collective on the data path.  Time is the max over ranks of the device time.
 
 Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
@@ -307,17 +307,25 @@ MTP_T = 4  # draft tokens verified per row (speculative decoding)
 
 
 def plan_kind(W, name, world, force="auto"):
-    """How prefill config `name` is split over `world` GPUs: None (one GPU), "seqs" (whole
-    sequences, longest-first packing; at least as many sequences as ranks), "heads" (q/k-head
-    groups with their v-heads; the default when there are fewer sequences than ranks, no
-    collective) or "segments" (one sequence as consecutive token segments chained through
-    their state maps, one all-gather per call; opt-in with force="segments")."""
+    """How prefill config `name` is split over `world` GPUs: None (one GPU), "heads" (every
+    GPU runs all sequences for its q/k-head group and the v-heads that read them), "seqs"
+    (whole sequences, longest-first packing) or "segments" (one sequence as consecutive
+    token segments chained through their state maps, one all-gather per call).  Neither of
+    the first two has a collective.  The default is head groups whenever the q/k heads
+    divide evenly: every GPU then gets the same mix of sequence lengths, so the ranks
+    finish together (P3 on one B200 per rank's share: 2.75 / 1.45 / 0.80 ms per step at
+    N = 2 / 4 / 8 against 3.18 / 1.46 / 0.85 ms for sequence packing).  `force` picks
+    "heads", "seqs" or "segments" (one sequence only) instead."""
     if world == 1:
         return None
     cfg = W.PREFILL_CONFIGS[name]
-    if cfg.n >= world:
+    if force == "segments" and cfg.n == 1:
+        return "segments"
+    if force == "seqs" and cfg.n >= world:
         return "seqs"
-    return "segments" if (force == "segments" and cfg.n == 1) else "heads"
+    if force == "heads" or W.HQ % world == 0 or cfg.n < world:
+        return "heads"
+    return "seqs"
 
 
 def prefill_plan(pkg, name, dist, force="auto"):
@@ -890,7 +898,8 @@ def run_ours(args, dist):
             "global_batch": 4 * dist.world}
         extra = {}
         names = [("P1", "auto"), ("P2", "auto")] if dist.world == 1 else \
-            [("P2", "heads"), ("P2_segment_scan", "segments"), ("P3", "auto")]
+            [("P2", "heads"), ("P2_segment_scan", "segments"), ("P3", "heads"),
+             ("P3_by_sequence", "seqs")]
         for label, force in names:
             nm = label.split("_")[0]
             shard = prefill_plan(pkg, nm, dist, force)
@@ -962,10 +971,12 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_b128")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-extra", action="store_true")
-    ap.add_argument("--prefill-plan", choices=["auto", "heads", "segments"], default="auto",
-                    help="multi-GPU split of a config with fewer sequences than GPUs "
-                         "(default: q/k-head groups, no collective; 'segments': token-segment "
-                         "scan of one sequence, one all-gather per call)")
+    ap.add_argument("--prefill-plan", choices=["auto", "heads", "seqs", "segments"],
+                    default="auto",
+                    help="multi-GPU split of a prefill config (default: q/k-head groups when "
+                         "the heads divide evenly, no collective; 'seqs': whole sequences by "
+                         "longest-first packing; 'segments': token-segment scan of one "
+                         "sequence, one all-gather per call)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()

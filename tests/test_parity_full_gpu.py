@@ -1,6 +1,6 @@
 """GPU parity at the measured sizes: P2 (one 32,768-token sequence with an initial state)
-and P3 (64 sequences, T = 275,479) against the CPU oracle, and P3's multi-GPU sequence
-shards reassembled bit for bit.
+and P3 (64 sequences, T = 275,479) against the CPU oracle, and P3's multi-GPU shares (by
+q/k-head group, the default plan, and by sequence) reassembled bit for bit.
 
 The oracle's token loop over the whole of P3 (or over all 32 v-heads of P2) would take
 minutes on the host, so it runs on a subset that keeps every token of the compared
@@ -127,7 +127,7 @@ def test_p3_full_vs_oracle_sampled(cuda, kernel):
 
 @pytest.mark.parametrize("world", [2, 8])
 def test_p3_sequence_shards_reassemble_bitwise(cuda, world):
-    """P3 dealt to `world` ranks by longest-first packing (the multi-GPU plan), each
+    """P3 dealt to `world` ranks by longest-first packing of whole sequences, each
     rank's share run as its own call on one GPU: the reassembled outputs and final
     states equal the unsharded call's bit for bit (each (sequence, v-head) scan depends
     only on its own tokens and heads)."""
@@ -147,6 +147,29 @@ def test_p3_sequence_shards_reassemble_bitwise(cuda, world):
     torch.cuda.synchronize()
     uo, us = S.prefill_unshard(inp["q"].shape[0], len(lens), inp["cu_seqlens"], plan, outs,
                                states)
+    assert torch.equal(uo, o.cpu()) and torch.equal(us, s.cpu())
+    assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_p3_head_group_shards_reassemble_bitwise(cuda, world):
+    """P3 dealt to `world` ranks by q/k-head group (the default multi-GPU plan: every rank
+    runs all 64 sequences for its heads), each share run as its own call on one GPU: the
+    reassembled outputs and final states equal the unsharded call's bit for bit."""
+    pkg = load_pkg()
+    S = pkg.sharding
+    inp = to(p3_inputs(), cuda)
+    keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")
+    o, s = pkg.gdn_prefill(*[inp[k_] for k_ in keys], use_qk_l2norm=True)
+    outs, states = [], []
+    for r in range(world):
+        lo, hi = S.head_range(inp["q"].shape[1], world, r)
+        sh = S.prefill_head_shard(inp, lo, hi)
+        ro, rs = pkg.gdn_prefill(*[sh[k_] for k_ in keys], use_qk_l2norm=True)
+        outs.append(ro)
+        states.append(rs)
+    torch.cuda.synchronize()
+    uo, us = S.prefill_head_unshard(outs, states)
     assert torch.equal(uo, o.cpu()) and torch.equal(us, s.cpu())
     assert pkg.device_error() == 0
 
