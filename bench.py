@@ -235,6 +235,7 @@ class DecodeWork:
         if not hasattr(self, "s_up"):
             self.s_up, self.s_down = torch.cuda.Stream(), torch.cuda.Stream()
         n = E2E_SLICES if self.batch % E2E_SLICES == 0 else 1
+        n = getattr(self, "slices", n)
         rows = self.batch // n
         di, d = self.d_in, self.inp
         self.s_up.wait_stream(cur)  # inputs of the previous step are consumed
@@ -718,9 +719,35 @@ def copy_reference(units, dev, reps=20):
     return 2 * n * 4 * reps / (t0.elapsed_time(t1) * 1e-3) / 1e9
 
 
+def pcie_reference(h2d, d2h, dev, reps=3):
+    """GB/s (both directions together) of one pinned host->device copy of `h2d` bytes
+    running beside one device->host copy of `d2h` bytes on a second stream: the PCIe rate
+    the end-to-end step's copies can reach, beside its measured rate."""
+    hu = torch.empty(max(1, h2d), dtype=torch.uint8).pin_memory()
+    hd = torch.empty(max(1, d2h), dtype=torch.uint8).pin_memory()
+    du = torch.empty(hu.numel(), dtype=torch.uint8, device=dev)
+    dd = torch.empty(hd.numel(), dtype=torch.uint8, device=dev)
+    s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def both():
+        with torch.cuda.stream(s_up):
+            du.copy_(hu, non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            hd.copy_(dd, non_blocking=True)
+    both()
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        both()
+    torch.cuda.synchronize()
+    return (h2d + d2h) * reps / (time.perf_counter() - t) / 1e9
+
+
 def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf16=False,
-                   graphs=True):
+                   graphs=True, e2e_slices=0):
     w = DecodeWork(pkg, batch, dev, seed=dist.rank, state_bf16=state_bf16)
+    if e2e_slices > 0 and batch % e2e_slices == 0:
+        w.slices = e2e_slices
     fn, keep = graph_steps(w, 2) if graphs else (w.step, None)
     flush = l2_flusher(w.units, dev)
     with ClockSampler(dev.index) as clk:
@@ -734,9 +761,12 @@ def measure_decode(pkg, dist, batch, steps, warmup, dev, with_e2e=True, state_bf
         h2d, d2h = w.host_copies()
         e2e_steps = max(3, min(steps, 20))
         e_ms, _ = time_steps(w.e2e_step, e2e_steps, 2, dist, per_launch_events=False)
+        pcie = pcie_reference(h2d, d2h, dev)
         res["e2e"] = {"value": total_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                      "ms_per_step": e_ms, "steps": e2e_steps}
+                      "ms_per_step": e_ms, "steps": e2e_steps,
+                      "pcie_same_bytes_gbs": round(pcie, 1),
+                      "frac_of_pcie": round((h2d + d2h) / (e_ms * 1e-3) / 1e9 / pcie, 4)}
     return res
 
 
@@ -864,7 +894,8 @@ def run_ours(args, dist):
                             graphs=not args.no_graphs)
         else:
             r = measure_decode(pkg, dist, param, args.steps, args.warmup, dev,
-                               state_bf16=kind == "decode_bf16state", graphs=not args.no_graphs)
+                               state_bf16=kind == "decode_bf16state", graphs=not args.no_graphs,
+                               e2e_slices=args.e2e_slices)
         value, bound, scaling = round(r["value"], 2), "hbm", "weak"
     else:
         shard = prefill_plan(pkg, param, dist, args.prefill_plan)
@@ -977,6 +1008,9 @@ def main():
                          "the heads divide evenly, no collective; 'seqs': whole sequences by "
                          "longest-first packing; 'segments': token-segment scan of one "
                          "sequence, one all-gather per call)")
+    ap.add_argument("--e2e-slices", type=int, default=0,
+                    help="batch slices of the pipelined end-to-end decode step (default %d)"
+                         % E2E_SLICES)
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
     args = ap.parse_args()
