@@ -314,9 +314,9 @@ def plan_kind(W, name, world, force="auto"):
     token segments chained through their state maps, one all-gather per call).  Neither of
     the first two has a collective.  The default is head groups whenever the q/k heads
     divide evenly: every GPU then gets the same mix of sequence lengths, so the ranks
-    finish together (P3 on one B200 per rank's share: 2.75 / 1.45 / 0.80 ms per step at
-    N = 2 / 4 / 8 against 3.18 / 1.46 / 0.85 ms for sequence packing).  `force` picks
-    "heads", "seqs" or "segments" (one sequence only) instead."""
+    finish together (P3, each rank's share timed on one B200: 0.797 ms at N = 8 against
+    0.853 ms for sequence packing).  `force` picks "heads", "seqs" or "segments" (one
+    sequence only) instead."""
     if world == 1:
         return None
     cfg = W.PREFILL_CONFIGS[name]
