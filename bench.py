@@ -158,13 +158,13 @@ class Dist:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
 
-    def init(self, backend="nccl"):
+    def init(self, backend="nccl", timeout_s=120):
         if self.world > 1:
             import datetime
             import torch.distributed as dist
             if backend == "nccl":
                 torch.cuda.set_device(self.local)
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
             self.pg = dist
 
     def barrier(self):

@@ -354,12 +354,23 @@ int gdn_segment_chain_launch(const float* maps, int num_maps, int rank, float* s
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
  * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory
- * stage of the streaming decode kernel was never released; -1 = the device
- * reported an error).  Every wait inside the kernels is bounded; a wait that runs out sets
+ * stage of the streaming decode kernel was never released, 16 = the wait of
+ * gdn_selftest_bounded_wait ran out; -1 = the device reported an error).  Every wait inside the kernels is bounded; a wait that runs out sets
  * a bit, the kernel releases its resources and returns instead of hanging.
  * The bits are cleared when `clear` != 0.  No counterpart in the reference.
  */
 int gdn_device_error(int clear);
+
+/*
+ * Self-test of the bounded-wait path (no counterpart in the reference): one CTA waits,
+ * with the same iteration-limited mbarrier wait every kernel of this library uses, on a
+ * barrier that expects one arrival.  arrive != 0: the waiting thread arrives first and
+ * the wait succeeds.  arrive == 0: nothing ever arrives, the wait gives up after `limit`
+ * polls (1 <= limit <= 2^24), bit 16 of gdn_device_error is set and the kernel returns
+ * normally -- the context stays usable.  `result` (device int, may be NULL) receives 1
+ * when the wait succeeded, 0 when it ran out.  Asynchronous on `stream`.
+ */
+int gdn_selftest_bounded_wait(unsigned int limit, int arrive, int* result, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

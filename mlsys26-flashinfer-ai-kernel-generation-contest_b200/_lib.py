@@ -55,6 +55,7 @@ SIGNATURES = {
     "gdn_segment_outputs_launch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gdn_segment_chain_launch": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_device_error": (_i, [_i]),
+    "gdn_selftest_bounded_wait": (_i, [ctypes.c_uint, _i, _vp, _vp]),
 }
 
 # Prefill kernel selection (gdn_prefill_launch_variant).
@@ -96,5 +97,6 @@ def check(where: str, status: int) -> None:
 
 def device_error(clear: bool = True) -> int:
     """Synchronise the current device and return the kernels' device-side error bits
-    (0 = none; 1 = a TMA wait ran out; 2 = a tensor-core wait ran out)."""
+    (0 = none; 1 = a TMA wait ran out; 2 = a tensor-core wait ran out; 8 = a streaming
+    stage was never released; 16 = the self-test's wait ran out)."""
     return int(LIB.gdn_device_error(int(bool(clear))))

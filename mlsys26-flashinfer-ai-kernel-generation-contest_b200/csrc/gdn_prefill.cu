@@ -224,8 +224,9 @@ extern "C" int gdn_device_error(int clear) {
   const unsigned b = gdn::read_split_device_error(clear != 0);
   const unsigned d = gdn::read_decode_device_error(clear != 0);
   const unsigned e = gdn::read_segment_device_error(clear != 0);
-  if (a == ~0u || b == ~0u || d == ~0u || e == ~0u) return -1;
-  return (int)(a | b | d | e);
+  const unsigned t = gdn::read_selftest_device_error(clear != 0);
+  if (a == ~0u || b == ~0u || d == ~0u || e == ~0u || t == ~0u) return -1;
+  return (int)(a | b | d | e | t);
 }
 
 extern "C" int gdn_prefill_launch_strided(

@@ -79,5 +79,7 @@ unsigned read_device_error(bool clear);
 // Same for the streaming decode kernel.
 unsigned read_decode_device_error(bool clear);
 unsigned read_segment_device_error(bool clear);
+// Same for the bounded-wait self-test kernel (gdn_selftest_bounded_wait).
+unsigned read_selftest_device_error(bool clear);
 
 }  // namespace gdn

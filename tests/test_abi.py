@@ -153,3 +153,10 @@ def test_row_stride_of_views():
     assert x.is_contiguous() and rs == 16 * 128
     odd = torch.zeros(10, 16 * 128 + 2, dtype=torch.bfloat16)[:, :16 * 128].view(10, 16, 128)
     assert C.row_stride(odd, 4) is None and C.row_stride(odd) == 16 * 128 + 2
+
+
+def test_selftest_argument_checks_return_before_launch():
+    lib = load_pkg().LIB
+    assert lib.gdn_selftest_bounded_wait(0, 0, None, None) == -1          # no polls
+    assert lib.gdn_selftest_bounded_wait((1 << 24) + 1, 0, None, None) == -1
+    assert lib.gdn_selftest_bounded_wait(16, 0, 0x1002, None) == -1       # misaligned

@@ -5,9 +5,10 @@
   the unsharded result, and the max-over-ranks timing reduction works;
 * one sequence split into segments over 2 and 3 ranks (segment-level scan, the segments'
   state maps exchanged with all_gather) gives the unsplit result;
-* failure detection on the host: a rank that dies before the barrier makes
-  the surviving rank's next collective end with an error within the process
-  group's short timeout instead of hanging.
+* failure detection on the host: a rank that dies before the barrier, or whose step
+  raises, makes the surviving rank's next collective end with an error within the
+  process group's short timeout instead of hanging; the same through bench.py's own
+  driver (barrier, max-over-ranks timing reduction).
 """
 import datetime
 import os
@@ -145,6 +146,57 @@ def _worker_failing(rank, world, port, q):
         q.put(("error", traceback.format_exc()))
 
 
+def _worker_raising(rank, world, port, q):
+    """Rank 1 raises inside its step (before the step's collective) and leaves; rank 0's
+    collective ends with an error within the short timeout."""
+    try:
+        _init(rank, world, port, 3)
+        try:
+            if rank == 1:
+                raise RuntimeError("step failed on rank 1")
+            t = torch.ones(4)
+            dist.all_reduce(t)
+            q.put(("no-error",))
+        except RuntimeError as e:
+            if rank == 1:
+                q.put(("raised", str(e)))
+                q.close()
+                q.join_thread()  # the message is out before the process leaves
+                os._exit(0)
+            q.put(("detected", type(e).__name__))
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
+def _worker_bench_dist(rank, world, port, q):
+    """bench.py's own driver plumbing on gloo: barrier and the max-over-ranks reduction,
+    then, with rank 1 gone, its barrier ends with an error instead of hanging."""
+    try:
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                          MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_bench_dist", REPO / "bench.py")
+        B = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = B
+        spec.loader.exec_module(B)
+        d = B.Dist()
+        d.init("gloo", timeout_s=3)
+        d.barrier()
+        m = d.max(1.5 * (rank + 1))
+        if rank == 1:
+            q.put(("max", m))
+            q.close()
+            q.join_thread()  # the message is out before the process leaves
+            os._exit(0)
+        try:
+            d.barrier()
+            q.put(("no-error", m))
+        except Exception as e:
+            q.put(("detected", m, type(e).__name__))
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
 def _run(fn, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -183,3 +235,16 @@ def test_segment_scan_over_ranks_matches_unsplit(world):
     assert items and all(i[0] == "ok" for i in items), items
     _, ok_out, err = items[0]
     assert ok_out and err < 1e-5
+
+
+def test_rank_that_raises_is_detected_not_hung():
+    items = _run(_worker_raising)
+    kinds = sorted(i[0] for i in items)
+    assert kinds == ["detected", "raised"], items
+
+
+def test_bench_driver_barrier_max_and_dead_rank():
+    items = _run(_worker_bench_dist)
+    by = {i[0]: i for i in items}
+    assert "max" in by and by["max"][1] == 3.0, items
+    assert "detected" in by and by["detected"][1] == 3.0, items
