@@ -43,31 +43,36 @@ def row_stride(x: torch.Tensor, align: int = 1):
     return rs if (rs >= inner and rs % align == 0) else None
 
 
-def rows_in(x: torch.Tensor, align: int = 1):
-    """(tensor, row stride) for a token-indexed input: strided rows are passed to the
-    kernels as they are; any other layout is first copied into a dense tensor on the
-    device."""
+def rows_in(x: torch.Tensor, align: int = 1, ptr_align: int = 2):
+    """(tensor, row stride) for a token-indexed input: strided rows whose stride is a
+    multiple of `align` elements and whose first element is `ptr_align`-byte aligned are
+    passed to the kernels as they are; anything else is first copied into a dense tensor
+    on the device (freshly allocated, so aligned)."""
     rs = row_stride(x, align)
-    if rs is None:
-        x = x.contiguous()
+    if rs is None or x.data_ptr() % ptr_align != 0:
+        x = x.clone(memory_format=torch.contiguous_format)
         rs = row_stride(x, align)
     return x, rs
 
 
-def rows_out(x: torch.Tensor, align: int = 1):
-    """(target, row stride, copy_back) for a token-indexed output: strided rows are
-    written in place; for any other layout the kernels write a dense temporary that the
-    caller copies into `x` afterwards (copy_back is True)."""
+def rows_out(x: torch.Tensor, align: int = 1, ptr_align: int = 2):
+    """(target, row stride, copy_back) for a token-indexed output: strided rows (stride a
+    multiple of `align`, first element `ptr_align`-byte aligned) are written in place; for
+    anything else the kernels write a dense temporary that the caller copies into `x`
+    afterwards (copy_back is True)."""
     rs = row_stride(x, align)
-    if rs is not None:
+    if rs is not None and x.data_ptr() % ptr_align == 0:
         return x, rs, False
     t = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     return t, row_stride(t, align), True
 
 
-def dense_or_copy(x):
-    """A contiguous tensor with x's values (x itself when it already is one)."""
-    return x if (x is None or x.is_contiguous()) else x.contiguous()
+def dense_or_copy(x, ptr_align: int = 4):
+    """A contiguous, `ptr_align`-byte aligned tensor with x's values (x itself when it
+    already is one)."""
+    if x is None or (x.is_contiguous() and x.data_ptr() % ptr_align == 0):
+        return x
+    return x.clone(memory_format=torch.contiguous_format)
 
 
 def shape(name: str, x: torch.Tensor, expected) -> None:

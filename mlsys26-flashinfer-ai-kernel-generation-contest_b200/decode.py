@@ -28,9 +28,9 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
     Like the reference, which hands every stride to its kernel, q, k, v, a, b and
     ``output`` may be views whose batch rows are strided (slices of a fused projection,
     say): with fp32 state they go to ``gdn_decode_launch_strided`` as they are.  Other
-    layouts (and strided rows with bf16 state) are copied into dense tensors on the
-    device first, and a non-dense ``output`` / ``new_state`` is written through a dense
-    temporary."""
+    layouts, strided rows with bf16 state, and q / k not 8-byte aligned (or a state not
+    16-byte aligned) are copied into dense tensors on the device first, and a non-dense
+    ``output`` / ``new_state`` is written through a dense temporary."""
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 4, dev, strided=True)
     C.tensor("k", k, torch.bfloat16, 4, dev, strided=True)
@@ -71,15 +71,15 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=None, new_sta
         C.shape("new_state", new_state, (B, HV, D, D))
     if B == 0:
         return output, new_state
-    state_in, A_log, dt_bias = C.dense_or_copy(state), C.dense_or_copy(A_log), \
+    state_in, A_log, dt_bias = C.dense_or_copy(state, 16), C.dense_or_copy(A_log), \
         C.dense_or_copy(dt_bias)
-    ns = new_state if new_state.is_contiguous() else torch.empty(
-        new_state.shape, dtype=sdt, device=dev)
+    ns = new_state if (new_state.is_contiguous() and new_state.data_ptr() % 16 == 0) else \
+        torch.empty(new_state.shape, dtype=sdt, device=dev)
     if ns is not new_state and state is not None and state_in.data_ptr() == new_state.data_ptr():
         state_in = state_in.clone()  # keep the in-place contract through the temporary
     if sdt == torch.bfloat16:  # dense rows only
         q, k, v, a, b = (C.dense_or_copy(x) for x in (q, k, v, a, b))
-    (q, qs), (k, ks) = C.rows_in(q, 4), C.rows_in(k, 4)
+    (q, qs), (k, ks) = C.rows_in(q, 4, 8), C.rows_in(k, 4, 8)  # 8-byte q / k loads
     (v, vs), (a, as_), (b, bs) = C.rows_in(v), C.rows_in(a), C.rows_in(b)
     out, os_, out_back = C.rows_out(output) if sdt == torch.float32 else (
         (output, None, False) if output.is_contiguous() else

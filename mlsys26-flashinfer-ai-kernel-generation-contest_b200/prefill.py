@@ -108,8 +108,11 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
     """Checks, then one launch.  Like the reference, which hands every stride to its
     kernel, q, k, v, a, b and ``output`` may be views whose token rows are strided (slices
     of a fused projection, say): those go to ``gdn_prefill_launch_strided`` as they are.
-    Other layouts are copied into dense tensors on the device first, and a non-dense
-    ``output`` / ``new_state`` is written through a dense temporary."""
+    Other layouts, and q / k / v / output whose rows or first element are not 16-byte
+    aligned, are copied into dense tensors on the device first (a non-dense or unaligned
+    ``output`` / ``new_state`` is written through a dense temporary), so that the
+    tensor-core kernels always apply; the C ABI itself runs the token-serial kernel for
+    such buffers."""
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 3, dev, strided=True)
     C.tensor("k", k, torch.bfloat16, 3, dev, strided=True)
@@ -154,16 +157,19 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
         C.shape("new_state", new_state, (N, H, D, D))
     if N == 0:
         return output, new_state
-    cu_seqlens = C.dense_or_copy(cu_seqlens)
-    state_in, A_log, dt_bias = C.dense_or_copy(state), C.dense_or_copy(A_log), \
+    cu_seqlens = C.dense_or_copy(cu_seqlens, 8)
+    state_in, A_log, dt_bias = C.dense_or_copy(state, 16), C.dense_or_copy(A_log), \
         C.dense_or_copy(dt_bias)
-    ns = new_state if new_state.is_contiguous() else torch.empty(
-        new_state.shape, dtype=torch.float32, device=dev)
+    ns = new_state if (new_state.is_contiguous() and new_state.data_ptr() % 16 == 0) else \
+        torch.empty(new_state.shape, dtype=torch.float32, device=dev)
     if ns is not new_state and state is not None and state_in.data_ptr() == new_state.data_ptr():
         state_in = state_in.clone()  # keep the in-place contract through the temporary
-    (q, qs), (k, ks) = C.rows_in(q, 4), C.rows_in(k, 4)
-    (v, vs), (a, as_), (b, bs) = C.rows_in(v), C.rows_in(a), C.rows_in(b)
-    out, os_, out_back = C.rows_out(output)
+    # the tensor-core kernels read q / k / v tiles by TMA and store 16-byte output pieces:
+    # views whose rows or first element are not 16-byte aligned are copied (else the call
+    # would fall back to the token-serial kernel)
+    (q, qs), (k, ks), (v, vs) = C.rows_in(q, 8, 16), C.rows_in(k, 8, 16), C.rows_in(v, 8, 16)
+    (a, as_), (b, bs) = C.rows_in(a), C.rows_in(b)
+    out, os_, out_back = C.rows_out(output, 8, 16)
     ws_n = workspace_bytes(T, N, HQ, HV, D, kernel)
     ws = _workspace(dev, ws_n) if ws_n > 0 else None
     head = (q.data_ptr(), k.data_ptr(), v.data_ptr(),

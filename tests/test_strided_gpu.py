@@ -64,20 +64,38 @@ def test_prefill_fused_projection_views(cuda, kernel):
     assert pkg.device_error() == 0
 
 
-def test_prefill_rows_not_16_byte_aligned_take_the_token_serial_kernel(cuda):
-    """Token rows 8 bytes longer than a multiple of 16: the tensor-core kernels need
-    16-byte rows, so the call runs the token-serial kernel on the views as they are."""
+def test_prefill_rows_not_16_byte_aligned(cuda):
+    """Token rows 8 bytes longer than a multiple of 16: the tensor-core kernels read rows
+    by TMA and need 16-byte rows.  Through the C ABI such views run the token-serial
+    kernel (and an explicit tensor-core variant is refused); the Python entry point copies
+    them into dense tensors first, so it gets the tensor-core result of the dense call."""
     pkg = load_pkg()
     inp = pkg.workloads.prefill_inputs([33, 100], hq=4, hv=8, seed=92)
     d = to(inp, cuda)
     sv = fused_views(d, (d["q"].shape[0],), pad=4)
     assert sv["q"].stride(0) % 8 == 4
-    o, s = pkg.gdn_prefill(*[sv[x] for x in ARGS_P], use_qk_l2norm=True)
-    o_ref, s_ref = pkg.gdn_prefill_recurrent(*[d[x] for x in ARGS_P], use_qk_l2norm=True)
+    T, N = d["q"].shape[0], 2
+    out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device=cuda)
+    ns = torch.empty(N, 8, 128, 128, device=cuda)
+
+    def abi(variant):
+        return pkg.LIB.gdn_prefill_launch_strided(
+            variant, sv["q"].data_ptr(), sv["k"].data_ptr(), sv["v"].data_ptr(),
+            d["state"].data_ptr(), d["A_log"].data_ptr(), sv["a"].data_ptr(),
+            d["dt_bias"].data_ptr(), sv["b"].data_ptr(), d["cu_seqlens"].data_ptr(), 0,
+            d["scale"], out.data_ptr(), ns.data_ptr(), T, N, 4, 4, 8, 128, 1,
+            sv["q"].stride(0), sv["k"].stride(0), sv["v"].stride(0), sv["a"].stride(0),
+            sv["b"].stride(0), out.stride(0), None, 0, torch.cuda.current_stream().cuda_stream)
+    assert abi(0) == 0                                   # AUTO: token-serial kernel
     torch.cuda.synchronize()
-    assert torch.equal(o, o_ref) and torch.equal(s, s_ref)
-    with pytest.raises(pkg.GDNError, match="UNSUPPORTED"):
-        pkg.gdn_prefill(*[sv[x] for x in ARGS_P], use_qk_l2norm=True, kernel="fused")
+    o_rec, s_rec = pkg.gdn_prefill_recurrent(*[d[x] for x in ARGS_P], use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, o_rec) and torch.equal(ns, s_rec)
+    assert pkg.LIB.gdn_status_string(abi(2)) == b"GDN_ERR_UNSUPPORTED"  # FUSED refused
+    o, s = pkg.gdn_prefill(*[sv[x] for x in ARGS_P], use_qk_l2norm=True, kernel="fused")
+    o_d, s_d = pkg.gdn_prefill(*[d[x] for x in ARGS_P], use_qk_l2norm=True, kernel="fused")
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_d) and torch.equal(s, s_d)
 
 
 def test_prefill_other_layouts_are_copied(cuda):
@@ -142,3 +160,29 @@ def test_dps_kernel_entry_points_take_views(cuda):
                                 torch.empty_like(d["state"]))
     torch.cuda.synchronize()
     assert torch.equal(o2, o) and torch.equal(s2, s)
+
+
+def test_misaligned_first_elements_are_copied(cuda):
+    """q/k/v views starting 2 bytes past an aligned address (a layout the kernels' vector
+    loads cannot take): the Python entry points copy them into aligned dense tensors, so
+    decode and prefill still give the dense calls' results."""
+    pkg = load_pkg()
+
+    def offset(t):
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=cuda)
+        view = buf[1:].view(t.shape)
+        view.copy_(t)
+        assert view.data_ptr() % 4 == 2
+        return view
+    dinp = to(pkg.workloads.decode_inputs(5, hq=2, hv=4, seed=98), cuda)
+    o, s = pkg.gdn_decode(*[dinp[x] for x in ARGS_D], use_qk_l2norm=True)
+    e = dict(dinp, q=offset(dinp["q"]), k=offset(dinp["k"]), v=offset(dinp["v"]))
+    o2, s2 = pkg.gdn_decode(*[e[x] for x in ARGS_D], use_qk_l2norm=True)
+    pinp = to(pkg.workloads.prefill_inputs([70, 9], hq=2, hv=4, seed=99), cuda)
+    po, ps = pkg.gdn_prefill(*[pinp[x] for x in ARGS_P], use_qk_l2norm=True)
+    f = dict(pinp, q=offset(pinp["q"]), k=offset(pinp["k"]), v=offset(pinp["v"]))
+    out = offset(torch.zeros_like(po))
+    po2, ps2 = pkg.gdn_prefill(*[f[x] for x in ARGS_P], out, None, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, o) and torch.equal(s2, s)
+    assert po2 is out and torch.equal(po2, po) and torch.equal(ps2, ps)
