@@ -78,6 +78,9 @@ def test_prefill_rows_not_16_byte_aligned(cuda):
     out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device=cuda)
     ns = torch.empty(N, 8, 128, 128, device=cuda)
 
+    wsb = pkg.LIB.gdn_prefill_workspace_size_variant(0, T, N, 4, 8, 128)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=cuda)
+
     def abi(variant):
         return pkg.LIB.gdn_prefill_launch_strided(
             variant, sv["q"].data_ptr(), sv["k"].data_ptr(), sv["v"].data_ptr(),
@@ -85,7 +88,8 @@ def test_prefill_rows_not_16_byte_aligned(cuda):
             d["dt_bias"].data_ptr(), sv["b"].data_ptr(), d["cu_seqlens"].data_ptr(), 0,
             d["scale"], out.data_ptr(), ns.data_ptr(), T, N, 4, 4, 8, 128, 1,
             sv["q"].stride(0), sv["k"].stride(0), sv["v"].stride(0), sv["a"].stride(0),
-            sv["b"].stride(0), out.stride(0), None, 0, torch.cuda.current_stream().cuda_stream)
+            sv["b"].stride(0), out.stride(0), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream().cuda_stream)
     assert abi(0) == 0                                   # AUTO: token-serial kernel
     torch.cuda.synchronize()
     o_rec, s_rec = pkg.gdn_prefill_recurrent(*[d[x] for x in ARGS_P], use_qk_l2norm=True)
