@@ -362,6 +362,7 @@ class PrefillWork:
         self.pkg, self.dev = pkg, dev
         inp = W.prefill_config_inputs(cfg_name, seed=seed, device="cpu")
         self.segments = shard is not None and shard[0] == "segments"
+        self.local_segments = 1
         if self.segments:
             self._init_segment(inp, shard[1], shard[2], dist)
             return
@@ -377,12 +378,21 @@ class PrefillWork:
         self.cpu_inp = inp
         T = self.inp["q"].shape[0]
         N = len(lens)
+        # one sequence whose v-heads leave most SMs idle (a head group of a multi-GPU plan):
+        # its token segments run side by side in one call (gdn_prefill_segmented)
+        self.local_segments = pkg.sharding.local_segments(self.inp["v"].shape[1], T) \
+            if (shard is not None and N == 1) else 1
         self.out = torch.empty(T, self.inp["v"].shape[1], 128, dtype=torch.bfloat16, device=dev)
         self.ns = torch.empty(N, self.inp["v"].shape[1], 128, 128, dtype=torch.float32, device=dev)
         # whole-sequence tokens this rank completes (a head group does a share of each)
         self.tokens = T * head_frac
         self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
         self.launches = pkg.prefill.launches_per_call(T, N, self.inp["q"].shape[1], self.inp["v"].shape[1])
+        if self.local_segments > 1:  # the call of 2 S - 1 runs, then chain + outputs per segment
+            runs = 2 * self.local_segments - 1
+            self.launches = pkg.prefill.launches_per_call(
+                T * runs // self.local_segments, runs, self.inp["q"].shape[1],
+                self.inp["v"].shape[1]) + 2 * (self.local_segments - 1)
 
     def _init_segment(self, inp, world, rank, dist):
         """Segment `rank` of the single sequence.  Rank 0 runs it from the initial state;
@@ -445,14 +455,23 @@ class PrefillWork:
             self.pkg.sharding.segment_assemble(self.maps, self.rank, self.dbl_out[:L],
                                                self.dbl_out[L:], out=self.out, final=self.ns)
 
+    def _call(self, d):
+        if self.local_segments > 1:
+            self.pkg.gdn_prefill_segmented(d["q"], d["k"], d["v"], d.get("state"), d["A_log"],
+                                           d["a"], d["dt_bias"], d["b"], d["scale"], self.out,
+                                           self.ns, segments=self.local_segments,
+                                           use_qk_l2norm=True)
+            return
+        self.pkg.gdn_prefill(d["q"], d["k"], d["v"], d.get("state"), d["A_log"], d["a"],
+                             d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
+                             use_qk_l2norm=True)
+
     def step(self):
         d = self.inp
         if self.segments:
             self._segment_step(d)
             return
-        self.pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
-                             d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,
-                             use_qk_l2norm=True)
+        self._call(d)
 
     def host_copies(self):
         d = self.inp
@@ -483,9 +502,7 @@ class PrefillWork:
             self.h_out.copy_(self.out, non_blocking=True)
             self.h_ns.copy_(self.ns, non_blocking=True)
             return
-        self.pkg.gdn_prefill(di["q"], di["k"], di["v"], di.get("state"), d["A_log"], di["a"],
-                             d["dt_bias"], di["b"], di["cu_seqlens"], d["scale"], self.out,
-                             self.ns, use_qk_l2norm=True)
+        self._call({**d, **di})
         self.h_out.copy_(self.out, non_blocking=True)
         self.h_ns.copy_(self.ns, non_blocking=True)
 
@@ -803,7 +820,8 @@ def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2
     res = {"ms": ms, "kern_ms": kern_ms, "value": tokens_all / (ms * 1e-3),
            "tflops": tokens_all * pkg.workloads.prefill_flops_per_token() / (ms * 1e-3) / 1e12,
            "achieved": w.flops / (kern_ms * 1e-3) / 1e12, "clocks": clk.summary(),
-           "launches": w.launches * steps, "tokens": w.tokens, "tokens_all": tokens_all}
+           "launches": w.launches * steps, "tokens": w.tokens, "tokens_all": tokens_all,
+           "local_segments": w.local_segments}
     if with_e2e:
         h2d, d2h = w.host_copies()
         e2e_steps = max(2, min(steps, 5))
@@ -938,7 +956,10 @@ def run_ours(args, dist):
                                 with_e2e=False)
             extra[label] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
                             "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
-                            "parallelism": plan_text(shard, dist.world),
+                            "parallelism": plan_text(shard, dist.world)
+                            + (f"; the sequence in {r['local_segments']} token segments side "
+                               f"by side in one call per rank" if r["local_segments"] > 1
+                               else ""),
                             # the committed traffic capture is of the unsharded call
                             "roofline": roofline("tensor", r["achieved"],
                                                  "prefill_" + nm.lower() if shard is None else "",

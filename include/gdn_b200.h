@@ -351,6 +351,19 @@ int gdn_segment_chain_launch(const float* maps, int num_maps, int rank, float* s
                              void* stream);
 
 /*
+ * The same chain for every segment in one pass (no counterpart in the reference): with
+ * maps as for gdn_segment_chain_launch, writes start_states[s - 1] = the start state of
+ * segment s for s = 1 .. num_maps - 1 ([num_maps - 1][num_v_heads][head_size][head_size]
+ * fp32) and final_state = the last segment's final state, in num_maps - 1 steps instead
+ * of one chain per segment.  Used when every segment of a sequence is assembled on one
+ * GPU (the segments of one call run side by side).  num_maps >= 2; all pointers 16-byte
+ * aligned; head_size must be 128.
+ */
+int gdn_segment_chain_all_launch(const float* maps, int num_maps, float* start_states,
+                                 float* final_state, int num_v_heads, int head_size,
+                                 void* stream);
+
+/*
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
  * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory

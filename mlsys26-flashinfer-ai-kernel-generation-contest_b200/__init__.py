@@ -20,11 +20,12 @@ The directory name is not a Python identifier; import it with
 from ._lib import LIB, LIB_PATH, GDNError, device_error  # noqa: F401
 from .decode import gdn_decode, kernel as decode_kernel  # noqa: F401
 from .prefill import (chunk_gated_delta_rule, gdn_prefill, gdn_prefill_recurrent,  # noqa: F401
-                      kernel as prefill_kernel, workspace_bytes)
+                      gdn_prefill_segmented, kernel as prefill_kernel, workspace_bytes)
 from .mtp import gdn_mtp, kernel as mtp_kernel  # noqa: F401
 from . import decode, mtp, prefill, sharding, workloads  # noqa: F401
 
-__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "gdn_mtp", "decode_kernel",
+__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_recurrent", "gdn_prefill_segmented",
+           "gdn_mtp", "decode_kernel",
            "mtp_kernel", "chunk_gated_delta_rule",
            "prefill_kernel", "workloads", "sharding", "GDNError", "LIB", "LIB_PATH", "workspace_bytes",
            "device_error"]

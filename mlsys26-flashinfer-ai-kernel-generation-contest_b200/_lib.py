@@ -54,6 +54,7 @@ SIGNATURES = {
                                     _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "gdn_segment_outputs_launch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gdn_segment_chain_launch": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp]),
+    "gdn_segment_chain_all_launch": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_device_error": (_i, [_i]),
     "gdn_selftest_bounded_wait": (_i, [ctypes.c_uint, _i, _vp, _vp]),
 }

@@ -228,7 +228,8 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 __global__ void __launch_bounds__(kChainThreads, 1)
     segment_chain_kernel(const float* __restrict__ maps, int rank, int HV,
-                         float* __restrict__ start_out, float* __restrict__ final_out) {
+                         float* __restrict__ start_out, float* __restrict__ final_out,
+                         float* __restrict__ starts_all) {
   extern __shared__ __align__(16) float csm[];
   float* S = csm + 2 * kD * kD;  // [row][kSLd]
   const int h = blockIdx.y, r0 = kChainRows * blockIdx.x;
@@ -249,11 +250,13 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     cp_async_commit();
   };
   prefetch(1, csm);
-  // S = B_0 (this CTA's rows)
+  // S = B_0 (this CTA's rows): the start state of segment 1
   for (int i = tid; i < kChainRows * kD / 4; i += kChainThreads) {
     const int r = i >> 5, c4 = i & 31;
-    *reinterpret_cast<float4*>(S + r * kSLd + 4 * c4) =
-        __ldg(reinterpret_cast<const float4*>(B(0) + (size_t)(r0 + r) * kD) + c4);
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(B(0) + (size_t)(r0 + r) * kD) + c4);
+    *reinterpret_cast<float4*>(S + r * kSLd + 4 * c4) = b0;
+    if (starts_all != nullptr)
+      reinterpret_cast<float4*>(starts_all + ((size_t)h * kD + r0 + r) * kD)[c4] = b0;
   }
   for (int m = 1; m <= rank; ++m) {
     const float* As = csm + ((m - 1) & 1) * kD * kD;
@@ -320,6 +323,15 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       float* d = S + (4 * rq + i) * kSLd;
       *reinterpret_cast<float4*>(d + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
       *reinterpret_cast<float4*>(d + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    }
+    if (starts_all != nullptr) {  // S is now the start state of segment m + 1
+      float* base = starts_all + (size_t)m * HV * kD * kD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float* dst = base + ((size_t)h * kD + r0 + 4 * rq + i) * kD;
+        *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      }
     }
   }
   // start state = S (rows of this CTA)
@@ -404,6 +416,34 @@ extern "C" int gdn_segment_chain_launch(const float* maps, int num_maps, int ran
   }
   const dim3 grid(kD / kChainRows, (unsigned)num_v_heads);
   segment_chain_kernel<<<grid, kChainThreads, kChainSmem, static_cast<cudaStream_t>(stream)>>>(
-      maps, rank, num_v_heads, start_state, final_state);
+      maps, rank, num_v_heads, start_state, final_state, nullptr);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+extern "C" int gdn_segment_chain_all_launch(const float* maps, int num_maps, float* start_states,
+                                            float* final_state, int num_v_heads, int head_size,
+                                            void* stream) {
+  if (num_v_heads <= 0 || num_v_heads > 65535 || num_maps < 2) return GDN_ERR_INVALID_ARGUMENT;
+  if (head_size != kD) return GDN_ERR_UNSUPPORTED;
+  if (maps == nullptr || start_states == nullptr || final_state == nullptr)
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (misaligned(maps, 16) || misaligned(start_states, 16) || misaligned(final_state, 16))
+    return GDN_ERR_INVALID_ARGUMENT;
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(segment_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kChainSmem) != cudaSuccess)
+      return GDN_ERR_LAUNCH;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  // one pass through every map: segment s's start state into start_states[s - 1] as the
+  // chain reaches it, the last segment's final state into final_state
+  const int rank = num_maps - 1;
+  float* last_start = start_states + (size_t)(rank - 1) * num_v_heads * kD * kD;
+  const dim3 grid(kD / kChainRows, (unsigned)num_v_heads);
+  segment_chain_kernel<<<grid, kChainThreads, kChainSmem, static_cast<cudaStream_t>(stream)>>>(
+      maps, rank, num_v_heads, last_start, final_state, start_states);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

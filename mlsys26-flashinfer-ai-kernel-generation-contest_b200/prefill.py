@@ -12,6 +12,7 @@ or int64), so the call never synchronises the host.
 """
 from __future__ import annotations
 
+import functools
 import threading
 
 import torch
@@ -190,6 +191,64 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
     if ns is not new_state:
         new_state.copy_(ns)
     return output, new_state
+
+
+@functools.lru_cache(maxsize=64)
+def _segment_layout(total_tokens: int, segments: int, device: torch.device):
+    from . import sharding
+    return sharding.segmented_layout(total_tokens, segments, device)
+
+
+def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=None,
+                          new_state=None, *, segments: int = 0, use_qk_l2norm: bool = False):
+    """Prefill of ONE sequence whose v-heads alone leave most SMs idle (a sequence sharded
+    by q/k-head group over several GPUs, or a model with few heads per GPU), split into
+    token segments that run side by side in a single prefill call: segment 0 from the
+    initial state, every later segment twice, from the identity with v = 0 (its state map
+    A and outputs o^I) and from a zero state (B and o^0).  Over a segment the recurrence
+    is affine in its start state, so the library's chain kernel then composes the maps and
+    its output kernel forms o = S_start o^I + o^0 for every later segment.  The serial
+    chunk chain shrinks from the whole sequence to one segment; there is no collective.
+
+    q, k [T, HQ, 128], v [T, HV, 128], a, b [T, HV] bf16; state [1, HV, 128, 128] fp32 or
+    None; returns (output [T, HV, 128] bf16, new_state [1, HV, 128, 128] fp32).
+    `segments` = 0 picks the largest count whose 2 S - 1 runs fit on the SMs at once
+    (sharding.local_segments); 1 is an ordinary gdn_prefill call.  The outputs of the
+    later segments carry one more bf16 rounding (of o^I); the final state is fp32
+    throughout."""
+    from . import sharding
+    dev = C.cuda_device(q)
+    C.tensor("v", v, torch.bfloat16, 3, dev, strided=True)
+    T, HV = q.shape[0], v.shape[1]
+    if state is not None:
+        C.tensor("state", state, torch.float32, 4, dev, strided=True)
+        C.shape("state", state, (1, HV, 128, 128))
+    for name, x, shp, dt in (("output", output, (T, HV, 128), torch.bfloat16),
+                             ("new_state", new_state, (1, HV, 128, 128), torch.float32)):
+        if x is not None:
+            C.tensor(name, x, dt, len(shp), dev, strided=True)
+            C.shape(name, x, shp)
+    S = segments if segments > 0 else sharding.local_segments(HV, T)
+    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    if S <= 1 or T == 0:
+        return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu, scale, output,
+                           new_state, use_qk_l2norm=use_qk_l2norm)
+    layout = _segment_layout(T, S, dev)
+    inp = {"q": q, "k": k, "v": v, "state": state, "a": a, "b": b}
+    run = sharding.segmented_inputs(inp, layout)
+    o_runs, f_runs = gdn_prefill(run["q"], run["k"], run["v"], run["state"], A_log, run["a"],
+                                 dt_bias, run["b"], run["cu_seqlens"], scale,
+                                 use_qk_l2norm=use_qk_l2norm)
+    # the assembly kernels write dense, 16-byte aligned results
+    dense = lambda x: x is not None and x.is_contiguous() and x.data_ptr() % 16 == 0  # noqa: E731
+    out, fin = sharding.segmented_finish(layout, o_runs, f_runs,
+                                         output if dense(output) else None,
+                                         new_state if dense(new_state) else None)
+    if output is not None and out is not output:
+        out = output.copy_(out)
+    if new_state is not None and fin is not new_state:
+        fin = new_state.copy_(fin)
+    return out, fin
 
 
 def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):

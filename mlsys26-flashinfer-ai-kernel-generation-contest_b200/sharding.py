@@ -339,3 +339,123 @@ def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
         out, fin = segment_assemble(stacked, r, maps[r][2], maps[r][3])
         parts.append(out)
     return torch.cat(parts, dim=0), fin
+
+
+# --------------------------------------------------------------------------------------
+# The same scan inside ONE call, for a single sequence whose (v-head) work leaves most SMs
+# idle (few heads per GPU, e.g. one sequence sharded by q/k-head group over 4 or 8 GPUs):
+# the segments run side by side as the sequences of one prefill call (segment 0 from the
+# initial state, every later segment twice: from the identity with v = 0 and from zero),
+# and the maps are chained on the same GPU afterwards.  No collective: the serial chain
+# falls from the whole sequence to one segment, paid for with twice the work on SMs that
+# would otherwise be idle.
+
+
+def local_segments(num_v_heads: int, total_tokens: int, sms: int = 148,
+                   ctas_per_head: int = 4, align: int = 64) -> int:
+    """Largest segment count S whose 2 S - 1 runs of one sequence (ctas_per_head CTAs per
+    v-head and run: the split state kernel's four 32-row v-blocks) all fit on `sms` SMs at
+    once, with at least one 64-token chunk per segment; 1 when segmenting cannot help."""
+    per_run = max(1, num_v_heads * ctas_per_head)
+    s = max(1, (sms // per_run + 1) // 2)
+    chunks = (total_tokens + align - 1) // align
+    return max(1, min(s, chunks))
+
+
+def segmented_layout(total_tokens: int, segments: int, device
+                     ) -> Tuple[List[Tuple[int, int]], torch.Tensor]:
+    """For one sequence of `total_tokens` tokens in `segments` equal segments (on 64-token
+    chunk boundaries): (bounds, cu_seqlens int32 of the 2 S - 1 runs of one call).  Run 0
+    is segment 0; runs 2 s - 1 and 2 s are segment s from the identity (v = 0) and from
+    zero.  `segments` is capped at the number of chunks, so that no segment is empty (an
+    empty run would return a zero state, not the identity map)."""
+    segments = max(1, min(segments, (total_tokens + 63) // 64))
+    bounds = segment_bounds(total_tokens, segments, first_weight=1)
+    cu = [0]
+    for s, (lo, hi) in enumerate(bounds):
+        for _ in range(1 if s == 0 else 2):
+            cu.append(cu[-1] + hi - lo)
+    return bounds, torch.tensor(cu, dtype=torch.int32, device=device)
+
+
+def segmented_inputs(inp: Dict[str, torch.Tensor], layout) -> Dict[str, torch.Tensor]:
+    """The one-call problem of `layout` (segmented_layout) built from a one-sequence
+    problem: q, k, a, b of every run, v of every run with zeros for the identity runs, and
+    the initial states [state or 0; I; 0; I; 0; ...] -- one concatenation per tensor."""
+    bounds, cu = layout
+    HV = inp["v"].shape[1]
+    dev = inp["v"].device
+    runs = [(lo, hi, s > 0 and r == 0) for s, (lo, hi) in enumerate(bounds)
+            for r in range(1 if s == 0 else 2)]
+    out = dict(inp)
+    for key in ("q", "k", "a", "b"):
+        x = inp[key]
+        out[key] = torch.cat([x[lo:hi] for lo, hi, _ in runs])
+    v = inp["v"]
+    longest = max(hi - lo for lo, hi in bounds)
+    zero_v = torch.zeros((longest,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev)
+    out["v"] = torch.cat([zero_v[:hi - lo] if ident else v[lo:hi] for lo, hi, ident in runs])
+    n = len(bounds)
+    first = inp["state"][0:1] if inp.get("state") is not None else \
+        torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
+    eye = torch.eye(128, dtype=torch.float32, device=dev).expand(1, HV, 128, 128)
+    zero = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
+    out["state"] = torch.cat([first] + [eye, zero] * (n - 1))
+    out["cu_seqlens"] = cu
+    return out
+
+
+def segmented_finish(layout, out_runs: torch.Tensor, fin_runs: torch.Tensor,
+                     output: torch.Tensor = None, final: torch.Tensor = None
+                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The sequence's output [T, HV, 128] and final state [1, HV, 128, 128] from the one
+    call's outputs and final states: segment 0's as they are, every later segment's from
+    its chained start state.  On the GPU: one pass of the library's chain kernel for every
+    start state (gdn_segment_chain_all_launch) and its output kernel per segment; on the
+    CPU the same algebra in torch."""
+    bounds = layout[0]
+    n = len(bounds)
+    starts = [0]
+    for s, (lo, hi) in enumerate(bounds):
+        for _ in range(1 if s == 0 else 2):
+            starts.append(starts[-1] + hi - lo)
+    T = bounds[-1][1]
+    HV = out_runs.shape[1]
+    if output is None:
+        output = torch.empty((T,) + tuple(out_runs.shape[1:]), dtype=out_runs.dtype,
+                             device=out_runs.device)
+    lo0, hi0 = bounds[0]
+    output[lo0:hi0].copy_(out_runs[starts[0]:starts[1]])
+    if n == 1:
+        fin = fin_runs[0:1]
+        return output, (final.copy_(fin) if final is not None else fin)
+    maps = torch.empty((n, 2) + tuple(fin_runs.shape[1:]), dtype=torch.float32,
+                       device=fin_runs.device)
+    maps[0, 0].zero_()
+    maps[0, 1] = fin_runs[0]
+    maps[1:, 0] = fin_runs[1::2]
+    maps[1:, 1] = fin_runs[2::2]
+    runs = [(out_runs[starts[2 * s - 1]:starts[2 * s]], out_runs[starts[2 * s]:starts[2 * s + 1]])
+            for s in range(1, n)]
+    if not maps.is_cuda:
+        fin = None
+        for s in range(1, n):
+            lo, hi = bounds[s]
+            _, fin = segment_assemble(maps, s, runs[s - 1][0], runs[s - 1][1],
+                                      out=output[lo:hi])
+        return output, (final.copy_(fin) if final is not None else fin)
+    from ._checks import stream_handle
+    from ._lib import LIB, check
+    stream = stream_handle(maps.device)
+    st = torch.empty((n - 1, HV, 128, 128), dtype=torch.float32, device=maps.device)
+    fin = final if final is not None else torch.empty(1, HV, 128, 128, dtype=torch.float32,
+                                                      device=maps.device)
+    check("gdn_segment_chain_all_launch", LIB.gdn_segment_chain_all_launch(
+        maps.data_ptr(), n, st.data_ptr(), fin.data_ptr(), HV, 128, stream))
+    for s in range(1, n):
+        lo, hi = bounds[s]
+        o_id, o_zero = runs[s - 1]
+        check("gdn_segment_outputs_launch", LIB.gdn_segment_outputs_launch(
+            o_id.data_ptr(), o_zero.data_ptr(), st[s - 1].data_ptr(), output[lo:hi].data_ptr(),
+            hi - lo, HV, 128, stream))
+    return output, fin

@@ -194,3 +194,39 @@ def test_p2_segment_scan_vs_oracle(cuda, world):
     ro, rs = p2_oracle()
     assert_parity(out, fin, ro, rs, what=f"P2 segment scan x{world}")
     assert pkg.device_error() == 0
+
+
+def test_p2_one_call_segmented_vs_oracle(cuda):
+    """gdn_prefill_segmented on P2's six sampled v-heads (three segments side by side in
+    one call, the maps chained on the GPU afterwards) against the oracle's unsplit scan of
+    all 32,768 tokens."""
+    pkg = load_pkg()
+    sub, _ = head_subset(p2_inputs(), P2_QK_HEADS)
+    d = to(sub, cuda)
+    assert pkg.sharding.local_segments(d["v"].shape[1], d["q"].shape[0]) == 3
+    out, fin = pkg.gdn_prefill_segmented(d["q"], d["k"], d["v"], d["state"], d["A_log"],
+                                         d["a"], d["dt_bias"], d["b"], d["scale"],
+                                         use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    ro, rs = p2_oracle()
+    assert_parity(out, fin, ro, rs, what="P2 one-call segmented")
+    assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("qk_heads,segments", [(4, 2), (2, 5)])
+def test_p2_head_group_segmented_vs_unsplit(cuda, qk_heads, segments):
+    """The multi-GPU P2 plan's per-rank call (a q/k-head group of 4 or 2 heads, i.e. 8 or
+    4 v-heads, over 4 or 8 GPUs): segmented in one call, against the unsplit call."""
+    pkg = load_pkg()
+    sh = pkg.sharding.prefill_head_shard(to(p2_inputs(), cuda), 0, qk_heads)
+    assert pkg.sharding.local_segments(sh["v"].shape[1], sh["q"].shape[0]) == segments
+    keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")
+    ro, rs = pkg.gdn_prefill(*[sh[k_] for k_ in keys], use_qk_l2norm=True)
+    out = torch.full_like(ro, float("nan"))
+    fin = torch.full_like(rs, float("nan"))
+    o, f = pkg.gdn_prefill_segmented(sh["q"], sh["k"], sh["v"], sh["state"], sh["A_log"],
+                                     sh["a"], sh["dt_bias"], sh["b"], sh["scale"], out, fin,
+                                     use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert o.data_ptr() == out.data_ptr() and f.data_ptr() == fin.data_ptr()
+    assert_parity(o, f, ro.cpu(), rs.cpu(), what=f"{qk_heads} q/k heads in {segments} segments")

@@ -118,3 +118,30 @@ def test_segment_chain_kernel_rejects_bad_arguments(cuda):
     assert lib.gdn_segment_chain_launch(p[0], 2, 2, p[1], p[2], 1, 128, None) == -1  # rank >= maps
     assert lib.gdn_segment_chain_launch(p[0], 2, 1, p[1], p[2], 1, 64, None) == -2   # head_size
     assert lib.gdn_segment_chain_launch(p[0] + 4, 2, 1, p[1], p[2], 1, 128, None) == -1
+
+
+@pytest.mark.parametrize("maps_n,hv", [(2, 3), (5, 4), (8, 32)])
+def test_segment_chain_all_matches_per_segment_chains(cuda, maps_n, hv):
+    """gdn_segment_chain_all_launch (every segment's start state in one pass) against one
+    gdn_segment_chain_launch per segment: the same fp32 arithmetic, bit for bit."""
+    pkg = load_pkg()
+    from importlib import import_module
+    lib = import_module(pkg.__name__ + "._lib").LIB
+    g = torch.Generator().manual_seed(maps_n * 10 + hv)
+    maps = (torch.randn(maps_n, 2, hv, 128, 128, generator=g) * 0.05).to(cuda)
+    maps[:, 0] += torch.eye(128, device=cuda) * 0.5
+    starts = torch.empty(maps_n - 1, hv, 128, 128, device=cuda)
+    fin = torch.empty(1, hv, 128, 128, device=cuda)
+    assert lib.gdn_segment_chain_all_launch(maps.data_ptr(), maps_n, starts.data_ptr(),
+                                            fin.data_ptr(), hv, 128, None) == 0
+    for r in range(1, maps_n):
+        st = torch.empty(1, hv, 128, 128, device=cuda)
+        fr = torch.empty(1, hv, 128, 128, device=cuda)
+        assert lib.gdn_segment_chain_launch(maps.data_ptr(), maps_n, r, st.data_ptr(),
+                                            fr.data_ptr(), hv, 128, None) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(st[0], starts[r - 1]), r
+        if r == maps_n - 1:
+            assert torch.equal(fr, fin)
+    assert lib.gdn_segment_chain_all_launch(maps.data_ptr(), 1, starts.data_ptr(),
+                                            fin.data_ptr(), hv, 128, None) == -1

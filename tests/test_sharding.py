@@ -128,3 +128,37 @@ def test_segment_scan_matches_unsegmented_oracle(world):
     out, fin = pkg.sharding.segment_scan_local(_oracle_run, short, 3)
     assert out.shape == ro.shape
     assert O.state_rel_err(fin, rs) < 1e-5
+
+
+@pytest.mark.parametrize("T,segments", [(200, 3), (130, 2), (64, 4), (1000, 5)])
+def test_one_call_segmented_scan_matches_unsplit(T, segments):
+    """One sequence laid out as the 2 S - 1 runs of one call (segment 0 from the initial
+    state; every later segment from the identity with v = 0 and from zero), run by the
+    oracle as one multi-sequence call and assembled: the unsplit result."""
+    pkg = load_pkg()
+    S = pkg.sharding
+    from oracle import gdn_oracle as O
+    inp = pkg.workloads.prefill_inputs([T], hq=2, hv=4, seed=T + segments)
+    q, k = O.l2norm(inp["q"]), O.l2norm(inp["k"])
+    ro, rs = O.prefill(q, k, inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"],
+                       inp["b"], inp["cu_seqlens"], inp["scale"])
+    layout = S.segmented_layout(T, segments, "cpu")
+    assert len(layout[0]) == min(segments, (T + 63) // 64)
+    run = S.segmented_inputs(dict(inp, q=q, k=k), layout)
+    assert run["cu_seqlens"].numel() == 2 * len(layout[0])
+    o_runs, f_runs = O.prefill(run["q"], run["k"], run["v"], run["state"], inp["A_log"],
+                               run["a"], inp["dt_bias"], run["b"], run["cu_seqlens"],
+                               inp["scale"])
+    out, fin = S.segmented_finish(layout, o_runs, f_runs)
+    ok, frac, mabs, _ = O.flashinfer_allclose(out, ro, 2e-2, 2e-2)
+    assert ok, (frac, mabs)
+    assert O.state_rel_err(fin, rs) < 1e-5
+
+
+def test_local_segment_count():
+    S = load_pkg().sharding
+    assert S.local_segments(32, 32768) == 1   # 128 CTAs per run: no room for a second
+    assert S.local_segments(16, 32768) == 1
+    assert S.local_segments(8, 32768) == 2    # 3 runs x 32 CTAs
+    assert S.local_segments(4, 32768) == 5    # 9 runs x 16 CTAs
+    assert S.local_segments(4, 100) == 2      # capped at the number of chunks
