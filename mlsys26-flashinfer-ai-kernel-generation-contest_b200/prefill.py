@@ -194,9 +194,11 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
 
 
 @functools.lru_cache(maxsize=64)
-def _segment_layout(total_tokens: int, segments: int, device: torch.device):
+def _segment_layout(total_tokens: int, segments: int, num_v_heads: int, device: torch.device):
+    """(layout, state template) of a segmented call; both are read-only for the calls."""
     from . import sharding
-    return sharding.segmented_layout(total_tokens, segments, device)
+    layout = sharding.segmented_layout(total_tokens, segments, device)
+    return layout, sharding.state_template(len(layout[0]), num_v_heads, device)
 
 
 def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=None,
@@ -233,17 +235,21 @@ def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=No
     if S <= 1 or T == 0:
         return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu, scale, output,
                            new_state, use_qk_l2norm=use_qk_l2norm)
-    layout = _segment_layout(T, S, dev)
+    layout, template = _segment_layout(T, S, HV, dev)
+    n = len(layout[0])
     inp = {"q": q, "k": k, "v": v, "state": state, "a": a, "b": b}
-    run = sharding.segmented_inputs(inp, layout)
+    run = sharding.segmented_inputs(inp, layout, template)
+    # the runs' final states land in the chain kernel's map tensor (entry 0 unused)
+    maps = torch.empty(n, 2, HV, 128, 128, dtype=torch.float32, device=dev)
     o_runs, f_runs = gdn_prefill(run["q"], run["k"], run["v"], run["state"], A_log, run["a"],
-                                 dt_bias, run["b"], run["cu_seqlens"], scale,
+                                 dt_bias, run["b"], run["cu_seqlens"], scale, None,
+                                 maps.view(2 * n, HV, 128, 128)[1:],
                                  use_qk_l2norm=use_qk_l2norm)
     # the assembly kernels write dense, 16-byte aligned results
     dense = lambda x: x is not None and x.is_contiguous() and x.data_ptr() % 16 == 0  # noqa: E731
     out, fin = sharding.segmented_finish(layout, o_runs, f_runs,
                                          output if dense(output) else None,
-                                         new_state if dense(new_state) else None)
+                                         new_state if dense(new_state) else None, maps=maps)
     if output is not None and out is not output:
         out = output.copy_(out)
     if new_state is not None and fin is not new_state:

@@ -378,10 +378,13 @@ def segmented_layout(total_tokens: int, segments: int, device
     return bounds, torch.tensor(cu, dtype=torch.int32, device=device)
 
 
-def segmented_inputs(inp: Dict[str, torch.Tensor], layout) -> Dict[str, torch.Tensor]:
+def segmented_inputs(inp: Dict[str, torch.Tensor], layout, template: torch.Tensor = None
+                     ) -> Dict[str, torch.Tensor]:
     """The one-call problem of `layout` (segmented_layout) built from a one-sequence
     problem: q, k, a, b of every run, v of every run with zeros for the identity runs, and
-    the initial states [state or 0; I; 0; I; 0; ...] -- one concatenation per tensor."""
+    the initial states [state or 0; I; 0; I; 0; ...] -- one concatenation per tensor.
+    `template` may hold the constant part [0; I; 0; I; 0; ...] (2 S - 1 states; its first
+    entry is overwritten by nothing and only used when there is no initial state)."""
     bounds, cu = layout
     HV = inp["v"].shape[1]
     dev = inp["v"].device
@@ -393,26 +396,36 @@ def segmented_inputs(inp: Dict[str, torch.Tensor], layout) -> Dict[str, torch.Te
         out[key] = torch.cat([x[lo:hi] for lo, hi, _ in runs])
     v = inp["v"]
     longest = max(hi - lo for lo, hi in bounds)
-    zero_v = torch.zeros((longest,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev)
+    zero_v = v.new_zeros((longest,) + tuple(v.shape[1:]))
     out["v"] = torch.cat([zero_v[:hi - lo] if ident else v[lo:hi] for lo, hi, ident in runs])
-    n = len(bounds)
-    first = inp["state"][0:1] if inp.get("state") is not None else \
-        torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
-    eye = torch.eye(128, dtype=torch.float32, device=dev).expand(1, HV, 128, 128)
-    zero = torch.zeros(1, HV, 128, 128, dtype=torch.float32, device=dev)
-    out["state"] = torch.cat([first] + [eye, zero] * (n - 1))
+    if template is None:
+        template = state_template(len(bounds), HV, dev)
+    if inp.get("state") is None:
+        out["state"] = template
+    else:
+        out["state"] = torch.cat([inp["state"][0:1], template[1:]])
     out["cu_seqlens"] = cu
     return out
 
 
+def state_template(segments: int, num_v_heads: int, device) -> torch.Tensor:
+    """Initial states [0; I; 0; I; 0; ...] of the 2 S - 1 runs of a segmented call."""
+    t = torch.zeros(2 * segments - 1, num_v_heads, 128, 128, dtype=torch.float32,
+                    device=device)
+    t[1::2] = torch.eye(128, dtype=torch.float32, device=device)
+    return t
+
+
 def segmented_finish(layout, out_runs: torch.Tensor, fin_runs: torch.Tensor,
-                     output: torch.Tensor = None, final: torch.Tensor = None
-                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+                     output: torch.Tensor = None, final: torch.Tensor = None,
+                     maps: torch.Tensor = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """The sequence's output [T, HV, 128] and final state [1, HV, 128, 128] from the one
     call's outputs and final states: segment 0's as they are, every later segment's from
     its chained start state.  On the GPU: one pass of the library's chain kernel for every
     start state (gdn_segment_chain_all_launch) and its output kernel per segment; on the
-    CPU the same algebra in torch."""
+    CPU the same algebra in torch.  `maps` may be the [S, 2, HV, 128, 128] tensor whose
+    flattened entries 1 .. 2 S - 1 are fin_runs (the call wrote its final states there):
+    then the maps need no copy."""
     bounds = layout[0]
     n = len(bounds)
     starts = [0]
@@ -429,15 +442,15 @@ def segmented_finish(layout, out_runs: torch.Tensor, fin_runs: torch.Tensor,
     if n == 1:
         fin = fin_runs[0:1]
         return output, (final.copy_(fin) if final is not None else fin)
-    maps = torch.empty((n, 2) + tuple(fin_runs.shape[1:]), dtype=torch.float32,
-                       device=fin_runs.device)
-    maps[0, 0].zero_()
-    maps[0, 1] = fin_runs[0]
-    maps[1:, 0] = fin_runs[1::2]
-    maps[1:, 1] = fin_runs[2::2]
+    if maps is None:
+        maps = torch.empty((n, 2) + tuple(fin_runs.shape[1:]), dtype=torch.float32,
+                           device=fin_runs.device)
+        maps.view(2 * n, *fin_runs.shape[1:])[1:].copy_(fin_runs)
     runs = [(out_runs[starts[2 * s - 1]:starts[2 * s]], out_runs[starts[2 * s]:starts[2 * s + 1]])
             for s in range(1, n)]
     if not maps.is_cuda:
+        maps = maps.clone()
+        maps[0, 0].zero_()
         fin = None
         for s in range(1, n):
             lo, hi = bounds[s]
