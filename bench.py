@@ -808,10 +808,15 @@ def measure_mtp(pkg, dist, batch, steps, warmup, dev, with_e2e=True, graphs=True
     return res
 
 
-def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True):
+def measure_prefill(pkg, dist, cfg_name, steps, warmup, dev, shard=None, with_e2e=True,
+                    graphs=True):
     w = PrefillWork(pkg, cfg_name, dev, seed=0, shard=shard, dist=dist)
+    # replayed from a CUDA graph like decode (the cross-GPU segment scan, whose step holds
+    # an NCCL all-gather, runs eagerly)
+    fn, keep = graph_steps(w, 1) if (graphs and not w.segments) else (w.step, None)
     with ClockSampler(dev.index) as clk:
-        ms, kern_ms = time_steps(w.step, steps, warmup, dist)
+        ms, kern_ms = time_steps(fn, steps, warmup, dist)
+    del keep
     tokens_all = w.tokens
     if dist.pg:
         t = torch.tensor([w.tokens], dtype=torch.float64, device=dev)
@@ -881,7 +886,9 @@ def workload_config(W, kind, param, world, args):
     lens = W.draw_seqlens(cfg.n, cfg.lo, cfg.hi, 0)
     return {"workload": f"GDN prefill {param}", "tokens": int(sum(lens)),
             "parallelism": plan_text(plan_kind(W, param, world, args.prefill_plan), world),
-            "l2": "inputs > L2"}
+            "l2": "inputs > L2",
+            "launch": launch if plan_kind(W, param, world, args.prefill_plan) != "segments"
+            else "eager"}
 
 
 def metric_of(kind):
@@ -917,7 +924,8 @@ def run_ours(args, dist):
         value, bound, scaling = round(r["value"], 2), "hbm", "weak"
     else:
         shard = prefill_plan(pkg, param, dist, args.prefill_plan)
-        r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard)
+        r = measure_prefill(pkg, dist, param, args.steps, args.warmup, dev, shard=shard,
+                            graphs=not args.no_graphs)
         value, bound = round(r["value"], 1), "tensor"
         scaling = "strong" if dist.world > 1 else "weak"
     line.update({
@@ -953,7 +961,7 @@ def run_ours(args, dist):
             nm = label.split("_")[0]
             shard = prefill_plan(pkg, nm, dist, force)
             r = measure_prefill(pkg, dist, nm, max(3, min(args.steps, 10)), 3, dev, shard=shard,
-                                with_e2e=False)
+                                with_e2e=False, graphs=not args.no_graphs)
             extra[label] = {"tokens_per_s": round(r["value"], 1), "ms_per_step": round(r["ms"], 4),
                             "tflops": round(r["tflops"], 2), "tokens": r["tokens_all"],
                             "parallelism": plan_text(shard, dist.world)
@@ -1033,7 +1041,8 @@ def main():
                     help="batch slices of the pipelined end-to-end decode step (default %d)"
                          % E2E_SLICES)
     ap.add_argument("--no-graphs", action="store_true",
-                    help="launch decode / multi-token decode steps eagerly (default: CUDA graphs)")
+                    help="launch decode, multi-token decode and prefill steps eagerly (default: "
+                         "CUDA graph replay)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps

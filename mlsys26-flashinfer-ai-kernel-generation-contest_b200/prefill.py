@@ -231,10 +231,12 @@ def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=No
             C.tensor(name, x, dt, len(shp), dev, strided=True)
             C.shape(name, x, shp)
     S = segments if segments > 0 else sharding.local_segments(HV, T)
-    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
     if S <= 1 or T == 0:
+        cu = _segment_layout(T, 1, HV, dev)[0][1]
         return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu, scale, output,
                            new_state, use_qk_l2norm=use_qk_l2norm)
+    # the layout lives on the device from the first call on (no host copy per call, so
+    # the call can be captured in a CUDA graph after a first eager call)
     layout, template = _segment_layout(T, S, HV, dev)
     n = len(layout[0])
     inp = {"q": q, "k": k, "v": v, "state": state, "a": a, "b": b}

@@ -67,3 +67,38 @@ def test_mtp_graph_replay_equals_eager(cuda):
     torch.cuda.synchronize()
     assert torch.equal(out, ref_out) and torch.equal(pool, ref_pool)
     assert torch.equal(inter, ref_inter)
+
+
+@pytest.mark.parametrize("kind", ["fused", "split", "segmented"])
+def test_prefill_graph_replay_equals_eager(cuda, kind):
+    """Prefill launched from a captured CUDA graph (how bench.py replays prefill steps):
+    the fused and split kernel families, and the one-call segmented scan of one sequence
+    (its input concatenations, the call, the chain and output kernels), bitwise the eager
+    results."""
+    pkg = load_pkg()
+    if kind == "segmented":
+        d = to(pkg.workloads.prefill_inputs([3000], hq=2, hv=4, seed=72), cuda)
+        args = [d[x] for x in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")]
+        out = torch.empty(3000, 4, 128, dtype=torch.bfloat16, device=cuda)
+        ns = torch.empty(1, 4, 128, 128, device=cuda)
+
+        def call(o=out, s=ns):
+            return pkg.gdn_prefill_segmented(*args, d["scale"], o, s, use_qk_l2norm=True)
+    else:
+        d = to(pkg.workloads.prefill_inputs([70, 0, 129, 300], seed=73), cuda)
+        args = [d[x] for x in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b",
+                               "cu_seqlens")]
+        out = torch.empty_like(d["v"])
+        ns = torch.empty_like(d["state"])
+
+        def call(o=out, s=ns):
+            return pkg.gdn_prefill(*args, d["scale"], o, s, use_qk_l2norm=True, kernel=kind)
+    g = _capture(call)
+    out.zero_()
+    ns.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    ro, rs = call(torch.empty_like(out), torch.empty_like(ns))
+    torch.cuda.synchronize()
+    assert torch.equal(out, ro) and torch.equal(ns, rs)
+    assert pkg.device_error() == 0
