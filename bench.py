@@ -388,11 +388,11 @@ class PrefillWork:
         self.tokens = T * head_frac
         self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
         self.launches = pkg.prefill.launches_per_call(T, N, self.inp["q"].shape[1], self.inp["v"].shape[1])
-        if self.local_segments > 1:  # the call of 2 S - 1 runs, then chain + outputs per segment
+        if self.local_segments > 1:  # the call of 2 S - 1 runs, one chain pass, S - 1 outputs
             runs = 2 * self.local_segments - 1
             self.launches = pkg.prefill.launches_per_call(
                 T * runs // self.local_segments, runs, self.inp["q"].shape[1],
-                self.inp["v"].shape[1]) + 2 * (self.local_segments - 1)
+                self.inp["v"].shape[1]) + self.local_segments
 
     def _init_segment(self, inp, world, rank, dist):
         """Segment `rank` of the single sequence.  Rank 0 runs it from the initial state;
