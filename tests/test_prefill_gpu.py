@@ -193,3 +193,28 @@ def test_recurrent_kernel_vs_oracle(cuda):
     torch.cuda.synchronize()
     ro, rs = oracle_prefill(inp, True)
     assert_parity(o, s, ro, rs, what="recurrent")
+
+
+_MANY = {}
+
+
+def _many_sequences():
+    """9,000 sequences of 0-5 tokens and their oracle result (computed once)."""
+    if not _MANY:
+        pkg = load_pkg()
+        g = torch.Generator().manual_seed(87)
+        lens = torch.randint(0, 6, (9000,), generator=g).tolist()
+        inp = pkg.workloads.prefill_inputs(lens, hq=1, hv=2, seed=88)
+        _MANY["v"] = (inp, oracle_prefill(inp, True))
+    return _MANY["v"]
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_more_sequences_than_the_longest_first_order_holds(cuda, kernel):
+    """9,000 short sequences (0-5 tokens): beyond the 8,192 the longest-first ordering
+    kernel sorts, so the CTAs take the sequences in their natural order; results unchanged."""
+    pkg = load_pkg()
+    inp, (ro, rs) = _many_sequences()
+    o, s = run(pkg, inp, True, cuda, kernel=kernel)
+    assert_parity(o, s, ro, rs, what=f"9000 sequences {kernel}")
+    assert pkg.device_error() == 0
