@@ -1022,6 +1022,54 @@ def run_reference(args, dist):
                     "d2h_bytes_per_step": 0}}
 
 
+class RankOnOneGpu:
+    """The slice of Dist a prefill share needs, for rank `rank` of `world` emulated on one
+    GPU (no process group: barriers and the max-over-ranks reduction are local)."""
+
+    def __init__(self, world, rank):
+        self.world, self.rank, self.local, self.pg = world, rank, 0, None
+
+    def barrier(self):
+        pass
+
+    def max(self, x):
+        return x
+
+
+def run_emulated_ranks(args):
+    """Each rank's share of a prefill config under the chosen multi-GPU plan, run on this
+    one GPU in turn (`--emulate-world N`, optionally `--emulate-rank r`): per-rank device
+    time, and the slowest rank's, which is the step a real N-GPU run would take without its
+    launch skew.  The cross-GPU segment plan needs its collective and is not emulated."""
+    pkg = importlib.import_module(PKG_NAME)
+    dev = torch.device("cuda", 0)
+    kind, param = WORKLOADS[args.workload]
+    if kind != "prefill":
+        raise SystemExit("--emulate-world applies to the prefill workloads")
+    world = args.emulate_world
+    ranks = [args.emulate_rank] if args.emulate_rank >= 0 else list(range(world))
+    per = {}
+    for r in ranks:
+        d = RankOnOneGpu(world, r)
+        shard = prefill_plan(pkg, param, d, args.prefill_plan)
+        if shard is not None and shard[0] == "segments":
+            raise SystemExit("the cross-GPU segment plan needs its all-gather: not emulated")
+        w = PrefillWork(pkg, param, dev, seed=0, shard=shard, dist=d)
+        fn, keep = graph_steps(w, 1) if not args.no_graphs else (w.step, None)
+        ms, _ = time_steps(fn, args.steps, args.warmup, d)
+        del keep
+        per[r] = {"ms_per_step": round(ms, 4), "local_segments": w.local_segments}
+    worst = max(v["ms_per_step"] for v in per.values())
+    return {"impl": "ours", "metric": "prefill ms per rank (ranks emulated on one GPU)",
+            "value": worst, "unit": "ms", "higher_is_better": False,
+            "emulated_world": world, "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": f"GDN prefill {param}",
+                       "parallelism": plan_text(plan_kind(pkg.workloads, param, world,
+                                                          args.prefill_plan), world),
+                       "launch": "eager" if args.no_graphs else "CUDA graph replay"},
+            "ranks": per}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1043,6 +1091,11 @@ def main():
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch decode, multi-token decode and prefill steps eagerly (default: "
                          "CUDA graph replay)")
+    ap.add_argument("--emulate-world", type=int, default=0,
+                    help="prefill workloads: run each rank's share of an N-GPU plan on this "
+                         "one GPU in turn and report per-rank times (not a bench line)")
+    ap.add_argument("--emulate-rank", type=int, default=-1,
+                    help="with --emulate-world: only this rank's share")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
@@ -1055,6 +1108,9 @@ def main():
     if not torch.cuda.is_available():
         print(json.dumps({"impl": "ours", "error": "no CUDA device"}), flush=True)
         sys.exit(1)
+    if args.emulate_world > 1:
+        print(json.dumps(run_emulated_ranks(args)), flush=True)
+        return
     dist.init("nccl")
     try:
         line = run_ours(args, dist)

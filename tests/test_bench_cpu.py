@@ -53,3 +53,18 @@ def test_reference_arm_process_never_maps_the_library():
                        timeout=240)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "MAPPED False False" in r.stdout
+
+
+def test_rank_shares_for_one_gpu_emulation():
+    """The per-rank shares the one-GPU emulation builds are the multi-GPU plan's."""
+    import importlib
+    B = load_bench()
+    pkg = importlib.import_module(PKG_NAME)
+    for r in range(8):
+        d = B.RankOnOneGpu(8, r)
+        assert d.max(1.5) == 1.5
+        plan = B.prefill_plan(pkg, "P3", d)
+        assert plan[0] == "heads" and plan[1:] == tuple(pkg.sharding.head_range(16, 8, r))
+        seqs = B.prefill_plan(pkg, "P3", d, "seqs")
+        assert seqs[0] == "seqs" and seqs[1] == pkg.sharding.lpt_assign(
+            pkg.workloads.draw_seqlens(64, 512, 8192, 0), 8)[r]
