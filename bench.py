@@ -380,7 +380,7 @@ class PrefillWork:
         N = len(lens)
         # one sequence whose v-heads leave most SMs idle (a head group of a multi-GPU plan):
         # its token segments run side by side in one call (gdn_prefill_segmented)
-        self.local_segments = pkg.sharding.local_segments(self.inp["v"].shape[1], T) \
+        self.local_segments = pkg.prefill.segments_auto(T, self.inp["v"].shape[1]) \
             if (shard is not None and N == 1) else 1
         self.out = torch.empty(T, self.inp["v"].shape[1], 128, dtype=torch.bfloat16, device=dev)
         self.ns = torch.empty(N, self.inp["v"].shape[1], 128, 128, dtype=torch.float32, device=dev)
@@ -388,11 +388,8 @@ class PrefillWork:
         self.tokens = T * head_frac
         self.flops = T * W.prefill_flops_per_token(inp["q"].shape[1], inp["v"].shape[1])
         self.launches = pkg.prefill.launches_per_call(T, N, self.inp["q"].shape[1], self.inp["v"].shape[1])
-        if self.local_segments > 1:  # the call of 2 S - 1 runs, one chain pass, S - 1 outputs
-            runs = 2 * self.local_segments - 1
-            self.launches = pkg.prefill.launches_per_call(
-                T * runs // self.local_segments, runs, self.inp["q"].shape[1],
-                self.inp["v"].shape[1]) + self.local_segments
+        if self.local_segments > 1:  # the call of 2 S - 1 runs, one chain pass, one output pass
+            self.launches = pkg.prefill.segmented_launches(self.local_segments)
 
     def _init_segment(self, inp, world, rank, dist):
         """Segment `rank` of the single sequence.  Rank 0 runs it from the initial state;

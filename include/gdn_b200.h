@@ -364,6 +364,39 @@ int gdn_segment_chain_all_launch(const float* maps, int num_maps, float* start_s
                                  void* stream);
 
 /*
+ * Prefill of ONE sequence as token segments that run side by side (no counterpart in the
+ * reference, whose prefill walks each sequence's chunks in order,
+ * gdn_prefill/solution/triton/kernel.py:122-247).  For a sequence whose v-heads alone
+ * leave most SMs idle (one sequence of a model sharded by q/k-head group over GPUs), the
+ * total_tokens tokens are cut into S segments on 64-token chunk boundaries; one launch of
+ * the split kernels runs segment 0 from `state` and every later segment twice (from zero,
+ * and from the identity with v = 0), reading the tokens in place; the state-map chain and
+ * the output kernel (see gdn_segment_chain_launch / gdn_segment_outputs_launch) then give
+ * every segment's start state, the outputs o = S_start o^I + o^0 and the final state.
+ * Same arguments and meaning as gdn_prefill_launch_strided for one sequence
+ * (cu_seqlens = [0, total_tokens]): q, k [total_tokens, num_q_heads, 128], v
+ * [total_tokens, num_v_heads, 128], a, b [total_tokens, num_v_heads] bf16 with the given
+ * token strides (elements; q / k / v rows 16-byte aligned), state / new_state
+ * [1, num_v_heads, 128, 128] fp32 (state may be NULL = zero, and may equal new_state),
+ * output [total_tokens, num_v_heads, 128] bf16 dense and 16-byte aligned.  segments = 0
+ * picks the largest S whose 2 S - 1 runs (four state CTAs per run and v-head) fit on the
+ * SMs at once (gdn_prefill_segments_auto); S is capped at the number of chunks and at 64;
+ * S = 1 is an ordinary split-kernel prefill.  The outputs of later segments carry one more
+ * bf16 rounding (of o^I); the final state is fp32 throughout.  workspace (1024-byte
+ * aligned) of gdn_prefill_segmented_workspace_size bytes; asynchronous on `stream`.
+ */
+int gdn_prefill_segments_auto(int total_tokens, int num_v_heads);
+size_t gdn_prefill_segmented_workspace_size(int total_tokens, int num_v_heads, int segments);
+int gdn_prefill_segmented_launch(const void* q, const void* k, const void* v, const float* state,
+                                 const float* A_log, const void* a, const float* dt_bias,
+                                 const void* b, float scale, void* output, float* new_state,
+                                 int total_tokens, int num_q_heads, int num_k_heads,
+                                 int num_v_heads, int head_size, int use_qk_l2norm, int segments,
+                                 long long q_stride, long long k_stride, long long v_stride,
+                                 long long a_stride, long long b_stride, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
  * Diagnostics: synchronises the current device and returns the device-side
  * error bits recorded by the kernels since the last call (0 = none; 1 = a TMA
  * or bulk-copy wait ran out, 2 = a tensor-core wait ran out, 8 = a shared-memory

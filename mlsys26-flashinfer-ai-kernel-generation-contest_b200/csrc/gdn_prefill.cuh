@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <climits>
+
 #include "gdn_common.cuh"
 
 namespace gdn {
@@ -45,6 +47,16 @@ struct PrefillArgs {
   // token strides of q, k, v, a, b and the output (elements); dense when not set by the
   // caller (the entry point fills them in)
   RowStrides rs{};
+  // segmented call of one sequence (split kernels only; gdn_prefill_segmented_launch): the
+  // runs' token rows are virtual, T of them, over src_rows rows of q, k, v, a, b.  Rows
+  // r >= vsplit belong to the identity runs: they read input row r - vsplit + vsrc, take
+  // v = 0, start from the identity state and write their outputs to out_alt row
+  // r - vsplit.  Only runs n < state_runs start from `state`; the others from zero.
+  long long src_rows = 0;
+  long long vsplit = LLONG_MAX;
+  long long vsrc = 0;
+  void* out_alt = nullptr;
+  int state_runs = INT_MAX;
 };
 
 // Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).
@@ -73,6 +85,19 @@ bool make_tile_map_box(CUtensorMap* m, const void* base, int heads, long long ro
 size_t prefill_split_workspace(long long T, int num_seqs, int HV);
 cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t st);
 unsigned read_split_device_error(bool clear);
+
+// Segment-scan kernels (gdn_segment.cu).  The state-map chain over maps A_m =
+// maps[a0 + m as], B_m = maps[b0 + m bs] (matrices of HV heads): segment `rank`'s start
+// and final states, and with starts_all every segment s's start state at starts_all[s - 1].
+cudaError_t launch_segment_chain(const float* maps, int a0, int as, int b0, int bs, int rank,
+                                 int HV, float* start_out, float* final_out, float* starts_all,
+                                 cudaStream_t s);
+// Outputs of nseg segments in one launch (segment s: rows [off[s], off[s] + len[s]) of o^I,
+// o^0 and the output, start state start_states[s]); o_zero may be the output itself.
+cudaError_t launch_segment_outputs(const void* o_identity, long long rows_id, const void* o_zero,
+                                   long long rows_zero, const float* start_states, void* output,
+                                   int nseg, const int* off, const int* len, int HV,
+                                   cudaStream_t s);
 
 // Device-side error flag set by a bounded wait that ran out (0 = none).
 unsigned read_device_error(bool clear);

@@ -37,6 +37,7 @@
 // gdn_device_error), lets its copies and MMAs in flight land (again boundedly),
 // releases TMEM and returns.
 #include <cudaTypedefs.h>
+#include <climits>
 
 #include "gdn_chunk_math.cuh"
 #include "gdn_common.cuh"
@@ -97,7 +98,19 @@ struct SplitParams {
   long long ckpt_cap;
   int ckpt_every;
   long long a_rs = 0, b_rs = 0, o_rs = 0;  // token strides of a, b and the output (elements)
+  // segmented call of one sequence (token rows are virtual): rows r >= vsplit belong to the
+  // identity runs, which read input row r - vsplit + vsrc, take v = 0, start from the
+  // identity state and write their outputs to out_alt row r - vsplit; only runs
+  // n < state_runs start from `state`, the others from zero
+  long long vsplit = LLONG_MAX, vsrc = 0;
+  __nv_bfloat16* out_alt = nullptr;
+  int state_runs = INT_MAX;
 };
+
+// Input row of virtual token row r (a chunk never straddles vsplit).
+__device__ __forceinline__ long long src_row(const SplitParams& p, long long r) {
+  return r >= p.vsplit ? r - p.vsplit + p.vsrc : r;
+}
 
 template <typename CuT>
 __device__ __forceinline__ void seq_range(const CuT* cu, int n, long long T, long long& s0,
@@ -189,8 +202,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   const int n = lo, c = g - p.chunk_base[n];
   long long s0, s1;
   seq_range(static_cast<const CuT*>(p.cu), n, p.T, s0, s1);
-  const long long t0 = s0 + (long long)kC * c;
-  const int Lc = (int)min((long long)kC, s1 - t0);
+  const long long tv = s0 + (long long)kC * c;  // virtual row of the chunk's first token
+  const int Lc = (int)min((long long)kC, s1 - tv);
+  const long long t0 = src_row(p, tv);           // its input row
   const int qh = h0 / p.ratio;
   if ((sb & 1023u) != 0) {
     if (tid == 0) atomicOr(&g_split_device_error, ERR_SMEM_ALIGN);
@@ -592,6 +606,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     return;
   }
   const int nchunks = (int)((L + kC - 1) / kC);
+  const bool ident = s0 >= p.vsplit;  // identity run of a segmented call: v = 0, no V copies
+  if (ident) {
+    for (int i = tid; i < (int)((V1 + 4096u - V0) / 16u); i += kThreads)
+      st_shared_v4(sb + V0 + 16u * (uint32_t)i, 0u, 0u, 0u, 0u);
+  }
   Bars* bars = reinterpret_cast<Bars*>(smem + BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BARS + sizeof(Bars));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + BARS + sizeof(Bars) + 4);
@@ -637,7 +656,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
       for (int cc = 0; cc < nchunks; ++cc) {
         const int bf = cc & 1;
         const uint32_t free_par = ((cc >> 1) + 1) & 1;  // phase cc/2 - 1 of the free barrier
-        const int y = (int)(s0 + (long long)kC * cc);
+        const int y = (int)src_row(p, s0 + (long long)kC * cc);
         if (cc >= 2 && !wait_or_abort(&bars->kq_free[bf], free_par, abort_flag, ERR_MMA_TIMEOUT))
           break;
         const uint32_t kq = bf ? KQ1 : KQ0;
@@ -652,8 +671,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
           break;
         const uint8_t* r = rec0 + (size_t)cc * rstride;
         fence_proxy_async();
-        mbar_arrive_expect_tx(&bars->vt[bf], 64 * kVB * 2 + p.rec_stride);
-        tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
+        mbar_arrive_expect_tx(&bars->vt[bf], (ident ? 0u : 64u * kVB * 2u) + p.rec_stride);
+        if (!ident) tma_load_2d(smem + (bf ? V1 : V0), &tm_v, &bars->vt[bf], h * 128 + kVB * vb, y);
         bulk_load(smem + (bf ? TP1 : TP0), r, kRecTpLo + p.rec_lo, &bars->vt[bf]);  // hi | lo
         bulk_load(smem + (bf ? VEC1 : VEC0), r + kRecTpLo + p.rec_lo, kRecVecBytes, &bars->vt[bf]);
         vt_issued = cc + 1;
@@ -731,13 +750,18 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     // initial state: S^T[k][v] -> TMEM (fp32; second half 0) and G1's [hi | lo] image
     {
       float sv[8];
+      bool loaded = false;
       if constexpr (HAS_STATE) {
-        const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
+        if (n < p.state_runs) {
+          const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sv[i] = __ldg(src + (size_t)(v_lo + i) * kHeadDim + row);
-      } else {
+          for (int i = 0; i < 8; ++i) sv[i] = __ldg(src + (size_t)(v_lo + i) * kHeadDim + row);
+          loaded = true;
+        }
+      }
+      if (!loaded) {  // zero, or the identity for an identity run (S^T[k][v] = [k == v])
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sv[i] = 0.f;
+        for (int i = 0; i < 8; ++i) sv[i] = (ident && v_lo + i == row) ? 1.f : 0.f;
       }
       const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       tmem_st8(tl + TST + vq, sv);
@@ -821,7 +845,9 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             w[e] = cvt_bf16x2(ct * (qs[i] + q2[i]) + scale * (pu[i] + p2[i]),
                               ct * (qs[i + 1] + q2[i + 1]) + scale * (pu[i + 1] + p2[i + 1]));
           }
-          *reinterpret_cast<uint4*>(p.out + (size_t)(t0 + t) * p.o_rs + (size_t)h * kHeadDim + v_lo) =
+          __nv_bfloat16* orow = ident ? p.out_alt + (size_t)(t0 + t - p.vsplit) * p.o_rs
+                                      : p.out + (size_t)(t0 + t) * p.o_rs;
+          *reinterpret_cast<uint4*>(orow + (size_t)h * kHeadDim + v_lo) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
@@ -946,8 +972,9 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   if (lay.slots * p.HV > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
     return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv;  // V in [64 tokens][32 v] boxes, unswizzled (read by the CUDA cores)
-  if (!make_tile_map(&mq, p.q, p.HQ, p.T, p.rs.q) || !make_tile_map(&mk, p.k, p.HQ, p.T, p.rs.k) ||
-      !make_tile_map_box(&mv, p.v, p.HV, p.T, p.rs.v, st::kVB, false))
+  const long long rows = p.src_rows > 0 ? p.src_rows : p.T;  // rows of q, k, v
+  if (!make_tile_map(&mq, p.q, p.HQ, rows, p.rs.q) || !make_tile_map(&mk, p.k, p.HQ, rows, p.rs.k) ||
+      !make_tile_map_box(&mv, p.v, p.HV, rows, p.rs.v, st::kVB, false))
     return cudaErrorInvalidValue;
   uint8_t* ws = static_cast<uint8_t*>(p.workspace);
   int* order = nullptr;
@@ -977,6 +1004,10 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   sp.a_rs = p.rs.a;
   sp.b_rs = p.rs.b;
   sp.o_rs = p.rs.o;
+  sp.vsplit = p.vsplit;
+  sp.vsrc = p.vsrc;
+  sp.out_alt = static_cast<__nv_bfloat16*>(p.out_alt);
+  sp.state_runs = p.state_runs;
   if (p.cu_int64)
     return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
   return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);

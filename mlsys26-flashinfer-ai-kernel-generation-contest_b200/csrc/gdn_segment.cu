@@ -48,31 +48,43 @@ __device__ __forceinline__ uint32_t img_off(uint32_t r, uint32_t ch) {
   return (ch >> 3) * 16384u + sw128(r, ch & 7u);
 }
 
-// o^I and o^0 of tile `tile` -> buffer at `buf` (four 64 x 64 boxes each; rows past the end
-// of the segment arrive as zeros), completion counted on `bar`.
+// o^I and o^0 of the tile starting at row `row0` -> buffer at `buf` (four 64 x 64 boxes
+// each; rows past the end of the tensors arrive as zeros), completion counted on `bar`.
 __device__ __forceinline__ void load_tile(uint8_t* buf, const CUtensorMap* m_id,
                                           const CUtensorMap* m_zero, uint64_t* bar, int h,
-                                          int tile) {
+                                          int row0) {
   mbar_arrive_expect_tx(bar, kBufBytes);
 #pragma unroll
   for (int half = 0; half < 2; ++half)
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) {
-      const int x = h * kD + 64 * half, y = tile * kTile + 64 * rb;
+      const int x = h * kD + 64 * half, y = row0 + 64 * rb;
       const uint32_t off = 16384u * half + 8192u * rb;
       tma_load_2d(buf + off, m_id, bar, x, y);
       tma_load_2d(buf + kOZ + off, m_zero, bar, x, y);
     }
 }
 
-// One CTA per (v-head, group of token tiles): S[h] is split once and stays in shared
-// memory; the tiles of the group stream through two buffers (the next tile's TMA loads run
-// while the current tile's MMAs and epilogue do).
+// Segments of one launch: segment s covers rows [off[s], off[s] + len[s]) of o^I, o^0 and
+// the output, and starts from start[s].
+constexpr int kMaxSegs = 64;
+struct OutSegs {
+  int n;
+  int off[kMaxSegs];
+  int len[kMaxSegs];
+};
+
+// One CTA per (segment, v-head, group of token tiles): S[h] is split once and stays in
+// shared memory; the tiles of the group stream through two buffers (the next tile's TMA
+// loads run while the current tile's MMAs and epilogue do).  A tile's rows past its
+// segment's end may belong to the next segment: they are read (and discarded), never
+// written, so o^0 may live in the output itself (each row is read by its own tile's copy
+// before that tile writes it).
 __global__ void __launch_bounds__(kThreads, 1)
     segment_outputs_kernel(const __grid_constant__ CUtensorMap m_id,
                            const __grid_constant__ CUtensorMap m_zero,
-                           const float* __restrict__ start, __nv_bfloat16* __restrict__ out,
-                           int L, int HV) {
+                           const float* __restrict__ start, __nv_bfloat16* out,
+                           const __grid_constant__ OutSegs segs, int HV) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -81,7 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_mma = bar_in + 2;
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + 28);
-  const int h = blockIdx.y, group = blockIdx.x, groups = gridDim.x;
+  const int h = blockIdx.y, group = blockIdx.x, groups = gridDim.x, seg = blockIdx.z;
+  const int L = segs.len[seg], y0 = segs.off[seg];
   const int ntiles = (L + kTile - 1) / kTile;
   const int mine = ntiles > group ? (ntiles - group + groups - 1) / groups : 0;  // tiles g, g+G, ..
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -104,10 +117,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&m_zero);
     for (; issued < 2 && issued < mine; ++issued)
       load_tile(smem + kBuf0 + issued * kBufBytes, &m_id, &m_zero, &bar_in[issued], h,
-                group + issued * groups);
+                y0 + (group + issued * groups) * kTile);
   }
   // S[h] rows v -> hi | lo images (8 fp32 per piece)
-  const float* sh = start + (size_t)h * kD * kD;
+  const float* sh = start + ((size_t)seg * HV + h) * kD * kD;
 #pragma unroll 4
   for (int k = 0; k < 16; ++k) {
     const int i = tid + k * kThreads, v = i >> 4, p = i & 15;
@@ -172,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tl + 32u * q, d);
       tmem_wait_ld();
       if (t < L) {
-        uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)t * HV + h) * kD + 32 * q);
+        uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)(y0 + t) * HV + h) * kD + 32 * q);
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           const uint4 zv = ld_shared_v4(buf + kOZ + img_off(r, 4 * q + p));
@@ -193,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // buffer b and the accumulator are free
     if (tid == 0 && issued < mine) {
       load_tile(smem + kBuf0 + b * kBufBytes, &m_id, &m_zero, &bar_in[b], h,
-                group + issued * groups);
+                y0 + (group + issued * groups) * kTile);
       ++issued;
     }
   }
@@ -207,17 +220,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Start state and final state of segment `rank` from every segment's state map
-// maps[m] = (A_m, B_m), each [HV][128][128] fp32:
+// (A_m, B_m), each [HV][128][128] fp32, A_m at maps[(a0 + m as) HV + h], B_m at
+// maps[(b0 + m bs) HV + h] (matrices):
 //   S = B_0;  S <- S A_m + B_m for m = 1 .. rank-1;  start = S;  final = S A_rank + B_rank.
 // Rows of S evolve independently (row i of S A depends on row i of S only), so each CTA
-// carries 32 rows of one v-head through the whole chain with no exchange between CTAs.
-// 128 threads, each 4 rows x 8 columns (32 FMAs per 8 A values read), fp32 FMAs.  A_m is
-// staged in shared memory, the next map's A copied in (cp.async) while a step computes.
-constexpr int kChainRows = 32;
+// carries 8 RPT rows of one v-head through the whole chain with no exchange between CTAs.
+// 128 threads, each RPT rows x 8 columns (8 RPT FMAs per 8 A values read), fp32 FMAs in
+// the same order for every RPT (the results do not depend on it).  A_m is staged in shared
+// memory, the next map's A copied in (cp.async) while a step computes.  RPT = 4 (32 rows,
+// 4 CTAs per v-head) when there are enough v-heads to fill the SMs, 2 or 1 otherwise.
+struct MapIndex {
+  int a0, as, b0, bs;
+};
 constexpr int kChainThreads = 128;
 constexpr int kSLd = kD + 4;  // padded S rows
 constexpr int kAPer = kD * kD / 4 / kChainThreads;  // 16-byte pieces of A per thread
-constexpr size_t kChainSmem = (size_t)(2 * kD * kD + kChainRows * kSLd) * sizeof(float);
+constexpr size_t chain_smem(int rpt) { return (size_t)(2 * kD * kD + 8 * rpt * kSLd) * sizeof(float); }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
@@ -226,20 +244,22 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+template <int RPT>
 __global__ void __launch_bounds__(kChainThreads, 1)
-    segment_chain_kernel(const float* __restrict__ maps, int rank, int HV,
+    segment_chain_kernel(const float* __restrict__ maps, const MapIndex mi, int rank, int HV,
                          float* __restrict__ start_out, float* __restrict__ final_out,
                          float* __restrict__ starts_all) {
+  constexpr int kRows = 8 * RPT;
   extern __shared__ __align__(16) float csm[];
   float* S = csm + 2 * kD * kD;  // [row][kSLd]
-  const int h = blockIdx.y, r0 = kChainRows * blockIdx.x;
+  const int h = blockIdx.y, r0 = kRows * blockIdx.x;
   const int tid = threadIdx.x, rq = tid >> 4, cb = tid & 15;
   // this thread's 8 columns: two groups of 4, 64 apart, so that the 16 column blocks of a
   // half-warp read 256 contiguous bytes of an A row (no bank conflicts)
   const int c0 = 4 * cb, c1 = 64 + 4 * cb;
   const size_t mat = (size_t)kD * kD;
-  auto A = [&](int m) { return maps + ((size_t)(2 * m) * HV + h) * mat; };
-  auto B = [&](int m) { return maps + ((size_t)(2 * m + 1) * HV + h) * mat; };
+  auto A = [&](int m) { return maps + ((size_t)(mi.a0 + m * mi.as) * HV + h) * mat; };
+  auto B = [&](int m) { return maps + ((size_t)(mi.b0 + m * mi.bs) * HV + h) * mat; };
   auto prefetch = [&](int m, float* dst) {
     const float* src = A(m);
 #pragma unroll 8
@@ -251,7 +271,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   };
   prefetch(1, csm);
   // S = B_0 (this CTA's rows): the start state of segment 1
-  for (int i = tid; i < kChainRows * kD / 4; i += kChainThreads) {
+  for (int i = tid; i < kRows * kD / 4; i += kChainThreads) {
     const int r = i >> 5, c4 = i & 31;
     const float4 b0 = __ldg(reinterpret_cast<const float4*>(B(0) + (size_t)(r0 + r) * kD) + c4);
     *reinterpret_cast<float4*>(S + r * kSLd + 4 * c4) = b0;
@@ -264,54 +284,54 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     __syncthreads();  // A_m and S in place; the other A buffer is no longer read
     if (m < rank) prefetch(m + 1, csm + (m & 1) * kD * kD);
     // B_m rows: loaded now, added after the product (their latency hides behind it)
-    float4 bq[4][2];
+    float4 bq[RPT][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float* brow = B(m) + (size_t)(r0 + 4 * rq + i) * kD;
+    for (int i = 0; i < RPT; ++i) {
+      const float* brow = B(m) + (size_t)(r0 + RPT * rq + i) * kD;
       bq[i][0] = __ldg(reinterpret_cast<const float4*>(brow + c0));
       bq[i][1] = __ldg(reinterpret_cast<const float4*>(brow + c1));
     }
-    float acc[4][8];
+    float acc[RPT][8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-    const float* srow = S + (4 * rq) * kSLd;
+    const float* srow = S + (RPT * rq) * kSLd;
     // software-pipelined: the shared-memory operands of step j + 1 are loaded while the
     // FMAs of step j issue (one warp per scheduler cannot hide the load latency otherwise)
     float4 x = *reinterpret_cast<const float4*>(As + c0);
     float4 y = *reinterpret_cast<const float4*>(As + c1);
-    float sv[4];
+    float sv[RPT];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sv[i] = srow[i * kSLd];
+    for (int i = 0; i < RPT; ++i) sv[i] = srow[i * kSLd];
 #pragma unroll 2
     for (int j = 0; j < kD; ++j) {
       const int jn = (j + 1) & (kD - 1);  // the last prefetch wraps to row 0 and is unused
       const float4 xn = *reinterpret_cast<const float4*>(As + jn * kD + c0);
       const float4 yn = *reinterpret_cast<const float4*>(As + jn * kD + c1);
-      float svn[4];
+      float svn[RPT];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) svn[i] = srow[i * kSLd + jn];
+      for (int i = 0; i < RPT; ++i) svn[i] = srow[i * kSLd + jn];
       const float av[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(sv[i], av[e], acc[i][e]);
       x = xn;
       y = yn;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sv[i] = svn[i];
+      for (int i = 0; i < RPT; ++i) sv[i] = svn[i];
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
       acc[i][0] += bq[i][0].x; acc[i][1] += bq[i][0].y; acc[i][2] += bq[i][0].z;
       acc[i][3] += bq[i][0].w; acc[i][4] += bq[i][1].x; acc[i][5] += bq[i][1].y;
       acc[i][6] += bq[i][1].z; acc[i][7] += bq[i][1].w;
     }
     if (m == rank) {  // the segment's own map: its final state; S holds its start state
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float* dst = final_out + ((size_t)h * kD + r0 + 4 * rq + i) * kD;
+      for (int i = 0; i < RPT; ++i) {
+        float* dst = final_out + ((size_t)h * kD + r0 + RPT * rq + i) * kD;
         *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
         *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
@@ -319,23 +339,23 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     }
     __syncthreads();  // every read of S done
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float* d = S + (4 * rq + i) * kSLd;
+    for (int i = 0; i < RPT; ++i) {
+      float* d = S + (RPT * rq + i) * kSLd;
       *reinterpret_cast<float4*>(d + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
       *reinterpret_cast<float4*>(d + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
     }
     if (starts_all != nullptr) {  // S is now the start state of segment m + 1
       float* base = starts_all + (size_t)m * HV * kD * kD;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float* dst = base + ((size_t)h * kD + r0 + 4 * rq + i) * kD;
+      for (int i = 0; i < RPT; ++i) {
+        float* dst = base + ((size_t)h * kD + r0 + RPT * rq + i) * kD;
         *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
         *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
     }
   }
   // start state = S (rows of this CTA)
-  for (int i = tid; i < kChainRows * kD / 4; i += kChainThreads) {
+  for (int i = tid; i < kRows * kD / 4; i += kChainThreads) {
     const int r = i >> 5, c4 = i & 31;
     reinterpret_cast<float4*>(start_out + ((size_t)h * kD + r0 + r) * kD)[c4] =
         *reinterpret_cast<const float4*>(S + r * kSLd + 4 * c4);
@@ -343,6 +363,33 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 }
 
 bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
+struct DeviceInfo {
+  bool ok = false;
+  int sms = 0;
+};
+
+// Shared-memory opt-in of the segment kernels and the SM count, once per device.
+const DeviceInfo* device_info() {
+  static DeviceInfo info[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  DeviceInfo& d = info[dev];
+  if (!d.ok) {
+    if (cudaFuncSetAttribute(segment_outputs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(segment_chain_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem(1)) != cudaSuccess ||
+        cudaFuncSetAttribute(segment_chain_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem(2)) != cudaSuccess ||
+        cudaFuncSetAttribute(segment_chain_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem(4)) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return nullptr;
+    d.ok = true;
+  }
+  return &d;
+}
 
 }  // namespace
 
@@ -355,6 +402,62 @@ unsigned read_segment_device_error(bool clear) {
     cudaMemcpyToSymbol(g_segment_device_error, &zero, sizeof(zero));
   }
   return v;
+}
+
+// The chain over maps A_m = maps[a0 + m as], B_m = maps[b0 + m bs] (matrices of HV heads):
+// segment `rank`'s start state into start_out and final state into final_out, and, when
+// starts_all is given, segment s's start state into starts_all[s - 1] for s = 1 .. rank.
+// Rows per CTA: as few as keep every CTA resident (more CTAs shorten each step).
+cudaError_t launch_segment_chain(const float* maps, int a0, int as, int b0, int bs, int rank,
+                                 int HV, float* start_out, float* final_out, float* starts_all,
+                                 cudaStream_t s) {
+  const DeviceInfo* d = device_info();
+  if (d == nullptr) return cudaErrorInvalidValue;
+  const MapIndex mi{a0, as, b0, bs};
+  const int rpt = 16 * HV <= d->sms ? 1 : (8 * HV <= d->sms ? 2 : 4);
+  const dim3 grid((unsigned)(kD / (8 * rpt)), (unsigned)HV);
+  if (rpt == 1)
+    segment_chain_kernel<1><<<grid, kChainThreads, chain_smem(1), s>>>(maps, mi, rank, HV, start_out,
+                                                                     final_out, starts_all);
+  else if (rpt == 2)
+    segment_chain_kernel<2><<<grid, kChainThreads, chain_smem(2), s>>>(maps, mi, rank, HV, start_out,
+                                                                     final_out, starts_all);
+  else
+    segment_chain_kernel<4><<<grid, kChainThreads, chain_smem(4), s>>>(maps, mi, rank, HV, start_out,
+                                                                     final_out, starts_all);
+  return cudaGetLastError();
+}
+
+// Outputs of nseg segments in one launch: segment s covers rows [off[s], off[s] + len[s])
+// of o^I (rows_id rows at o_identity), o^0 (rows_zero rows at o_zero) and the output, and
+// starts from start_states[s].  o_zero may be the output itself.
+cudaError_t launch_segment_outputs(const void* o_identity, long long rows_id, const void* o_zero,
+                                   long long rows_zero, const float* start_states, void* output,
+                                   int nseg, const int* off, const int* len, int HV,
+                                   cudaStream_t s) {
+  const DeviceInfo* d = device_info();
+  if (d == nullptr || nseg <= 0 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+  OutSegs segs{};
+  segs.n = nseg;
+  int max_tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    segs.off[i] = off[i];
+    segs.len[i] = len[i];
+    max_tiles = std::max(max_tiles, (len[i] + kTile - 1) / kTile);
+  }
+  if (max_tiles == 0) return cudaSuccess;
+  CUtensorMap m_id, m_zero;
+  const long long row = (long long)HV * kD;
+  if (!make_tile_map(&m_id, o_identity, HV, rows_id, row) ||
+      !make_tile_map(&m_zero, o_zero, HV, rows_zero, row))
+    return cudaErrorInvalidValue;
+  // about one CTA per SM: the SMs split over the (segment, v-head) pairs, each CTA a group
+  // of token tiles
+  const int groups = std::max(1, std::min(max_tiles, d->sms / (HV * nseg)));
+  const dim3 grid((unsigned)groups, (unsigned)HV, (unsigned)nseg);
+  segment_outputs_kernel<<<grid, kThreads, kSmem, s>>>(m_id, m_zero, start_states,
+                                                       static_cast<__nv_bfloat16*>(output), segs, HV);
+  return cudaGetLastError();
 }
 }  // namespace gdn
 
@@ -370,29 +473,12 @@ extern "C" int gdn_segment_outputs_launch(const void* o_identity, const void* o_
   if (misaligned(o_identity, 16) || misaligned(start_state, 16) || misaligned(o_zero, 16) ||
       misaligned(output, 16))
     return GDN_ERR_INVALID_ARGUMENT;
-  static bool configured[64] = {};
-  static int sms[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(segment_outputs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmem) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    configured[dev] = true;
-  }
-  CUtensorMap m_id, m_zero;
-  const long long row = (long long)num_v_heads * 128;
-  if (!gdn::make_tile_map(&m_id, o_identity, num_v_heads, num_tokens, row) ||
-      !gdn::make_tile_map(&m_zero, o_zero, num_v_heads, num_tokens, row))
-    return GDN_ERR_UNSUPPORTED;
-  // one CTA per SM: the SMs split over the v-heads, each CTA a group of token tiles
-  const int ntiles = (num_tokens + kTile - 1) / kTile;
-  const int groups = std::max(1, std::min(ntiles, sms[dev] / num_v_heads));
-  const dim3 grid((unsigned)groups, (unsigned)num_v_heads);
-  segment_outputs_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(
-      m_id, m_zero, start_state, static_cast<__nv_bfloat16*>(output), num_tokens, num_v_heads);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  const int off = 0;
+  const cudaError_t e = gdn::launch_segment_outputs(o_identity, num_tokens, o_zero, num_tokens,
+                                                    start_state, output, 1, &off, &num_tokens,
+                                                    num_v_heads, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue) return GDN_ERR_UNSUPPORTED;
+  return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 extern "C" int gdn_segment_chain_launch(const float* maps, int num_maps, int rank,
@@ -405,19 +491,11 @@ extern "C" int gdn_segment_chain_launch(const float* maps, int num_maps, int ran
     return GDN_ERR_INVALID_ARGUMENT;
   if (misaligned(maps, 16) || misaligned(start_state, 16) || misaligned(final_state, 16))
     return GDN_ERR_INVALID_ARGUMENT;
-  static bool configured[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(segment_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kChainSmem) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
-  const dim3 grid(kD / kChainRows, (unsigned)num_v_heads);
-  segment_chain_kernel<<<grid, kChainThreads, kChainSmem, static_cast<cudaStream_t>(stream)>>>(
-      maps, rank, num_v_heads, start_state, final_state, nullptr);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  // maps [num_maps][2][HV][128][128]: A_m = entry 2 m, B_m = entry 2 m + 1
+  const cudaError_t e = gdn::launch_segment_chain(maps, 0, 2, 1, 2, rank, num_v_heads, start_state,
+                                                  final_state, nullptr,
+                                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 extern "C" int gdn_segment_chain_all_launch(const float* maps, int num_maps, float* start_states,
@@ -429,21 +507,12 @@ extern "C" int gdn_segment_chain_all_launch(const float* maps, int num_maps, flo
     return GDN_ERR_INVALID_ARGUMENT;
   if (misaligned(maps, 16) || misaligned(start_states, 16) || misaligned(final_state, 16))
     return GDN_ERR_INVALID_ARGUMENT;
-  static bool configured[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(segment_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kChainSmem) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
   // one pass through every map: segment s's start state into start_states[s - 1] as the
   // chain reaches it, the last segment's final state into final_state
   const int rank = num_maps - 1;
   float* last_start = start_states + (size_t)(rank - 1) * num_v_heads * kD * kD;
-  const dim3 grid(kD / kChainRows, (unsigned)num_v_heads);
-  segment_chain_kernel<<<grid, kChainThreads, kChainSmem, static_cast<cudaStream_t>(stream)>>>(
-      maps, rank, num_v_heads, last_start, final_state, start_states);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  const cudaError_t e = gdn::launch_segment_chain(maps, 0, 2, 1, 2, rank, num_v_heads, last_start,
+                                                  final_state, start_states,
+                                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

@@ -12,7 +12,6 @@ or int64), so the call never synchronises the host.
 """
 from __future__ import annotations
 
-import functools
 import threading
 
 import torch
@@ -193,70 +192,98 @@ def _prefill(launch, name, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, sca
     return output, new_state
 
 
-@functools.lru_cache(maxsize=64)
-def _segment_layout(total_tokens: int, segments: int, num_v_heads: int, device: torch.device):
-    """(layout, state template) of a segmented call; both are read-only for the calls."""
-    from . import sharding
-    layout = sharding.segmented_layout(total_tokens, segments, device)
-    return layout, sharding.state_template(len(layout[0]), num_v_heads, device)
+def segments_auto(total_tokens: int, num_v_heads: int) -> int:
+    """Segment count gdn_prefill_segmented picks for `segments` = 0 on the current device:
+    the largest S whose 2 S - 1 runs (four state CTAs per run and v-head) fit on the SMs
+    at once, capped at the number of 64-token chunks."""
+    return int(LIB.gdn_prefill_segments_auto(total_tokens, num_v_heads))
+
+
+def segmented_launches(segments: int) -> int:
+    """Number of this library's kernels one gdn_prefill_segmented call launches."""
+    if segments <= 1:  # run offsets, chunk offsets, preparation, state
+        return 4
+    # + longest-first order, state-map chain, outputs
+    return 7
 
 
 def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=None,
                           new_state=None, *, segments: int = 0, use_qk_l2norm: bool = False):
     """Prefill of ONE sequence whose v-heads alone leave most SMs idle (a sequence sharded
     by q/k-head group over several GPUs, or a model with few heads per GPU), split into
-    token segments that run side by side in a single prefill call: segment 0 from the
-    initial state, every later segment twice, from the identity with v = 0 (its state map
-    A and outputs o^I) and from a zero state (B and o^0).  Over a segment the recurrence
+    token segments that run side by side in a single launch of the split kernels
+    (``gdn_prefill_segmented_launch``): segment 0 from the initial state, every later
+    segment twice, from a zero state (its map's B and outputs o^0) and from the identity
+    with v = 0 (A and o^I), all reading the tokens in place.  Over a segment the recurrence
     is affine in its start state, so the library's chain kernel then composes the maps and
     its output kernel forms o = S_start o^I + o^0 for every later segment.  The serial
     chunk chain shrinks from the whole sequence to one segment; there is no collective.
 
-    q, k [T, HQ, 128], v [T, HV, 128], a, b [T, HV] bf16; state [1, HV, 128, 128] fp32 or
-    None; returns (output [T, HV, 128] bf16, new_state [1, HV, 128, 128] fp32).
-    `segments` = 0 picks the largest count whose 2 S - 1 runs fit on the SMs at once
-    (sharding.local_segments); 1 is an ordinary gdn_prefill call.  The outputs of the
-    later segments carry one more bf16 rounding (of o^I); the final state is fp32
-    throughout."""
-    from . import sharding
+    q, k [T, HQ, 128], v [T, HV, 128], a, b [T, HV] bf16 (token rows may be strided);
+    state [1, HV, 128, 128] fp32 or None; returns (output [T, HV, 128] bf16, new_state
+    [1, HV, 128, 128] fp32).  `segments` = 0 picks the largest count whose 2 S - 1 runs
+    fit on the SMs at once (segments_auto); 1 is an ordinary split-kernel prefill.  The
+    outputs of the later segments carry one more bf16 rounding (of o^I); the final state
+    is fp32 throughout."""
     dev = C.cuda_device(q)
+    C.tensor("q", q, torch.bfloat16, 3, dev, strided=True)
+    C.tensor("k", k, torch.bfloat16, 3, dev, strided=True)
     C.tensor("v", v, torch.bfloat16, 3, dev, strided=True)
-    T, HV = q.shape[0], v.shape[1]
+    T, HQ, D = q.shape
+    HK, HV = k.shape[1], v.shape[1]
+    C.heads(HQ, HK, HV, D)
+    C.shape("k", k, (T, HK, D))
+    C.shape("v", v, (T, HV, D))
+    for name, x, shp in (("A_log", A_log, (HV,)), ("dt_bias", dt_bias, (HV,))):
+        C.tensor(name, x, torch.float32, 1, dev, strided=True)
+        C.shape(name, x, shp)
+    for name, x in (("a", a), ("b", b)):
+        C.tensor(name, x, torch.bfloat16, 2, dev, strided=True)
+        C.shape(name, x, (T, HV))
     if state is not None:
         C.tensor("state", state, torch.float32, 4, dev, strided=True)
-        C.shape("state", state, (1, HV, 128, 128))
-    for name, x, shp, dt in (("output", output, (T, HV, 128), torch.bfloat16),
-                             ("new_state", new_state, (1, HV, 128, 128), torch.float32)):
+        C.shape("state", state, (1, HV, D, D))
+    for name, x, shp, dt in (("output", output, (T, HV, D), torch.bfloat16),
+                             ("new_state", new_state, (1, HV, D, D), torch.float32)):
         if x is not None:
             C.tensor(name, x, dt, len(shp), dev, strided=True)
             C.shape(name, x, shp)
-    S = segments if segments > 0 else sharding.local_segments(HV, T)
-    if S <= 1 or T == 0:
-        cu = _segment_layout(T, 1, HV, dev)[0][1]
-        return gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu, scale, output,
-                           new_state, use_qk_l2norm=use_qk_l2norm)
-    # the layout lives on the device from the first call on (no host copy per call, so
-    # the call can be captured in a CUDA graph after a first eager call)
-    layout, template = _segment_layout(T, S, HV, dev)
-    n = len(layout[0])
-    inp = {"q": q, "k": k, "v": v, "state": state, "a": a, "b": b}
-    run = sharding.segmented_inputs(inp, layout, template)
-    # the runs' final states land in the chain kernel's map tensor (entry 0 unused)
-    maps = torch.empty(n, 2, HV, 128, 128, dtype=torch.float32, device=dev)
-    o_runs, f_runs = gdn_prefill(run["q"], run["k"], run["v"], run["state"], A_log, run["a"],
-                                 dt_bias, run["b"], run["cu_seqlens"], scale, None,
-                                 maps.view(2 * n, HV, 128, 128)[1:],
-                                 use_qk_l2norm=use_qk_l2norm)
-    # the assembly kernels write dense, 16-byte aligned results
-    dense = lambda x: x is not None and x.is_contiguous() and x.data_ptr() % 16 == 0  # noqa: E731
-    out, fin = sharding.segmented_finish(layout, o_runs, f_runs,
-                                         output if dense(output) else None,
-                                         new_state if dense(new_state) else None, maps=maps)
-    if output is not None and out is not output:
-        out = output.copy_(out)
-    if new_state is not None and fin is not new_state:
-        fin = new_state.copy_(fin)
-    return out, fin
+    if segments < 0:
+        raise ValueError("segments must be >= 0")
+    sc = C.scale_arg(scale)
+    if output is None:
+        output = torch.empty(T, HV, D, dtype=torch.bfloat16, device=dev)
+    if new_state is None:
+        new_state = torch.empty(1, HV, D, D, dtype=torch.float32, device=dev)
+    if T == 0:  # an empty sequence's final state is zero (definition semantics)
+        return output, new_state.zero_()
+    state_in, A_log, dt_bias = C.dense_or_copy(state, 16), C.dense_or_copy(A_log), \
+        C.dense_or_copy(dt_bias)
+    dense = lambda x: x.is_contiguous() and x.data_ptr() % 16 == 0  # noqa: E731
+    ns = new_state if dense(new_state) else torch.empty(1, HV, D, D, dtype=torch.float32,
+                                                        device=dev)
+    if ns is not new_state and state is not None and state_in.data_ptr() == new_state.data_ptr():
+        state_in = state_in.clone()  # keep the in-place contract through the temporary
+    out = output if dense(output) else torch.empty(T, HV, D, dtype=torch.bfloat16, device=dev)
+    (q, qs), (k, ks), (v, vs) = C.rows_in(q, 8, 16), C.rows_in(k, 8, 16), C.rows_in(v, 8, 16)
+    (a, as_), (b, bs) = C.rows_in(a), C.rows_in(b)
+    ws_n = int(LIB.gdn_prefill_segmented_workspace_size(T, HV, segments))
+    ws = _workspace(dev, ws_n + 1024) if ws_n > 0 else None
+    ws_ptr = ws_len = 0
+    if ws is not None:  # the launch wants its workspace 1024-byte aligned
+        ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024
+        ws_len = ws.numel() - (ws_ptr - ws.data_ptr())
+    check("gdn_prefill_segmented_launch", LIB.gdn_prefill_segmented_launch(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        state_in.data_ptr() if state_in is not None else None, A_log.data_ptr(), a.data_ptr(),
+        dt_bias.data_ptr(), b.data_ptr(), sc, out.data_ptr(), ns.data_ptr(), T, HQ, HK, HV, D,
+        int(bool(use_qk_l2norm)), segments, qs, ks, vs, as_, bs, ws_ptr or None, ws_len,
+        C.stream_handle(dev)))
+    if out is not output:
+        output.copy_(out)
+    if ns is not new_state:
+        new_state.copy_(ns)
+    return output, new_state
 
 
 def kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):

@@ -160,3 +160,26 @@ def test_selftest_argument_checks_return_before_launch():
     assert lib.gdn_selftest_bounded_wait(0, 0, None, None) == -1          # no polls
     assert lib.gdn_selftest_bounded_wait((1 << 24) + 1, 0, None, None) == -1
     assert lib.gdn_selftest_bounded_wait(16, 0, 0x1002, None) == -1       # misaligned
+
+
+def test_segmented_argument_checks_return_before_launch():
+    lib = load_pkg().LIB
+    fake = 0x10000
+
+    def call(T=256, hq=2, hk=2, hv=4, hd=128, segments=2, ns=fake, qs=256):
+        return lib.gdn_prefill_segmented_launch(
+            fake, fake, fake, None, fake, fake, fake, fake, 0.0, fake, ns, T, hq, hk, hv, hd, 1,
+            segments, qs, 256, 512, 4, 4, fake, 1 << 30, None)
+    assert call(T=-1) == -1                      # GDN_ERR_INVALID_ARGUMENT
+    assert call(segments=-1) == -1
+    assert call(ns=None) == -1
+    assert call(ns=fake + 4) == -1               # new_state not 16-byte aligned
+    assert call(hk=4) == -2                      # GDN_ERR_UNSUPPORTED
+    assert call(hd=64) == -2
+    assert call(qs=128) == -1                    # q rows overlap
+    # sizes need no device: S = min(segments, chunks); one segment has no scratch rows
+    assert lib.gdn_prefill_segmented_workspace_size(0, 4, 2) == 0
+    two = lib.gdn_prefill_segmented_workspace_size(256, 4, 2)
+    assert two > lib.gdn_prefill_segmented_workspace_size(256, 4, 1) > 0
+    assert lib.gdn_prefill_segmented_workspace_size(256, 4, 64) == \
+        lib.gdn_prefill_segmented_workspace_size(256, 4, 4)   # capped at the 4 chunks
