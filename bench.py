@@ -456,8 +456,7 @@ class PrefillWork:
         if self.local_segments > 1:
             self.pkg.gdn_prefill_segmented(d["q"], d["k"], d["v"], d.get("state"), d["A_log"],
                                            d["a"], d["dt_bias"], d["b"], d["scale"], self.out,
-                                           self.ns, segments=self.local_segments,
-                                           use_qk_l2norm=True)
+                                           self.ns, use_qk_l2norm=True)  # the library's plan
             return
         self.pkg.gdn_prefill(d["q"], d["k"], d["v"], d.get("state"), d["A_log"], d["a"],
                              d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], self.out, self.ns,

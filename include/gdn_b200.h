@@ -378,21 +378,36 @@ int gdn_segment_chain_all_launch(const float* maps, int num_maps, float* start_s
  * [total_tokens, num_v_heads, 128], a, b [total_tokens, num_v_heads] bf16 with the given
  * token strides (elements; q / k / v rows 16-byte aligned), state / new_state
  * [1, num_v_heads, 128, 128] fp32 (state may be NULL = zero, and may equal new_state),
- * output [total_tokens, num_v_heads, 128] bf16 dense and 16-byte aligned.  segments = 0
- * picks the largest S whose 2 S - 1 runs (four state CTAs per run and v-head) fit on the
- * SMs at once (gdn_prefill_segments_auto); S is capped at the number of chunks and at 64;
- * S = 1 is an ordinary split-kernel prefill.  The outputs of later segments carry one more
+ * output [total_tokens, num_v_heads, 128] bf16 dense and 16-byte aligned.  segments > 0
+ * cuts S equal segments (capped at the number of chunks and at 64); segments = 0 takes
+ * the plan of gdn_prefill_segment_plan for the current device; segment_bounds (host
+ * memory, may be NULL) gives the bounds of segments = S > 0 segments instead: S + 1 token
+ * offsets, 0 first, total_tokens last, strictly increasing, interior ones multiples of 64
+ * (else GDN_ERR_INVALID_ARGUMENT; the workspace size function takes the same pair and
+ * returns 0 for invalid bounds).  S = 1 is an ordinary split-kernel prefill.  The outputs of later segments carry one more
  * bf16 rounding (of o^I); the final state is fp32 throughout.  workspace (1024-byte
  * aligned) of gdn_prefill_segmented_workspace_size bytes; asynchronous on `stream`.
  */
 int gdn_prefill_segments_auto(int total_tokens, int num_v_heads);
-size_t gdn_prefill_segmented_workspace_size(int total_tokens, int num_v_heads, int segments);
+/*
+ * The segment bounds gdn_prefill_segmented_launch uses: returns S and writes
+ * bounds[0..S] (token offsets, bounds[0] = 0, bounds[S] = total_tokens; up to `capacity`
+ * entries).  segments > 0: S equal shares of the 64-token chunks (capped at the chunks and
+ * at 64).  segments = 0: the plan of a cost model of the kernels on num_sms SMs (<= 0: the
+ * current device's): segment 0 of x chunks and S - 1 equal later segments, S <= 16 and x
+ * chosen to minimise the modelled time; one segment unless that saves at least 5 %.
+ */
+int gdn_prefill_segment_plan(int total_tokens, int num_v_heads, int segments, int num_sms,
+                             int* bounds, int capacity);
+size_t gdn_prefill_segmented_workspace_size(int total_tokens, int num_v_heads, int segments,
+                                            const int* segment_bounds);
 int gdn_prefill_segmented_launch(const void* q, const void* k, const void* v, const float* state,
                                  const float* A_log, const void* a, const float* dt_bias,
                                  const void* b, float scale, void* output, float* new_state,
                                  int total_tokens, int num_q_heads, int num_k_heads,
                                  int num_v_heads, int head_size, int use_qk_l2norm, int segments,
-                                 long long q_stride, long long k_stride, long long v_stride,
+                                 const int* segment_bounds, long long q_stride,
+                                 long long k_stride, long long v_stride,
                                  long long a_stride, long long b_stride, void* workspace,
                                  size_t workspace_bytes, void* stream);
 

@@ -56,10 +56,11 @@ SIGNATURES = {
     "gdn_segment_chain_launch": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_segment_chain_all_launch": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_prefill_segments_auto": (_i, [_i, _i]),
-    "gdn_prefill_segmented_workspace_size": (_sz, [_i, _i, _i]),
+    "gdn_prefill_segment_plan": (_i, [_i, _i, _i, _i, _vp, _i]),
+    "gdn_prefill_segmented_workspace_size": (_sz, [_i, _i, _i, _vp]),
     "gdn_prefill_segmented_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
-                                          _i, _i, _i, _i, _i, _i, _i, _ll, _ll, _ll, _ll, _ll,
-                                          _vp, _sz, _vp]),
+                                          _i, _i, _i, _i, _i, _i, _i, _vp, _ll, _ll, _ll, _ll,
+                                          _ll, _vp, _sz, _vp]),
     "gdn_device_error": (_i, [_i]),
     "gdn_selftest_bounded_wait": (_i, [ctypes.c_uint, _i, _vp, _vp]),
 }

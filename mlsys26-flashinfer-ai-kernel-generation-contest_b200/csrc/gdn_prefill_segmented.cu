@@ -17,6 +17,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <queue>
+#include <tuple>
+#include <vector>
 
 #include "gdn_b200.h"
 #include "gdn_common.cuh"
@@ -37,8 +43,7 @@ __global__ void run_offsets_kernel(const RunOffsets ro, int* cu) {
   for (int i = threadIdx.x; i < ro.n; i += blockDim.x) cu[i] = ro.v[i];
 }
 
-// Segment bounds of `segments` equal shares of the sequence's chunks: b[0] = 0,
-// b[s] = 64 floor(chunks s / S) for 0 < s < S, b[S] = T.
+// Segment bounds b[0] = 0 < b[1] < .. < b[S] = T, interior bounds on 64-token chunks.
 struct Plan {
   int S = 1;
   long long T = 0;
@@ -47,14 +52,120 @@ struct Plan {
   long long virtual_rows() const { return S > 1 ? 2 * T - b[1] : T; }
 };
 
-Plan make_plan(long long T, int segments) {
+// Segment 0 of x chunks, the other chunks - x in S - 1 equal shares.
+Plan lead_plan(long long T, int S, long long x) {
   Plan p;
   p.T = T;
+  p.S = S;
   const long long chunks = (T + 63) / 64;
-  p.S = (int)std::max(1LL, std::min<long long>({(long long)segments, chunks, kMaxSegments}));
-  for (int s = 0; s < p.S; ++s) p.b[s] = std::min(64 * (chunks * s / p.S), T);
-  p.b[p.S] = T;
+  p.b[0] = 0;
+  for (int s = 1; s < S; ++s)
+    p.b[s] = std::min(64 * (x + (chunks - x) * (s - 1) / (S - 1)), T);
+  p.b[S] = T;
   return p;
+}
+
+// `segments` equal shares of the sequence's chunks: b[s] = 64 floor(chunks s / S).
+Plan equal_plan(long long T, int segments) {
+  const long long chunks = (T + 63) / 64;
+  const int S = (int)std::max(1LL, std::min<long long>({(long long)segments, chunks,
+                                                        (long long)kMaxSegments}));
+  Plan p;
+  p.T = T;
+  p.S = S;
+  for (int s = 0; s < S; ++s) p.b[s] = std::min(64 * (chunks * s / S), T);
+  p.b[S] = T;
+  return p;
+}
+
+// Cost model of a plan, in units of one chunk step of the split state kernel (2.2 us on
+// B200): the state kernel's makespan when its CTAs (4 per run and v-head, longest run
+// first, one per SM) are dealt to the SMs as they free up, each costing its run's chunks
+// plus kCtaStart; the preparation kernel before it (3 CTAs per SM, one per chunk and pair
+// of v-heads, ~20 us per wave); one chain step per later segment (~3.5 us); the output
+// pass over the later segments' tokens (3 x 256 bytes per token and v-head at ~3.5 TB/s).
+// Constants measured on B200 with P2's head shares of 2, 4 and 8 GPUs.
+constexpr double kStepUs = 2.2, kCtaStart = 3.0, kPrepWaveUs = 20.0, kChainStepUs = 3.5;
+constexpr double kOutBytesPerUs = 3.5e6;
+
+double plan_cost(const Plan& p, int HV, int sms) {
+  std::vector<long long> len;
+  len.reserve(p.runs());
+  for (int s = 0; s < p.S; ++s) {
+    const long long c = (p.b[s + 1] - p.b[s] + 63) / 64;
+    len.push_back(c);
+    if (s > 0) len.push_back(c);
+  }
+  std::stable_sort(len.begin(), len.end(), [](long long a, long long b) { return a > b; });
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < sms; ++i) free_at.push(0.0);
+  double makespan = 0.0;
+  long long vchunks = 0;
+  for (long long c : len) {
+    vchunks += c;
+    for (int j = 0; j < 4 * HV; ++j) {
+      const double t = free_at.top() + (double)c + kCtaStart;
+      free_at.pop();
+      free_at.push(t);
+      makespan = std::max(makespan, t);
+    }
+  }
+  const double prep_ctas = (double)vchunks * std::max(1, HV / 2);
+  double us = std::ceil(prep_ctas / (3.0 * sms)) * kPrepWaveUs;
+  if (p.S > 1)
+    us += kChainStepUs * (p.S - 1) + (double)(p.T - p.b[1]) * HV * 768.0 / kOutBytesPerUs;
+  return makespan + us / kStepUs;
+}
+
+// The plan for segments = 0: segment 0 of x chunks (run once) and S - 1 equal later
+// segments (run twice each), S <= 16 and x chosen by the cost model; segmenting is taken
+// only when the model predicts at least 5 % less time than one segment.  When every run
+// fits on the SMs at once this gives about equal segments; with more runs x v-heads x 4
+// CTAs than SMs it lets segment 0 run long on its own SMs while the shorter later runs
+// pass over the other SMs in several waves.
+Plan auto_plan(long long T, int HV, int sms) {
+  const long long chunks = (T + 63) / 64;
+  Plan best = equal_plan(T, 1);
+  if (sms <= 0 || chunks < 2) return best;
+  const double one = plan_cost(best, HV, sms);
+  double best_cost = one;
+  const int smax = (int)std::min<long long>(16, chunks);
+  for (int S = 2; S <= smax; ++S) {
+    // x from chunks / S (equal) up to chunks - (S - 1): a coarse scan, then halving steps
+    const long long lo = (chunks + S - 1) / S, hi = chunks - (S - 1);
+    if (lo > hi) continue;
+    long long step = std::max(1LL, (hi - lo) / 32), bx = lo;
+    double bc = plan_cost(lead_plan(T, S, lo), HV, sms);
+    for (long long x = lo + step; x <= hi; x += step) {
+      const double c = plan_cost(lead_plan(T, S, x), HV, sms);
+      if (c < bc) bc = c, bx = x;
+    }
+    while (step > 1) {
+      step /= 2;
+      for (long long x : {bx - step, bx + step}) {
+        if (x < lo || x > hi) continue;
+        const double c = plan_cost(lead_plan(T, S, x), HV, sms);
+        if (c < bc) bc = c, bx = x;
+      }
+    }
+    if (bc < best_cost) best_cost = bc, best = lead_plan(T, S, bx);
+  }
+  return best_cost < 0.95 * one ? best : equal_plan(T, 1);
+}
+
+// A plan from caller-given bounds (host memory, S + 1 token offsets): b[0] = 0, strictly
+// increasing, interior bounds on 64-token chunks, b[S] = T, S <= 64.
+bool bounds_plan(long long T, int S, const int* bounds, Plan* p) {
+  if (S < 1 || S > kMaxSegments || bounds == nullptr || bounds[0] != 0 || bounds[S] != T)
+    return false;
+  p->T = T;
+  p->S = S;
+  for (int s = 0; s <= S; ++s) {
+    if (s > 0 && bounds[s] <= bounds[s - 1]) return false;
+    if (s > 0 && s < S && bounds[s] % 64 != 0) return false;
+    p->b[s] = bounds[s];
+  }
+  return true;
 }
 
 int sm_count() {
@@ -65,12 +176,22 @@ int sm_count() {
   return sms;
 }
 
-int resolve_segments(long long T, int HV, int segments) {
-  if (segments > 0) return segments;
-  // the largest count whose runs all hold an SM at once: 4 state CTAs per (run, v-head)
-  const int sms = sm_count();
-  const int per_run = std::max(1, 4 * HV);
-  return std::max(1, (sms / per_run + 1) / 2);
+// Plans for segments = 0 are cached per (T, HV, SMs): the search takes milliseconds.
+Plan make_plan(long long T, int HV, int segments, int sms) {
+  if (segments > 0 || T <= 0) return equal_plan(T, std::max(1, segments));
+  static std::mutex mu;
+  static std::map<std::tuple<long long, int, int>, Plan> cache;
+  const auto key = std::make_tuple(T, HV, sms);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const Plan p = auto_plan(T, HV, sms);
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 256) cache.clear();
+  cache[key] = p;
+  return p;
 }
 
 struct Layout {
@@ -95,15 +216,30 @@ inline bool misaligned(const void* p, uintptr_t n) {
 
 }  // namespace
 
+extern "C" int gdn_prefill_segment_plan(int total_tokens, int num_v_heads, int segments,
+                                        int num_sms, int* bounds, int capacity) {
+  if (total_tokens < 0 || num_v_heads <= 0 || segments < 0 || capacity < 0 ||
+      (capacity > 0 && bounds == nullptr))
+    return GDN_ERR_INVALID_ARGUMENT;
+  const Plan p = make_plan(total_tokens, num_v_heads, segments,
+                           num_sms > 0 ? num_sms : (segments > 0 ? 0 : sm_count()));
+  for (int s = 0; s <= p.S && s < capacity; ++s) bounds[s] = (int)p.b[s];
+  return p.S;
+}
+
 extern "C" int gdn_prefill_segments_auto(int total_tokens, int num_v_heads) {
-  if (total_tokens < 0 || num_v_heads <= 0) return GDN_ERR_INVALID_ARGUMENT;
-  return make_plan(total_tokens, resolve_segments(total_tokens, num_v_heads, 0)).S;
+  return gdn_prefill_segment_plan(total_tokens, num_v_heads, 0, 0, nullptr, 0);
 }
 
 extern "C" size_t gdn_prefill_segmented_workspace_size(int total_tokens, int num_v_heads,
-                                                       int segments) {
+                                                       int segments, const int* segment_bounds) {
   if (total_tokens <= 0 || num_v_heads <= 0 || segments < 0) return 0;
-  const Plan p = make_plan(total_tokens, resolve_segments(total_tokens, num_v_heads, segments));
+  Plan p;
+  if (segment_bounds != nullptr) {
+    if (!bounds_plan(total_tokens, segments, segment_bounds, &p)) return 0;
+  } else {
+    p = make_plan(total_tokens, num_v_heads, segments, segments > 0 ? 0 : sm_count());
+  }
   return make_layout(p, num_v_heads).total;
 }
 
@@ -111,7 +247,8 @@ extern "C" int gdn_prefill_segmented_launch(
     const void* q, const void* k, const void* v, const float* state, const float* A_log,
     const void* a, const float* dt_bias, const void* b, float scale, void* output,
     float* new_state, int total_tokens, int num_q_heads, int num_k_heads, int num_v_heads,
-    int head_size, int use_qk_l2norm, int segments, long long q_stride, long long k_stride,
+    int head_size, int use_qk_l2norm, int segments, const int* segment_bounds,
+    long long q_stride, long long k_stride,
     long long v_stride, long long a_stride, long long b_stride, void* workspace,
     size_t workspace_bytes, void* stream) {
   using namespace gdn;
@@ -137,7 +274,12 @@ extern "C" int gdn_prefill_segmented_launch(
     if (rs.q < qk_row || rs.k < qk_row || rs.v < v_row || rs.a < HV || rs.b < HV)
       return GDN_ERR_INVALID_ARGUMENT;
   }
-  const Plan plan = make_plan(total_tokens, resolve_segments(total_tokens, HV, segments));
+  Plan plan;
+  if (segment_bounds != nullptr) {
+    if (!bounds_plan(total_tokens, segments, segment_bounds, &plan)) return GDN_ERR_INVALID_ARGUMENT;
+  } else {
+    plan = make_plan(total_tokens, HV, segments, segments > 0 ? 0 : sm_count());
+  }
   const Layout lay = make_layout(plan, HV);
   if (workspace == nullptr || workspace_bytes < lay.total) return GDN_ERR_WORKSPACE;
   if (misaligned(workspace, 1024)) return GDN_ERR_INVALID_ARGUMENT;

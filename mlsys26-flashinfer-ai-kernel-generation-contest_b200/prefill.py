@@ -12,6 +12,7 @@ or int64), so the call never synchronises the host.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -199,6 +200,17 @@ def segments_auto(total_tokens: int, num_v_heads: int) -> int:
     return int(LIB.gdn_prefill_segments_auto(total_tokens, num_v_heads))
 
 
+def segment_plan(total_tokens: int, num_v_heads: int, segments: int = 0, sms: int = 0):
+    """Token bounds [0, b_1, .., T] of the segments gdn_prefill_segmented cuts: `segments`
+    equal shares of the chunks, or for 0 the plan of the library's cost model on `sms`
+    SMs (0: the current device's)."""
+    buf = (ctypes.c_int * 66)()
+    S = int(LIB.gdn_prefill_segment_plan(total_tokens, num_v_heads, segments, sms, buf, 66))
+    if S < 1:
+        raise ValueError(f"gdn_prefill_segment_plan: {LIB.gdn_status_string(S).decode()}")
+    return [int(buf[i]) for i in range(S + 1)]
+
+
 def segmented_launches(segments: int) -> int:
     """Number of this library's kernels one gdn_prefill_segmented call launches."""
     if segments <= 1:  # run offsets, chunk offsets, preparation, state
@@ -208,7 +220,8 @@ def segmented_launches(segments: int) -> int:
 
 
 def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=None,
-                          new_state=None, *, segments: int = 0, use_qk_l2norm: bool = False):
+                          new_state=None, *, segments: int = 0, bounds=None,
+                          use_qk_l2norm: bool = False):
     """Prefill of ONE sequence whose v-heads alone leave most SMs idle (a sequence sharded
     by q/k-head group over several GPUs, or a model with few heads per GPU), split into
     token segments that run side by side in a single launch of the split kernels
@@ -221,10 +234,11 @@ def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=No
 
     q, k [T, HQ, 128], v [T, HV, 128], a, b [T, HV] bf16 (token rows may be strided);
     state [1, HV, 128, 128] fp32 or None; returns (output [T, HV, 128] bf16, new_state
-    [1, HV, 128, 128] fp32).  `segments` = 0 picks the largest count whose 2 S - 1 runs
-    fit on the SMs at once (segments_auto); 1 is an ordinary split-kernel prefill.  The
-    outputs of the later segments carry one more bf16 rounding (of o^I); the final state
-    is fp32 throughout."""
+    [1, HV, 128, 128] fp32).  `segments` = S > 0 cuts S equal segments, 0 takes the
+    library's plan for the device (segment_plan); `bounds` = [0, b_1, .., T] (interior
+    bounds multiples of 64) gives the segments explicitly.  One segment is an ordinary
+    split-kernel prefill.  The outputs of the later segments carry one more bf16 rounding
+    (of o^I); the final state is fp32 throughout."""
     dev = C.cuda_device(q)
     C.tensor("q", q, torch.bfloat16, 3, dev, strided=True)
     C.tensor("k", k, torch.bfloat16, 3, dev, strided=True)
@@ -267,7 +281,12 @@ def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=No
     out = output if dense(output) else torch.empty(T, HV, D, dtype=torch.bfloat16, device=dev)
     (q, qs), (k, ks), (v, vs) = C.rows_in(q, 8, 16), C.rows_in(k, 8, 16), C.rows_in(v, 8, 16)
     (a, as_), (b, bs) = C.rows_in(a), C.rows_in(b)
-    ws_n = int(LIB.gdn_prefill_segmented_workspace_size(T, HV, segments))
+    cb = None
+    if bounds is not None:
+        bounds = [int(x) for x in bounds]
+        segments = len(bounds) - 1
+        cb = (ctypes.c_int * len(bounds))(*bounds)
+    ws_n = int(LIB.gdn_prefill_segmented_workspace_size(T, HV, segments, cb))
     ws = _workspace(dev, ws_n + 1024) if ws_n > 0 else None
     ws_ptr = ws_len = 0
     if ws is not None:  # the launch wants its workspace 1024-byte aligned
@@ -277,7 +296,7 @@ def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=No
         q.data_ptr(), k.data_ptr(), v.data_ptr(),
         state_in.data_ptr() if state_in is not None else None, A_log.data_ptr(), a.data_ptr(),
         dt_bias.data_ptr(), b.data_ptr(), sc, out.data_ptr(), ns.data_ptr(), T, HQ, HK, HV, D,
-        int(bool(use_qk_l2norm)), segments, qs, ks, vs, as_, bs, ws_ptr or None, ws_len,
+        int(bool(use_qk_l2norm)), segments, cb, qs, ks, vs, as_, bs, ws_ptr or None, ws_len,
         C.stream_handle(dev)))
     if out is not output:
         output.copy_(out)

@@ -351,26 +351,19 @@ def segment_scan_local(run, inp: Dict[str, torch.Tensor], world: int
 # would otherwise be idle.
 
 
-def local_segments(num_v_heads: int, total_tokens: int, sms: int = 148,
-                   ctas_per_head: int = 4, align: int = 64) -> int:
-    """Largest segment count S whose 2 S - 1 runs of one sequence (ctas_per_head CTAs per
-    v-head and run: the split state kernel's four 32-row v-blocks) all fit on `sms` SMs at
-    once, with at least one 64-token chunk per segment; 1 when segmenting cannot help."""
-    per_run = max(1, num_v_heads * ctas_per_head)
-    s = max(1, (sms // per_run + 1) // 2)
-    chunks = (total_tokens + align - 1) // align
-    return max(1, min(s, chunks))
-
-
-def segmented_layout(total_tokens: int, segments: int, device
+def segmented_layout(total_tokens: int, segments: int, device, bounds: List[int] = None
                      ) -> Tuple[List[Tuple[int, int]], torch.Tensor]:
     """For one sequence of `total_tokens` tokens in `segments` equal segments (on 64-token
-    chunk boundaries): (bounds, cu_seqlens int32 of the 2 S - 1 runs of one call).  Run 0
-    is segment 0; runs 2 s - 1 and 2 s are segment s from the identity (v = 0) and from
-    zero.  `segments` is capped at the number of chunks, so that no segment is empty (an
-    empty run would return a zero state, not the identity map)."""
-    segments = max(1, min(segments, (total_tokens + 63) // 64))
-    bounds = segment_bounds(total_tokens, segments, first_weight=1)
+    chunk boundaries), or at the token offsets `bounds` = [0, b_1, .., total_tokens] when
+    given: (bounds, cu_seqlens int32 of the 2 S - 1 runs of one call).  Run 0 is segment
+    0; runs 2 s - 1 and 2 s are segment s from the identity (v = 0) and from zero.
+    `segments` is capped at the number of chunks, so that no segment is empty (an empty
+    run would return a zero state, not the identity map)."""
+    if bounds is None:
+        segments = max(1, min(segments, (total_tokens + 63) // 64))
+        bounds = segment_bounds(total_tokens, segments, first_weight=1)
+    else:
+        bounds = [(int(bounds[i]), int(bounds[i + 1])) for i in range(len(bounds) - 1)]
     cu = [0]
     for s, (lo, hi) in enumerate(bounds):
         for _ in range(1 if s == 0 else 2):

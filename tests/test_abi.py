@@ -169,7 +169,7 @@ def test_segmented_argument_checks_return_before_launch():
     def call(T=256, hq=2, hk=2, hv=4, hd=128, segments=2, ns=fake, qs=256):
         return lib.gdn_prefill_segmented_launch(
             fake, fake, fake, None, fake, fake, fake, fake, 0.0, fake, ns, T, hq, hk, hv, hd, 1,
-            segments, qs, 256, 512, 4, 4, fake, 1 << 30, None)
+            segments, None, qs, 256, 512, 4, 4, fake, 1 << 30, None)
     assert call(T=-1) == -1                      # GDN_ERR_INVALID_ARGUMENT
     assert call(segments=-1) == -1
     assert call(ns=None) == -1
@@ -178,8 +178,16 @@ def test_segmented_argument_checks_return_before_launch():
     assert call(hd=64) == -2
     assert call(qs=128) == -1                    # q rows overlap
     # sizes need no device: S = min(segments, chunks); one segment has no scratch rows
-    assert lib.gdn_prefill_segmented_workspace_size(0, 4, 2) == 0
-    two = lib.gdn_prefill_segmented_workspace_size(256, 4, 2)
-    assert two > lib.gdn_prefill_segmented_workspace_size(256, 4, 1) > 0
-    assert lib.gdn_prefill_segmented_workspace_size(256, 4, 64) == \
-        lib.gdn_prefill_segmented_workspace_size(256, 4, 4)   # capped at the 4 chunks
+    size = lib.gdn_prefill_segmented_workspace_size
+    assert size(0, 4, 2, None) == 0
+    assert size(256, 4, 2, None) > size(256, 4, 1, None) > 0
+    assert size(256, 4, 64, None) == size(256, 4, 4, None)   # capped at the 4 chunks
+    import ctypes
+    arr = lambda *x: (ctypes.c_int * len(x))(*x)  # noqa: E731
+    assert size(256, 4, 2, arr(0, 128, 256)) == size(256, 4, 2, None)
+    assert size(256, 4, 2, arr(0, 192, 256)) < size(256, 4, 2, None)   # fewer scratch rows
+    for bad in (arr(0, 100, 256), arr(0, 256, 256), arr(64, 128, 256), arr(0, 128, 255)):
+        assert size(256, 4, 2, bad) == 0
+        assert lib.gdn_prefill_segmented_launch(
+            fake, fake, fake, None, fake, fake, fake, fake, 0.0, fake, fake, 256, 2, 2, 4, 128,
+            1, 2, bad, 256, 256, 512, 4, 4, fake, 1 << 30, None) == -1

@@ -203,7 +203,7 @@ def test_p2_one_call_segmented_vs_oracle(cuda):
     pkg = load_pkg()
     sub, _ = head_subset(p2_inputs(), P2_QK_HEADS)
     d = to(sub, cuda)
-    assert pkg.sharding.local_segments(d["v"].shape[1], d["q"].shape[0]) == 3
+    assert pkg.prefill.segments_auto(d["q"].shape[0], d["v"].shape[1]) > 1
     out, fin = pkg.gdn_prefill_segmented(d["q"], d["k"], d["v"], d["state"], d["A_log"],
                                          d["a"], d["dt_bias"], d["b"], d["scale"],
                                          use_qk_l2norm=True)
@@ -213,13 +213,14 @@ def test_p2_one_call_segmented_vs_oracle(cuda):
     assert pkg.device_error() == 0
 
 
-@pytest.mark.parametrize("qk_heads,segments", [(4, 2), (2, 5)])
+@pytest.mark.parametrize("qk_heads,segments", [(8, 4), (4, 8), (2, 5)])
 def test_p2_head_group_segmented_vs_unsplit(cuda, qk_heads, segments):
-    """The multi-GPU P2 plan's per-rank call (a q/k-head group of 4 or 2 heads, i.e. 8 or
-    4 v-heads, over 4 or 8 GPUs): segmented in one call, against the unsplit call."""
+    """The multi-GPU P2 plan's per-rank call (a q/k-head group of 8, 4 or 2 heads, i.e.
+    16, 8 or 4 v-heads, over 2, 4 or 8 GPUs): segmented in one call by the library's own
+    plan, against the unsplit call."""
     pkg = load_pkg()
     sh = pkg.sharding.prefill_head_shard(to(p2_inputs(), cuda), 0, qk_heads)
-    assert pkg.sharding.local_segments(sh["v"].shape[1], sh["q"].shape[0]) == segments
+    assert pkg.prefill.segments_auto(sh["q"].shape[0], sh["v"].shape[1]) == segments
     keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")
     ro, rs = pkg.gdn_prefill(*[sh[k_] for k_ in keys], use_qk_l2norm=True)
     out = torch.full_like(ro, float("nan"))

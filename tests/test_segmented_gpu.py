@@ -12,11 +12,11 @@ from gpu_util import assert_parity, oracle_prefill, to
 pytestmark = pytest.mark.gpu
 
 
-def composed(pkg, d, segments):
+def composed(pkg, d, segments, bounds=None):
     """The segmented scan built from a split-kernel call on concatenated runs."""
     S = pkg.sharding
     T, HV = d["q"].shape[0], d["v"].shape[1]
-    layout = S.segmented_layout(T, segments, d["q"].device)
+    layout = S.segmented_layout(T, segments, d["q"].device, bounds)
     run = S.segmented_inputs(d, layout)
     n = len(layout[0])
     o_runs, f_runs = pkg.gdn_prefill(run["q"], run["k"], run["v"], run["state"], d["A_log"],
@@ -54,6 +54,29 @@ def test_native_equals_composed_and_oracle(cuda, T, hv, segments, with_state):
     assert_parity(o, s, ro, rs, what=f"segmented T={T} x{segments}")
 
 
+@pytest.mark.parametrize("hv", [16, 8])
+def test_planned_uneven_segments_equal_composed(cuda, hv):
+    """segments = 0 with the library's plan for a head share of 2 or 4 GPUs (a long
+    segment 0, shorter equal later segments; P2's length), against the composition with
+    the same bounds, bit for bit, and the unsplit call within the bounds."""
+    pkg = load_pkg()
+    T = 32768
+    bounds = pkg.prefill.segment_plan(T, hv)
+    later = [bounds[i + 1] - bounds[i] for i in range(1, len(bounds) - 1)]
+    assert len(bounds) > 3 and bounds[1] > max(later)
+    inp = pkg.workloads.prefill_inputs([T], hq=hv // 2, hv=hv, seed=hv)
+    d = to(inp, cuda)
+    o, s = native(pkg, d, 0)
+    co, cs = composed(pkg, d, 0, bounds)
+    ro, rs = pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
+                             d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"],
+                             use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert pkg.device_error() == 0
+    assert torch.equal(o, co) and torch.equal(s, cs)
+    assert_parity(o, s, ro.cpu(), rs.cpu(), what=f"planned segments hv={hv}")
+
+
 def test_one_segment_is_the_split_call(cuda):
     pkg = load_pkg()
     d = to(pkg.workloads.prefill_inputs([1000], hq=2, hv=4, seed=71), cuda)
@@ -72,7 +95,7 @@ def test_strided_views_in_place_state_and_auto_count(cuda):
     from test_strided_gpu import fused_views
     d = to(pkg.workloads.prefill_inputs([5000], hq=2, hv=4, seed=72), cuda)
     S = pkg.prefill.segments_auto(5000, 4)
-    assert S == pkg.sharding.local_segments(4, 5000) and S > 1
+    assert S == len(pkg.prefill.segment_plan(5000, 4)) - 1 and S > 1
     o, s = native(pkg, d, 0)
     sv = fused_views(d, (5000,))
     st = d["state"].clone()
@@ -103,7 +126,7 @@ def test_c_abi_rejections(cuda):
     d = to(pkg.workloads.prefill_inputs([256], hq=2, hv=4, seed=74), cuda)
     out = torch.empty(256, 4, 128, dtype=torch.bfloat16, device=cuda)
     ns = torch.empty(1, 4, 128, 128, device=cuda)
-    nbytes = L.gdn_prefill_segmented_workspace_size(256, 4, 2)
+    nbytes = L.gdn_prefill_segmented_workspace_size(256, 4, 2, None)
     ws = torch.empty(nbytes + 2048, dtype=torch.uint8, device=cuda)
     base = (ws.data_ptr() + 1023) // 1024 * 1024
 
@@ -112,7 +135,7 @@ def test_c_abi_rejections(cuda):
             d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["state"].data_ptr(),
             d["A_log"].data_ptr(), d["a"].data_ptr(), d["dt_bias"].data_ptr(),
             d["b"].data_ptr(), 0.0, out_ptr, ns.data_ptr(), 256, 2, hk, 4, 128, 1, segments,
-            qs, 256, 512, 4, 4, ws_ptr, ws_len, torch.cuda.current_stream().cuda_stream)
+            None, qs, 256, 512, 4, 4, ws_ptr, ws_len, torch.cuda.current_stream().cuda_stream)
     name = lambda st: L.gdn_status_string(st).decode()  # noqa: E731
     assert name(call(ws_len=nbytes - 1)) == "GDN_ERR_WORKSPACE"
     assert name(call(ws_ptr=base + 16)) == "GDN_ERR_INVALID_ARGUMENT"   # not 1024-aligned

@@ -155,10 +155,23 @@ def test_one_call_segmented_scan_matches_unsplit(T, segments):
     assert O.state_rel_err(fin, rs) < 1e-5
 
 
-def test_local_segment_count():
-    S = load_pkg().sharding
-    assert S.local_segments(32, 32768) == 1   # 128 CTAs per run: no room for a second
-    assert S.local_segments(16, 32768) == 1
-    assert S.local_segments(8, 32768) == 2    # 3 runs x 32 CTAs
-    assert S.local_segments(4, 32768) == 5    # 9 runs x 16 CTAs
-    assert S.local_segments(4, 100) == 2      # capped at the number of chunks
+def test_segment_plans_of_the_library():
+    """The segmented call's plans (gdn_prefill_segment_plan, host-only): explicit counts
+    are the equal shares of sharding.segment_bounds; the automatic plan for B200's 148 SMs
+    keeps one segment where the runs cannot spread (32 v-heads), and otherwise a long
+    segment 0 with equal later segments."""
+    pkg = load_pkg()
+    S = pkg.sharding
+    plan = pkg.prefill.segment_plan
+    for T, n in ((32768, 5), (5000, 3), (200, 9), (130, 2), (1, 4)):
+        b = plan(T, 4, n)
+        assert [(b[i], b[i + 1]) for i in range(len(b) - 1)] == \
+            S.segment_bounds(T, min(n, (T + 63) // 64), first_weight=1)
+    assert plan(32768, 32, 0, sms=148) == [0, 32768]
+    for hv, count in ((16, 4), (8, 8), (4, 5)):
+        b = plan(32768, hv, 0, sms=148)
+        assert len(b) == count + 1 and b[0] == 0 and b[-1] == 32768
+        assert all(x % 64 == 0 for x in b[:-1])
+        later = [b[i + 1] - b[i] for i in range(1, count)]
+        assert b[1] >= max(later) and max(later) - min(later) <= 64
+    assert plan(0, 4, 0, sms=148) == [0, 0]
