@@ -9,7 +9,7 @@
 // state goes to final_state[idx[b]]; the pool may be updated in place.
 //
 // Same HBM-streaming structure as the decode kernel (gdn_decode.cu): 8 lanes own
-// one 512-byte state row, the rows of one (b, v-head) are spread over 1-4 CTAs, and
+// one 512-byte state row, the rows of one (b, v-head) are spread over 2-4 CTAs, and
 // the state stays in registers across the T tokens, so the pool slot is read once
 // and written once.  The next token's q/k/v/gates are loaded while the current
 // token is applied.  A batch row whose index lies outside [0, pool_size) is a
@@ -45,8 +45,8 @@ __device__ __forceinline__ void mtp_load_token(const __nv_bfloat16* __restrict__
   tk.beta = sigmoid_f(bf2f(b[bt * HV + h]));
 }
 
-template <int RPW, bool L2NORM, bool INTER, typename IdxT, typename ST>
-__global__ void __launch_bounds__(256)
+template <int RPW, int MINB, bool L2NORM, bool INTER, typename IdxT, typename ST>
+__global__ void __launch_bounds__(256, MINB)
     mtp_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                const __nv_bfloat16* __restrict__ v, const ST* pool,
                const IdxT* __restrict__ indices, const float* __restrict__ A_log,
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256)
   for (int r = 0; r < NG; ++r) RS::store(nsp + r * 4 * kHeadDim, j, S[r]);
 }
 
-template <int RPW, typename IdxT, typename ST>
+template <int RPW, int MINB, typename IdxT, typename ST>
 cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const ST* pool,
                            const void* indices, const float* A_log, const void* a,
                            const float* dt_bias, const void* b, float scale, void* out,
@@ -171,7 +171,7 @@ cudaError_t launch_mtp_rpw(const void* q, const void* k, const void* v, const ST
   auto I = static_cast<const IdxT*>(indices);
   const int ratio = HV / HQ;
 #define GDN_MTP_LAUNCH(L2, IN)                                                                \
-  mtp_kernel<RPW, L2, IN, IdxT, ST><<<grid, block, 0, st>>>(Q, K, V, pool, I, A_log, A, dt_bias, \
+  mtp_kernel<RPW, MINB, L2, IN, IdxT, ST><<<grid, block, 0, st>>>(Q, K, V, pool, I, A_log, A, dt_bias, \
                                                         Bt, scale, O, new_pool, inter, T,    \
                                                         pool_size, HQ, HV, ratio)
   if (inter != nullptr) {
@@ -189,16 +189,17 @@ cudaError_t launch_mtp(const void* q, const void* k, const void* v, const ST* po
                        const float* dt_bias, const void* b, float scale, void* out,
                        ST* new_pool, ST* inter, int batch, int T, long long pool_size,
                        int HQ, int HV, bool l2norm, cudaStream_t st) {
-  // same CTA sizing as the decode kernel: enough CTAs to fill 148 SMs several times
+  // Write-heavy (with the rollback buffer, T + 1 state writes per read): what matters is
+  // how many stores each SM keeps in flight.  64 rows per CTA at two CTAs per SM (registers
+  // capped at 128, no spills) overlaps one CTA's state loads with the other's stores; at
+  // B = 128, T = 4 that is 259 us against 279 us for 128 rows at one CTA per SM, the rate of
+  // a plain stream with the same 1 : 5 read / write mix.  Small batches: 32 rows per CTA.
   const long long heads = (long long)batch * HV;
-  if (heads >= 4 * 148)
-    return launch_mtp_rpw<16, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
-                                    new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
   if (heads >= 2 * 148)
-    return launch_mtp_rpw<8, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
-                                   new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
-  return launch_mtp_rpw<4, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
-                                 new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
+    return launch_mtp_rpw<8, 2, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+                                          new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
+  return launch_mtp_rpw<4, 1, IdxT, ST>(q, k, v, pool, indices, A_log, a, dt_bias, b, scale, out,
+                                        new_pool, inter, batch, T, pool_size, HQ, HV, l2norm, st);
 }
 
 inline bool misaligned(const void* p, uintptr_t n) {
