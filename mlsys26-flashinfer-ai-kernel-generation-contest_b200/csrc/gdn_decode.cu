@@ -28,8 +28,8 @@
 namespace gdn {
 namespace {
 
-template <int RPW, bool L2NORM, bool HAS_STATE, typename ST>
-__global__ void __launch_bounds__(256)
+template <int RPW, int MINB, bool L2NORM, bool HAS_STATE, typename ST>
+__global__ void __launch_bounds__(256, MINB)
     decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                   const __nv_bfloat16* __restrict__ v, const ST* state,
                   const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ a,
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-template <int RPW, typename ST>
+template <int RPW, int MINB, typename ST>
 cudaError_t launch_rpw(const void* q, const void* k, const void* v, const ST* state,
                        const float* A_log, const void* a, const float* dt_bias, const void* b,
                        float scale, void* out, ST* new_state, int batch, int HQ, int HV,
@@ -139,14 +139,14 @@ cudaError_t launch_rpw(const void* q, const void* k, const void* v, const ST* st
   auto O = static_cast<__nv_bfloat16*>(out);
   if (state != nullptr) {
     if (l2norm)
-      decode_kernel<RPW, true, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
+      decode_kernel<RPW, MINB, true, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
     else
-      decode_kernel<RPW, false, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
+      decode_kernel<RPW, MINB, false, true, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
   } else {
     if (l2norm)
-      decode_kernel<RPW, true, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
+      decode_kernel<RPW, MINB, true, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
     else
-      decode_kernel<RPW, false, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
+      decode_kernel<RPW, MINB, false, false, ST><<<grid, block, 0, stream>>>(Q, K, V, state, A_log, A, dt_bias, Bt, scale, O, new_state, rs, HV, ratio);
   }
   return cudaGetLastError();
 }
@@ -425,12 +425,17 @@ int decode_entry(const void* q, const void* k, const void* v, const ST* state, c
   if (state != nullptr && stream_pays<ST>(heads) && rows16)
     err = launch_stream<ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch,
                             num_q_heads, num_v_heads, rs, l2, st);
-  else if (heads >= 4 * 148)
-    err = launch_rpw<16, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
-  else if (heads >= 2 * 148)
-    err = launch_rpw<8, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
+  // CTA sizing, measured on B200 with L2 cold (ncu launch times, 32 v-heads): from 256
+  // heads on, 128 rows per CTA at two CTAs per SM (B = 8: 7.7 us against 8.9 us with 32
+  // rows; B = 16: 11.5 against 13.0 us with 64); below that 32 rows per CTA, four CTAs per
+  // SM (registers capped at 64) once three per SM would need a second wave (B = 4: 5.8
+  // against 6.4 us), else three per SM (B = 1: 4.0 us; the cap costs 0.6 us there).
+  else if (heads >= 256)
+    err = launch_rpw<16, 2, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
+  else if (heads * 4 > 3 * 148 && sizeof(ST) == 4)  // (the bf16 variant would spill)
+    err = launch_rpw<4, 4, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
   else
-    err = launch_rpw<4, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
+    err = launch_rpw<4, 1, ST>(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, batch, num_q_heads, num_v_heads, rs, l2, st);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 }  // namespace
