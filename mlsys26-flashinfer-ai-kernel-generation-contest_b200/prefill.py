@@ -28,16 +28,22 @@ _LPT_MAX_SEQS = 8192  # the longest-first ordering kernel's capacity
 
 _ws_lock = threading.Lock()
 _ws_cache = {}
+_ws_retired = []  # superseded buffers: a CUDA graph captured over an earlier call still uses them
 
 
 def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     """Persistent per-device scratch buffer, grown on demand (contents are
-    rewritten by every call that uses them)."""
+    rewritten by every call that uses them).  A buffer that is outgrown is kept
+    alive, not freed, so that CUDA graphs captured over earlier calls stay valid;
+    growth at least doubles, so few are ever retired."""
     key = (dev.index if dev.index is not None else torch.cuda.current_device())
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+            grow = max(nbytes, 1 << 20, 2 * buf.numel() if buf is not None else 0)
+            if buf is not None:
+                _ws_retired.append(buf)
+            buf = torch.empty(grow, dtype=torch.uint8, device=dev)
             _ws_cache[key] = buf
         return buf
 

@@ -68,3 +68,25 @@ def test_rank_shares_for_one_gpu_emulation():
         seqs = B.prefill_plan(pkg, "P3", d, "seqs")
         assert seqs[0] == "seqs" and seqs[1] == pkg.sharding.lpt_assign(
             pkg.workloads.draw_seqlens(64, 512, 8192, 0), 8)[r]
+
+
+def test_workspace_growth_keeps_old_buffers_alive(monkeypatch):
+    """A grown prefill workspace never frees the buffer a captured CUDA graph may hold."""
+    import importlib
+    import torch
+    pre = importlib.import_module(PKG_NAME + ".prefill")
+    made = []
+
+    def fake_empty(n, dtype=None, device=None):
+        made.append(n)
+        return torch.zeros(n, dtype=dtype)
+    monkeypatch.setattr(pre.torch, "empty", fake_empty)
+    monkeypatch.setattr(pre, "_ws_cache", {})
+    monkeypatch.setattr(pre, "_ws_retired", [])
+    dev = torch.device("cuda", 7)
+    a = pre._workspace(dev, 10)
+    assert pre._workspace(dev, 100) is a                       # 1 MiB minimum
+    b = pre._workspace(dev, (1 << 20) + 1)
+    assert b is not a and b.numel() == 2 << 20 and pre._ws_retired == [a]
+    assert pre._workspace(dev, 5 << 20).numel() == 5 << 20
+    assert made == [1 << 20, 2 << 20, 5 << 20]
