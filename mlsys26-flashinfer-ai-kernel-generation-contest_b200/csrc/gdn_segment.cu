@@ -225,24 +225,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   S = B_0;  S <- S A_m + B_m for m = 1 .. rank-1;  start = S;  final = S A_rank + B_rank.
 // Rows of S evolve independently (row i of S A depends on row i of S only), so each CTA
 // carries 8 RPT rows of one v-head through the whole chain with no exchange between CTAs.
-// 128 threads, each RPT rows x 8 columns (8 RPT FMAs per 8 A values read), fp32 FMAs in
-// the same order for every RPT (the results do not depend on it).  A_m is staged in shared
-// memory, the next map's A copied in (cp.async) while a step computes.  RPT = 4 (32 rows,
+// 256 threads, each RPT rows x 4 columns (4 RPT FMAs per 4 A values read; two warps per
+// scheduler hide the shared-memory latency), fp32 FMAs in the same order for every RPT
+// and thread layout (the results do not depend on them).  A_m is staged in shared
+// memory, the next map's A copied in (one bulk copy) while a step computes.  RPT = 4 (32 rows,
 // 4 CTAs per v-head) when there are enough v-heads to fill the SMs, 2 or 1 otherwise.
 struct MapIndex {
   int a0, as, b0, bs;
 };
-constexpr int kChainThreads = 128;
+constexpr int kChainThreads = 256;
 constexpr int kSLd = kD + 4;  // padded S rows
-constexpr int kAPer = kD * kD / 4 / kChainThreads;  // 16-byte pieces of A per thread
 constexpr size_t chain_smem(int rpt) { return (size_t)(2 * kD * kD + 8 * rpt * kSLd) * sizeof(float); }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <int RPT>
 __global__ void __launch_bounds__(kChainThreads, 1)
@@ -253,23 +247,33 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   extern __shared__ __align__(16) float csm[];
   float* S = csm + 2 * kD * kD;  // [row][kSLd]
   const int h = blockIdx.y, r0 = kRows * blockIdx.x;
-  const int tid = threadIdx.x, rq = tid >> 4, cb = tid & 15;
-  // this thread's 8 columns: two groups of 4, 64 apart, so that the 16 column blocks of a
-  // half-warp read 256 contiguous bytes of an A row (no bank conflicts)
-  const int c0 = 4 * cb, c1 = 64 + 4 * cb;
+  // warp rq owns rows RPT rq .. RPT rq + RPT - 1 of the CTA's rows, lane cb columns 4 cb ..
+  // 4 cb + 3: a warp reads one 512-byte row of A per step (no bank conflicts) and one
+  // broadcast element of S per row
+  const int tid = threadIdx.x, rq = tid >> 5, cb = tid & 31;
+  const int c0 = 4 * cb;
   const size_t mat = (size_t)kD * kD;
   auto A = [&](int m) { return maps + ((size_t)(mi.a0 + m * mi.as) * HV + h) * mat; };
   auto B = [&](int m) { return maps + ((size_t)(mi.b0 + m * mi.bs) * HV + h) * mat; };
-  auto prefetch = [&](int m, float* dst) {
-    const float* src = A(m);
-#pragma unroll 8
-    for (int k = 0; k < kAPer; ++k) {
-      const int i = tid + k * kChainThreads;
-      cp_async16(dst + 4 * i, src + 4 * i);
+  // A_m (64 KiB, contiguous) arrives in one bulk copy into buffer (m - 1) & 1, counted on
+  // that buffer's mbarrier; buffer b completes its phase p at step m = 2 p + b + 1
+  __shared__ __align__(8) uint64_t abar[2];
+  if (tid == 0) {
+    mbar_init(&abar[0], 1);
+    mbar_init(&abar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto prefetch = [&](int m) {
+    if (tid == 0) {
+      fence_proxy_async();  // earlier reads of the buffer before the copy's writes
+      uint64_t* bar = &abar[(m - 1) & 1];
+      mbar_arrive_expect_tx(bar, (uint32_t)(mat * sizeof(float)));
+      bulk_load(csm + ((m - 1) & 1) * kD * kD, A(m), (uint32_t)(mat * sizeof(float)), bar);
     }
-    cp_async_commit();
   };
-  prefetch(1, csm);
+  int issued = 1;  // maps whose copies were issued (A_1 .. A_issued)
+  prefetch(1);
   // S = B_0 (this CTA's rows): the start state of segment 1
   for (int i = tid; i < kRows * kD / 4; i += kChainThreads) {
     const int r = i >> 5, c4 = i & 31;
@@ -280,60 +284,61 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   }
   for (int m = 1; m <= rank; ++m) {
     const float* As = csm + ((m - 1) & 1) * kD * kD;
-    cp_async_wait_all();
-    __syncthreads();  // A_m and S in place; the other A buffer is no longer read
-    if (m < rank) prefetch(m + 1, csm + (m & 1) * kD * kD);
-    // B_m rows: loaded now, added after the product (their latency hides behind it)
-    float4 bq[RPT][2];
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const float* brow = B(m) + (size_t)(r0 + RPT * rq + i) * kD;
-      bq[i][0] = __ldg(reinterpret_cast<const float4*>(brow + c0));
-      bq[i][1] = __ldg(reinterpret_cast<const float4*>(brow + c1));
+    const bool landed = mbar_wait(&abar[(m - 1) & 1], ((m - 1) >> 1) & 1, kWaitLimit);
+    if (__syncthreads_or(!landed)) {  // A_m and S in place; the other A buffer is free
+      if (tid == 0) {  // let the copies in flight land before the CTA exits (bounded)
+        atomicOr(&g_segment_device_error, kErrTmaTimeout);
+        for (int q = max(m, issued - 1); q <= issued; ++q)
+          mbar_wait(&abar[(q - 1) & 1], ((q - 1) >> 1) & 1, kWaitLimit);
+      }
+      return;
     }
-    float acc[RPT][8];
+    if (m < rank) {
+      prefetch(m + 1);
+      issued = m + 1;
+    }
+    // B_m rows: loaded now, added after the product (their latency hides behind it)
+    float4 bq[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i)
+      bq[i] = __ldg(reinterpret_cast<const float4*>(B(m) + (size_t)(r0 + RPT * rq + i) * kD + c0));
+    float acc[RPT][4];
 #pragma unroll
     for (int i = 0; i < RPT; ++i)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+      for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
     const float* srow = S + (RPT * rq) * kSLd;
     // software-pipelined: the shared-memory operands of step j + 1 are loaded while the
-    // FMAs of step j issue (one warp per scheduler cannot hide the load latency otherwise)
+    // FMAs of step j issue
     float4 x = *reinterpret_cast<const float4*>(As + c0);
-    float4 y = *reinterpret_cast<const float4*>(As + c1);
     float sv[RPT];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) sv[i] = srow[i * kSLd];
-#pragma unroll 2
+#pragma unroll 4
     for (int j = 0; j < kD; ++j) {
       const int jn = (j + 1) & (kD - 1);  // the last prefetch wraps to row 0 and is unused
       const float4 xn = *reinterpret_cast<const float4*>(As + jn * kD + c0);
-      const float4 yn = *reinterpret_cast<const float4*>(As + jn * kD + c1);
       float svn[RPT];
 #pragma unroll
       for (int i = 0; i < RPT; ++i) svn[i] = srow[i * kSLd + jn];
-      const float av[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+      const float av[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
       for (int i = 0; i < RPT; ++i)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(sv[i], av[e], acc[i][e]);
+        for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(sv[i], av[e], acc[i][e]);
       x = xn;
-      y = yn;
 #pragma unroll
       for (int i = 0; i < RPT; ++i) sv[i] = svn[i];
     }
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      acc[i][0] += bq[i][0].x; acc[i][1] += bq[i][0].y; acc[i][2] += bq[i][0].z;
-      acc[i][3] += bq[i][0].w; acc[i][4] += bq[i][1].x; acc[i][5] += bq[i][1].y;
-      acc[i][6] += bq[i][1].z; acc[i][7] += bq[i][1].w;
+      acc[i][0] += bq[i].x; acc[i][1] += bq[i].y; acc[i][2] += bq[i].z; acc[i][3] += bq[i].w;
     }
     if (m == rank) {  // the segment's own map: its final state; S holds its start state
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
         float* dst = final_out + ((size_t)h * kD + r0 + RPT * rq + i) * kD;
         *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
       break;
     }
@@ -342,7 +347,6 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     for (int i = 0; i < RPT; ++i) {
       float* d = S + (RPT * rq + i) * kSLd;
       *reinterpret_cast<float4*>(d + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-      *reinterpret_cast<float4*>(d + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
     }
     if (starts_all != nullptr) {  // S is now the start state of segment m + 1
       float* base = starts_all + (size_t)m * HV * kD * kD;
@@ -350,7 +354,6 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       for (int i = 0; i < RPT; ++i) {
         float* dst = base + ((size_t)h * kD + r0 + RPT * rq + i) * kD;
         *reinterpret_cast<float4*>(dst + c0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        *reinterpret_cast<float4*>(dst + c1) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
     }
   }
