@@ -57,6 +57,10 @@ struct PrefillArgs {
   long long vsrc = 0;
   void* out_alt = nullptr;
   int state_runs = INT_MAX;
+  // Only runs n < prep_runs get their per-chunk records prepared; an identity run reads
+  // the records of run n - rec_alias (it covers the same tokens as that run).
+  int prep_runs = INT_MAX;
+  int rec_alias = 0;
 };
 
 // Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).

@@ -101,8 +101,8 @@ double plan_cost(const Plan& p, int HV, int sms) {
   for (int i = 0; i < sms; ++i) free_at.push(0.0);
   double makespan = 0.0;
   long long vchunks = 0;
+  for (int s = 0; s < p.S; ++s) vchunks += (p.b[s + 1] - p.b[s] + 63) / 64;  // prepared once
   for (long long c : len) {
-    vchunks += c;
     for (int j = 0; j < 4 * HV; ++j) {
       const double t = free_at.top() + (double)c + kCtaStart;
       free_at.pop();
@@ -299,6 +299,8 @@ extern "C" int gdn_prefill_segmented_launch(
     p.vsplit = T;
     p.vsrc = b1;
     p.out_alt = ws + lay.alt;
+    p.prep_runs = S;     // the identity run of segment s reads the records of run s
+    p.rec_alias = S - 1;
   }
   if (!prefill_chunked_supported(p)) return GDN_ERR_UNSUPPORTED;
 

@@ -37,6 +37,7 @@
 // gdn_device_error), lets its copies and MMAs in flight land (again boundedly),
 // releases TMEM and returns.
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <climits>
 
 #include "gdn_chunk_math.cuh"
@@ -105,6 +106,9 @@ struct SplitParams {
   long long vsplit = LLONG_MAX, vsrc = 0;
   __nv_bfloat16* out_alt = nullptr;
   int state_runs = INT_MAX;
+  // records: only runs n < prep_runs are prepared; an identity run (rows >= vsplit) reads
+  // the records of run n - rec_alias (the same tokens, hence the same records)
+  int prep_runs = INT_MAX, rec_alias = 0;
 };
 
 // Input row of virtual token row r (a chunk never straddles vsplit).
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
   const int hpc = (p.ratio % 2 == 0) ? 2 : 1;
   const int hgroups = p.HV / hpc;
   const int g = blockIdx.x / hgroups, h0 = (blockIdx.x - g * hgroups) * hpc;
-  const int total = p.chunk_base[p.N];
+  const int total = p.chunk_base[p.prep_runs < p.N ? p.prep_runs : p.N];
   if (g >= total) return;
   int lo = 0, hi = p.N - 1;  // the sequence of chunk g: largest n with base[n] <= g
   while (lo < hi) {
@@ -652,7 +656,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       const size_t rstride = (size_t)HV * p.rec_stride;
-      const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[n] * HV + h) * p.rec_stride;
+      const int nrec = ident ? n - p.rec_alias : n;  // the run whose records these are
+      const uint8_t* rec0 = p.rec + ((size_t)p.chunk_base[nrec] * HV + h) * p.rec_stride;
       for (int cc = 0; cc < nchunks; ++cc) {
         const int bf = cc & 1;
         const uint32_t free_par = ((cc >> 1) + 1) & 1;  // phase cc/2 - 1 of the free barrier
@@ -1008,9 +1013,15 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   sp.vsrc = p.vsrc;
   sp.out_alt = static_cast<__nv_bfloat16*>(p.out_alt);
   sp.state_runs = p.state_runs;
+  sp.prep_runs = p.prep_runs;
+  sp.rec_alias = p.rec_alias;
+  // chunks to prepare: those of the first prep_runs runs (each run's chunks are at most
+  // its tokens / 64 + 1, and those runs' tokens are the input rows)
+  const long long prep_slots =
+      p.prep_runs < p.N ? std::min(lay.slots, (rows + kC - 1) / kC + p.prep_runs) : lay.slots;
   if (p.cu_int64)
-    return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
-  return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, lay.slots, s);
+    return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots, s);
+  return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots, s);
 }
 
 unsigned read_split_device_error(bool clear) {
