@@ -61,6 +61,10 @@ struct PrefillArgs {
   // the records of run n - rec_alias (it covers the same tokens as that run).
   int prep_runs = INT_MAX;
   int rec_alias = 0;
+  // Chunk offsets [N + 1] and longest-first sequence order [N] already written to device
+  // memory by the caller on the same stream (null: computed on the device from cu).
+  const int* ready_base = nullptr;
+  const int* ready_order = nullptr;
 };
 
 // Token-serial recurrent kernel over sequences [seq_offset, seq_offset + nseq).

@@ -34,13 +34,21 @@ constexpr int kMaxSegments = 64;           // runs' offsets travel as kernel par
 constexpr long long kMaxTokens = 1LL << 30;
 constexpr size_t kMat = (size_t)gdn::kHeadDim * gdn::kHeadDim * sizeof(float);
 
+// The runs' token offsets (cu), chunk offsets and longest-first order, known on the host,
+// written to the workspace by one small launch (no device-side scans).
 struct RunOffsets {
-  int n;                          // entries of v (runs + 1)
+  int n;                          // entries of v and base (runs + 1); order has n - 1
   int v[2 * kMaxSegments];
+  int base[2 * kMaxSegments];
+  int order[2 * kMaxSegments];
 };
 
-__global__ void run_offsets_kernel(const RunOffsets ro, int* cu) {
-  for (int i = threadIdx.x; i < ro.n; i += blockDim.x) cu[i] = ro.v[i];
+__global__ void run_offsets_kernel(const RunOffsets ro, int* cu, int* base, int* order) {
+  for (int i = threadIdx.x; i < ro.n; i += blockDim.x) {
+    cu[i] = ro.v[i];
+    base[i] = ro.base[i];
+    if (i + 1 < ro.n) order[i] = ro.order[i];
+  }
 }
 
 // Segment bounds b[0] = 0 < b[1] < .. < b[S] = T, interior bounds on 64-token chunks.
@@ -202,7 +210,7 @@ Layout make_layout(const Plan& p, int HV) {
   const auto up = [](size_t x) { return (x + 1023) / 1024 * 1024; };
   Layout l{};
   l.cu = 0;
-  l.split = up((size_t)(p.runs() + 1) * sizeof(int));
+  l.split = up((size_t)3 * (2 * kMaxSegments) * sizeof(int));  // cu | base | order
   l.fin = up(l.split + gdn::prefill_split_workspace(p.virtual_rows(), p.runs(), HV));
   l.starts = up(l.fin + (p.S > 1 ? (size_t)p.runs() * HV * kMat : 0));
   l.alt = up(l.starts + (size_t)(p.S - 1) * HV * kMat);
@@ -295,6 +303,8 @@ extern "C" int gdn_prefill_segmented_launch(
   p.rs = rs;
   p.src_rows = T;
   p.state_runs = 1;
+  p.ready_base = cu + 2 * kMaxSegments;
+  p.ready_order = plan.runs() > 1 ? cu + 4 * kMaxSegments : nullptr;
   if (S > 1) {
     p.vsplit = T;
     p.vsrc = b1;
@@ -309,7 +319,16 @@ extern "C" int gdn_prefill_segmented_launch(
   ro.n = plan.runs() + 1;
   for (int s = 0; s <= S; ++s) ro.v[s] = (int)plan.b[s];
   for (int s = 2; s <= S; ++s) ro.v[S + s - 1] = (int)(T + plan.b[s] - b1);
-  run_offsets_kernel<<<1, 128, 0, st>>>(ro, cu);
+  ro.base[0] = 0;
+  for (int r = 0; r < plan.runs(); ++r) {
+    ro.base[r + 1] = ro.base[r] + (ro.v[r + 1] - ro.v[r] + 63) / 64;
+    ro.order[r] = r;
+  }
+  // longest run first, ties by index (the order the library's device-side sort gives)
+  std::stable_sort(ro.order, ro.order + plan.runs(), [&](int x, int y) {
+    return ro.v[x + 1] - ro.v[x] > ro.v[y + 1] - ro.v[y];
+  });
+  run_offsets_kernel<<<1, 128, 0, st>>>(ro, cu, cu + 2 * kMaxSegments, cu + 4 * kMaxSegments);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   if (launch_prefill_split(p, st) != cudaSuccess) return GDN_ERR_LAUNCH;
   if (S == 1) return GDN_OK;

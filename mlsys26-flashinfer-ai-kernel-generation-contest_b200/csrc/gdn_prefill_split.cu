@@ -936,14 +936,18 @@ bool configure(uint32_t smem) {  // once per (kernel, device)
 
 template <bool L2, bool HS, typename CuT>
 cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                           const SplitParams& sp, long long slots, cudaStream_t s) {
+                           const SplitParams& sp, long long slots, bool base_ready,
+                           cudaStream_t s) {
   constexpr auto ka = split_prep_kernel<L2, CuT>;
   constexpr auto kb = split_state_kernel<HS, CuT>;
   if (!configure<ka>(prep::SMEM) || !configure<kb>(st::SMEM)) return cudaErrorInvalidValue;
-  chunk_base_kernel<CuT><<<1, 1024, 0, s>>>(static_cast<const CuT*>(sp.cu), sp.N, sp.T,
-                                            const_cast<int*>(sp.chunk_base));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  cudaError_t e;
+  if (!base_ready) {
+    chunk_base_kernel<CuT><<<1, 1024, 0, s>>>(static_cast<const CuT*>(sp.cu), sp.N, sp.T,
+                                              const_cast<int*>(sp.chunk_base));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   const int hpc = (sp.ratio % 2 == 0) ? 2 : 1;  // v-heads per preparation CTA
   ka<<<dim3((unsigned)(slots * (sp.HV / hpc))), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk,
                                                                                       sp);
@@ -957,11 +961,11 @@ cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const C
 template <typename CuT>
 cudaError_t launch_split_cu(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                             const SplitParams& sp, bool l2, bool hs, long long slots,
-                            cudaStream_t s) {
-  if (l2) return hs ? launch_split_t<true, true, CuT>(mq, mk, mv, sp, slots, s)
-                    : launch_split_t<true, false, CuT>(mq, mk, mv, sp, slots, s);
-  return hs ? launch_split_t<false, true, CuT>(mq, mk, mv, sp, slots, s)
-            : launch_split_t<false, false, CuT>(mq, mk, mv, sp, slots, s);
+                            bool base_ready, cudaStream_t s) {
+  if (l2) return hs ? launch_split_t<true, true, CuT>(mq, mk, mv, sp, slots, base_ready, s)
+                    : launch_split_t<true, false, CuT>(mq, mk, mv, sp, slots, base_ready, s);
+  return hs ? launch_split_t<false, true, CuT>(mq, mk, mv, sp, slots, base_ready, s)
+            : launch_split_t<false, false, CuT>(mq, mk, mv, sp, slots, base_ready, s);
 }
 
 }  // namespace
@@ -982,8 +986,8 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
       !make_tile_map_box(&mv, p.v, p.HV, rows, p.rs.v, st::kVB, false))
     return cudaErrorInvalidValue;
   uint8_t* ws = static_cast<uint8_t*>(p.workspace);
-  int* order = nullptr;
-  if (p.N > 1 && p.N <= kLptMaxSeqs) {
+  int* order = const_cast<int*>(p.ready_order);
+  if (order == nullptr && p.N > 1 && p.N <= kLptMaxSeqs) {
     order = reinterpret_cast<int*>(ws + lay.order);
     int P = 1;
     while (P < p.N) P <<= 1;
@@ -1002,7 +1006,8 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   SplitParams sp{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
                  p.A_log, p.dt_bias, p.cu, p.state, p.new_state,
                  static_cast<__nv_bfloat16*>(p.out), order,
-                 reinterpret_cast<const int*>(ws + lay.base), ws + lay.rec,
+                 p.ready_base ? p.ready_base : reinterpret_cast<const int*>(ws + lay.base),
+                 ws + lay.rec,
                  rec_bytes(p.l2norm), rec_lo_bytes(p.l2norm), p.T, p.N, p.HV, p.HV / p.HQ,
                  p.scale, p.gates_pre, p.g_alpha, p.g_beta, p.ckpt, p.ckpt_starts,
                  p.ckpt_capacity, p.ckpt_every};
@@ -1020,8 +1025,10 @@ cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
   const long long prep_slots =
       p.prep_runs < p.N ? std::min(lay.slots, (rows + kC - 1) / kC + p.prep_runs) : lay.slots;
   if (p.cu_int64)
-    return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots, s);
-  return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots, s);
+    return launch_split_cu<long long>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots,
+                                      p.ready_base != nullptr, s);
+  return launch_split_cu<int>(mq, mk, mv, sp, p.l2norm, p.state != nullptr, prep_slots,
+                              p.ready_base != nullptr, s);
 }
 
 unsigned read_split_device_error(bool clear) {

@@ -219,10 +219,10 @@ def segment_plan(total_tokens: int, num_v_heads: int, segments: int = 0, sms: in
 
 def segmented_launches(segments: int) -> int:
     """Number of this library's kernels one gdn_prefill_segmented call launches."""
-    if segments <= 1:  # run offsets, chunk offsets, preparation, state
-        return 4
-    # + longest-first order, state-map chain, outputs
-    return 7
+    if segments <= 1:  # run and chunk offsets, preparation, state
+        return 3
+    # + state-map chain, outputs
+    return 5
 
 
 def gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, scale, output=None,
