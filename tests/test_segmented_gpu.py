@@ -67,6 +67,7 @@ def test_planned_uneven_segments_equal_composed(cuda, hv):
     inp = pkg.workloads.prefill_inputs([T], hq=hv // 2, hv=hv, seed=hv)
     d = to(inp, cuda)
     o, s = native(pkg, d, 0)
+    o2, s2 = native(pkg, d, 0, bounds=bounds)   # the same plan given explicitly
     co, cs = composed(pkg, d, 0, bounds)
     ro, rs = pkg.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
                              d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"],
@@ -74,6 +75,7 @@ def test_planned_uneven_segments_equal_composed(cuda, hv):
     torch.cuda.synchronize()
     assert pkg.device_error() == 0
     assert torch.equal(o, co) and torch.equal(s, cs)
+    assert torch.equal(o2, o) and torch.equal(s2, s)
     assert_parity(o, s, ro.cpu(), rs.cpu(), what=f"planned segments hv={hv}")
 
 
