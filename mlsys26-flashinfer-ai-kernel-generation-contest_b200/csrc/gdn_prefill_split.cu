@@ -39,6 +39,8 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <climits>
+#include <cmath>
+#include <mutex>
 
 #include "gdn_chunk_math.cuh"
 #include "gdn_common.cuh"
@@ -109,6 +111,9 @@ struct SplitParams {
   // records: only runs n < prep_runs are prepared; an identity run (rows >= vsplit) reads
   // the records of run n - rec_alias (the same tokens, hence the same records)
   int prep_runs = INT_MAX, rec_alias = 0;
+  // an empty sequence passes its initial state through instead of ending at zero (the
+  // second piece of a pipelined call, whose tokens may all lie in the first piece)
+  bool empty_keeps_state = false;
 };
 
 // Input row of virtual token row r (a chunk never straddles vsplit).
@@ -161,6 +166,26 @@ __global__ void __launch_bounds__(1024) chunk_base_kernel(const CuT* __restrict_
     run += nch(i);
   }
   if (tid == 1023) base[N] = part[1023];
+}
+
+// Token and chunk offsets of the two pieces of a pipelined one-sequence call: piece 1 is
+// the sequence's first T1 tokens (or all of it), piece 2 the rest; out = [cu1 (2) | cu2 (2) |
+// base1 (2) | base2 (2)].
+template <typename CuT>
+__global__ void piece_offsets_kernel(const CuT* __restrict__ cu, long long T, long long T1,
+                                     int* __restrict__ out) {
+  if (threadIdx.x != 0) return;
+  const long long c1 = min(max((long long)cu[1], 0LL), T);
+  const long long c0 = min(max((long long)cu[0], 0LL), c1);
+  const long long m = min(c0 + T1, c1);
+  out[0] = (int)c0;
+  out[1] = (int)m;
+  out[2] = (int)m;
+  out[3] = (int)c1;
+  out[4] = 0;
+  out[5] = (int)((m - c0 + kC - 1) / kC);
+  out[6] = 0;
+  out[7] = (int)((c1 - m + kC - 1) / kC);
 }
 
 // ============================================================ preparation kernel
@@ -600,8 +625,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
   float* ns = p.new_state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
   if (L <= 0) {  // empty sequence: zero final state (definition semantics)
     if (tid < kCompute) {
+      const float* src = p.state + ((size_t)n * HV + h) * kHeadDim * kHeadDim;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ns[(size_t)(v_lo + i) * kHeadDim + row] = 0.f;
+      for (int i = 0; i < 8; ++i)
+        ns[(size_t)(v_lo + i) * kHeadDim + row] =
+            (HAS_STATE && p.empty_keeps_state) ? src[(size_t)(v_lo + i) * kHeadDim + row] : 0.f;
     }
     return;
   }
@@ -934,6 +962,116 @@ bool configure(uint32_t smem) {  // once per (kernel, device)
   return true;
 }
 
+// ------------------------------------------------------------ pipelined one-sequence call
+// One sequence whose state kernel leaves SMs idle (4 CTAs per v-head: 128 of 148 SMs for 32
+// v-heads) runs as two pieces with the state carried between them, so that the second
+// piece's preparation kernel runs on the idle SMs while the first piece's state kernel runs:
+//   stream s:    offsets | prep(piece 1, whole GPU) | state(piece 1) ...... | state(piece 2)
+//   side stream:                                    | prep(piece 2, idle SMs) |
+// The state kernels launch at the highest stream priority and the side preparation at the
+// lowest, so that the state kernel's CTAs take their SMs first.  The pieces meet on a
+// 64-token chunk boundary and piece 1's fp32 final state is piece 2's initial state, so the
+// results equal the one-piece call's bit for bit.  Piece 1's length balances its state
+// kernel against piece 2's preparation on the idle SMs (measured on B200: ~2.15 us per
+// state chunk step; ~16.3 us per preparation CTA at three per SM).
+constexpr double kStateChunkUs = 2.15, kPrepCtaUs = 16.3;
+
+size_t pipe_workspace(long long T, int HV) {
+  // offsets | carried state | piece-1 layout | piece-2 layout (each 1024-aligned)
+  const auto up = [](size_t x) { return (x + 1023) / 1024 * 1024; };
+  return 1024 + up((size_t)HV * kHeadDim * kHeadDim * sizeof(float)) +
+         up(split_layout(T, 1, HV).total) + (size_t)HV * kRecBytesMax + 2048;
+}
+
+struct PipeRes {
+  bool tried = false, ok = false;
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  int prio_hi = 0, prio_lo = 0, sms = 0;
+};
+std::mutex g_pipe_mu;
+
+// The side stream and events of the current device, created on its first pipelined call
+// (null if they could not be created: the call then runs unpipelined).
+PipeRes* pipe_res() {
+  static PipeRes res[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  PipeRes& r = res[dev];
+  if (!r.tried) {
+    r.tried = true;
+    int least = 0, greatest = 0;
+    r.ok = cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess &&
+           cudaDeviceGetAttribute(&r.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+           cudaStreamCreateWithPriority(&r.side, cudaStreamNonBlocking, least) == cudaSuccess &&
+           cudaEventCreateWithFlags(&r.fork, cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&r.join, cudaEventDisableTiming) == cudaSuccess;
+    r.prio_hi = greatest;
+    r.prio_lo = least;
+  }
+  return r.ok ? &r : nullptr;
+}
+
+// Tokens of piece 1 (a multiple of 64), or 0 when the call should not be pipelined.
+long long pipe_split(const PrefillArgs& p, int sms) {
+  if (p.N != 1 || p.ckpt != nullptr || p.vsplit != LLONG_MAX || p.ready_base != nullptr ||
+      p.ready_order != nullptr || p.src_rows > 0)
+    return 0;
+  const long long chunks = (p.T + kC - 1) / kC;
+  const int idle = sms - p.HV * st::kSplitV;
+  if (chunks < 64 || idle < 8) return 0;
+  const int hpc = (p.HV / p.HQ) % 2 == 0 ? 2 : 1;
+  const double prep_idle_us = (double)(p.HV / hpc) * kPrepCtaUs / (3.0 * idle);  // per chunk
+  const double r = prep_idle_us / kStateChunkUs;
+  const long long m = (long long)std::llround((double)chunks * r / (1.0 + r));
+  if (m < 16 || m > chunks - 16) return 0;
+  return kC * m;
+}
+
+template <auto kern, typename... Args>
+cudaError_t launch_prio(dim3 grid, dim3 block, uint32_t smem, cudaStream_t s, int prio,
+                        Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributePriority;
+  attr[0].val.priority = prio;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <bool L2, bool HS>
+cudaError_t launch_pipe_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                          const SplitParams& sp1, const SplitParams& sp2, long long slots1,
+                          long long slots2, const PipeRes& r, cudaStream_t s) {
+  constexpr auto ka = split_prep_kernel<L2, int>;
+  constexpr auto kb1 = split_state_kernel<HS, int>;
+  constexpr auto kb2 = split_state_kernel<true, int>;  // starts from piece 1's state
+  if (!configure<ka>(prep::SMEM) || !configure<kb1>(st::SMEM) || !configure<kb2>(st::SMEM))
+    return cudaErrorInvalidValue;
+  const int hpc = (sp1.ratio % 2 == 0) ? 2 : 1;
+  const dim3 sgrid((unsigned)(sp1.HV * st::kSplitV));
+  cudaError_t e;
+  ka<<<dim3((unsigned)(slots1 * (sp1.HV / hpc))), dim3(prep::kThreads), prep::SMEM, s>>>(mq, mk,
+                                                                                        sp1);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = cudaEventRecord(r.fork, s)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(r.side, r.fork, 0)) != cudaSuccess) return e;
+  if ((e = launch_prio<kb1>(sgrid, dim3(st::kThreads), st::SMEM, s, r.prio_hi, mq, mk, mv,
+                            sp1)) != cudaSuccess)
+    return e;
+  if ((e = launch_prio<ka>(dim3((unsigned)(slots2 * (sp2.HV / hpc))), dim3(prep::kThreads),
+                           prep::SMEM, r.side, r.prio_lo, mq, mk, sp2)) != cudaSuccess)
+    return e;
+  if ((e = cudaEventRecord(r.join, r.side)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(s, r.join, 0)) != cudaSuccess) return e;
+  return launch_prio<kb2>(sgrid, dim3(st::kThreads), st::SMEM, s, r.prio_hi, mq, mk, mv, sp2);
+}
+
 template <bool L2, bool HS, typename CuT>
 cudaError_t launch_split_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                            const SplitParams& sp, long long slots, bool base_ready,
@@ -972,10 +1110,64 @@ cudaError_t launch_split_cu(const CUtensorMap& mq, const CUtensorMap& mk, const 
 
 size_t prefill_split_workspace(long long T, int num_seqs, int HV) {
   if (T <= 0 || num_seqs <= 0) return 0;
+  if (num_seqs == 1) return pipe_workspace(T, HV);  // room for a pipelined call
   return split_layout(T, num_seqs, HV).total;
 }
 
+namespace {
+template <typename CuT>
+cudaError_t launch_prefill_split_piped(const PrefillArgs& p, long long T1, const PipeRes& r,
+                                       cudaStream_t s) {
+  const auto up = [](size_t x) { return (x + 1023) / 1024 * 1024; };
+  if (p.workspace == nullptr || p.workspace_bytes < pipe_workspace(p.T, p.HV))
+    return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv;
+  if (!make_tile_map(&mq, p.q, p.HQ, p.T, p.rs.q) || !make_tile_map(&mk, p.k, p.HQ, p.T, p.rs.k) ||
+      !make_tile_map_box(&mv, p.v, p.HV, p.T, p.rs.v, st::kVB, false))
+    return cudaErrorInvalidValue;
+  uint8_t* ws = static_cast<uint8_t*>(p.workspace);
+  int* offs = reinterpret_cast<int*>(ws);  // cu1 | cu2 | base1 | base2
+  float* carried = reinterpret_cast<float*>(ws + 1024);  // piece 1's final state
+  uint8_t* w1 = ws + 1024 + up((size_t)p.HV * kHeadDim * kHeadDim * sizeof(float));
+  const SplitLayout l1 = split_layout(T1, 1, p.HV), l2 = split_layout(p.T - T1, 1, p.HV);
+  uint8_t* w2 = w1 + up(l1.total);
+  if ((size_t)(w2 - ws) + l2.total > p.workspace_bytes) return cudaErrorInvalidValue;
+  piece_offsets_kernel<CuT><<<1, 32, 0, s>>>(static_cast<const CuT*>(p.cu), p.T, T1, offs);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  SplitParams sp1{static_cast<const __nv_bfloat16*>(p.a), static_cast<const __nv_bfloat16*>(p.b),
+                  p.A_log, p.dt_bias, offs, p.state, carried,
+                  static_cast<__nv_bfloat16*>(p.out), nullptr, offs + 4, w1 + l1.rec,
+                  rec_bytes(p.l2norm), rec_lo_bytes(p.l2norm), p.T, 1, p.HV, p.HV / p.HQ,
+                  p.scale, p.gates_pre, p.g_alpha, p.g_beta, nullptr, nullptr, 0, 0};
+  sp1.a_rs = p.rs.a;
+  sp1.b_rs = p.rs.b;
+  sp1.o_rs = p.rs.o;
+  SplitParams sp2 = sp1;
+  sp2.cu = offs + 2;
+  sp2.state = carried;
+  sp2.new_state = p.new_state;
+  sp2.chunk_base = offs + 6;
+  sp2.rec = w2 + l2.rec;
+  sp2.empty_keeps_state = true;
+  const long long slots1 = T1 / kC + 1, slots2 = (p.T - T1 + kC - 1) / kC + 1;
+  std::lock_guard<std::mutex> g(g_pipe_mu);  // the side stream and events serve one call at a time
+  const bool hs = p.state != nullptr;
+  if (p.l2norm) return hs ? launch_pipe_t<true, true>(mq, mk, mv, sp1, sp2, slots1, slots2, r, s)
+                          : launch_pipe_t<true, false>(mq, mk, mv, sp1, sp2, slots1, slots2, r, s);
+  return hs ? launch_pipe_t<false, true>(mq, mk, mv, sp1, sp2, slots1, slots2, r, s)
+            : launch_pipe_t<false, false>(mq, mk, mv, sp1, sp2, slots1, slots2, r, s);
+}
+}  // namespace
+
 cudaError_t launch_prefill_split(const PrefillArgs& p, cudaStream_t s) {
+  if (p.N == 1 && p.ckpt == nullptr && p.vsplit == LLONG_MAX && p.ready_base == nullptr) {
+    const PipeRes* r = pipe_res();
+    const long long T1 = r != nullptr ? pipe_split(p, r->sms) : 0;
+    if (T1 > 0)
+      return p.cu_int64 ? launch_prefill_split_piped<long long>(p, T1, *r, s)
+                        : launch_prefill_split_piped<int>(p, T1, *r, s);
+  }
   const SplitLayout lay = split_layout(p.T, p.N, p.HV);
   if (p.workspace == nullptr || p.workspace_bytes < lay.total) return cudaErrorInvalidValue;
   if (lay.slots * p.HV > 0x7fffffffLL || (long long)p.N * p.HV * st::kSplitV > 0x7fffffffLL)
