@@ -178,6 +178,11 @@ size_t gdn_prefill_workspace_size(int total_tokens, int num_seqs, int num_q_head
  *              must not be shared by calls that overlap on the GPU.
  * A sequence of length 0 gets an all-zero new_state slice (as the
  * flashinfer-bench definition reference does).
+ * One long sequence over few v-heads (split kernels, at least 64 chunks, SMs left idle by
+ * the state kernel) runs in two pieces, the second piece's preparation on a library-owned
+ * side stream overlapping the first piece's state kernel; `stream` waits for it before the
+ * call's last kernel (event fork / join).  The first such call on a device creates that
+ * side stream and two events: make it before capturing the stream into a CUDA graph.
  * Replaces gdn_prefill_chunk_kernel (gdn_prefill/solution/triton/kernel.py:28-250)
  * and its host wrapper's zero-fill / state copy passes (:281-299).
  */
