@@ -998,6 +998,7 @@ PipeRes* pipe_res() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   PipeRes& r = res[dev];
+  std::lock_guard<std::mutex> g(g_pipe_mu);
   if (!r.tried) {
     r.tried = true;
     int least = 0, greatest = 0;
